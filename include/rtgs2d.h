@@ -1,0 +1,188 @@
+/*
+ * rtgs2d -- B200 (sm_100a) Stage-1 2D gaussian splatting: C ABI.
+ *
+ * Plain C: device pointers, sizes and a CUDA stream passed as `void*` (a cudaStream_t; NULL is the
+ * legacy default stream). Every function returns RTGS2D_OK (0) or a negative RTGS2D_ERR_* code;
+ * rtgs2d_last_error() then returns a message (thread-local, valid until the next call on the same
+ * thread). Functions act on the calling thread's current CUDA device. Unless stated otherwise
+ * a call enqueues its work on `stream` and returns; calls that must read a device-side count
+ * back to the host (the tile-entry count of a render) synchronise `stream` once.
+ *
+ * Array layouts follow the reference Python API (src/rtgs/image2gs/renderer2d.py:72-125):
+ *   xy (M,2), chol (M,3) = (l11, l21, l22), color (M,3), weight (M,) float32, contiguous;
+ *   images (B,H,W,3) and densities (B,H,W) float32, channel-last. In the batched entry points
+ *   M = B*N and gaussian i belongs to view i / N.
+ *
+ * Results are deterministic: per-tile lists are in ascending gaussian index and gradients are
+ * reduced in a fixed order, so repeated calls on the same inputs return identical bits.
+ */
+#ifndef RTGS2D_H_
+#define RTGS2D_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define RTGS2D_API __attribute__((visibility("default")))
+#else
+#define RTGS2D_API
+#endif
+
+#define RTGS2D_ABI_VERSION 1
+
+#define RTGS2D_OK 0
+#define RTGS2D_ERR_INVALID (-1)  /* bad argument (shape, size, null pointer, wrong device) */
+#define RTGS2D_ERR_CUDA (-2)     /* a CUDA runtime call or kernel launch failed */
+#define RTGS2D_ERR_ALLOC (-3)    /* device or pinned allocation failed */
+#define RTGS2D_ERR_CAPACITY (-4) /* problem larger than the 32-bit entry indexing supports */
+
+/* No reference counterpart: version and error string of this library. */
+RTGS2D_API int rtgs2d_abi_version(void);
+RTGS2D_API const char* rtgs2d_last_error(void);
+
+/*
+ * Scratch arena: owns the growable device buffers that projection, tile binning and the raster
+ * kernels need (records, tile entries, sort buffers, per-entry gradient moments). One arena
+ * serves one device; it grows on demand (cudaMalloc) and is reused across calls. Not safe for
+ * concurrent use from two host threads. Replaces the per-call torch::zeros allocations of the
+ * reference extension (src/rtgs/image2gs/cuda/renderer2d_ext.cu:198-199,234-237).
+ */
+typedef struct rtgs2d_arena rtgs2d_arena;
+RTGS2D_API int rtgs2d_arena_create(rtgs2d_arena** out);
+RTGS2D_API int rtgs2d_arena_destroy(rtgs2d_arena* arena);
+/* Entries ((gaussian, tile) pairs) and pixel pairs of the last render/backward on this arena. */
+RTGS2D_API int rtgs2d_arena_last_stats(const rtgs2d_arena* arena, int64_t* entries, int64_t* pairs);
+
+/*
+ * Reference ABI, forward. Replaces the pybind `forward` of
+ * src/rtgs/image2gs/cuda/renderer2d_ext.cpp:87-101 (kernel renderer2d_ext.cu:26-85,186-218):
+ *   xy (M,2), conics (M,3) = Sigma^-1 entries (i00, i01, i11), colors (M,3), weights (M,)
+ *   float32; rects (M,4) int32 (x0, x1, y0, y1) inclusive pixel bounds, x1 < x0 when empty;
+ *   view_index (M,) int32 in [0, n_views). Writes out (n_views,H,W,3) and, if den != NULL,
+ *   den (n_views,H,W); every element is written (no pre-zeroing needed). A pair contributes
+ *   exp(-q/2)*weight*color only if q < cutoff; non-finite means are dropped.
+ */
+RTGS2D_API int rtgs2d_forward(rtgs2d_arena* arena, const float* xy, const float* conics, const float* colors,
+                   const float* weights, const int32_t* rects, const int32_t* view_index,
+                   int64_t m, int64_t n_views, int64_t height, int64_t width, double cutoff,
+                   float* out, float* den, void* stream);
+
+/*
+ * Reference ABI, backward. Replaces the pybind `backward` of
+ * src/rtgs/image2gs/cuda/renderer2d_ext.cpp:103-128 (kernel renderer2d_ext.cu:87-182,220-260).
+ * grad_out (n_views,H,W,3) and grad_den (n_views,H,W) may be NULL (treated as zeros). Writes
+ * grad_xy (M,2), grad_conics (M,3) (dL/d(i00, i01, i11) with q = i00 dx^2 + 2 i01 dx dy + i11 dy^2),
+ * grad_colors (M,3), grad_weights (M,).
+ */
+RTGS2D_API int rtgs2d_backward(rtgs2d_arena* arena, const float* grad_out, const float* grad_den,
+                    const float* xy, const float* conics, const float* colors,
+                    const float* weights, const int32_t* rects, const int32_t* view_index,
+                    int64_t m, int64_t n_views, int64_t height, int64_t width, double cutoff,
+                    float* grad_xy, float* grad_conics, float* grad_colors, float* grad_weights,
+                    void* stream);
+
+/*
+ * Batched render from Cholesky factors. Replaces
+ * src/rtgs/image2gs/cuda_backend.py:127-170 `render_batched_cuda` (which built conics and support
+ * rectangles with torch ops before calling the extension): conics, rectangles
+ * (renderer2d.py:156-181, bit-exact) and tile binning are computed on the device.
+ * xy (B*N,2), chol (B*N,3), color (B*N,3), weight (B*N,). Writes out (B,H,W,3) and, if den is
+ * not NULL, den (B,H,W).
+ */
+RTGS2D_API int rtgs2d_render_forward(rtgs2d_arena* arena, const float* xy, const float* chol,
+                          const float* color, const float* weight, int64_t n_views, int64_t n,
+                          int64_t height, int64_t width, float* out, float* den, void* stream);
+
+/*
+ * Gradients of rtgs2d_render_forward with respect to xy, chol, color and weight (the autograd
+ * path of cuda_backend.py:87-124 plus the conic -> Cholesky chain rule of gaussians2d.py:34-44).
+ * grad_out / grad_den may be NULL (zeros). Any output pointer may be NULL to skip it.
+ */
+RTGS2D_API int rtgs2d_render_backward(rtgs2d_arena* arena, const float* grad_out, const float* grad_den,
+                           const float* xy, const float* chol, const float* color,
+                           const float* weight, int64_t n_views, int64_t n, int64_t height,
+                           int64_t width, float* grad_xy, float* grad_chol, float* grad_color,
+                           float* grad_weight, void* stream);
+
+/*
+ * Support rectangles on the device, bit-exact with src/rtgs/image2gs/renderer2d.py:156-181 and in
+ * the rectangle convention of src/rtgs/image2gs/cuda_backend.py:153-158: rects (M,4) int32
+ * (x0, x1, y0, y1) with x1 = x0 - 1 when the support is empty, counts (M,) int64 pixels inside.
+ * Either output may be NULL.
+ */
+RTGS2D_API int rtgs2d_support_rects(const float* xy, const float* chol, int64_t m, int64_t height,
+                                    int64_t width, int32_t* rects, int64_t* counts, void* stream);
+
+/*
+ * No reference counterpart (the reference has no binning): copies the tile binning of the last
+ * render/backward on `arena` to HOST memory -- gids (entries,) uint32 gaussian ids grouped by
+ * tile, ascending inside a tile, and ranges (n_tiles, 2) int32 [start, end). Copies at most
+ * max_entries ids and max_tiles ranges; reports the full sizes. Synchronises `stream`.
+ */
+RTGS2D_API int rtgs2d_arena_copy_binning(const rtgs2d_arena* arena, int64_t max_entries,
+                                         uint32_t* gids, int64_t max_tiles, int32_t* ranges,
+                                         int64_t* n_entries, int64_t* n_tiles, void* stream);
+
+/*
+ * Fit engine: the native Stage-1 fit loop on the device (fit.py:355-554 for one image,
+ * batched.py:39-170 for stacked views). Each iteration runs projection from the raw parameters,
+ * tile binning, one fused forward + L2-loss-gradient + backward raster kernel and one fused
+ * chain-rule + Adam kernel; the host only advances the cosine learning rate
+ * (CosineAnnealingLR(T_max=iterations, eta_min=0.1*lr), fit.py:419-422).
+ */
+typedef struct rtgs2d_fit rtgs2d_fit;
+
+#define RTGS2D_LOSS_MSE 0          /* sum over views of per-view MSE (fit.py:561, batched.py:142) */
+#define RTGS2D_LOSS_MASK_WEIGHTED 1 /* mean((r-t)^2 * (0.1 + 0.9 mask)) per view (fit.py:562-563) */
+#define RTGS2D_LOSS_MASK_ONLY 2    /* squared error over mask pixels / (3 * mask pixels) per view */
+
+typedef struct rtgs2d_fit_options {
+  double lr;               /* Adam learning rate (FitConfig.lr, default 1e-2) */
+  int64_t iterations;      /* cosine schedule length T_max (FitConfig.iterations) */
+  int64_t log_every;       /* record loss sums at it % log_every == 0 and at the last iteration */
+  int64_t check_every;     /* also record at (it + 1) % check_every == 0 (0: never) */
+  int32_t freeze_geometry; /* nonzero: only color/weight are optimised (FitConfig.freeze_geometry) */
+  int32_t loss_mode;       /* RTGS2D_LOSS_* */
+} rtgs2d_fit_options;
+
+RTGS2D_API int rtgs2d_fit_create(int64_t n_views, int64_t n, int64_t height, int64_t width,
+                      const rtgs2d_fit_options* options, rtgs2d_fit** out);
+RTGS2D_API int rtgs2d_fit_destroy(rtgs2d_fit* fit);
+/* targets (B,H,W,3) float32 (copied); mask_bits (B, ceil(H*W/8)) uint8 little-endian bit order
+ * (numpy packbits(bitorder="little") of the row-major mask), required for the mask loss modes.
+ * Synchronises `stream` (per-view mask pixel counts are read back). */
+RTGS2D_API int rtgs2d_fit_set_targets(rtgs2d_fit* fit, const float* targets, const uint8_t* mask_bits,
+                           void* stream);
+/* Raw (unconstrained) parameters in the reference layout: xy_raw (B,N,2), diag_raw (B,N,2),
+ * off_raw (B,N), color_raw (B,N,3), weight_raw (B,N) (fit.py:375-380). Resets the Adam state
+ * and the iteration counter. */
+RTGS2D_API int rtgs2d_fit_set_raw(rtgs2d_fit* fit, const float* xy_raw, const float* diag_raw,
+                       const float* off_raw, const float* color_raw, const float* weight_raw,
+                       void* stream);
+/* Runs `n_iterations` more iterations (capped at `iterations`). Synchronises `stream`. */
+RTGS2D_API int rtgs2d_fit_run(rtgs2d_fit* fit, int64_t n_iterations, void* stream);
+RTGS2D_API int rtgs2d_fit_get_raw(rtgs2d_fit* fit, float* xy_raw, float* diag_raw, float* off_raw,
+                       float* color_raw, float* weight_raw, void* stream);
+/* Constrained parameters (build(), fit.py:402-417): xy (B,N,2), chol (B,N,3), color (B,N,3),
+ * weight (B,N). */
+RTGS2D_API int rtgs2d_fit_get_params(rtgs2d_fit* fit, float* xy, float* chol, float* color, float* weight,
+                          void* stream);
+/* Renders the current parameters; writes render (B,H,W,3) if not NULL and the per-view loss and
+ * clamped-PSNR numerators to host sums (B,2). Synchronises `stream`. */
+RTGS2D_API int rtgs2d_fit_evaluate(rtgs2d_fit* fit, float* render, double* sums, void* stream);
+/* Recorded loss sums: copies up to max_rows rows; iters (rows,), sums (rows,B,2) on the host. */
+RTGS2D_API int rtgs2d_fit_history(const rtgs2d_fit* fit, int64_t max_rows, int64_t* iters, double* sums,
+                       int64_t* n_rows);
+/* Completed iterations, entries/pairs of the last iteration, pairs summed over all iterations. */
+RTGS2D_API int rtgs2d_fit_stats(const rtgs2d_fit* fit, int64_t* step, int64_t* last_entries,
+                     int64_t* last_pairs, double* total_pairs);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RTGS2D_H_ */

@@ -1,0 +1,140 @@
+"""CPU oracle: the native Stage-1 fit loop, restated from the reference.
+
+TEST INFRASTRUCTURE ONLY -- imported by tests/, __graft_entry__.smoke() and bench.py's CPU
+baseline leg; never by the product package.
+
+Restated reference behaviour (paths relative to the reference project):
+  - raw reparameterisation and its inverse   src/rtgs/image2gs/fit.py:374-417
+  - torch Adam + CosineAnnealingLR(eta_min=0.1*lr)   src/rtgs/image2gs/fit.py:419-422
+  - loop: zero_grad, build, render, MSE, backward, step, sched, PSNR log   fit.py:451-540
+  - final render and PSNR                    src/rtgs/image2gs/fit.py:542-554
+  - stacked multi-view loop, loss = sum_b mean_b   src/rtgs/image2gs/batched.py:79-170
+  - psnr                                     src/rtgs/core/metrics.py:12-15
+The renderer is ``oracle.render2d`` (the reference's pure-PyTorch scatter renderer, restated).
+A mask-restricted loss (mean over mask pixels x 3 channels, the denominator of
+``masked_psnr`` in src/rtgs/core/metrics.py:18-29) is provided for the masked batched workload,
+which the reference's batched path does not implement (batched.py:55-56 rejects masks).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from oracle import render2d
+
+MIN_DIAG = 0.3
+
+
+def softplus_inv(x: torch.Tensor) -> torch.Tensor:
+    return x + torch.log(-torch.expm1(-x))
+
+
+def to_raw(xy, chol, color, weight, height: int, width: int) -> dict[str, torch.Tensor]:
+    """Raw (unconstrained) parameters from constrained ones (fit.py:375-380); works on (..., k)."""
+    wh = xy.new_tensor([width, height])
+    return {
+        "xy_raw": torch.logit((xy / wh).clamp(1e-4, 1 - 1e-4)),
+        "diag_raw": softplus_inv(chol[..., [0, 2]] - MIN_DIAG),
+        "off_raw": chol[..., 1].clone(),
+        "color_raw": torch.logit(color.clamp(1e-3, 1 - 1e-3)),
+        "weight_raw": torch.logit(weight.clamp(1e-3, 1 - 1e-3)),
+    }
+
+
+def build(raw: dict[str, torch.Tensor], height: int, width: int):
+    """Constrained (xy, chol, color, weight) from raw parameters (fit.py:402-417)."""
+    wh = raw["xy_raw"].new_tensor([width, height])
+    diag = torch.nn.functional.softplus(raw["diag_raw"]) + MIN_DIAG
+    chol = torch.stack([diag[..., 0], raw["off_raw"], diag[..., 1]], dim=-1)
+    return (
+        torch.sigmoid(raw["xy_raw"]) * wh,
+        chol,
+        torch.sigmoid(raw["color_raw"]),
+        torch.sigmoid(raw["weight_raw"]),
+    )
+
+
+def psnr(pred: torch.Tensor, target: torch.Tensor) -> float:
+    mse = torch.nn.functional.mse_loss(pred, target).clamp_min(1e-12)
+    return float(-10.0 * torch.log10(mse))
+
+
+def masked_psnr(pred: torch.Tensor, target: torch.Tensor, mask: torch.Tensor) -> float:
+    w = mask.to(pred).clamp(0, 1)
+    mse = (((pred - target) ** 2) * w[..., None]).sum() / (w.sum() * pred.shape[-1])
+    return float(-10.0 * torch.log10(mse.clamp_min(1e-12)))
+
+
+def fit_views(
+    targets: torch.Tensor,
+    init: tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor],
+    iterations: int,
+    lr: float = 1e-2,
+    log_every: int = 50,
+    masks: torch.Tensor | None = None,
+    freeze_geometry: bool = False,
+):
+    """Fit stacked (B, H, W, 3) targets from a stacked (B, N, .) initialisation.
+
+    Returns (params (xy, chol, color, weight) stacked, histories). With B == 1 and no mask this is
+    the single-image native fit (the per-view MSE mean is the serial loss); with a (B, H, W) mask
+    the loss is the mask-restricted mean and PSNR is ``masked_psnr``.
+    """
+    n_views, height, width = targets.shape[:3]
+    xy0, chol0, color0, weight0 = init
+    raw = to_raw(xy0, chol0, color0, weight0, height, width)
+    names = ("color_raw", "weight_raw") if freeze_geometry else tuple(raw)
+    for name, value in raw.items():
+        value.requires_grad_(name in names)
+    params = [raw[n] for n in names]
+    opt = torch.optim.Adam(params, lr=lr)
+    sched = torch.optim.lr_scheduler.CosineAnnealingLR(opt, T_max=iterations, eta_min=lr * 0.1)
+    hist = [{"psnr": [], "stopped_iter": iterations - 1} for _ in range(n_views)]
+    if masks is not None:
+        mw = masks.to(targets).clamp(0, 1)
+        denom = mw.sum(dim=(1, 2)) * 3.0
+
+    def loss_and_log(rendered, it, log):
+        if masks is None:
+            loss = (rendered - targets).square().mean(dim=(1, 2, 3)).sum()
+        else:
+            loss = (((rendered - targets) ** 2) * mw[..., None]).sum(dim=(1, 2, 3)).div(denom).sum()
+        if log:
+            with torch.no_grad():
+                for b in range(n_views):
+                    pred = rendered[b].clamp(0, 1)
+                    val = psnr(pred, targets[b]) if masks is None else masked_psnr(pred, targets[b], masks[b])
+                    hist[b]["psnr"].append((it, val))
+        return loss
+
+    for it in range(iterations):
+        opt.zero_grad()
+        xy, chol, color, weight = build(raw, height, width)
+        rendered = render2d.render_batched(xy, chol, color, weight, height, width)
+        log = it % log_every == 0 or it == iterations - 1
+        loss = loss_and_log(rendered, it, log)
+        loss.backward()
+        opt.step()
+        sched.step()
+    with torch.no_grad():
+        xy, chol, color, weight = build(raw, height, width)
+        final = render2d.render_batched(xy, chol, color, weight, height, width)
+        for b in range(n_views):
+            pred = final[b].clamp(0, 1)
+            full = psnr(pred, targets[b])
+            hist[b]["final_psnr_full"] = full
+            hist[b]["final_psnr"] = full if masks is None else masked_psnr(pred, targets[b], masks[b])
+    return (xy, chol, color, weight), hist
+
+
+def adam_first_step(raw: torch.Tensor, grad: torch.Tensor, lr: float) -> torch.Tensor:
+    """Closed form of torch Adam's first update (bias-corrected; betas 0.9/0.999, eps 1e-8).
+
+    Mirrors the reference's own pin of the first update (tests/test_stage1_fit_seam.py:239-254).
+    """
+    beta1, beta2, eps = 0.9, 0.999, 1e-8
+    exp_avg = (1 - beta1) * grad
+    exp_avg_sq = (1 - beta2) * grad * grad
+    step_size = lr / (1.0 - beta1)
+    denom = exp_avg_sq.sqrt() / (1.0 - beta2) ** 0.5 + eps
+    return raw - step_size * exp_avg / denom

@@ -1,0 +1,288 @@
+// C ABI: error handling, device buffers, scratch arena and the render entry points.
+#include <cmath>
+#include <cstdio>
+#include <new>
+#include <string>
+
+#include "../../include/rtgs2d.h"
+#include "internal.h"
+
+namespace rtgs2d {
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+int set_error(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int check_cuda(cudaError_t err, const char* what) {
+  if (err == cudaSuccess) return 0;
+  const int code = (err == cudaErrorMemoryAllocation) ? RTGS2D_ERR_ALLOC : RTGS2D_ERR_CUDA;
+  return set_error(code, std::string(what) + ": " + cudaGetErrorName(err) + " (" +
+                             cudaGetErrorString(err) + ")");
+}
+
+int DevBuf::ensure(size_t need, cudaStream_t stream) {
+  if (need <= bytes && ptr != nullptr) return 0;
+  if (ptr != nullptr) {
+    // Queued kernels may still read the old allocation.
+    RTGS_CUDA(cudaStreamSynchronize(stream), "sync before buffer growth");
+    cudaFree(ptr);
+    ptr = nullptr;
+    bytes = 0;
+  }
+  size_t grow = need + need / 4;  // headroom so slowly growing workloads do not reallocate often
+  grow = (grow + 255) & ~static_cast<size_t>(255);
+  if (grow == 0) grow = 256;
+  RTGS_CUDA(cudaMalloc(&ptr, grow), "cudaMalloc");
+  bytes = grow;
+  return 0;
+}
+
+void DevBuf::release() {
+  if (ptr) cudaFree(ptr);
+  ptr = nullptr;
+  bytes = 0;
+}
+
+void BinBuffers::release() {
+  for (DevBuf* b : {&records, &weights, &spans, &counts, &offsets, &keys[0], &keys[1], &vals[0],
+                    &vals[1], &ranges, &partials, &partial_d, &cub_temp, &stats}) {
+    b->release();
+  }
+  if (host_stats) cudaFreeHost(host_stats);
+  host_stats = nullptr;
+}
+
+BinBuffers::~BinBuffers() { release(); }
+
+}  // namespace rtgs2d
+
+using namespace rtgs2d;
+
+struct rtgs2d_arena {
+  int device = 0;
+  BinBuffers bb;
+  int64_t n_tiles = 0;  // tiles of the last binning
+};
+
+namespace {
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+int check_arena(const rtgs2d_arena* a) {
+  if (!a) return set_error(RTGS2D_ERR_INVALID, "arena is NULL");
+  int dev = -1;
+  RTGS_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev != a->device) {
+    return set_error(RTGS2D_ERR_INVALID, "arena was created on device " + std::to_string(a->device) +
+                                             " but the current device is " + std::to_string(dev));
+  }
+  return 0;
+}
+
+int check_dims(int64_t m, int64_t n_views, int64_t height, int64_t width) {
+  if (m < 0) return set_error(RTGS2D_ERR_INVALID, "number of gaussians must be non-negative");
+  if (n_views <= 0) return set_error(RTGS2D_ERR_INVALID, "n_views must be positive");
+  if (height <= 0 || width <= 0) {
+    return set_error(RTGS2D_ERR_INVALID, "height and width must be positive");
+  }
+  if (height > 32768 || width > 32768) {
+    return set_error(RTGS2D_ERR_CAPACITY, "height and width must be at most 32768");
+  }
+  const int64_t tiles = n_views * ((height + kTile - 1) / kTile) * ((width + kTile - 1) / kTile);
+  if (tiles > INT32_MAX) return set_error(RTGS2D_ERR_CAPACITY, "too many tiles (views x tiles)");
+  if (m > INT32_MAX) return set_error(RTGS2D_ERR_CAPACITY, "more than 2^31 gaussians");
+  return 0;
+}
+
+int require(const void* p, const char* name) {
+  if (p == nullptr) return set_error(RTGS2D_ERR_INVALID, std::string(name) + " is NULL");
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int rtgs2d_abi_version(void) { return RTGS2D_ABI_VERSION; }
+
+const char* rtgs2d_last_error(void) { return rtgs2d::g_last_error.c_str(); }
+
+int rtgs2d_arena_create(rtgs2d_arena** out) {
+  if (!out) return set_error(RTGS2D_ERR_INVALID, "out is NULL");
+  *out = nullptr;
+  int dev = 0;
+  RTGS_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  rtgs2d_arena* a = new (std::nothrow) rtgs2d_arena();
+  if (!a) return set_error(RTGS2D_ERR_ALLOC, "host allocation failed");
+  a->device = dev;
+  *out = a;
+  return RTGS2D_OK;
+}
+
+int rtgs2d_arena_destroy(rtgs2d_arena* arena) {
+  if (!arena) return RTGS2D_OK;
+  const int dev = arena->device;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (prev != dev) cudaSetDevice(dev);
+  delete arena;
+  if (prev != dev) cudaSetDevice(prev);
+  return RTGS2D_OK;
+}
+
+int rtgs2d_arena_last_stats(const rtgs2d_arena* arena, int64_t* entries, int64_t* pairs) {
+  if (!arena) return set_error(RTGS2D_ERR_INVALID, "arena is NULL");
+  if (entries) *entries = arena->bb.n_entries;
+  if (pairs) *pairs = arena->bb.n_pairs;
+  return RTGS2D_OK;
+}
+
+int rtgs2d_forward(rtgs2d_arena* arena, const float* xy, const float* conics, const float* colors,
+                   const float* weights, const int32_t* rects, const int32_t* view_index,
+                   int64_t m, int64_t n_views, int64_t height, int64_t width, double cutoff,
+                   float* out, float* den, void* stream) {
+  RTGS_TRY(check_arena(arena));
+  RTGS_TRY(check_dims(m, n_views, height, width));
+  RTGS_TRY(require(out, "out"));
+  if (m > 0) {
+    RTGS_TRY(require(xy, "xy"));
+    RTGS_TRY(require(conics, "conics"));
+    RTGS_TRY(require(colors, "colors"));
+    RTGS_TRY(require(weights, "weights"));
+    RTGS_TRY(require(rects, "rects"));
+    RTGS_TRY(require(view_index, "view_index"));
+  }
+  cudaStream_t s = as_stream(stream);
+  const Geometry g = make_geometry(static_cast<int>(n_views), static_cast<int>(height),
+                                   static_cast<int>(width));
+  BinBuffers& bb = arena->bb;
+  RTGS_TRY(launch_project_conic(bb, g, xy, conics, colors, weights, rects, view_index, m,
+                                den != nullptr, s));
+  RTGS_TRY(bin_entries(bb, g, m, s));
+  arena->n_tiles = g.n_tiles();
+  return launch_raster_forward(bb, g, static_cast<float>(cutoff), out, den, s);
+}
+
+int rtgs2d_backward(rtgs2d_arena* arena, const float* grad_out, const float* grad_den,
+                    const float* xy, const float* conics, const float* colors,
+                    const float* weights, const int32_t* rects, const int32_t* view_index,
+                    int64_t m, int64_t n_views, int64_t height, int64_t width, double cutoff,
+                    float* grad_xy, float* grad_conics, float* grad_colors, float* grad_weights,
+                    void* stream) {
+  RTGS_TRY(check_arena(arena));
+  RTGS_TRY(check_dims(m, n_views, height, width));
+  if (m == 0) return RTGS2D_OK;
+  RTGS_TRY(require(xy, "xy"));
+  RTGS_TRY(require(conics, "conics"));
+  RTGS_TRY(require(colors, "colors"));
+  RTGS_TRY(require(weights, "weights"));
+  RTGS_TRY(require(rects, "rects"));
+  RTGS_TRY(require(view_index, "view_index"));
+  RTGS_TRY(require(grad_xy, "grad_xy"));
+  RTGS_TRY(require(grad_conics, "grad_conics"));
+  RTGS_TRY(require(grad_colors, "grad_colors"));
+  RTGS_TRY(require(grad_weights, "grad_weights"));
+  cudaStream_t s = as_stream(stream);
+  const Geometry g = make_geometry(static_cast<int>(n_views), static_cast<int>(height),
+                                   static_cast<int>(width));
+  BinBuffers& bb = arena->bb;
+  const bool den = grad_den != nullptr;
+  RTGS_TRY(launch_project_conic(bb, g, xy, conics, colors, weights, rects, view_index, m, den, s));
+  RTGS_TRY(bin_entries(bb, g, m, s));
+  arena->n_tiles = g.n_tiles();
+  RTGS_TRY(launch_raster_backward(bb, g, static_cast<float>(cutoff), grad_out, grad_den, s));
+  return launch_finalize_conic(bb, m, conics, colors, weights, den, grad_xy, grad_conics,
+                               grad_colors, grad_weights, s);
+}
+
+int rtgs2d_render_forward(rtgs2d_arena* arena, const float* xy, const float* chol,
+                          const float* color, const float* weight, int64_t n_views, int64_t n,
+                          int64_t height, int64_t width, float* out, float* den, void* stream) {
+  RTGS_TRY(check_arena(arena));
+  if (n < 0) return set_error(RTGS2D_ERR_INVALID, "n must be non-negative");
+  const int64_t m = n_views * n;
+  RTGS_TRY(check_dims(m, n_views, height, width));
+  RTGS_TRY(require(out, "out"));
+  if (m > 0) {
+    RTGS_TRY(require(xy, "xy"));
+    RTGS_TRY(require(chol, "chol"));
+    RTGS_TRY(require(color, "color"));
+    RTGS_TRY(require(weight, "weight"));
+  }
+  cudaStream_t s = as_stream(stream);
+  const Geometry g = make_geometry(static_cast<int>(n_views), static_cast<int>(height),
+                                   static_cast<int>(width));
+  BinBuffers& bb = arena->bb;
+  RTGS_TRY(launch_project_chol(bb, g, xy, chol, color, weight, m, n > 0 ? n : 1, den != nullptr, s));
+  RTGS_TRY(bin_entries(bb, g, m, s));
+  arena->n_tiles = g.n_tiles();
+  return launch_raster_forward(bb, g, kCutoff, out, den, s);
+}
+
+int rtgs2d_render_backward(rtgs2d_arena* arena, const float* grad_out, const float* grad_den,
+                           const float* xy, const float* chol, const float* color,
+                           const float* weight, int64_t n_views, int64_t n, int64_t height,
+                           int64_t width, float* grad_xy, float* grad_chol, float* grad_color,
+                           float* grad_weight, void* stream) {
+  RTGS_TRY(check_arena(arena));
+  if (n < 0) return set_error(RTGS2D_ERR_INVALID, "n must be non-negative");
+  const int64_t m = n_views * n;
+  RTGS_TRY(check_dims(m, n_views, height, width));
+  if (m == 0) return RTGS2D_OK;
+  RTGS_TRY(require(xy, "xy"));
+  RTGS_TRY(require(chol, "chol"));
+  RTGS_TRY(require(color, "color"));
+  RTGS_TRY(require(weight, "weight"));
+  cudaStream_t s = as_stream(stream);
+  const Geometry g = make_geometry(static_cast<int>(n_views), static_cast<int>(height),
+                                   static_cast<int>(width));
+  BinBuffers& bb = arena->bb;
+  const bool den = grad_den != nullptr;
+  RTGS_TRY(launch_project_chol(bb, g, xy, chol, color, weight, m, n, den, s));
+  RTGS_TRY(bin_entries(bb, g, m, s));
+  arena->n_tiles = g.n_tiles();
+  RTGS_TRY(launch_raster_backward(bb, g, kCutoff, grad_out, grad_den, s));
+  return launch_finalize_chol(bb, m, chol, color, weight, den, grad_xy, grad_chol, grad_color,
+                              grad_weight, s);
+}
+
+int rtgs2d_support_rects(const float* xy, const float* chol, int64_t m, int64_t height,
+                         int64_t width, int32_t* rects, int64_t* counts, void* stream) {
+  RTGS_TRY(check_dims(m, 1, height, width));
+  if (m == 0) return RTGS2D_OK;
+  RTGS_TRY(require(xy, "xy"));
+  RTGS_TRY(require(chol, "chol"));
+  return launch_support_rects(xy, chol, m, static_cast<int>(height), static_cast<int>(width), rects,
+                              counts, as_stream(stream));
+}
+
+int rtgs2d_arena_copy_binning(const rtgs2d_arena* arena, int64_t max_entries, uint32_t* gids,
+                              int64_t max_tiles, int32_t* ranges, int64_t* n_entries,
+                              int64_t* n_tiles, void* stream) {
+  RTGS_TRY(check_arena(arena));
+  const BinBuffers& bb = arena->bb;
+  if (n_entries) *n_entries = bb.n_entries;
+  if (n_tiles) *n_tiles = arena->n_tiles;
+  cudaStream_t s = as_stream(stream);
+  const int64_t ce = bb.n_entries < max_entries ? bb.n_entries : max_entries;
+  const int64_t ct = arena->n_tiles < max_tiles ? arena->n_tiles : max_tiles;
+  if (gids && ce > 0) {
+    RTGS_CUDA(cudaMemcpyAsync(gids, bb.vals[bb.sorted_sel].ptr, static_cast<size_t>(ce) * sizeof(uint32_t),
+                              cudaMemcpyDeviceToHost, s),
+              "copy gids");
+  }
+  if (ranges && ct > 0) {
+    RTGS_CUDA(cudaMemcpyAsync(ranges, bb.ranges.ptr, static_cast<size_t>(ct) * 2 * sizeof(int32_t),
+                              cudaMemcpyDeviceToHost, s),
+              "copy ranges");
+  }
+  RTGS_CUDA(cudaStreamSynchronize(s), "copy binning sync");
+  return RTGS2D_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,421 @@
+// Fit engine: the native Stage-1 fit loop, driven from C++ (no Python per iteration).
+//
+// Per iteration (fit.py:451-482, batched.py:128-145):
+//   project_raw   raw params -> build() -> conic, support rectangle, tile span    (1 kernel)
+//   bin_entries   scan + entry-count readback + emit + radix sort + tile ranges
+//   raster fit    forward, L2-loss gradient, backward -> per-entry moments   (1 kernel)
+//   loss reduce   only at logging iterations                                  (1 kernel)
+//   adam          entry sums -> chain rule -> Adam on all 9 raw params       (1 kernel)
+// The host advances torch's CosineAnnealingLR recursion in double precision and passes the
+// bias-corrected step size to the Adam kernel.
+#include <cmath>
+#include <new>
+#include <vector>
+
+#include "../../include/rtgs2d.h"
+#include "internal.h"
+
+using namespace rtgs2d;
+
+struct rtgs2d_fit {
+  int device = 0;
+  int64_t n_views = 0, n = 0, m = 0;
+  int height = 0, width = 0;
+  rtgs2d_fit_options opt{};
+  Geometry geo;
+  BinBuffers bb;
+  DevBuf raw, m1, m2;  // planar (9, M)
+  DevBuf targets;      // (B, H, W, 3)
+  DevBuf mask;         // (B, mask_bytes)
+  int64_t mask_bytes = 0;
+  DevBuf mask_counts;  // (B,) int
+  DevBuf view_scale;   // (B,) float
+  DevBuf tile_loss;    // (n_tiles, 2) double
+  DevBuf log;          // (max_logs, B, 2) double
+  DevBuf eval_sums;    // (B, 2) double
+  int64_t max_logs = 0;
+  std::vector<int64_t> log_iters;
+  int64_t step = 0;
+  double lr_current = 0.0;
+  double total_pairs = 0.0;
+  int64_t last_entries = 0, last_pairs = 0;
+  bool have_targets = false, have_raw = false;
+};
+
+namespace {
+
+constexpr int kThreads = 256;
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+unsigned grid_for(int64_t m) { return static_cast<unsigned>((m + kThreads - 1) / kThreads); }
+
+// Reference layout (M,2)/(M,2)/(M,)/(M,3)/(M,) <-> planar (9, M).
+__global__ void pack_raw_kernel(int64_t m, const float* __restrict__ xy, const float* __restrict__ diag,
+                                const float* __restrict__ off, const float* __restrict__ color,
+                                const float* __restrict__ weight, float* __restrict__ raw) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  if (i >= m) return;
+  raw[kXr * m + i] = xy[2 * i];
+  raw[kYr * m + i] = xy[2 * i + 1];
+  raw[kD0 * m + i] = diag[2 * i];
+  raw[kD1 * m + i] = diag[2 * i + 1];
+  raw[kOff * m + i] = off[i];
+  raw[kCr * m + i] = color[3 * i];
+  raw[kCg * m + i] = color[3 * i + 1];
+  raw[kCb * m + i] = color[3 * i + 2];
+  raw[kWr * m + i] = weight[i];
+}
+
+__global__ void unpack_raw_kernel(int64_t m, const float* __restrict__ raw, float* xy, float* diag,
+                                  float* off, float* color, float* weight) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  if (i >= m) return;
+  if (xy) {
+    xy[2 * i] = raw[kXr * m + i];
+    xy[2 * i + 1] = raw[kYr * m + i];
+  }
+  if (diag) {
+    diag[2 * i] = raw[kD0 * m + i];
+    diag[2 * i + 1] = raw[kD1 * m + i];
+  }
+  if (off) off[i] = raw[kOff * m + i];
+  if (color) {
+    color[3 * i] = raw[kCr * m + i];
+    color[3 * i + 1] = raw[kCg * m + i];
+    color[3 * i + 2] = raw[kCb * m + i];
+  }
+  if (weight) weight[i] = raw[kWr * m + i];
+}
+
+__global__ void mask_count_kernel(const uint8_t* __restrict__ bits, int64_t bytes_per_view,
+                                  int64_t pixels_per_view, int* __restrict__ counts) {
+  __shared__ int s[kThreads];
+  const int view = blockIdx.x;
+  const uint8_t* v = bits + static_cast<int64_t>(view) * bytes_per_view;
+  int c = 0;
+  for (int64_t b = threadIdx.x; b < bytes_per_view; b += kThreads) {
+    unsigned byte = v[b];
+    const int64_t valid = pixels_per_view - 8 * b;  // bits past the last pixel are padding
+    if (valid < 8) byte &= (1u << valid) - 1u;
+    c += __popc(byte);
+  }
+  s[threadIdx.x] = c;
+  __syncthreads();
+  for (int stride = kThreads / 2; stride > 0; stride >>= 1) {
+    if (threadIdx.x < stride) s[threadIdx.x] += s[threadIdx.x + stride];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) counts[view] = s[0];
+}
+
+int check_fit(const rtgs2d_fit* f) {
+  if (!f) return set_error(RTGS2D_ERR_INVALID, "fit is NULL");
+  int dev = -1;
+  RTGS_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev != f->device) {
+    return set_error(RTGS2D_ERR_INVALID, "fit engine belongs to device " + std::to_string(f->device) +
+                                             ", current device is " + std::to_string(dev));
+  }
+  return 0;
+}
+
+bool is_log_iter(const rtgs2d_fit_options& o, int64_t it) {
+  if (o.log_every > 0 && it % o.log_every == 0) return true;
+  if (it == o.iterations - 1) return true;
+  if (o.check_every > 0 && (it + 1) % o.check_every == 0) return true;
+  return false;
+}
+
+// torch.optim.lr_scheduler.CosineAnnealingLR.get_lr() for last_epoch = epoch >= 1 (recursive form).
+double cosine_next_lr(double lr, double base_lr, double eta_min, int64_t epoch, int64_t t_max) {
+  const int64_t period = 2 * t_max;
+  int64_t r = (epoch - 1 - t_max) % period;
+  if (r < 0) r += period;
+  if (r == 0) {
+    return lr + (base_lr - eta_min) * (1.0 - std::cos(M_PI / static_cast<double>(t_max))) / 2.0;
+  }
+  return (1.0 + std::cos(M_PI * static_cast<double>(epoch) / static_cast<double>(t_max))) /
+             (1.0 + std::cos(M_PI * static_cast<double>(epoch - 1) / static_cast<double>(t_max))) *
+             (lr - eta_min) +
+         eta_min;
+}
+
+int project_and_bin(rtgs2d_fit* f, cudaStream_t s) {
+  RTGS_TRY(launch_project_raw(f->bb, f->geo, f->raw.as<float>(), f->m, f->n, s));
+  RTGS_TRY(bin_entries(f->bb, f->geo, f->m, s));
+  f->last_entries = f->bb.n_entries;
+  f->last_pairs = f->bb.n_pairs;
+  return 0;
+}
+
+FitRasterArgs raster_args(rtgs2d_fit* f) {
+  FitRasterArgs fa;
+  fa.targets = f->targets.as<float>();
+  fa.mask_bits = f->mask.as<uint8_t>();
+  fa.mask_bytes_per_view = f->mask_bytes;
+  fa.view_scale = f->view_scale.as<float>();
+  fa.loss_mode = f->opt.loss_mode;
+  fa.tile_loss = f->tile_loss.as<double>();
+  fa.render_out = nullptr;
+  return fa;
+}
+
+}  // namespace
+
+extern "C" {
+
+int rtgs2d_fit_create(int64_t n_views, int64_t n, int64_t height, int64_t width,
+                      const rtgs2d_fit_options* options, rtgs2d_fit** out) {
+  if (!out || !options) return set_error(RTGS2D_ERR_INVALID, "out/options is NULL");
+  *out = nullptr;
+  if (n_views <= 0 || n < 0 || height <= 0 || width <= 0) {
+    return set_error(RTGS2D_ERR_INVALID, "n_views, height, width must be positive and n >= 0");
+  }
+  if (height > 32768 || width > 32768 || n_views * n > INT32_MAX) {
+    return set_error(RTGS2D_ERR_CAPACITY, "problem too large for 32-bit indexing");
+  }
+  if (options->iterations < 0 || !(options->lr > 0.0)) {
+    return set_error(RTGS2D_ERR_INVALID, "iterations must be >= 0 and lr > 0");
+  }
+  if (options->loss_mode < RTGS2D_LOSS_MSE || options->loss_mode > RTGS2D_LOSS_MASK_ONLY) {
+    return set_error(RTGS2D_ERR_INVALID, "unknown loss_mode");
+  }
+  rtgs2d_fit* f = new (std::nothrow) rtgs2d_fit();
+  if (!f) return set_error(RTGS2D_ERR_ALLOC, "host allocation failed");
+  int rc = 0;
+  do {
+    if ((rc = check_cuda(cudaGetDevice(&f->device), "cudaGetDevice"))) break;
+    f->n_views = n_views;
+    f->n = n;
+    f->m = n_views * n;
+    f->height = static_cast<int>(height);
+    f->width = static_cast<int>(width);
+    f->opt = *options;
+    f->geo = make_geometry(static_cast<int>(n_views), f->height, f->width);
+    f->lr_current = options->lr;
+    f->mask_bytes = (height * width + 7) / 8;
+    for (int64_t it = 0; it < options->iterations; ++it) f->max_logs += is_log_iter(options[0], it);
+    const size_t mm = static_cast<size_t>(f->m > 0 ? f->m : 1);
+    cudaStream_t s = nullptr;
+    if ((rc = f->raw.ensure(kRawSlots * mm * sizeof(float), s))) break;
+    if ((rc = f->m1.ensure(kRawSlots * mm * sizeof(float), s))) break;
+    if ((rc = f->m2.ensure(kRawSlots * mm * sizeof(float), s))) break;
+    if ((rc = f->targets.ensure(static_cast<size_t>(n_views * height * width * 3) * sizeof(float), s))) break;
+    if ((rc = f->view_scale.ensure(static_cast<size_t>(n_views) * sizeof(float), s))) break;
+    if ((rc = f->mask_counts.ensure(static_cast<size_t>(n_views) * sizeof(int), s))) break;
+    if ((rc = f->tile_loss.ensure(static_cast<size_t>(f->geo.n_tiles()) * 2 * sizeof(double), s))) break;
+    if ((rc = f->eval_sums.ensure(static_cast<size_t>(n_views) * 2 * sizeof(double), s))) break;
+    if ((rc = f->log.ensure(static_cast<size_t>(f->max_logs > 0 ? f->max_logs : 1) * n_views * 2 * sizeof(double), s))) break;
+    if (options->loss_mode != RTGS2D_LOSS_MSE) {
+      if ((rc = f->mask.ensure(static_cast<size_t>(n_views * f->mask_bytes), s))) break;
+    }
+  } while (false);
+  if (rc) {
+    delete f;
+    return rc;
+  }
+  *out = f;
+  return RTGS2D_OK;
+}
+
+int rtgs2d_fit_destroy(rtgs2d_fit* fit) {
+  if (!fit) return RTGS2D_OK;
+  const int dev = fit->device;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (prev != dev) cudaSetDevice(dev);
+  fit->raw.release();
+  fit->m1.release();
+  fit->m2.release();
+  fit->targets.release();
+  fit->mask.release();
+  fit->mask_counts.release();
+  fit->view_scale.release();
+  fit->tile_loss.release();
+  fit->log.release();
+  fit->eval_sums.release();
+  delete fit;
+  if (prev != dev) cudaSetDevice(prev);
+  return RTGS2D_OK;
+}
+
+int rtgs2d_fit_set_targets(rtgs2d_fit* f, const float* targets, const uint8_t* mask_bits,
+                           void* stream) {
+  RTGS_TRY(check_fit(f));
+  if (!targets) return set_error(RTGS2D_ERR_INVALID, "targets is NULL");
+  const bool masked = f->opt.loss_mode != RTGS2D_LOSS_MSE;
+  if (masked && !mask_bits) return set_error(RTGS2D_ERR_INVALID, "mask loss mode needs mask_bits");
+  cudaStream_t s = as_stream(stream);
+  const size_t tbytes = static_cast<size_t>(f->n_views) * f->height * f->width * 3 * sizeof(float);
+  RTGS_CUDA(cudaMemcpyAsync(f->targets.ptr, targets, tbytes, cudaMemcpyDeviceToDevice, s),
+            "copy targets");
+  std::vector<float> scale(static_cast<size_t>(f->n_views));
+  const double numel = 3.0 * f->height * f->width;
+  if (f->opt.loss_mode == RTGS2D_LOSS_MASK_ONLY) {
+    RTGS_CUDA(cudaMemcpyAsync(f->mask.ptr, mask_bits, static_cast<size_t>(f->n_views * f->mask_bytes),
+                              cudaMemcpyDeviceToDevice, s),
+              "copy mask");
+    mask_count_kernel<<<static_cast<unsigned>(f->n_views), kThreads, 0, s>>>(
+        f->mask.as<uint8_t>(), f->mask_bytes, static_cast<int64_t>(f->height) * f->width,
+        f->mask_counts.as<int>());
+    RTGS_CUDA(cudaGetLastError(), "mask_count_kernel");
+    std::vector<int> counts(static_cast<size_t>(f->n_views));
+    RTGS_CUDA(cudaMemcpyAsync(counts.data(), f->mask_counts.ptr, counts.size() * sizeof(int),
+                              cudaMemcpyDeviceToHost, s),
+              "mask counts readback");
+    RTGS_CUDA(cudaStreamSynchronize(s), "mask counts sync");
+    for (size_t b = 0; b < counts.size(); ++b) {
+      scale[b] = counts[b] > 0 ? static_cast<float>(2.0 / (3.0 * counts[b])) : 0.0f;
+    }
+  } else {
+    if (masked) {
+      RTGS_CUDA(cudaMemcpyAsync(f->mask.ptr, mask_bits, static_cast<size_t>(f->n_views * f->mask_bytes),
+                                cudaMemcpyDeviceToDevice, s),
+                "copy mask");
+    }
+    for (auto& v : scale) v = static_cast<float>(2.0 / numel);
+  }
+  RTGS_CUDA(cudaMemcpyAsync(f->view_scale.ptr, scale.data(), scale.size() * sizeof(float),
+                            cudaMemcpyHostToDevice, s),
+            "view scale upload");
+  RTGS_CUDA(cudaStreamSynchronize(s), "set_targets sync");
+  f->have_targets = true;
+  return RTGS2D_OK;
+}
+
+int rtgs2d_fit_set_raw(rtgs2d_fit* f, const float* xy_raw, const float* diag_raw,
+                       const float* off_raw, const float* color_raw, const float* weight_raw,
+                       void* stream) {
+  RTGS_TRY(check_fit(f));
+  if (f->m > 0 && (!xy_raw || !diag_raw || !off_raw || !color_raw || !weight_raw)) {
+    return set_error(RTGS2D_ERR_INVALID, "raw parameter pointer is NULL");
+  }
+  cudaStream_t s = as_stream(stream);
+  const size_t bytes = static_cast<size_t>(kRawSlots) * (f->m > 0 ? f->m : 1) * sizeof(float);
+  RTGS_CUDA(cudaMemsetAsync(f->m1.ptr, 0, bytes, s), "zero exp_avg");
+  RTGS_CUDA(cudaMemsetAsync(f->m2.ptr, 0, bytes, s), "zero exp_avg_sq");
+  if (f->m > 0) {
+    pack_raw_kernel<<<grid_for(f->m), kThreads, 0, s>>>(f->m, xy_raw, diag_raw, off_raw, color_raw,
+                                                        weight_raw, f->raw.as<float>());
+    RTGS_CUDA(cudaGetLastError(), "pack_raw_kernel");
+  }
+  f->step = 0;
+  f->lr_current = f->opt.lr;
+  f->log_iters.clear();
+  f->total_pairs = 0.0;
+  f->have_raw = true;
+  return RTGS2D_OK;
+}
+
+int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
+  RTGS_TRY(check_fit(f));
+  if (!f->have_targets || !f->have_raw) {
+    return set_error(RTGS2D_ERR_INVALID, "set targets and raw parameters before running");
+  }
+  cudaStream_t s = as_stream(stream);
+  const double base_lr = f->opt.lr;
+  const double eta_min = f->opt.lr * 0.1;
+  const int64_t t_max = f->opt.iterations;
+  for (int64_t k = 0; k < n_iterations && f->step < t_max; ++k) {
+    const int64_t it = f->step;
+    RTGS_TRY(project_and_bin(f, s));
+    f->total_pairs += static_cast<double>(f->last_pairs);
+    RTGS_TRY(launch_raster_fit(f->bb, f->geo, kCutoff, raster_args(f), true, s));
+    if (is_log_iter(f->opt, it)) {
+      const int64_t slot = static_cast<int64_t>(f->log_iters.size());
+      if (slot < f->max_logs) {
+        RTGS_TRY(launch_loss_reduce(f->tile_loss.as<double>(), f->geo,
+                                    f->log.as<double>() + slot * f->n_views * 2, s));
+        f->log_iters.push_back(it);
+      }
+    }
+    const double t = static_cast<double>(it + 1);
+    const double bc1 = 1.0 - std::pow(0.9, t);
+    const double bc2 = 1.0 - std::pow(0.999, t);
+    const double step_size = f->lr_current / bc1;
+    AdamScalars a;
+    a.neg_step_size = static_cast<float>(-step_size);
+    a.bc2_sqrt = static_cast<float>(std::pow(bc2, 0.5));
+    a.beta1 = 0.9f;
+    a.beta2 = 0.999f;
+    a.one_minus_beta1 = static_cast<float>(1.0 - 0.9);
+    a.one_minus_beta2 = static_cast<float>(1.0 - 0.999);
+    a.eps = 1e-8f;
+    a.freeze_geometry = f->opt.freeze_geometry;
+    RTGS_TRY(launch_adam_fit(f->bb, f->m, f->height, f->width, f->raw.as<float>(),
+                             f->m1.as<float>(), f->m2.as<float>(), a, s));
+    f->step += 1;
+    f->lr_current = cosine_next_lr(f->lr_current, base_lr, eta_min, f->step, t_max);
+  }
+  RTGS_CUDA(cudaStreamSynchronize(s), "fit run sync");
+  return RTGS2D_OK;
+}
+
+int rtgs2d_fit_get_raw(rtgs2d_fit* f, float* xy_raw, float* diag_raw, float* off_raw,
+                       float* color_raw, float* weight_raw, void* stream) {
+  RTGS_TRY(check_fit(f));
+  if (f->m == 0) return RTGS2D_OK;
+  unpack_raw_kernel<<<grid_for(f->m), kThreads, 0, as_stream(stream)>>>(
+      f->m, f->raw.as<float>(), xy_raw, diag_raw, off_raw, color_raw, weight_raw);
+  return check_cuda(cudaGetLastError(), "unpack_raw_kernel");
+}
+
+int rtgs2d_fit_get_params(rtgs2d_fit* f, float* xy, float* chol, float* color, float* weight,
+                          void* stream) {
+  RTGS_TRY(check_fit(f));
+  if (f->m > 0 && (!xy || !chol || !color || !weight)) {
+    return set_error(RTGS2D_ERR_INVALID, "output pointer is NULL");
+  }
+  return launch_build_params(f->raw.as<float>(), f->m, f->height, f->width, xy, chol, color,
+                             weight, as_stream(stream));
+}
+
+int rtgs2d_fit_evaluate(rtgs2d_fit* f, float* render, double* sums, void* stream) {
+  RTGS_TRY(check_fit(f));
+  if (!f->have_targets || !f->have_raw) {
+    return set_error(RTGS2D_ERR_INVALID, "set targets and raw parameters before evaluating");
+  }
+  cudaStream_t s = as_stream(stream);
+  RTGS_TRY(project_and_bin(f, s));
+  FitRasterArgs fa = raster_args(f);
+  fa.render_out = render;
+  RTGS_TRY(launch_raster_fit(f->bb, f->geo, kCutoff, fa, false, s));
+  RTGS_TRY(launch_loss_reduce(f->tile_loss.as<double>(), f->geo, f->eval_sums.as<double>(), s));
+  if (sums) {
+    RTGS_CUDA(cudaMemcpyAsync(sums, f->eval_sums.ptr, static_cast<size_t>(f->n_views) * 2 * sizeof(double),
+                              cudaMemcpyDeviceToHost, s),
+              "eval sums readback");
+  }
+  RTGS_CUDA(cudaStreamSynchronize(s), "evaluate sync");
+  return RTGS2D_OK;
+}
+
+int rtgs2d_fit_history(const rtgs2d_fit* f, int64_t max_rows, int64_t* iters, double* sums,
+                       int64_t* n_rows) {
+  RTGS_TRY(check_fit(f));
+  const int64_t rows = static_cast<int64_t>(f->log_iters.size());
+  if (n_rows) *n_rows = rows;
+  const int64_t copy = rows < max_rows ? rows : max_rows;
+  if (copy <= 0) return RTGS2D_OK;
+  if (iters) {
+    for (int64_t r = 0; r < copy; ++r) iters[r] = f->log_iters[static_cast<size_t>(r)];
+  }
+  if (sums) {
+    RTGS_CUDA(cudaMemcpy(sums, f->log.ptr, static_cast<size_t>(copy * f->n_views * 2) * sizeof(double),
+                         cudaMemcpyDeviceToHost),
+              "history readback");
+  }
+  return RTGS2D_OK;
+}
+
+int rtgs2d_fit_stats(const rtgs2d_fit* f, int64_t* step, int64_t* last_entries,
+                     int64_t* last_pairs, double* total_pairs) {
+  if (!f) return set_error(RTGS2D_ERR_INVALID, "fit is NULL");
+  if (step) *step = f->step;
+  if (last_entries) *last_entries = f->last_entries;
+  if (last_pairs) *last_pairs = f->last_pairs;
+  if (total_pairs) *total_pairs = f->total_pairs;
+  return RTGS2D_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,134 @@
+// Host-side internal interfaces shared by the translation units of librtgs2d.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "common.cuh"
+
+namespace rtgs2d {
+
+// ---- error reporting --------------------------------------------------------------------------
+// Every C entry point returns 0 or a negative RTGS2D_ERR_* code and leaves a message that
+// rtgs2d_last_error() returns (thread-local).
+int set_error(int code, const std::string& msg);
+int check_cuda(cudaError_t err, const char* what);
+#define RTGS_TRY(expr)            \
+  do {                            \
+    int _rc = (expr);             \
+    if (_rc != 0) return _rc;     \
+  } while (0)
+#define RTGS_CUDA(expr, what) RTGS_TRY(::rtgs2d::check_cuda((expr), (what)))
+
+// ---- device memory ------------------------------------------------------------------------------
+// A growable device buffer. ensure() reallocates only when more bytes are needed; before freeing
+// the old allocation it synchronises `stream` so no queued kernel still reads it.
+struct DevBuf {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  DevBuf() = default;
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  ~DevBuf() { release(); }
+  int ensure(size_t need, cudaStream_t stream);
+  void release();
+  template <typename T>
+  T* as() const { return static_cast<T*>(ptr); }
+};
+
+// Scratch used by projection + tile binning + raster for one render / one fit iteration.
+struct BinBuffers {
+  DevBuf records;   // GaussRecord[M]
+  DevBuf weights;   // float[M] (density variants)
+  DevBuf spans;     // TileSpan[M]
+  DevBuf counts;    // int[M]  tiles per gaussian
+  DevBuf offsets;   // int[M]  exclusive scan of counts (entry index of each gaussian's first tile)
+  DevBuf keys[2];   // uint32[E] tile keys (double buffer for the radix sort)
+  DevBuf vals[2];   // uint32[E] gaussian ids
+  DevBuf ranges;    // int2[n_tiles] [start, end) into the sorted entries
+  DevBuf partials;  // float[E][8] per (gaussian, tile) gradient moments
+  DevBuf partial_d; // float[E]   per (gaussian, tile) density-gradient moment
+  DevBuf cub_temp;
+  DevBuf stats;     // unsigned long long[2]: entries, pairs
+  unsigned long long* host_stats = nullptr;  // pinned mirror of `stats`
+  int sorted_sel = 0;                         // which of keys/vals holds the sorted result
+  int64_t n_entries = 0;
+  int64_t n_pairs = 0;
+  ~BinBuffers();
+  void release();
+};
+
+struct Geometry {
+  int n_views = 1;
+  int height = 0, width = 0;
+  int tiles_x = 0, tiles_y = 0, tiles_per_view = 0;
+  int64_t n_tiles() const { return static_cast<int64_t>(n_views) * tiles_per_view; }
+};
+Geometry make_geometry(int n_views, int height, int width);
+
+// ---- projection (project.cu) --------------------------------------------------------------------
+// All projection launchers zero bb.stats first and fill records/spans/counts (+weights if asked).
+int launch_project_chol(BinBuffers& bb, const Geometry& g, const float* xy, const float* chol,
+                        const float* color, const float* weight, int64_t m, int64_t n_per_view,
+                        bool want_weights, cudaStream_t s);
+int launch_project_conic(BinBuffers& bb, const Geometry& g, const float* xy, const float* conics,
+                         const float* colors, const float* weights, const int32_t* rects,
+                         const int32_t* view_index, int64_t m, bool want_weights, cudaStream_t s);
+int launch_project_raw(BinBuffers& bb, const Geometry& g, const float* raw, int64_t m,
+                       int64_t n_per_view, cudaStream_t s);
+// Bit-exact support rectangles only: rects (M,4) (x0, x1, y0, y1; x1 = x0 - 1 if empty), counts (M,).
+int launch_support_rects(const float* xy, const float* chol, int64_t m, int height, int width,
+                         int32_t* rects, int64_t* counts, cudaStream_t s);
+// raw (planar 9 x M) -> constrained (xy (M,2), chol (M,3), color (M,3), weight (M))
+int launch_build_params(const float* raw, int64_t m, int height, int width, float* xy, float* chol,
+                        float* color, float* weight, cudaStream_t s);
+
+// ---- binning (binning.cu) -----------------------------------------------------------------------
+// Scan counts, read the entry count back to the host (synchronises `s`), emit (tile key, gaussian
+// id) entries, stable radix sort by key, and build per-tile ranges. Requires bb.counts/spans/stats
+// from a projection launcher.
+int bin_entries(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s);
+
+// ---- raster (raster.cu) -------------------------------------------------------------------------
+enum LossMode : int { kLossMse = 0, kLossMaskWeighted = 1, kLossMaskOnly = 2 };
+
+struct FitRasterArgs {
+  const float* targets = nullptr;     // (B, H, W, 3)
+  const uint8_t* mask_bits = nullptr; // (B, mask_bytes_per_view) little-endian bits, or null
+  int64_t mask_bytes_per_view = 0;
+  const float* view_scale = nullptr;  // (B,) loss-gradient scale per view
+  int loss_mode = kLossMse;
+  double* tile_loss = nullptr;        // (n_tiles, 2): loss numerator, clamped PSNR numerator
+  float* render_out = nullptr;        // optional (B, H, W, 3)
+};
+
+int launch_raster_forward(const BinBuffers& bb, const Geometry& g, float cutoff, float* out,
+                          float* den, cudaStream_t s);
+int launch_raster_backward(BinBuffers& bb, const Geometry& g, float cutoff, const float* grad_out,
+                           const float* grad_den, cudaStream_t s);
+int launch_raster_fit(BinBuffers& bb, const Geometry& g, float cutoff, const FitRasterArgs& fa,
+                      bool backward, cudaStream_t s);
+// Deterministic per-view sum of tile_loss -> dst[(view, 2)].
+int launch_loss_reduce(const double* tile_loss, const Geometry& g, double* dst, cudaStream_t s);
+
+// ---- gradient finalisation + Adam (optim.cu) ----------------------------------------------------
+int launch_finalize_chol(const BinBuffers& bb, int64_t m, const float* chol, const float* color,
+                         const float* weight, bool with_density, float* grad_xy, float* grad_chol,
+                         float* grad_color, float* grad_weight, cudaStream_t s);
+int launch_finalize_conic(const BinBuffers& bb, int64_t m, const float* conics,
+                          const float* colors, const float* weights, bool with_density,
+                          float* grad_xy, float* grad_conics, float* grad_colors,
+                          float* grad_weights, cudaStream_t s);
+
+struct AdamScalars {
+  float neg_step_size;   // -(lr / (1 - beta1^t))
+  float bc2_sqrt;        // sqrt(1 - beta2^t)
+  float beta1, beta2, one_minus_beta1, one_minus_beta2, eps;
+  int freeze_geometry;
+};
+int launch_adam_fit(const BinBuffers& bb, int64_t m, int height, int width, float* raw, float* m1,
+                    float* m2, const AdamScalars& a, cudaStream_t s);
+
+}  // namespace rtgs2d

@@ -1,0 +1,486 @@
+// Per-tile raster kernels for the accumulated 2D splatting renderer (sm_100a).
+//
+// One CTA per 16x16 tile. Each warp owns an 8 x (4*PPT) pixel sub-block and each lane PPT
+// pixels of one column (rows r, r+4, ...). The tile's gaussian list (ascending gaussian index,
+// from the binning step) is staged through shared memory in batches; while staging, every
+// record gets a bit mask of the warps whose sub-block its support rectangle touches, so a warp
+// walks only the records that can reach its pixels (ballot + ffs), with no per-record test in
+// the inner loop.
+//
+//   forward   pixel accumulators live in registers; the list order is the reference's
+//             summation order, so a render is deterministic and no atomics are used.
+//   backward  per (warp, gaussian): 8 moments over the warp's pixels
+//               Sdx = sum dq*dx, Sdy = sum dq*dy, Sxx = sum dq*dx^2, Sxy = sum dq*dx*dy,
+//               Syy = sum dq*dy^2, Sr/Sg/Sb = sum e*g_rgb       (e = exp(-q/2), dq = e * g.A)
+//             reduced with an 8-way transpose butterfly, combined across warps in a fixed order
+//             in shared memory and written once per (gaussian, tile) entry. A per-gaussian pass
+//             (optim.cu) sums a gaussian's entries in order and applies the chain rule, so
+//             gradients are deterministic as well and no global atomics are issued.
+//   fit       forward -> L2 loss gradient in registers -> backward, in one kernel: the rendered
+//             image and dL/dout never leave the SM.
+//
+// Reference semantics: renderer2d_ext.cu:69-84 (forward), :142-171 (backward); parity of the
+// support set with renderer2d.py:233-248.
+#include "internal.h"
+
+namespace rtgs2d {
+namespace {
+
+constexpr int kBatch = 128;
+
+template <int PPT>
+struct Layout {
+  static constexpr int kSubW = 8;
+  static constexpr int kSubH = 4 * PPT;
+  static constexpr int kSubX = kTile / kSubW;
+  static constexpr int kSubY = kTile / kSubH;
+  static constexpr int kWarps = kSubX * kSubY;
+  static constexpr int kThreads = kWarps * 32;
+};
+
+enum Mode : int { kFwd = 0, kBwd = 1, kFit = 2, kEval = 3 };
+
+struct RasterArgs {
+  const GaussRecord* records;
+  const float* weights;       // density variants
+  const TileSpan* spans;      // backward: entry index
+  const int* offsets;         // backward: entry index
+  const uint32_t* gids;       // sorted gaussian ids
+  const int2* ranges;         // per tile
+  int height, width, tiles_x, tiles_per_view;
+  float cutoff;
+  // forward outputs
+  float* out;  // (B,H,W,3)
+  float* den;  // (B,H,W) or null
+  // backward inputs / outputs
+  const float* grad_out;  // (B,H,W,3) or null (zero)
+  const float* grad_den;  // (B,H,W) or null (zero)
+  float4* partials;       // (E, 2) float4
+  float* partial_d;       // (E,) density moment
+  // fit
+  FitRasterArgs fit;
+};
+
+__device__ __forceinline__ float warp_transpose_reduce8(const float (&v)[8], int lane) {
+  const bool u16 = lane & 16, u8 = lane & 8, u4 = lane & 4;
+  float a[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float send = u16 ? v[k] : v[k + 4];
+    const float keep = u16 ? v[k + 4] : v[k];
+    a[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+  float b[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const float send = u8 ? a[k] : a[k + 2];
+    const float keep = u8 ? a[k + 2] : a[k];
+    b[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  const float send = u4 ? b[0] : b[1];
+  const float keep = u4 ? b[1] : b[0];
+  float c = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  c += __shfl_xor_sync(0xffffffffu, c, 2);
+  c += __shfl_xor_sync(0xffffffffu, c, 1);
+  return c;  // sum of v[(lane >> 2) & 7] over the warp
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+__device__ __forceinline__ bool mask_bit(const uint8_t* bits, int64_t idx) {
+  return (bits[idx >> 3] >> (idx & 7)) & 1;
+}
+
+template <int PPT, int MODE, bool DEN>
+__global__ void __launch_bounds__(Layout<PPT>::kThreads)
+raster_kernel(const RasterArgs a) {
+  using L = Layout<PPT>;
+  constexpr bool kDoFwd = MODE != kBwd;
+  constexpr bool kDoBwd = MODE == kBwd || MODE == kFit;
+
+  __shared__ float4 s_geo[kBatch];
+  __shared__ float4 s_app[kBatch];
+  __shared__ int4 s_rect[kBatch];
+  __shared__ uint32_t s_mask[kBatch];
+  __shared__ float s_wt[DEN ? kBatch : 1];
+  __shared__ int s_entry[kDoBwd ? kBatch : 1];
+  __shared__ float s_part[kDoBwd ? L::kWarps * kAccum : 1][kBatch + 1];
+  __shared__ float s_partd[(kDoBwd && DEN) ? L::kWarps : 1][kBatch + 1];
+  __shared__ double s_loss[L::kWarps][2];
+
+  const int tile = blockIdx.x;
+  const int view = tile / a.tiles_per_view;
+  const int tin = tile - view * a.tiles_per_view;
+  const int tile_y = tin / a.tiles_x;
+  const int tile_x = tin - tile_y * a.tiles_x;
+  const int ox = tile_x * kTile, oy = tile_y * kTile;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sbx = warp % L::kSubX, sby = warp / L::kSubX;
+  const int px = ox + sbx * L::kSubW + (lane & 7);
+  const float pxc = static_cast<float>(px) + 0.5f;
+  int py[PPT];
+  float pyc[PPT];
+  bool inimg[PPT];
+#pragma unroll
+  for (int k = 0; k < PPT; ++k) {
+    py[k] = oy + sby * L::kSubH + (lane >> 3) + 4 * k;
+    pyc[k] = static_cast<float>(py[k]) + 0.5f;
+    inimg[k] = px < a.width && py[k] < a.height;
+  }
+  const int64_t view_base = static_cast<int64_t>(view) * a.height * a.width;
+  const int2 range = a.ranges[tile];
+
+  // Stage records [base, base + n) of this tile's list into shared memory.
+  auto stage = [&](int base, int n, bool with_entry) {
+    for (int j = threadIdx.x; j < n; j += L::kThreads) {
+      const uint32_t gid = a.gids[base + j];
+      const GaussRecord r = a.records[gid];
+      s_geo[j] = r.geo;
+      s_app[j] = r.app;
+      s_rect[j] = r.rect;
+      const int rx0 = r.rect.x - ox, rx1 = rx0 + r.rect.z;
+      const int ry0 = r.rect.y - oy, ry1 = ry0 + r.rect.w;
+      uint32_t m = 0;
+#pragma unroll
+      for (int sy = 0; sy < L::kSubY; ++sy) {
+#pragma unroll
+        for (int sx = 0; sx < L::kSubX; ++sx) {
+          const bool hit = rx0 <= sx * L::kSubW + L::kSubW - 1 && rx1 >= sx * L::kSubW &&
+                           ry0 <= sy * L::kSubH + L::kSubH - 1 && ry1 >= sy * L::kSubH;
+          m |= static_cast<uint32_t>(hit) << (sy * L::kSubX + sx);
+        }
+      }
+      s_mask[j] = m;
+      if constexpr (DEN) s_wt[j] = a.weights[gid];
+      if constexpr (kDoBwd) {
+        if (with_entry) {
+          const TileSpan sp = a.spans[gid];
+          s_entry[j] = a.offsets[gid] + (tile_y - sp.ty0) * sp.ntx + (tile_x - sp.tx0);
+        }
+      }
+    }
+  };
+
+  // ------------------------------------------------------------------ forward
+  float acc[PPT][3];
+  float accd[PPT];
+#pragma unroll
+  for (int k = 0; k < PPT; ++k) {
+    acc[k][0] = acc[k][1] = acc[k][2] = 0.f;
+    accd[k] = 0.f;
+  }
+  if constexpr (kDoFwd) {
+    for (int base = range.x; base < range.y; base += kBatch) {
+      const int n = min(kBatch, range.y - base);
+      __syncthreads();
+      stage(base, n, false);
+      __syncthreads();
+      for (int c = 0; c < n; c += 32) {
+        const int j = c + lane;
+        unsigned bits = __ballot_sync(0xffffffffu, j < n && ((s_mask[j] >> warp) & 1u));
+        while (bits) {
+          const int jj = c + __ffs(bits) - 1;
+          bits &= bits - 1;
+          const float4 geo = s_geo[jj];
+          const float4 app = s_app[jj];
+          const int4 rc = s_rect[jj];
+          const float dx = __fsub_rn(pxc, geo.x);
+          const bool inx = static_cast<unsigned>(px - rc.x) <= static_cast<unsigned>(rc.z);
+#pragma unroll
+          for (int k = 0; k < PPT; ++k) {
+            const float dy = __fsub_rn(pyc[k], geo.y);
+            const float q = pair_q(dx, dy, geo.z, geo.w, app.x);
+            const bool in = inx &&
+                            static_cast<unsigned>(py[k] - rc.y) <= static_cast<unsigned>(rc.w) &&
+                            q < a.cutoff;
+            if (in) {
+              const float e = __expf(-0.5f * q);
+              acc[k][0] = fmaf(e, app.y, acc[k][0]);
+              acc[k][1] = fmaf(e, app.z, acc[k][1]);
+              acc[k][2] = fmaf(e, app.w, acc[k][2]);
+              if constexpr (DEN) accd[k] = fmaf(e, s_wt[jj], accd[k]);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  if constexpr (MODE == kFwd) {
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+      if (!inimg[k]) continue;
+      const int64_t p = view_base + static_cast<int64_t>(py[k]) * a.width + px;
+      a.out[3 * p] = acc[k][0];
+      a.out[3 * p + 1] = acc[k][1];
+      a.out[3 * p + 2] = acc[k][2];
+      if constexpr (DEN) a.den[p] = accd[k];
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ upstream gradient
+  float g[PPT][3];
+  float gd[PPT];
+#pragma unroll
+  for (int k = 0; k < PPT; ++k) {
+    g[k][0] = g[k][1] = g[k][2] = 0.f;
+    gd[k] = 0.f;
+  }
+  if constexpr (MODE == kBwd) {
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+      if (!inimg[k]) continue;
+      const int64_t p = view_base + static_cast<int64_t>(py[k]) * a.width + px;
+      if (a.grad_out) {
+        g[k][0] = a.grad_out[3 * p];
+        g[k][1] = a.grad_out[3 * p + 1];
+        g[k][2] = a.grad_out[3 * p + 2];
+      }
+      if constexpr (DEN) {
+        if (a.grad_den) gd[k] = a.grad_den[p];
+      }
+    }
+  }
+  if constexpr (MODE == kFit || MODE == kEval) {
+    const FitRasterArgs& f = a.fit;
+    const float scale = f.view_scale ? f.view_scale[view] : 0.f;
+    float sse = 0.f, sse_c = 0.f;
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+      if (!inimg[k]) continue;
+      const int64_t p = view_base + static_cast<int64_t>(py[k]) * a.width + px;
+      float wpix = 1.f, wpsnr = 1.f;
+      if (f.loss_mode != kLossMse) {
+        const bool mb = mask_bit(f.mask_bits + static_cast<int64_t>(view) * f.mask_bytes_per_view,
+                                 static_cast<int64_t>(py[k]) * a.width + px);
+        if (f.loss_mode == kLossMaskWeighted) {
+          wpix = mb ? 1.0f : 0.1f;  // 0.1 + 0.9 * mask (fit.py:562)
+        } else {
+          wpix = mb ? 1.f : 0.f;
+          wpsnr = wpix;
+        }
+      }
+#pragma unroll
+      for (int ch = 0; ch < 3; ++ch) {
+        const float t = f.targets[3 * p + ch];
+        const float r = acc[k][ch];
+        const float res = __fsub_rn(r, t);
+        const float rc = __fsub_rn(fminf(fmaxf(r, 0.f), 1.f), t);
+        sse = fmaf(wpix * res, res, sse);
+        sse_c = fmaf(wpsnr * rc, rc, sse_c);
+        if constexpr (MODE == kFit) g[k][ch] = __fmul_rn(__fmul_rn(res, scale), wpix);
+        if (f.render_out) f.render_out[3 * p + ch] = r;
+      }
+    }
+    // Deterministic CTA reduction of the loss numerators.
+    const double ws = static_cast<double>(warp_sum(sse));
+    const double wc = static_cast<double>(warp_sum(sse_c));
+    if (lane == 0) {
+      s_loss[warp][0] = ws;
+      s_loss[warp][1] = wc;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && f.tile_loss) {
+      double t0 = 0.0, t1 = 0.0;
+      for (int w = 0; w < L::kWarps; ++w) {
+        t0 += s_loss[w][0];
+        t1 += s_loss[w][1];
+      }
+      f.tile_loss[2 * tile] = t0;
+      f.tile_loss[2 * tile + 1] = t1;
+    }
+  }
+
+  if constexpr (kDoBwd) {
+    // ---------------------------------------------------------------- backward
+    for (int base = range.x; base < range.y; base += kBatch) {
+      const int n = min(kBatch, range.y - base);
+      __syncthreads();
+      stage(base, n, true);
+      __syncthreads();
+      for (int c = 0; c < n; c += 32) {
+        const int j = c + lane;
+        unsigned bits = __ballot_sync(0xffffffffu, j < n && ((s_mask[j] >> warp) & 1u));
+        while (bits) {
+          const int jj = c + __ffs(bits) - 1;
+          bits &= bits - 1;
+          const float4 geo = s_geo[jj];
+          const float4 app = s_app[jj];
+          const int4 rc = s_rect[jj];
+          float wt = 0.f;
+          if constexpr (DEN) wt = s_wt[jj];
+          float S[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          float Sd = 0.f;
+          bool any = false;
+          const float dx = __fsub_rn(pxc, geo.x);
+          const bool inx = static_cast<unsigned>(px - rc.x) <= static_cast<unsigned>(rc.z);
+#pragma unroll
+          for (int k = 0; k < PPT; ++k) {
+            const float dy = __fsub_rn(pyc[k], geo.y);
+            const float q = pair_q(dx, dy, geo.z, geo.w, app.x);
+            const bool in = inx &&
+                            static_cast<unsigned>(py[k] - rc.y) <= static_cast<unsigned>(rc.w) &&
+                            q < a.cutoff;
+            if (in) {
+              any = true;
+              const float e = __expf(-0.5f * q);
+              float v = g[k][0] * app.y;
+              v = fmaf(g[k][1], app.z, v);
+              v = fmaf(g[k][2], app.w, v);
+              if constexpr (DEN) v = fmaf(gd[k], wt, v);
+              const float dq = e * v;
+              const float ex = dq * dx;
+              const float fy = dq * dy;
+              S[0] += ex;
+              S[1] += fy;
+              S[2] = fmaf(ex, dx, S[2]);
+              S[3] = fmaf(ex, dy, S[3]);
+              S[4] = fmaf(fy, dy, S[4]);
+              S[5] = fmaf(e, g[k][0], S[5]);
+              S[6] = fmaf(e, g[k][1], S[6]);
+              S[7] = fmaf(e, g[k][2], S[7]);
+              if constexpr (DEN) Sd = fmaf(e, gd[k], Sd);
+            }
+          }
+          float red = 0.f, redd = 0.f;
+          if (__any_sync(0xffffffffu, any)) {
+            red = warp_transpose_reduce8(S, lane);
+            if constexpr (DEN) redd = warp_sum(Sd);
+          }
+          if ((lane & 3) == 0) s_part[warp * kAccum + (lane >> 2)][jj] = red;
+          if constexpr (DEN) {
+            if (lane == 0) s_partd[warp][jj] = redd;
+          }
+        }
+      }
+      __syncthreads();
+      // Fixed-order combination across warps, one store per (gaussian, tile) entry.
+      for (int j = threadIdx.x; j < n; j += L::kThreads) {
+        const uint32_t m = s_mask[j];
+        float t[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        float td = 0.f;
+#pragma unroll
+        for (int w = 0; w < L::kWarps; ++w) {
+          if ((m >> w) & 1u) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) t[q] += s_part[w * kAccum + q][j];
+            if constexpr (DEN) td += s_partd[w][j];
+          }
+        }
+        const int e = s_entry[j];
+        a.partials[2 * static_cast<int64_t>(e)] = make_float4(t[0], t[1], t[2], t[3]);
+        a.partials[2 * static_cast<int64_t>(e) + 1] = make_float4(t[4], t[5], t[6], t[7]);
+        if constexpr (DEN) a.partial_d[e] = td;
+      }
+    }
+  }
+}
+
+// Deterministic per-view reduction of tile loss numerators: one block per view.
+__global__ void __launch_bounds__(256)
+loss_reduce_kernel(const double* __restrict__ tile_loss, int tiles_per_view, double* dst) {
+  __shared__ double s[2][256];
+  const int view = blockIdx.x;
+  double a0 = 0.0, a1 = 0.0;
+  for (int t = threadIdx.x; t < tiles_per_view; t += 256) {
+    const int64_t idx = static_cast<int64_t>(view) * tiles_per_view + t;
+    a0 += tile_loss[2 * idx];
+    a1 += tile_loss[2 * idx + 1];
+  }
+  s[0][threadIdx.x] = a0;
+  s[1][threadIdx.x] = a1;
+  __syncthreads();
+  for (int stride = 128; stride > 0; stride >>= 1) {
+    if (threadIdx.x < stride) {
+      s[0][threadIdx.x] += s[0][threadIdx.x + stride];
+      s[1][threadIdx.x] += s[1][threadIdx.x + stride];
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    dst[2 * view] = s[0][0];
+    dst[2 * view + 1] = s[1][0];
+  }
+}
+
+constexpr int kPPT = 2;
+
+RasterArgs base_args(const BinBuffers& bb, const Geometry& g, float cutoff) {
+  RasterArgs a{};
+  a.records = bb.records.as<GaussRecord>();
+  a.weights = bb.weights.as<float>();
+  a.spans = bb.spans.as<TileSpan>();
+  a.offsets = bb.offsets.as<int>();
+  a.gids = bb.vals[bb.sorted_sel].as<uint32_t>();
+  a.ranges = bb.ranges.as<int2>();
+  a.height = g.height;
+  a.width = g.width;
+  a.tiles_x = g.tiles_x;
+  a.tiles_per_view = g.tiles_per_view;
+  a.cutoff = cutoff;
+  return a;
+}
+
+template <int MODE, bool DEN>
+int launch(const RasterArgs& a, const Geometry& g, cudaStream_t s, const char* name) {
+  const int64_t n_tiles = g.n_tiles();
+  if (n_tiles == 0) return 0;
+  if (n_tiles > INT32_MAX) return set_error(-1, "too many tiles");
+  raster_kernel<kPPT, MODE, DEN>
+      <<<static_cast<unsigned>(n_tiles), Layout<kPPT>::kThreads, 0, s>>>(a);
+  return check_cuda(cudaGetLastError(), name);
+}
+
+int ensure_partials(BinBuffers& bb, bool den, cudaStream_t s) {
+  const size_t e = static_cast<size_t>(bb.n_entries > 0 ? bb.n_entries : 1);
+  RTGS_TRY(bb.partials.ensure(e * kAccum * sizeof(float), s));
+  if (den) RTGS_TRY(bb.partial_d.ensure(e * sizeof(float), s));
+  return 0;
+}
+
+}  // namespace
+
+int launch_raster_forward(const BinBuffers& bb, const Geometry& g, float cutoff, float* out,
+                          float* den, cudaStream_t s) {
+  RasterArgs a = base_args(bb, g, cutoff);
+  a.out = out;
+  a.den = den;
+  if (den) return launch<kFwd, true>(a, g, s, "raster forward (density)");
+  return launch<kFwd, false>(a, g, s, "raster forward");
+}
+
+int launch_raster_backward(BinBuffers& bb, const Geometry& g, float cutoff, const float* grad_out,
+                           const float* grad_den, cudaStream_t s) {
+  const bool den = grad_den != nullptr;
+  RTGS_TRY(ensure_partials(bb, den, s));
+  RasterArgs a = base_args(bb, g, cutoff);
+  a.grad_out = grad_out;
+  a.grad_den = grad_den;
+  a.partials = bb.partials.as<float4>();
+  a.partial_d = bb.partial_d.as<float>();
+  if (den) return launch<kBwd, true>(a, g, s, "raster backward (density)");
+  return launch<kBwd, false>(a, g, s, "raster backward");
+}
+
+int launch_raster_fit(BinBuffers& bb, const Geometry& g, float cutoff, const FitRasterArgs& fa,
+                      bool backward, cudaStream_t s) {
+  RTGS_TRY(ensure_partials(bb, false, s));
+  RasterArgs a = base_args(bb, g, cutoff);
+  a.partials = bb.partials.as<float4>();
+  a.fit = fa;
+  if (backward) return launch<kFit, false>(a, g, s, "raster fit");
+  return launch<kEval, false>(a, g, s, "raster eval");
+}
+
+int launch_loss_reduce(const double* tile_loss, const Geometry& g, double* dst, cudaStream_t s) {
+  if (g.n_views == 0) return 0;
+  loss_reduce_kernel<<<g.n_views, 256, 0, s>>>(tile_loss, g.tiles_per_view, dst);
+  return check_cuda(cudaGetLastError(), "loss_reduce_kernel");
+}
+
+}  // namespace rtgs2d

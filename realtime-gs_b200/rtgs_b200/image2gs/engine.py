@@ -1,0 +1,187 @@
+"""Python handle over the C fit engine (rtgs2d_fit_* in include/rtgs2d.h).
+
+The whole iteration loop runs in C++/CUDA; Python only moves tensors in and out.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import numpy as np
+import torch
+
+from rtgs_b200 import _native
+
+_RAW_SHAPES = (("xy_raw", 2), ("diag_raw", 2), ("off_raw", 0), ("color_raw", 3), ("weight_raw", 0))
+
+
+def pack_mask_bits(masks: torch.Tensor) -> torch.Tensor:
+    """(B, H, W) masks -> (B, ceil(H*W/8)) uint8, bit i of byte k = pixel 8k+i (little-endian).
+
+    Same bit order as numpy ``packbits(bitorder="little")`` used by the reference's PackedAlpha
+    (src/rtgs/data/compact_views.py:279-284). A pixel is in the mask when its value is > 0.5.
+    """
+    b = masks.shape[0]
+    flat = (masks.reshape(b, -1) > 0.5).to(torch.uint8)
+    pad = (-flat.shape[1]) % 8
+    if pad:
+        flat = torch.cat([flat, flat.new_zeros(b, pad)], dim=1)
+    weights = (2 ** torch.arange(8, device=flat.device, dtype=torch.int32)).to(torch.uint8)
+    return (flat.reshape(b, -1, 8) * weights).sum(dim=2, dtype=torch.int32).to(torch.uint8).contiguous()
+
+
+class FitEngine:
+    """Device-resident fit state for B views x N gaussians of an H x W image."""
+
+    def __init__(
+        self,
+        n_views: int,
+        n: int,
+        height: int,
+        width: int,
+        *,
+        lr: float,
+        iterations: int,
+        log_every: int,
+        check_every: int = 0,
+        freeze_geometry: bool = False,
+        loss_mode: int = _native.LOSS_MSE,
+        device: torch.device | None = None,
+    ) -> None:
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        self.n_views, self.n, self.height, self.width = int(n_views), int(n), int(height), int(width)
+        self.iterations = int(iterations)
+        opts = _native.FitOptions(
+            lr=float(lr), iterations=int(iterations), log_every=int(log_every),
+            check_every=int(check_every), freeze_geometry=int(bool(freeze_geometry)),
+            loss_mode=int(loss_mode),
+        )
+        self._lib = _native.lib()
+        handle = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _native.check(
+                self._lib.rtgs2d_fit_create(self.n_views, self.n, self.height, self.width,
+                                            ctypes.byref(opts), ctypes.byref(handle))
+            )
+        self._h = handle.value
+
+    # -- lifecycle -------------------------------------------------------------------------------
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            with torch.cuda.device(self.device):
+                self._lib.rtgs2d_fit_destroy(self._h)
+            self._h = None
+
+    def __del__(self) -> None:  # pragma: no cover - interpreter shutdown order
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self) -> FitEngine:
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+    def _stream(self) -> int:
+        return _native.stream_ptr(self.device)
+
+    # -- inputs ----------------------------------------------------------------------------------
+    def set_targets(self, targets: torch.Tensor, mask_bits: torch.Tensor | None = None) -> None:
+        targets = targets.to(self.device, torch.float32).contiguous()
+        if targets.shape != (self.n_views, self.height, self.width, 3):
+            raise ValueError("targets must be (B, H, W, 3)")
+        if mask_bits is not None:
+            mask_bits = mask_bits.to(self.device, torch.uint8).contiguous()
+        with torch.cuda.device(self.device):
+            _native.check(
+                self._lib.rtgs2d_fit_set_targets(self._h, targets.data_ptr(), _native.ptr(mask_bits), self._stream())
+            )
+
+    def set_raw(self, raw: dict[str, torch.Tensor]) -> None:
+        ts = []
+        for name, k in _RAW_SHAPES:
+            t = raw[name].to(self.device, torch.float32).contiguous()
+            want = (self.n_views, self.n, k) if k else (self.n_views, self.n)
+            if tuple(t.shape) != want:
+                raise ValueError(f"{name} must have shape {want}, got {tuple(t.shape)}")
+            ts.append(t)
+        with torch.cuda.device(self.device):
+            _native.check(self._lib.rtgs2d_fit_set_raw(self._h, *(t.data_ptr() for t in ts), self._stream()))
+            torch.cuda.current_stream(self.device).synchronize()
+
+    # -- running ---------------------------------------------------------------------------------
+    def run(self, n_iterations: int) -> None:
+        with torch.cuda.device(self.device):
+            _native.check(self._lib.rtgs2d_fit_run(self._h, int(n_iterations), self._stream()))
+
+    def params(self) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+        b, n = self.n_views, self.n
+        kw = dict(device=self.device, dtype=torch.float32)
+        xy = torch.empty(b, n, 2, **kw)
+        chol = torch.empty(b, n, 3, **kw)
+        color = torch.empty(b, n, 3, **kw)
+        weight = torch.empty(b, n, **kw)
+        with torch.cuda.device(self.device):
+            _native.check(
+                self._lib.rtgs2d_fit_get_params(self._h, xy.data_ptr(), chol.data_ptr(), color.data_ptr(),
+                                                weight.data_ptr(), self._stream())
+            )
+        return xy, chol, color, weight
+
+    def raw(self) -> dict[str, torch.Tensor]:
+        b, n = self.n_views, self.n
+        out = {}
+        for name, k in _RAW_SHAPES:
+            out[name] = torch.empty((b, n, k) if k else (b, n), device=self.device, dtype=torch.float32)
+        with torch.cuda.device(self.device):
+            _native.check(
+                self._lib.rtgs2d_fit_get_raw(self._h, *(out[nm].data_ptr() for nm, _ in _RAW_SHAPES), self._stream())
+            )
+        return out
+
+    def evaluate(self, want_render: bool = True) -> tuple[torch.Tensor | None, np.ndarray]:
+        """Render the current parameters; returns (render (B,H,W,3) or None, sums (B, 2))."""
+        render = None
+        if want_render:
+            render = torch.empty(self.n_views, self.height, self.width, 3, device=self.device, dtype=torch.float32)
+        sums = np.zeros((self.n_views, 2), dtype=np.float64)
+        with torch.cuda.device(self.device):
+            _native.check(
+                self._lib.rtgs2d_fit_evaluate(self._h, _native.ptr(render), sums.ctypes.data, self._stream())
+            )
+        return render, sums
+
+    def history(self) -> tuple[np.ndarray, np.ndarray]:
+        """(iterations (R,), sums (R, B, 2)) recorded so far."""
+        n_rows = ctypes.c_int64()
+        _native.check(self._lib.rtgs2d_fit_history(self._h, 0, None, None, ctypes.byref(n_rows)))
+        rows = int(n_rows.value)
+        iters = np.zeros(rows, dtype=np.int64)
+        sums = np.zeros((rows, self.n_views, 2), dtype=np.float64)
+        if rows:
+            with torch.cuda.device(self.device):
+                _native.check(
+                    self._lib.rtgs2d_fit_history(self._h, rows, iters.ctypes.data, sums.ctypes.data, ctypes.byref(n_rows))
+                )
+        return iters, sums
+
+    def stats(self) -> dict[str, float]:
+        step, e, p = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+        total = ctypes.c_double()
+        _native.check(self._lib.rtgs2d_fit_stats(self._h, ctypes.byref(step), ctypes.byref(e), ctypes.byref(p), ctypes.byref(total)))
+        return {"step": int(step.value), "last_entries": int(e.value), "last_pairs": int(p.value),
+                "total_pairs": float(total.value)}
+
+
+def psnr_values(sums: np.ndarray, counts: np.ndarray) -> list[float]:
+    """PSNR (dB) per view from clamped squared-error sums and value counts (metrics.py:12-15)."""
+    out = []
+    for s, c in zip(sums, counts):
+        mse = max(float(s) / float(c), 1e-12) if c > 0 else 1e-12
+        out.append(-10.0 * math.log10(mse))
+    return out

@@ -1,0 +1,167 @@
+"""Generate the golden fixtures in this folder by running the reference implementation.
+
+Run from the repository root, in a container where the reference project is mounted:
+
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py /root/reference/src
+
+It imports the reference's pure-PyTorch Stage-1 code (renderer, fit loop, batched fit,
+initialiser), evaluates it on small seeded inputs on the CPU and writes compressed ``.npz``
+files next to this script. Nothing at test time reads the reference; the tests read only these
+fixtures. Each fixture stores its inputs and the reference outputs.
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+
+
+def _save(name: str, **arrays) -> None:
+    out = {}
+    for key, value in arrays.items():
+        if value is None:
+            continue
+        if isinstance(value, torch.Tensor):
+            value = value.detach().cpu().numpy()
+        out[key] = np.asarray(value)
+    np.savez_compressed(HERE / f"{name}.npz", **out)
+    print(f"wrote {name}.npz", {k: v.shape for k, v in out.items()})
+
+
+def _stacked(seed: int, n_views: int, n: int, height: int, width: int, margin: float = 4.0):
+    """Random stacked gaussians incl. off-image and edge-straddling centres (reference test style)."""
+    gen = torch.Generator().manual_seed(seed)
+    span = torch.tensor([width + 2 * margin, height + 2 * margin])
+    xy = torch.rand(n_views, n, 2, generator=gen) * span - margin
+    chol = torch.zeros(n_views, n, 3)
+    chol[..., 0] = 0.5 + 3.0 * torch.rand(n_views, n, generator=gen)
+    chol[..., 2] = 0.5 + 3.0 * torch.rand(n_views, n, generator=gen)
+    chol[..., 1] = 0.5 * torch.randn(n_views, n, generator=gen)
+    color = torch.rand(n_views, n, 3, generator=gen)
+    weight = torch.rand(n_views, n, generator=gen)
+    return xy, chol, color, weight
+
+
+def main(ref_src: str) -> None:
+    sys.path.insert(0, ref_src)
+    from rtgs.core.gaussians2d import Gaussians2D, chol_covariance, chol_inverse_covariance
+    from rtgs.data.synthetic import make_synthetic_scene
+    from rtgs.image2gs.batched import fit_views_batched
+    from rtgs.image2gs.fit import FitConfig, fit_image_from_initialization, init_gaussians_2d
+    from rtgs.image2gs.renderer2d import (
+        _support_rects,
+        render_gaussian_coverage_2d,
+        render_gaussians_2d,
+        render_gaussians_2d_batched,
+    )
+
+    torch.manual_seed(0)
+
+    # 1. Support rectangles and conics: wide random sweep plus hand-picked edge cases.
+    gen = torch.Generator().manual_seed(11)
+    m = 4096
+    height, width = 37, 53
+    xy = torch.rand(m, 2, generator=gen) * torch.tensor([width + 40.0, height + 40.0]) - 20.0
+    chol = torch.empty(m, 3)
+    chol[:, 0] = torch.exp(torch.rand(m, generator=gen) * 5.0 - 2.5)
+    chol[:, 2] = torch.exp(torch.rand(m, generator=gen) * 5.0 - 2.5)
+    chol[:, 1] = torch.randn(m, generator=gen) * 2.0
+    # Centres exactly on pixel centres / pixel edges, and tiny / huge factors.
+    xy[:64, 0] = torch.arange(64).float() * 0.5
+    xy[64:128, 1] = torch.arange(64).float() * 0.5
+    chol[128:160] = torch.tensor([0.05, 0.0, 0.05])
+    chol[160:192] = torch.tensor([40.0, 5.0, 30.0])
+    xy[192:200] = torch.tensor([[1e6, 5.0], [-1e6, 5.0], [5.0, 1e6], [5.0, -1e6],
+                                [1e12, 1e12], [-0.49, -0.49], [width - 0.51, height - 0.51], [0.0, 0.0]])
+    cov = chol_covariance(chol)
+    x0, x1, y0, y1, nx, counts = _support_rects(xy, cov, height, width)
+    inv = chol_inverse_covariance(chol)
+    _save(
+        "rects",
+        xy=xy, chol=chol, height=height, width=width,
+        x0=x0, x1=x1, y0=y0, y1=y1, counts=counts,
+        cov=cov, conics=torch.stack([inv[:, 0, 0], inv[:, 0, 1], inv[:, 1, 1]], -1),
+    )
+
+    # 2. Forward renders (the reference CUDA-parity case, a larger mixed case, coverage).
+    xy, chol, color, weight = _stacked(7, 2, 64, 24, 20)
+    img = render_gaussians_2d_batched(xy, chol, color, weight, 24, 20, renderer="torch")
+    xy2, chol2, color2, weight2 = _stacked(21, 3, 400, 45, 61, margin=8.0)
+    chol2[0, :50, 0] *= 6.0
+    chol2[1, :50, 2] *= 6.0
+    img2 = render_gaussians_2d_batched(xy2, chol2, color2, weight2, 45, 61, renderer="torch")
+    bg = torch.tensor([0.1, 0.2, 0.3])
+    img2_bg = render_gaussians_2d_batched(xy2, chol2, color2, weight2, 45, 61, background=bg)
+    g_single = Gaussians2D(xy2[2], chol2[2], color2[2], weight2[2])
+    cover = render_gaussian_coverage_2d(g_single, 45, 61)
+    _save("render_fwd", xy=xy, chol=chol, color=color, weight=weight, image=img,
+          xy2=xy2, chol2=chol2, color2=color2, weight2=weight2, image2=img2,
+          background=bg, image2_bg=img2_bg, coverage2=cover)
+
+    # 3. Gradients: the reference CUDA-parity backward case and a squared-sum case.
+    grads = {}
+    leaves = [t.clone().requires_grad_(True) for t in _stacked(7, 2, 48, 20, 16)]
+    image = render_gaussians_2d_batched(*leaves, 20, 16, renderer="torch")
+    (image * torch.linspace(0.5, 1.5, image.numel()).view_as(image)).sum().backward()
+    for name, leaf in zip(("xy", "chol", "color", "weight"), leaves):
+        grads[f"in_{name}"] = leaf.detach()
+        grads[f"grad_{name}"] = leaf.grad
+    leaves2 = [t.clone().requires_grad_(True) for t in _stacked(5, 2, 200, 33, 47, margin=6.0)]
+    render_gaussians_2d_batched(*leaves2, 33, 47).square().sum().backward()
+    for name, leaf in zip(("xy", "chol", "color", "weight"), leaves2):
+        grads[f"in2_{name}"] = leaf.detach()
+        grads[f"grad2_{name}"] = leaf.grad
+    # Coverage (density channel) gradient.
+    leaves3 = [t.clone().requires_grad_(True) for t in _stacked(9, 1, 60, 24, 28)]
+    g3 = Gaussians2D(*(t[0] for t in leaves3))
+    cov3 = render_gaussian_coverage_2d(g3, 24, 28)
+    (cov3 * torch.linspace(-1.0, 2.0, cov3.numel()).view_as(cov3)).sum().backward()
+    for name, leaf in zip(("xy", "chol", "color", "weight"), leaves3):
+        grads[f"in3_{name}"] = leaf.detach()
+        grads[f"grad3_{name}"] = leaf.grad
+    _save("render_bwd", **grads)
+
+    # 4. The standard reference test scene images (8 views 32x32, first two) + initialiser.
+    scene = make_synthetic_scene(n_gaussians=25, n_cameras=8, image_size=32, seed=0)
+    images = torch.stack([scene.images[0], scene.images[1]])
+    g_init = init_gaussians_2d(images[0], 80, 0.7, torch.Generator().manual_seed(0))
+    _save("scene", images=images, init_xy=g_init.xy, init_chol=g_init.chol,
+          init_color=g_init.color, init_weight=g_init.weight)
+
+    # 5. Single-image native fit from a supplied initialisation (fit.py:309-352).
+    cfg = FitConfig(n_gaussians=80, iterations=40, log_every=10, lr=1e-2)
+    fitted, hist = fit_image_from_initialization(images[0], g_init, cfg)
+    _save("fit_single", image=images[0], init_xy=g_init.xy, init_chol=g_init.chol,
+          init_color=g_init.color, init_weight=g_init.weight,
+          iterations=cfg.iterations, log_every=cfg.log_every, lr=cfg.lr,
+          out_xy=fitted.xy, out_chol=fitted.chol, out_color=fitted.color, out_weight=fitted.weight,
+          psnr_iters=np.array([i for i, _ in hist["psnr"]]),
+          psnr_vals=np.array([v for _, v in hist["psnr"]]),
+          final_psnr=hist["final_psnr"], final_psnr_full=hist["final_psnr_full"])
+
+    # 6. Batched fit (batched.py:39-170) on the two scene views, seeds 0 and 1.
+    bcfg = FitConfig(n_gaussians=60, iterations=30, log_every=10, batch_views=True)
+    gs, hists = fit_views_batched([images[0], images[1]], bcfg, seed=0)
+    inits = [init_gaussians_2d(images[i], 60, 0.7, torch.Generator().manual_seed(i)) for i in range(2)]
+    _save("fit_batched", images=images, iterations=bcfg.iterations, log_every=bcfg.log_every,
+          init_xy=torch.stack([g.xy for g in inits]), init_chol=torch.stack([g.chol for g in inits]),
+          init_color=torch.stack([g.color for g in inits]), init_weight=torch.stack([g.weight for g in inits]),
+          out_xy=torch.stack([g.xy for g in gs]), out_chol=torch.stack([g.chol for g in gs]),
+          out_color=torch.stack([g.color for g in gs]), out_weight=torch.stack([g.weight for g in gs]),
+          psnr_vals=np.array([[v for _, v in h["psnr"]] for h in hists]),
+          psnr_iters=np.array([i for i, _ in hists[0]["psnr"]]),
+          final_psnr=np.array([h["final_psnr"] for h in hists]))
+
+    # 7. Single-gaussian known answers (tests/test_image2gs.py:14-39 in the reference).
+    single = Gaussians2D(torch.tensor([[8.5, 8.5]]), torch.tensor([[2.0, 0.0, 2.0]]),
+                         torch.tensor([[1.0, 0.5, 0.25]]), torch.tensor([1.0]))
+    _save("single", image=render_gaussians_2d(single, 17, 17))
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
