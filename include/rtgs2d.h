@@ -177,6 +177,13 @@ RTGS2D_API int rtgs2d_fit_evaluate(rtgs2d_fit* fit, float* render, double* sums,
 /* Recorded loss sums: copies up to max_rows rows; iters (rows,), sums (rows,B,2) on the host. */
 RTGS2D_API int rtgs2d_fit_history(const rtgs2d_fit* fit, int64_t max_rows, int64_t* iters, double* sums,
                        int64_t* n_rows);
+/* No reference counterpart: stage timing. When enabled, every iteration records CUDA events on
+ * `stream` around projection + binning, the fused raster kernel and the Adam kernel; the
+ * accumulated device milliseconds are returned by rtgs2d_fit_stage_times (after a run). */
+RTGS2D_API int rtgs2d_fit_set_profiling(rtgs2d_fit* fit, int32_t enable);
+RTGS2D_API int rtgs2d_fit_stage_times(const rtgs2d_fit* fit, double* bin_ms, double* raster_ms,
+                                      double* adam_ms, int64_t* iterations_timed,
+                                      double* pairs_timed);
 /* Completed iterations, entries/pairs of the last iteration, pairs summed over all iterations. */
 RTGS2D_API int rtgs2d_fit_stats(const rtgs2d_fit* fit, int64_t* step, int64_t* last_entries,
                      int64_t* last_pairs, double* total_pairs);

@@ -40,6 +40,15 @@ struct rtgs2d_fit {
   double total_pairs = 0.0;
   int64_t last_entries = 0, last_pairs = 0;
   bool have_targets = false, have_raw = false;
+  // stage timing (rtgs2d_fit_set_profiling)
+  bool profiling = false;
+  std::vector<cudaEvent_t> events;  // 4 per iteration of the current run
+  double bin_ms = 0.0, raster_ms = 0.0, adam_ms = 0.0, pairs_timed = 0.0;
+  int64_t iterations_timed = 0;
+  void release_events() {
+    for (cudaEvent_t e : events) cudaEventDestroy(e);
+    events.clear();
+  }
 };
 
 namespace {
@@ -140,6 +149,15 @@ double cosine_next_lr(double lr, double base_lr, double eta_min, int64_t epoch, 
          eta_min;
 }
 
+int ensure_events(rtgs2d_fit* f, size_t need) {
+  while (f->events.size() < need) {
+    cudaEvent_t e;
+    RTGS_CUDA(cudaEventCreate(&e), "cudaEventCreate");
+    f->events.push_back(e);
+  }
+  return 0;
+}
+
 int project_and_bin(rtgs2d_fit* f, cudaStream_t s) {
   RTGS_TRY(launch_project_raw(f->bb, f->geo, f->raw.as<float>(), f->m, f->n, s));
   RTGS_TRY(bin_entries(f->bb, f->geo, f->m, s));
@@ -234,6 +252,7 @@ int rtgs2d_fit_destroy(rtgs2d_fit* fit) {
   fit->tile_loss.release();
   fit->log.release();
   fit->eval_sums.release();
+  fit->release_events();
   delete fit;
   if (prev != dev) cudaSetDevice(prev);
   return RTGS2D_OK;
@@ -316,11 +335,22 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
   const double base_lr = f->opt.lr;
   const double eta_min = f->opt.lr * 0.1;
   const int64_t t_max = f->opt.iterations;
+  int64_t planned = t_max - f->step < n_iterations ? t_max - f->step : n_iterations;
+  if (planned < 0) planned = 0;
+  if (f->profiling) RTGS_TRY(ensure_events(f, static_cast<size_t>(4 * planned)));
+  std::vector<double> run_pairs;
   for (int64_t k = 0; k < n_iterations && f->step < t_max; ++k) {
     const int64_t it = f->step;
+    cudaEvent_t* ev = f->profiling ? &f->events[static_cast<size_t>(4 * k)] : nullptr;
+    if (ev) RTGS_CUDA(cudaEventRecord(ev[0], s), "event record");
     RTGS_TRY(project_and_bin(f, s));
     f->total_pairs += static_cast<double>(f->last_pairs);
+    if (ev) {
+      run_pairs.push_back(static_cast<double>(f->last_pairs));
+      RTGS_CUDA(cudaEventRecord(ev[1], s), "event record");
+    }
     RTGS_TRY(launch_raster_fit(f->bb, f->geo, kCutoff, raster_args(f), true, s));
+    if (ev) RTGS_CUDA(cudaEventRecord(ev[2], s), "event record");
     if (is_log_iter(f->opt, it)) {
       const int64_t slot = static_cast<int64_t>(f->log_iters.size());
       if (slot < f->max_logs) {
@@ -344,10 +374,43 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
     a.freeze_geometry = f->opt.freeze_geometry;
     RTGS_TRY(launch_adam_fit(f->bb, f->m, f->height, f->width, f->raw.as<float>(),
                              f->m1.as<float>(), f->m2.as<float>(), a, s));
+    if (ev) RTGS_CUDA(cudaEventRecord(ev[3], s), "event record");
     f->step += 1;
     f->lr_current = cosine_next_lr(f->lr_current, base_lr, eta_min, f->step, t_max);
   }
   RTGS_CUDA(cudaStreamSynchronize(s), "fit run sync");
+  if (f->profiling) {
+    for (size_t k = 0; k < run_pairs.size(); ++k) {
+      float t01 = 0.f, t12 = 0.f, t23 = 0.f;
+      RTGS_CUDA(cudaEventElapsedTime(&t01, f->events[4 * k], f->events[4 * k + 1]), "elapsed");
+      RTGS_CUDA(cudaEventElapsedTime(&t12, f->events[4 * k + 1], f->events[4 * k + 2]), "elapsed");
+      RTGS_CUDA(cudaEventElapsedTime(&t23, f->events[4 * k + 2], f->events[4 * k + 3]), "elapsed");
+      f->bin_ms += t01;
+      f->raster_ms += t12;
+      f->adam_ms += t23;
+      f->pairs_timed += run_pairs[k];
+      f->iterations_timed += 1;
+    }
+  }
+  return RTGS2D_OK;
+}
+
+int rtgs2d_fit_set_profiling(rtgs2d_fit* f, int32_t enable) {
+  RTGS_TRY(check_fit(f));
+  f->profiling = enable != 0;
+  f->bin_ms = f->raster_ms = f->adam_ms = f->pairs_timed = 0.0;
+  f->iterations_timed = 0;
+  return RTGS2D_OK;
+}
+
+int rtgs2d_fit_stage_times(const rtgs2d_fit* f, double* bin_ms, double* raster_ms, double* adam_ms,
+                           int64_t* iterations_timed, double* pairs_timed) {
+  if (!f) return set_error(RTGS2D_ERR_INVALID, "fit is NULL");
+  if (bin_ms) *bin_ms = f->bin_ms;
+  if (raster_ms) *raster_ms = f->raster_ms;
+  if (adam_ms) *adam_ms = f->adam_ms;
+  if (iterations_timed) *iterations_timed = f->iterations_timed;
+  if (pairs_timed) *pairs_timed = f->pairs_timed;
   return RTGS2D_OK;
 }
 

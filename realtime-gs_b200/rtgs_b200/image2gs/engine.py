@@ -170,6 +170,18 @@ class FitEngine:
                 )
         return iters, sums
 
+    def set_profiling(self, enable: bool = True) -> None:
+        """Record CUDA events around binning, the raster kernel and Adam in every iteration."""
+        _native.check(self._lib.rtgs2d_fit_set_profiling(self._h, int(bool(enable))))
+
+    def stage_times(self) -> dict[str, float]:
+        b, r, a, p = ctypes.c_double(), ctypes.c_double(), ctypes.c_double(), ctypes.c_double()
+        n = ctypes.c_int64()
+        _native.check(self._lib.rtgs2d_fit_stage_times(self._h, ctypes.byref(b), ctypes.byref(r), ctypes.byref(a),
+                                                       ctypes.byref(n), ctypes.byref(p)))
+        return {"bin_ms": b.value, "raster_ms": r.value, "adam_ms": a.value, "iterations": int(n.value),
+                "pairs": p.value}
+
     def stats(self) -> dict[str, float]:
         step, e, p = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
         total = ctypes.c_double()

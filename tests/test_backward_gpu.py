@@ -127,7 +127,8 @@ def test_reference_abi_forward_and_backward_match_oracle():
     up_d = torch.randn(views, h, w, generator=gen)
     ((rimg * up.reshape(-1, 3)).sum() + (rden * up_d.reshape(-1)).sum()).backward()
     grads = [torch.empty_like(x) for x in (d[0], d[1], d[2], d[3])]
-    _native.check(lib.rtgs2d_backward(arena, up.to(DEV).data_ptr(), up_d.to(DEV).data_ptr(),
+    up_dev, up_d_dev = up.to(DEV), up_d.to(DEV)  # keep alive until the kernels have run
+    _native.check(lib.rtgs2d_backward(arena, up_dev.data_ptr(), up_d_dev.data_ptr(),
                                       *(x.data_ptr() for x in d), views * n, views, h, w, 12.0,
                                       *(g.data_ptr() for g in grads), None))
     torch.cuda.synchronize()
