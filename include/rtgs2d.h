@@ -86,6 +86,28 @@ RTGS2D_API int rtgs2d_backward(rtgs2d_arena* arena, const float* grad_out, const
                     void* stream);
 
 /*
+ * No counterpart in the reference. rtgs2d_forward for callers that cannot allocate device
+ * memory: a plugin whose host application owns all device memory, a latency-critical loop where
+ * cudaMalloc/cudaFree would synchronise the device, or a process whose free device memory is
+ * already reserved by another allocator. Same arguments (minus the arena) and same results as
+ * rtgs2d_forward; all scratch comes from one 32 MiB static device array that every GPU loading
+ * this library holds until exit, and nothing is allocated on the device or the host.
+ *   - Problems that need more than 32 MiB of scratch (about 76 bytes per gaussian, 16 bytes per
+ *     (gaussian, 16x16 tile) entry, 8 bytes per tile, plus sort/scan temporaries) fail with
+ *     RTGS2D_ERR_CAPACITY and a message; use rtgs2d_forward for those.
+ *   - Every call on a device shares the array and it keeps the last call's contents; calls whose
+ *     GPU work overlaps (different host threads, or streams not ordered with each other) race.
+ *   - The first call on each device looks the array's address up with that device current;
+ *     make that first call before any stream capture.
+ *   - Synchronises `stream` once (the tile-entry count is read back to the host).
+ */
+RTGS2D_API int rtgs2d_forward_noalloc(const float* xy, const float* conics, const float* colors,
+                                      const float* weights, const int32_t* rects,
+                                      const int32_t* view_index, int64_t m, int64_t n_views,
+                                      int64_t height, int64_t width, double cutoff, float* out,
+                                      float* den, void* stream);
+
+/*
  * Batched render from Cholesky factors. Replaces
  * src/rtgs/image2gs/cuda_backend.py:127-170 `render_batched_cuda` (which built conics and support
  * rectangles with torch ops before calling the extension): conics, rectangles

@@ -1,0 +1,178 @@
+// rtgs2d_forward_noalloc: the reference-ABI forward render for callers that must not allocate.
+//
+// Some callers cannot call cudaMalloc: a plugin whose host application owns every byte of device
+// memory and forbids the plugin from allocating behind its back, a latency-critical loop in which
+// cudaMalloc / cudaFree would implicitly synchronise the device and stall its other streams, or a
+// process whose free device memory is already fully reserved by another allocator. For them this
+// entry point takes all of its scratch (gaussian records, tile spans, per-gaussian tile counts and
+// offsets, tile entries and their sort buffers, per-tile ranges, radix-sort and scan temporaries)
+// from one file-scope static device array of kScratchBytes per device, loaded with the library.
+// The caller still passes inputs and outputs; the host side allocates nothing either (the entry
+// count is read back into static host memory).
+//
+// Behaviour is that of rtgs2d_forward (same kernels, same results); the differences are:
+//   - problems whose scratch does not fit kScratchBytes are rejected with RTGS2D_ERR_CAPACITY
+//     and a message giving the bytes needed, before the entries that do not fit are written;
+//   - all calls on one device share the one array and it keeps the last call's contents, so calls
+//     whose GPU work overlaps (two host threads, or two streams without ordering between them)
+//     race and corrupt each other; calls ordered on one stream are safe;
+//   - the first call on each device looks up the array's device address (cudaGetSymbolAddress)
+//     with that device current; make that first call before any stream capture.
+#include <cub/device/device_radix_sort.cuh>
+#include <cub/device/device_scan.cuh>
+
+#include <mutex>
+#include <string>
+
+#include "../../include/rtgs2d.h"
+#include "internal.h"
+
+namespace {
+
+constexpr size_t kScratchBytes = size_t{32} << 20;  // 32 MiB per device
+constexpr int kMaxDevices = 64;
+
+// The scratch itself. In host code `g_scratch` is only a host-side stand-in for the symbol, never
+// a device address: the address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
+
+std::mutex g_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+unsigned long long g_host_stats[2];  // entry-count readback (pageable, no host allocation)
+
+int scratch_base(unsigned char** out) {
+  int dev = -1;
+  RTGS_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) {
+    return rtgs2d::set_error(RTGS2D_ERR_INVALID, "device index out of range for the static scratch table");
+  }
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    RTGS_CUDA(cudaGetSymbolAddress(&p, g_scratch), "cudaGetSymbolAddress(static scratch)");
+    g_scratch_addr[dev] = p;
+  }
+  *out = static_cast<unsigned char*>(g_scratch_addr[dev]);
+  return 0;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~size_t{255}; }
+
+// Bins whose buffers are views into the static array: every view is sized to what the launchers
+// ask for, so DevBuf::ensure never reallocates, and the views are detached before the BinBuffers
+// destructor runs, so nothing is ever freed.
+struct BorrowedBins {
+  rtgs2d::BinBuffers bb;
+  ~BorrowedBins() {
+    for (rtgs2d::DevBuf* b : {&bb.records, &bb.weights, &bb.spans, &bb.counts, &bb.offsets,
+                              &bb.keys[0], &bb.keys[1], &bb.vals[0], &bb.vals[1], &bb.ranges,
+                              &bb.partials, &bb.partial_d, &bb.cub_temp, &bb.stats}) {
+      b->ptr = nullptr;
+      b->bytes = 0;
+    }
+    bb.host_stats = nullptr;
+  }
+};
+
+struct Carver {
+  unsigned char* base;
+  size_t used = 0;
+  bool take(rtgs2d::DevBuf& buf, size_t bytes) {
+    bytes = bytes ? bytes : 1;
+    const size_t at = align256(used);
+    if (at + bytes > kScratchBytes) return false;
+    buf.ptr = base + at;
+    buf.bytes = bytes;
+    used = at + bytes;
+    return true;
+  }
+};
+
+int key_bits(int64_t n_tiles) {
+  int b = 1;
+  while ((int64_t{1} << b) < n_tiles) ++b;
+  return b;
+}
+
+int too_big(size_t need_hint) {
+  return rtgs2d::set_error(RTGS2D_ERR_CAPACITY,
+                           "rtgs2d_forward_noalloc: problem needs more than the " +
+                               std::to_string(kScratchBytes >> 20) +
+                               " MiB static scratch (at least " + std::to_string(need_hint) +
+                               " bytes); use rtgs2d_forward with an arena");
+}
+
+}  // namespace
+
+extern "C" int rtgs2d_forward_noalloc(const float* xy, const float* conics, const float* colors,
+                                      const float* weights, const int32_t* rects,
+                                      const int32_t* view_index, int64_t m, int64_t n_views,
+                                      int64_t height, int64_t width, double cutoff, float* out,
+                                      float* den, void* stream) {
+  using namespace rtgs2d;
+  if (m < 0 || n_views <= 0 || height <= 0 || width <= 0) {
+    return set_error(RTGS2D_ERR_INVALID, "m >= 0 and positive n_views, height, width are required");
+  }
+  if (height > 32768 || width > 32768 || m > INT32_MAX) {
+    return set_error(RTGS2D_ERR_CAPACITY, "height/width at most 32768 and m below 2^31");
+  }
+  if (!out) return set_error(RTGS2D_ERR_INVALID, "out is NULL");
+  if (m > 0 && (!xy || !conics || !colors || !weights || !rects || !view_index)) {
+    return set_error(RTGS2D_ERR_INVALID, "an input pointer is NULL");
+  }
+  const Geometry g = make_geometry(static_cast<int>(n_views), static_cast<int>(height),
+                                   static_cast<int>(width));
+  if (g.n_tiles() > INT32_MAX) return set_error(RTGS2D_ERR_CAPACITY, "too many tiles");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  unsigned char* base = nullptr;
+  RTGS_TRY(scratch_base(&base));
+  BorrowedBins holder;
+  BinBuffers& bb = holder.bb;
+  bb.host_stats = g_host_stats;
+
+  // Per-gaussian and per-tile buffers (the sizes the projection and binning launchers request).
+  const size_t mm = static_cast<size_t>(m > 0 ? m : 1);
+  const size_t tiles = static_cast<size_t>(g.n_tiles() > 0 ? g.n_tiles() : 1);
+  size_t scan_bytes = 0;
+  RTGS_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, scan_bytes, static_cast<int*>(nullptr),
+                                          static_cast<int*>(nullptr), static_cast<int>(m), s),
+            "scan size query");
+  Carver c{base};
+  const size_t need_m = mm * (sizeof(GaussRecord) + sizeof(TileSpan) + 3 * sizeof(int)) +
+                        tiles * sizeof(int2) + scan_bytes;
+  if (!c.take(bb.records, mm * sizeof(GaussRecord)) || !c.take(bb.spans, mm * sizeof(TileSpan)) ||
+      !c.take(bb.counts, mm * sizeof(int)) || !c.take(bb.offsets, mm * sizeof(int)) ||
+      !c.take(bb.stats, 2 * sizeof(unsigned long long)) ||
+      !c.take(bb.ranges, tiles * sizeof(int2)) ||
+      (den != nullptr && !c.take(bb.weights, mm * sizeof(float)))) {
+    return too_big(need_m);
+  }
+
+  RTGS_TRY(launch_project_conic(bb, g, xy, conics, colors, weights, rects, view_index, m,
+                                den != nullptr, s));
+  // Entry count, to size the entry buffers before the binning writes any entry.
+  RTGS_CUDA(cudaMemcpyAsync(g_host_stats, bb.stats.ptr, 2 * sizeof(unsigned long long),
+                            cudaMemcpyDeviceToHost, s),
+            "entry count readback");
+  RTGS_CUDA(cudaStreamSynchronize(s), "entry count sync");
+  const unsigned long long entries = g_host_stats[0];
+  if (entries > static_cast<unsigned long long>(INT32_MAX)) return too_big(entries * 16);
+  const size_t e = static_cast<size_t>(entries > 0 ? entries : 1);
+  size_t sort_bytes = 0;
+  {
+    cub::DoubleBuffer<uint32_t> dk(nullptr, nullptr);
+    cub::DoubleBuffer<uint32_t> dv(nullptr, nullptr);
+    RTGS_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, dk, dv, static_cast<int>(e), 0,
+                                              key_bits(g.n_tiles()), s),
+              "sort size query");
+  }
+  const size_t temp_bytes = scan_bytes > sort_bytes ? scan_bytes : sort_bytes;
+  if (!c.take(bb.keys[0], e * sizeof(uint32_t)) || !c.take(bb.keys[1], e * sizeof(uint32_t)) ||
+      !c.take(bb.vals[0], e * sizeof(uint32_t)) || !c.take(bb.vals[1], e * sizeof(uint32_t)) ||
+      !c.take(bb.cub_temp, temp_bytes)) {
+    return too_big(c.used + 4 * e * sizeof(uint32_t) + temp_bytes);
+  }
+  RTGS_TRY(bin_entries(bb, g, m, s));
+  return launch_raster_forward(bb, g, static_cast<float>(cutoff), out, den, s);
+}

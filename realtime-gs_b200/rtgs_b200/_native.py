@@ -50,6 +50,10 @@ _SIGNATURES = {
          _vp, _vp, _vp, _vp, _vp],
         ctypes.c_int,
     ),
+    "rtgs2d_forward_noalloc": (
+        [_vp, _vp, _vp, _vp, _vp, _vp, _c_int64, _c_int64, _c_int64, _c_int64, _dbl, _vp, _vp, _vp],
+        ctypes.c_int,
+    ),
     "rtgs2d_render_forward": (
         [_vp, _vp, _vp, _vp, _vp, _c_int64, _c_int64, _c_int64, _c_int64, _vp, _vp, _vp],
         ctypes.c_int,
