@@ -199,6 +199,12 @@ RTGS2D_API int rtgs2d_fit_evaluate(rtgs2d_fit* fit, float* render, double* sums,
 /* Recorded loss sums: copies up to max_rows rows; iters (rows,), sums (rows,B,2) on the host. */
 RTGS2D_API int rtgs2d_fit_history(const rtgs2d_fit* fit, int64_t max_rows, int64_t* iters, double* sums,
                        int64_t* n_rows);
+/* No reference counterpart: tile-entry capacity of the fit loop. The loop bins into a fixed number
+ * of (gaussian, tile) entries; a chunk of iterations that needed more is rolled back and re-run
+ * with more room (results are unchanged). rtgs2d_fit_reserve pre-sizes the capacity;
+ * rtgs2d_fit_capacity reports it and the number of re-run chunks. */
+RTGS2D_API int rtgs2d_fit_reserve(rtgs2d_fit* fit, int64_t entries, void* stream);
+RTGS2D_API int rtgs2d_fit_capacity(const rtgs2d_fit* fit, int64_t* entries, int64_t* retries);
 /* No reference counterpart: stage timing. When enabled, every iteration records CUDA events on
  * `stream` around projection + binning, the fused raster kernel and the Adam kernel; the
  * accumulated device milliseconds are returned by rtgs2d_fit_stage_times (after a run). */

@@ -3,6 +3,7 @@
 #include <cstdio>
 #include <new>
 #include <string>
+#include <vector>
 
 #include "../../include/rtgs2d.h"
 #include "internal.h"
@@ -20,6 +21,8 @@ int set_error(int code, const std::string& msg) {
 
 int check_cuda(cudaError_t err, const char* what) {
   if (err == cudaSuccess) return 0;
+  // Clear the runtime's last-error slot so a later, unrelated launch check does not report it.
+  cudaGetLastError();
   const int code = (err == cudaErrorMemoryAllocation) ? RTGS2D_ERR_ALLOC : RTGS2D_ERR_CUDA;
   return set_error(code, std::string(what) + ": " + cudaGetErrorName(err) + " (" +
                              cudaGetErrorString(err) + ")");
@@ -49,8 +52,8 @@ void DevBuf::release() {
 }
 
 void BinBuffers::release() {
-  for (DevBuf* b : {&records, &weights, &spans, &counts, &offsets, &keys[0], &keys[1], &vals[0],
-                    &vals[1], &ranges, &partials, &partial_d, &cub_temp, &stats}) {
+  for (DevBuf* b : {&records, &weights, &spans, &counts, &offsets, &entries[0], &entries[1],
+                    &ranges, &partials, &partial_d, &cub_temp, &sort_counts, &stats}) {
     b->release();
   }
   if (host_stats) cudaFreeHost(host_stats);
@@ -271,10 +274,12 @@ int rtgs2d_arena_copy_binning(const rtgs2d_arena* arena, int64_t max_entries, ui
   cudaStream_t s = as_stream(stream);
   const int64_t ce = bb.n_entries < max_entries ? bb.n_entries : max_entries;
   const int64_t ct = arena->n_tiles < max_tiles ? arena->n_tiles : max_tiles;
+  std::vector<uint64_t> packed;
   if (gids && ce > 0) {
-    RTGS_CUDA(cudaMemcpyAsync(gids, bb.vals[bb.sorted_sel].ptr, static_cast<size_t>(ce) * sizeof(uint32_t),
-                              cudaMemcpyDeviceToHost, s),
-              "copy gids");
+    packed.resize(static_cast<size_t>(ce));
+    RTGS_CUDA(cudaMemcpyAsync(packed.data(), bb.entries[bb.sorted_sel].ptr,
+                              static_cast<size_t>(ce) * sizeof(uint64_t), cudaMemcpyDeviceToHost, s),
+              "copy entries");
   }
   if (ranges && ct > 0) {
     RTGS_CUDA(cudaMemcpyAsync(ranges, bb.ranges.ptr, static_cast<size_t>(ct) * 2 * sizeof(int32_t),
@@ -282,6 +287,7 @@ int rtgs2d_arena_copy_binning(const rtgs2d_arena* arena, int64_t max_entries, ui
               "copy ranges");
   }
   RTGS_CUDA(cudaStreamSynchronize(s), "copy binning sync");
+  for (size_t i = 0; i < packed.size(); ++i) gids[i] = static_cast<uint32_t>(packed[i]);
   return RTGS2D_OK;
 }
 

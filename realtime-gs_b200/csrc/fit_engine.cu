@@ -2,12 +2,16 @@
 //
 // Per iteration (fit.py:451-482, batched.py:128-145):
 //   project_raw   raw params -> build() -> conic, support rectangle, tile span    (1 kernel)
-//   bin_entries   scan + entry-count readback + emit + radix sort + tile ranges
+//   binning       scan + emit + radix sort with the device-side entry count + tile ranges
 //   raster fit    forward, L2-loss gradient, backward -> per-entry moments   (1 kernel)
 //   loss reduce   only at logging iterations                                  (1 kernel)
 //   adam          entry sums -> chain rule -> Adam on all 9 raw params       (1 kernel)
 // The host advances torch's CosineAnnealingLR recursion in double precision and passes the
-// bias-corrected step size to the Adam kernel.
+// bias-corrected step size to the Adam kernel. Nothing is read back inside an iteration: the
+// iterations of a chunk are enqueued back to back, and the entry buffers have a fixed capacity.
+// At the end of a chunk the largest entry count of the chunk is read back; if it exceeded the
+// capacity (entries were dropped), the chunk is rolled back to a device snapshot of the raw
+// parameters and Adam moments taken at its start and re-run with a larger capacity.
 #include <cmath>
 #include <new>
 #include <vector>
@@ -25,6 +29,7 @@ struct rtgs2d_fit {
   Geometry geo;
   BinBuffers bb;
   DevBuf raw, m1, m2;  // planar (9, M)
+  DevBuf snap;         // raw, m1, m2 at the start of the current chunk (overflow roll-back)
   DevBuf targets;      // (B, H, W, 3)
   DevBuf mask;         // (B, mask_bytes)
   int64_t mask_bytes = 0;
@@ -39,6 +44,7 @@ struct rtgs2d_fit {
   double lr_current = 0.0;
   double total_pairs = 0.0;
   int64_t last_entries = 0, last_pairs = 0;
+  int64_t retries = 0;  // chunks re-run after an entry-capacity overflow
   bool have_targets = false, have_raw = false;
   // stage timing (rtgs2d_fit_set_profiling)
   bool profiling = false;
@@ -158,11 +164,28 @@ int ensure_events(rtgs2d_fit* f, size_t need) {
   return 0;
 }
 
+// Projection + synchronous binning (exact entry count; used outside the iteration loop).
 int project_and_bin(rtgs2d_fit* f, cudaStream_t s) {
   RTGS_TRY(launch_project_raw(f->bb, f->geo, f->raw.as<float>(), f->m, f->n, s));
   RTGS_TRY(bin_entries(f->bb, f->geo, f->m, s));
   f->last_entries = f->bb.n_entries;
   f->last_pairs = f->bb.n_pairs;
+  return 0;
+}
+
+constexpr int64_t kChunk = 64;
+
+// Copy raw/m1/m2 to the snapshot (to_snap) or back.
+int snapshot(rtgs2d_fit* f, bool to_snap, cudaStream_t s) {
+  const size_t bytes = static_cast<size_t>(kRawSlots) * (f->m > 0 ? f->m : 1) * sizeof(float);
+  RTGS_TRY(f->snap.ensure(3 * bytes, s));
+  char* sp = f->snap.as<char>();
+  DevBuf* bufs[3] = {&f->raw, &f->m1, &f->m2};
+  for (int k = 0; k < 3; ++k) {
+    void* dst = to_snap ? static_cast<void*>(sp + k * bytes) : bufs[k]->ptr;
+    const void* src = to_snap ? static_cast<const void*>(bufs[k]->ptr) : static_cast<const void*>(sp + k * bytes);
+    RTGS_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, s), "snapshot copy");
+  }
   return 0;
 }
 
@@ -252,6 +275,7 @@ int rtgs2d_fit_destroy(rtgs2d_fit* fit) {
   fit->tile_loss.release();
   fit->log.release();
   fit->eval_sums.release();
+  fit->snap.release();
   fit->release_events();
   delete fit;
   if (prev != dev) cudaSetDevice(prev);
@@ -335,63 +359,123 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
   const double base_lr = f->opt.lr;
   const double eta_min = f->opt.lr * 0.1;
   const int64_t t_max = f->opt.iterations;
-  int64_t planned = t_max - f->step < n_iterations ? t_max - f->step : n_iterations;
-  if (planned < 0) planned = 0;
-  if (f->profiling) RTGS_TRY(ensure_events(f, static_cast<size_t>(4 * planned)));
-  std::vector<double> run_pairs;
-  for (int64_t k = 0; k < n_iterations && f->step < t_max; ++k) {
-    const int64_t it = f->step;
-    cudaEvent_t* ev = f->profiling ? &f->events[static_cast<size_t>(4 * k)] : nullptr;
-    if (ev) RTGS_CUDA(cudaEventRecord(ev[0], s), "event record");
+  BinBuffers& bb = f->bb;
+  if (!bb.host_stats) {
+    RTGS_CUDA(cudaMallocHost(reinterpret_cast<void**>(&bb.host_stats),
+                             kStatSlots * sizeof(unsigned long long)),
+              "pinned stats");
+  }
+  if (!bb.stats.ptr) {
+    RTGS_TRY(bb.stats.ensure(kStatSlots * sizeof(unsigned long long), s));
+    RTGS_CUDA(cudaMemsetAsync(bb.stats.ptr, 0, kStatSlots * sizeof(unsigned long long), s),
+              "zero stats");
+  }
+  // Initial capacity: the current entry count with headroom (gaussians grow and shrink).
+  if (bb.capacity == 0) {
     RTGS_TRY(project_and_bin(f, s));
-    f->total_pairs += static_cast<double>(f->last_pairs);
-    if (ev) {
-      run_pairs.push_back(static_cast<double>(f->last_pairs));
-      RTGS_CUDA(cudaEventRecord(ev[1], s), "event record");
-    }
-    RTGS_TRY(launch_raster_fit(f->bb, f->geo, kCutoff, raster_args(f), true, s));
-    if (ev) RTGS_CUDA(cudaEventRecord(ev[2], s), "event record");
-    if (is_log_iter(f->opt, it)) {
-      const int64_t slot = static_cast<int64_t>(f->log_iters.size());
-      if (slot < f->max_logs) {
-        RTGS_TRY(launch_loss_reduce(f->tile_loss.as<double>(), f->geo,
-                                    f->log.as<double>() + slot * f->n_views * 2, s));
-        f->log_iters.push_back(it);
+    RTGS_TRY(ensure_entry_capacity(bb, f->last_entries + f->last_entries / 2 + 4096, false, s));
+  }
+  int64_t remaining = t_max - f->step < n_iterations ? t_max - f->step : n_iterations;
+  while (remaining > 0) {
+    const int64_t chunk = remaining < kChunk ? remaining : kChunk;
+    // Host state to restore if the chunk must be re-run.
+    const int64_t step0 = f->step;
+    const double lr0 = f->lr_current;
+    const size_t logs0 = f->log_iters.size();
+    RTGS_TRY(snapshot(f, true, s));
+    RTGS_CUDA(cudaMemsetAsync(bb.stats.as<unsigned long long>() + kStatPairsTotal, 0,
+                              2 * sizeof(unsigned long long), s),
+              "reset chunk stats");
+    if (f->profiling) RTGS_TRY(ensure_events(f, static_cast<size_t>(4 * chunk)));
+    // Iteration k: [projection] binning, raster, Adam. The Adam step of iteration k also projects
+    // the updated parameters for iteration k + 1 (one kernel); only the chunk's first projection
+    // is a separate launch and its last Adam step projects nothing.
+    RTGS_TRY(launch_project_raw(bb, f->geo, f->raw.as<float>(), f->m, f->n, s));
+    for (int64_t k = 0; k < chunk; ++k) {
+      const int64_t it = f->step;
+      cudaEvent_t* ev = f->profiling ? &f->events[static_cast<size_t>(4 * k)] : nullptr;
+      if (ev) RTGS_CUDA(cudaEventRecord(ev[0], s), "event record");
+      RTGS_TRY(bin_entries_async(bb, f->geo, f->m, s));
+      if (ev) RTGS_CUDA(cudaEventRecord(ev[1], s), "event record");
+      RTGS_TRY(launch_raster_fit(bb, f->geo, kCutoff, raster_args(f), true, s));
+      if (ev) RTGS_CUDA(cudaEventRecord(ev[2], s), "event record");
+      if (is_log_iter(f->opt, it)) {
+        const int64_t slot = static_cast<int64_t>(f->log_iters.size());
+        if (slot < f->max_logs) {
+          RTGS_TRY(launch_loss_reduce(f->tile_loss.as<double>(), f->geo,
+                                      f->log.as<double>() + slot * f->n_views * 2, s));
+          f->log_iters.push_back(it);
+        }
       }
+      const double t = static_cast<double>(it + 1);
+      const double bc1 = 1.0 - std::pow(0.9, t);
+      const double bc2 = 1.0 - std::pow(0.999, t);
+      const double step_size = f->lr_current / bc1;
+      AdamScalars a;
+      a.neg_step_size = static_cast<float>(-step_size);
+      a.bc2_sqrt = static_cast<float>(std::pow(bc2, 0.5));
+      a.beta1 = 0.9f;
+      a.beta2 = 0.999f;
+      a.one_minus_beta1 = static_cast<float>(1.0 - 0.9);
+      a.one_minus_beta2 = static_cast<float>(1.0 - 0.999);
+      a.eps = 1e-8f;
+      a.freeze_geometry = f->opt.freeze_geometry;
+      RTGS_TRY(launch_adam_fit(bb, f->geo, f->m, f->n, f->raw.as<float>(), f->m1.as<float>(),
+                               f->m2.as<float>(), a, k + 1 < chunk, s));
+      if (ev) RTGS_CUDA(cudaEventRecord(ev[3], s), "event record");
+      f->step += 1;
+      f->lr_current = cosine_next_lr(f->lr_current, base_lr, eta_min, f->step, t_max);
     }
-    const double t = static_cast<double>(it + 1);
-    const double bc1 = 1.0 - std::pow(0.9, t);
-    const double bc2 = 1.0 - std::pow(0.999, t);
-    const double step_size = f->lr_current / bc1;
-    AdamScalars a;
-    a.neg_step_size = static_cast<float>(-step_size);
-    a.bc2_sqrt = static_cast<float>(std::pow(bc2, 0.5));
-    a.beta1 = 0.9f;
-    a.beta2 = 0.999f;
-    a.one_minus_beta1 = static_cast<float>(1.0 - 0.9);
-    a.one_minus_beta2 = static_cast<float>(1.0 - 0.999);
-    a.eps = 1e-8f;
-    a.freeze_geometry = f->opt.freeze_geometry;
-    RTGS_TRY(launch_adam_fit(f->bb, f->m, f->height, f->width, f->raw.as<float>(),
-                             f->m1.as<float>(), f->m2.as<float>(), a, s));
-    if (ev) RTGS_CUDA(cudaEventRecord(ev[3], s), "event record");
-    f->step += 1;
-    f->lr_current = cosine_next_lr(f->lr_current, base_lr, eta_min, f->step, t_max);
-  }
-  RTGS_CUDA(cudaStreamSynchronize(s), "fit run sync");
-  if (f->profiling) {
-    for (size_t k = 0; k < run_pairs.size(); ++k) {
-      float t01 = 0.f, t12 = 0.f, t23 = 0.f;
-      RTGS_CUDA(cudaEventElapsedTime(&t01, f->events[4 * k], f->events[4 * k + 1]), "elapsed");
-      RTGS_CUDA(cudaEventElapsedTime(&t12, f->events[4 * k + 1], f->events[4 * k + 2]), "elapsed");
-      RTGS_CUDA(cudaEventElapsedTime(&t23, f->events[4 * k + 2], f->events[4 * k + 3]), "elapsed");
-      f->bin_ms += t01;
-      f->raster_ms += t12;
-      f->adam_ms += t23;
-      f->pairs_timed += run_pairs[k];
-      f->iterations_timed += 1;
+    RTGS_CUDA(cudaMemcpyAsync(bb.host_stats, bb.stats.ptr, kStatSlots * sizeof(unsigned long long),
+                              cudaMemcpyDeviceToHost, s),
+              "chunk stats readback");
+    RTGS_CUDA(cudaStreamSynchronize(s), "chunk sync");
+    const int64_t max_entries = static_cast<int64_t>(bb.host_stats[kStatMaxEntries]);
+    if (max_entries > bb.capacity) {
+      // Entries were dropped in this chunk: roll back and re-run it with room for them.
+      if (max_entries > INT32_MAX) return set_error(RTGS2D_ERR_CAPACITY, "more than 2^31 tile entries");
+      RTGS_TRY(snapshot(f, false, s));
+      f->step = step0;
+      f->lr_current = lr0;
+      f->log_iters.resize(logs0);
+      f->retries += 1;
+      RTGS_TRY(ensure_entry_capacity(bb, max_entries + max_entries / 2 + 4096, false, s));
+      continue;
     }
+    f->last_entries = static_cast<int64_t>(bb.host_stats[kStatEntries]);
+    f->last_pairs = static_cast<int64_t>(bb.host_stats[kStatPairs]);
+    const double chunk_pairs = static_cast<double>(bb.host_stats[kStatPairsTotal]);
+    f->total_pairs += chunk_pairs;
+    if (f->profiling) {
+      for (int64_t k = 0; k < chunk; ++k) {
+        float t01 = 0.f, t12 = 0.f, t23 = 0.f;
+        const size_t e = static_cast<size_t>(4 * k);
+        RTGS_CUDA(cudaEventElapsedTime(&t01, f->events[e], f->events[e + 1]), "elapsed");
+        RTGS_CUDA(cudaEventElapsedTime(&t12, f->events[e + 1], f->events[e + 2]), "elapsed");
+        RTGS_CUDA(cudaEventElapsedTime(&t23, f->events[e + 2], f->events[e + 3]), "elapsed");
+        f->bin_ms += t01;
+        f->raster_ms += t12;
+        f->adam_ms += t23;
+      }
+      f->pairs_timed += chunk_pairs;
+      f->iterations_timed += chunk;
+    }
+    remaining -= chunk;
   }
+  return RTGS2D_OK;
+}
+
+int rtgs2d_fit_reserve(rtgs2d_fit* f, int64_t entries, void* stream) {
+  RTGS_TRY(check_fit(f));
+  if (entries < 0 || entries > INT32_MAX) return set_error(RTGS2D_ERR_CAPACITY, "entries out of range");
+  if (entries <= f->bb.capacity) return RTGS2D_OK;
+  return ensure_entry_capacity(f->bb, entries, false, as_stream(stream));
+}
+
+int rtgs2d_fit_capacity(const rtgs2d_fit* f, int64_t* entries, int64_t* retries) {
+  if (!f) return set_error(RTGS2D_ERR_INVALID, "fit is NULL");
+  if (entries) *entries = f->bb.capacity;
+  if (retries) *retries = f->retries;
   return RTGS2D_OK;
 }
 
@@ -474,6 +558,7 @@ int rtgs2d_fit_history(const rtgs2d_fit* f, int64_t max_rows, int64_t* iters, do
 int rtgs2d_fit_stats(const rtgs2d_fit* f, int64_t* step, int64_t* last_entries,
                      int64_t* last_pairs, double* total_pairs) {
   if (!f) return set_error(RTGS2D_ERR_INVALID, "fit is NULL");
+  if (last_entries) *last_entries = f->last_entries;
   if (step) *step = f->step;
   if (last_entries) *last_entries = f->last_entries;
   if (last_pairs) *last_pairs = f->last_pairs;

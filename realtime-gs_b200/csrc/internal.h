@@ -38,23 +38,36 @@ struct DevBuf {
   T* as() const { return static_cast<T*>(ptr); }
 };
 
+// Blocks of every radix-sort pass (sort.cu); the per-pass digit-count array holds 256 x this.
+constexpr int kSortGrid = 592;
+
+// Device statistics slots (unsigned long long each).
+enum StatSlot : int {
+  kStatEntries = 0,     // (gaussian, tile) entries of the current projection
+  kStatPairs = 1,       // (gaussian, pixel-in-rectangle) pairs of the current projection
+  kStatPairsTotal = 2,  // pairs accumulated over projections until reset by the caller
+  kStatMaxEntries = 3,  // largest entry count binned since reset by the caller (capacity check)
+  kStatSlots = 4
+};
+
 // Scratch used by projection + tile binning + raster for one render / one fit iteration.
 struct BinBuffers {
-  DevBuf records;   // GaussRecord[M]
-  DevBuf weights;   // float[M] (density variants)
-  DevBuf spans;     // TileSpan[M]
-  DevBuf counts;    // int[M]  tiles per gaussian
-  DevBuf offsets;   // int[M]  exclusive scan of counts (entry index of each gaussian's first tile)
-  DevBuf keys[2];   // uint32[E] tile keys (double buffer for the radix sort)
-  DevBuf vals[2];   // uint32[E] gaussian ids
-  DevBuf ranges;    // int2[n_tiles] [start, end) into the sorted entries
-  DevBuf partials;  // float[E][8] per (gaussian, tile) gradient moments
-  DevBuf partial_d; // float[E]   per (gaussian, tile) density-gradient moment
-  DevBuf cub_temp;
-  DevBuf stats;     // unsigned long long[2]: entries, pairs
+  DevBuf records;     // GaussRecord[M]
+  DevBuf weights;     // float[M] (density variants)
+  DevBuf spans;       // TileSpan[M]
+  DevBuf counts;      // int[M]  tiles per gaussian
+  DevBuf offsets;     // int[M]  exclusive scan of counts (entry index of each gaussian's first tile)
+  DevBuf entries[2];  // uint64[capacity] (tile key << 32 | gaussian id), sort double buffer
+  DevBuf ranges;      // int2[n_tiles] [start, end) into the sorted entries
+  DevBuf partials;    // float[capacity][8] per (gaussian, tile) gradient moments
+  DevBuf partial_d;   // float[capacity]   per (gaussian, tile) density-gradient moment
+  DevBuf cub_temp;    // exclusive-scan temporaries
+  DevBuf sort_counts; // int[256 * kSortGrid] radix-sort digit counts
+  DevBuf stats;       // unsigned long long[kStatSlots]
   unsigned long long* host_stats = nullptr;  // pinned mirror of `stats`
-  int sorted_sel = 0;                         // which of keys/vals holds the sorted result
-  int64_t n_entries = 0;
+  int sorted_sel = 0;                         // which entries buffer holds the sorted result
+  int64_t capacity = 0;                       // entries the entry buffers can hold
+  int64_t n_entries = 0;                      // host-known entry count (synchronous binning)
   int64_t n_pairs = 0;
   ~BinBuffers();
   void release();
@@ -85,11 +98,23 @@ int launch_support_rects(const float* xy, const float* chol, int64_t m, int heig
 int launch_build_params(const float* raw, int64_t m, int height, int width, float* xy, float* chol,
                         float* color, float* weight, cudaStream_t s);
 
-// ---- binning (binning.cu) -----------------------------------------------------------------------
-// Scan counts, read the entry count back to the host (synchronises `s`), emit (tile key, gaussian
-// id) entries, stable radix sort by key, and build per-tile ranges. Requires bb.counts/spans/stats
-// from a projection launcher.
+// ---- binning (binning.cu, sort.cu) --------------------------------------------------------------
+// Synchronous binning: scan counts, read the entry count back to the host (synchronises `s`),
+// grow the entry buffers to fit, then bin_entries_async. Requires bb.counts/spans/stats from a
+// projection launcher.
 int bin_entries(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s);
+// Asynchronous binning into the current capacity (no host synchronisation): scan, emit (entries
+// past the capacity are dropped and show up as stats[kStatMaxEntries] > capacity), stable radix
+// sort with the device-side count, per-tile ranges.
+int bin_entries_async(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s);
+// Allocate the entry-sized buffers (entries, partials[, partial_d]) for `capacity` entries.
+int ensure_entry_capacity(BinBuffers& bb, int64_t capacity, bool density, cudaStream_t s);
+// Stable LSD radix sort of packed entries by their key bits; the count is read on the device.
+int radix_sort_entries(uint64_t* buf0, uint64_t* buf1, const unsigned long long* d_n, int64_t cap,
+                       int key_bits, int* counts, cudaStream_t s, int* result_sel);
+int sort_plan_passes(int key_bits);
+size_t sort_counts_bytes();
+int key_bits_for(int64_t n_tiles);
 
 // ---- raster (raster.cu) -------------------------------------------------------------------------
 enum LossMode : int { kLossMse = 0, kLossMaskWeighted = 1, kLossMaskOnly = 2 };
@@ -128,7 +153,9 @@ struct AdamScalars {
   float beta1, beta2, one_minus_beta1, one_minus_beta2, eps;
   int freeze_geometry;
 };
-int launch_adam_fit(const BinBuffers& bb, int64_t m, int height, int width, float* raw, float* m1,
-                    float* m2, const AdamScalars& a, cudaStream_t s);
+// Adam step from the last raster's entry moments; with project_next the updated parameters are
+// also projected (records, spans, counts, stats) for the next iteration's binning.
+int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_view, float* raw,
+                    float* m1, float* m2, const AdamScalars& a, bool project_next, cudaStream_t s);
 
 }  // namespace rtgs2d

@@ -1,0 +1,181 @@
+// Device helpers shared by the projection, finalisation and Adam kernels.
+#pragma once
+
+#include "internal.h"
+
+namespace rtgs2d {
+
+constexpr int kSmallEntries = 32;  // gaussians with more entries are summed by the whole warp
+
+struct ProjOut {
+  GaussRecord* records;
+  float* weights;  // nullable
+  TileSpan* spans;
+  int* counts;
+  unsigned long long* stats;  // [entries, pairs]
+};
+
+__device__ __forceinline__ void project_tail(int64_t i, bool active, float mx, float my, Conic k,
+                                             int x0, int x1, int y0, int y1, long long pixels,
+                                             float w, float cr, float cg, float cb, int view,
+                                             int tiles_x, int tiles_per_view, const ProjOut& o) {
+  int cnt = 0;
+  long long pairs = 0;
+  if (active) {
+    if (pixels > 0 && isfinite(mx) && isfinite(my)) {
+      const int tx0 = x0 / kTile, tx1 = x1 / kTile;
+      const int ty0 = y0 / kTile, ty1 = y1 / kTile;
+      const int ntx = tx1 - tx0 + 1;
+      cnt = ntx * (ty1 - ty0 + 1);
+      pairs = pixels;
+      TileSpan sp;
+      sp.tx0 = tx0;
+      sp.ty0 = ty0;
+      sp.ntx = ntx;
+      sp.key_base = view * tiles_per_view;
+      o.spans[i] = sp;
+      GaussRecord r;
+      r.geo = make_float4(mx, my, k.i00, __fmul_rn(2.0f, k.i01));
+      r.app = make_float4(k.i11, __fmul_rn(w, cr), __fmul_rn(w, cg), __fmul_rn(w, cb));
+      r.rect = make_int4(x0, y0, x1 - x0, y1 - y0);
+      o.records[i] = r;
+    }
+    if (o.weights) o.weights[i] = w;
+    o.counts[i] = cnt;
+  }
+  // Warp-aggregated totals (all lanes reach this point).
+  unsigned long long e = static_cast<unsigned long long>(cnt);
+  unsigned long long p = static_cast<unsigned long long>(pairs);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    e += __shfl_xor_sync(0xffffffffu, e, off);
+    p += __shfl_xor_sync(0xffffffffu, p, off);
+  }
+  if ((threadIdx.x & 31) == 0 && (e | p)) {
+    atomicAdd(&o.stats[kStatEntries], e);
+    atomicAdd(&o.stats[kStatPairs], p);
+    atomicAdd(&o.stats[kStatPairsTotal], p);
+  }
+}
+
+// Entries at or past the entry capacity were never written (an overflowed binning, whose results
+// the caller discards); never read them.
+__device__ __forceinline__ int clamp_to_capacity(int cnt, int off, int64_t cap) {
+  const int64_t room = cap - off;
+  if (room <= 0) return 0;
+  return cnt < room ? cnt : static_cast<int>(room);
+}
+
+struct Moments {
+  float s[8];
+  float sd;
+};
+
+// Sum a gaussian's entries [off, off + cnt) in index order. Small counts: the owning thread;
+// larger counts: the whole warp, lanes striding and a fixed butterfly -- the choice depends only
+// on the count, so results are reproducible run to run.
+template <bool DEN>
+__device__ __forceinline__ Moments gather_moments(const float4* __restrict__ partials,
+                                                  const float* __restrict__ partial_d, int cnt,
+                                                  int off) {
+  Moments mo;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) mo.s[k] = 0.f;
+  mo.sd = 0.f;
+  if (cnt > 0 && cnt <= kSmallEntries) {
+    const float4* p = partials + 2 * static_cast<int64_t>(off);
+    int j = 0;
+    // Four entries' loads in flight at a time; the additions keep the sequential entry order.
+    for (; j + 4 <= cnt; j += 4) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = p[2 * j + u];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        mo.s[0] += v[2 * u].x; mo.s[1] += v[2 * u].y; mo.s[2] += v[2 * u].z; mo.s[3] += v[2 * u].w;
+        mo.s[4] += v[2 * u + 1].x; mo.s[5] += v[2 * u + 1].y; mo.s[6] += v[2 * u + 1].z;
+        mo.s[7] += v[2 * u + 1].w;
+      }
+      if constexpr (DEN) {
+        for (int u = 0; u < 4; ++u) mo.sd += partial_d[off + j + u];
+      }
+    }
+    for (; j < cnt; ++j) {
+      const float4 p0 = p[2 * j];
+      const float4 p1 = p[2 * j + 1];
+      mo.s[0] += p0.x; mo.s[1] += p0.y; mo.s[2] += p0.z; mo.s[3] += p0.w;
+      mo.s[4] += p1.x; mo.s[5] += p1.y; mo.s[6] += p1.z; mo.s[7] += p1.w;
+      if constexpr (DEN) mo.sd += partial_d[off + j];
+    }
+  }
+  const int lane = threadIdx.x & 31;
+  unsigned big = __ballot_sync(0xffffffffu, cnt > kSmallEntries);
+  while (big) {
+    const int src = __ffs(big) - 1;
+    big &= big - 1;
+    const int c = __shfl_sync(0xffffffffu, cnt, src);
+    const int o = __shfl_sync(0xffffffffu, off, src);
+    float t[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float td = 0.f;
+    for (int j = lane; j < c; j += 32) {
+      const float4 p0 = partials[2 * static_cast<int64_t>(o + j)];
+      const float4 p1 = partials[2 * static_cast<int64_t>(o + j) + 1];
+      t[0] += p0.x; t[1] += p0.y; t[2] += p0.z; t[3] += p0.w;
+      t[4] += p1.x; t[5] += p1.y; t[6] += p1.z; t[7] += p1.w;
+      if constexpr (DEN) td += partial_d[o + j];
+    }
+#pragma unroll
+    for (int sh = 16; sh > 0; sh >>= 1) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) t[k] += __shfl_xor_sync(0xffffffffu, t[k], sh);
+      if constexpr (DEN) td += __shfl_xor_sync(0xffffffffu, td, sh);
+    }
+    if (lane == src) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mo.s[k] = t[k];
+      mo.sd = td;
+    }
+  }
+  return mo;
+}
+
+struct GeoGrad {
+  float gmx, gmy, gi00, gi01, gi11;  // conic gradient (reference grad_conics convention)
+  float gl11, gl21, gl22;            // Cholesky gradient
+};
+
+__device__ __forceinline__ GeoGrad geo_grad(const Moments& mo, float i00, float i01, float i11,
+                                            float l11, float l21, float l22, bool want_chol) {
+  GeoGrad r;
+  r.gmx = fmaf(i00, mo.s[0], i01 * mo.s[1]);
+  r.gmy = fmaf(i01, mo.s[0], i11 * mo.s[1]);
+  r.gi00 = -0.5f * mo.s[2];
+  r.gi01 = -mo.s[3];
+  r.gi11 = -0.5f * mo.s[4];
+  r.gl11 = r.gl21 = r.gl22 = 0.f;
+  if (want_chol) {
+    const float a = 1.0f / l11;
+    const float b = -l21 / (l11 * l22);
+    const float c = 1.0f / l22;
+    const float ga = 2.0f * a * r.gi00;
+    const float gb = fmaf(2.0f * b, r.gi00, c * r.gi01);
+    const float gc = fmaf(b, r.gi01, 2.0f * c * r.gi11);
+    r.gl11 = -a * fmaf(ga, a, gb * b);
+    r.gl21 = -gb * a * c;
+    r.gl22 = -c * fmaf(gb, b, gc * c);
+  }
+  return r;
+}
+
+// One Adam update of a single float parameter, in the order of torch's single-tensor Adam
+// (exp_avg.lerp_, exp_avg_sq.mul_.addcmul_, denom = sqrt(v)/bc2_sqrt + eps, p.addcdiv_).
+__device__ __forceinline__ void adam_update(float& p, float& m1, float& m2, float g,
+                                            const AdamScalars& a) {
+  m1 = __fadd_rn(m1, __fmul_rn(a.one_minus_beta1, __fsub_rn(g, m1)));
+  m2 = __fadd_rn(__fmul_rn(m2, a.beta2), __fmul_rn(__fmul_rn(a.one_minus_beta2, g), g));
+  const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(m2), a.bc2_sqrt), a.eps);
+  p = __fadd_rn(p, __fmul_rn(a.neg_step_size, __fdiv_rn(m1, denom)));
+}
+
+
+}  // namespace rtgs2d

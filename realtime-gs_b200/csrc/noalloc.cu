@@ -18,7 +18,6 @@
 //     race and corrupt each other; calls ordered on one stream are safe;
 //   - the first call on each device looks up the array's device address (cudaGetSymbolAddress)
 //     with that device current; make that first call before any stream capture.
-#include <cub/device/device_radix_sort.cuh>
 #include <cub/device/device_scan.cuh>
 
 #include <mutex>
@@ -38,7 +37,7 @@ static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 
 std::mutex g_mu;
 void* g_scratch_addr[kMaxDevices] = {};
-unsigned long long g_host_stats[2];  // entry-count readback (pageable, no host allocation)
+unsigned long long g_host_stats[rtgs2d::kStatSlots];  // entry-count readback (pageable, no host allocation)
 
 int scratch_base(unsigned char** out) {
   int dev = -1;
@@ -65,8 +64,8 @@ struct BorrowedBins {
   rtgs2d::BinBuffers bb;
   ~BorrowedBins() {
     for (rtgs2d::DevBuf* b : {&bb.records, &bb.weights, &bb.spans, &bb.counts, &bb.offsets,
-                              &bb.keys[0], &bb.keys[1], &bb.vals[0], &bb.vals[1], &bb.ranges,
-                              &bb.partials, &bb.partial_d, &bb.cub_temp, &bb.stats}) {
+                              &bb.entries[0], &bb.entries[1], &bb.ranges, &bb.partials,
+                              &bb.partial_d, &bb.cub_temp, &bb.sort_counts, &bb.stats}) {
       b->ptr = nullptr;
       b->bytes = 0;
     }
@@ -87,12 +86,6 @@ struct Carver {
     return true;
   }
 };
-
-int key_bits(int64_t n_tiles) {
-  int b = 1;
-  while ((int64_t{1} << b) < n_tiles) ++b;
-  return b;
-}
 
 int too_big(size_t need_hint) {
   return rtgs2d::set_error(RTGS2D_ERR_CAPACITY,
@@ -140,11 +133,12 @@ extern "C" int rtgs2d_forward_noalloc(const float* xy, const float* conics, cons
             "scan size query");
   Carver c{base};
   const size_t need_m = mm * (sizeof(GaussRecord) + sizeof(TileSpan) + 3 * sizeof(int)) +
-                        tiles * sizeof(int2) + scan_bytes;
+                        tiles * sizeof(int2) + scan_bytes + sort_counts_bytes();
   if (!c.take(bb.records, mm * sizeof(GaussRecord)) || !c.take(bb.spans, mm * sizeof(TileSpan)) ||
       !c.take(bb.counts, mm * sizeof(int)) || !c.take(bb.offsets, mm * sizeof(int)) ||
-      !c.take(bb.stats, 2 * sizeof(unsigned long long)) ||
-      !c.take(bb.ranges, tiles * sizeof(int2)) ||
+      !c.take(bb.stats, kStatSlots * sizeof(unsigned long long)) ||
+      !c.take(bb.ranges, tiles * sizeof(int2)) || !c.take(bb.cub_temp, scan_bytes) ||
+      !c.take(bb.sort_counts, sort_counts_bytes()) ||
       (den != nullptr && !c.take(bb.weights, mm * sizeof(float)))) {
     return too_big(need_m);
   }
@@ -156,23 +150,13 @@ extern "C" int rtgs2d_forward_noalloc(const float* xy, const float* conics, cons
                             cudaMemcpyDeviceToHost, s),
             "entry count readback");
   RTGS_CUDA(cudaStreamSynchronize(s), "entry count sync");
-  const unsigned long long entries = g_host_stats[0];
+  const unsigned long long entries = g_host_stats[kStatEntries];
   if (entries > static_cast<unsigned long long>(INT32_MAX)) return too_big(entries * 16);
   const size_t e = static_cast<size_t>(entries > 0 ? entries : 1);
-  size_t sort_bytes = 0;
-  {
-    cub::DoubleBuffer<uint32_t> dk(nullptr, nullptr);
-    cub::DoubleBuffer<uint32_t> dv(nullptr, nullptr);
-    RTGS_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, dk, dv, static_cast<int>(e), 0,
-                                              key_bits(g.n_tiles()), s),
-              "sort size query");
+  if (!c.take(bb.entries[0], e * sizeof(uint64_t)) || !c.take(bb.entries[1], e * sizeof(uint64_t))) {
+    return too_big(c.used + 2 * e * sizeof(uint64_t));
   }
-  const size_t temp_bytes = scan_bytes > sort_bytes ? scan_bytes : sort_bytes;
-  if (!c.take(bb.keys[0], e * sizeof(uint32_t)) || !c.take(bb.keys[1], e * sizeof(uint32_t)) ||
-      !c.take(bb.vals[0], e * sizeof(uint32_t)) || !c.take(bb.vals[1], e * sizeof(uint32_t)) ||
-      !c.take(bb.cub_temp, temp_bytes)) {
-    return too_big(c.used + 4 * e * sizeof(uint32_t) + temp_bytes);
-  }
+  bb.capacity = static_cast<int64_t>(e);  // binning then fits without growing any buffer
   RTGS_TRY(bin_entries(bb, g, m, s));
   return launch_raster_forward(bb, g, static_cast<float>(cutoff), out, den, s);
 }

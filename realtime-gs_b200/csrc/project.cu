@@ -6,61 +6,12 @@
 //   - reference ABI (xy, conics, colors, weights, rects, view_index): renderer2d_ext.cpp:87-128;
 //   - raw fit parameters (planar 9 x M): the fit loop's build() (fit.py:402-417) fused in.
 #include "internal.h"
+#include "kernels.cuh"
 
 namespace rtgs2d {
 namespace {
 
 constexpr int kThreads = 256;
-
-struct ProjOut {
-  GaussRecord* records;
-  float* weights;  // nullable
-  TileSpan* spans;
-  int* counts;
-  unsigned long long* stats;  // [entries, pairs]
-};
-
-__device__ __forceinline__ void project_tail(int64_t i, bool active, float mx, float my, Conic k,
-                                             int x0, int x1, int y0, int y1, long long pixels,
-                                             float w, float cr, float cg, float cb, int view,
-                                             int tiles_x, int tiles_per_view, const ProjOut& o) {
-  int cnt = 0;
-  long long pairs = 0;
-  if (active) {
-    if (pixels > 0 && isfinite(mx) && isfinite(my)) {
-      const int tx0 = x0 / kTile, tx1 = x1 / kTile;
-      const int ty0 = y0 / kTile, ty1 = y1 / kTile;
-      const int ntx = tx1 - tx0 + 1;
-      cnt = ntx * (ty1 - ty0 + 1);
-      pairs = pixels;
-      TileSpan sp;
-      sp.tx0 = tx0;
-      sp.ty0 = ty0;
-      sp.ntx = ntx;
-      sp.key_base = view * tiles_per_view;
-      o.spans[i] = sp;
-      GaussRecord r;
-      r.geo = make_float4(mx, my, k.i00, __fmul_rn(2.0f, k.i01));
-      r.app = make_float4(k.i11, __fmul_rn(w, cr), __fmul_rn(w, cg), __fmul_rn(w, cb));
-      r.rect = make_int4(x0, y0, x1 - x0, y1 - y0);
-      o.records[i] = r;
-    }
-    if (o.weights) o.weights[i] = w;
-    o.counts[i] = cnt;
-  }
-  // Warp-aggregated totals (all lanes reach this point).
-  unsigned long long e = static_cast<unsigned long long>(cnt);
-  unsigned long long p = static_cast<unsigned long long>(pairs);
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-    e += __shfl_xor_sync(0xffffffffu, e, off);
-    p += __shfl_xor_sync(0xffffffffu, p, off);
-  }
-  if ((threadIdx.x & 31) == 0 && (e | p)) {
-    atomicAdd(&o.stats[0], e);
-    atomicAdd(&o.stats[1], p);
-  }
-}
 
 __global__ void __launch_bounds__(kThreads)
 project_chol_kernel(const float* __restrict__ xy, const float* __restrict__ chol,
@@ -193,7 +144,7 @@ int prepare(BinBuffers& bb, int64_t m, bool want_weights, cudaStream_t s, ProjOu
   RTGS_TRY(bb.spans.ensure(mm * sizeof(TileSpan), s));
   RTGS_TRY(bb.counts.ensure(mm * sizeof(int), s));
   RTGS_TRY(bb.offsets.ensure(mm * sizeof(int), s));
-  RTGS_TRY(bb.stats.ensure(2 * sizeof(unsigned long long), s));
+  RTGS_TRY(bb.stats.ensure(kStatSlots * sizeof(unsigned long long), s));
   if (want_weights) RTGS_TRY(bb.weights.ensure(mm * sizeof(float), s));
   RTGS_CUDA(cudaMemsetAsync(bb.stats.ptr, 0, 2 * sizeof(unsigned long long), s), "memset stats");
   o->records = bb.records.as<GaussRecord>();

@@ -9,13 +9,16 @@
 //
 //   forward   pixel accumulators live in registers; the list order is the reference's
 //             summation order, so a render is deterministic and no atomics are used.
-//   backward  per (warp, gaussian): 8 moments over the warp's pixels
+//   backward  the tile's upstream gradients are staged in shared memory; for every (gaussian,
+//             tile) entry the exact piece = support rectangle x tile is evaluated and 8 moments
 //               Sdx = sum dq*dx, Sdy = sum dq*dy, Sxx = sum dq*dx^2, Sxy = sum dq*dx*dy,
 //               Syy = sum dq*dy^2, Sr/Sg/Sb = sum e*g_rgb       (e = exp(-q/2), dq = e * g.A)
-//             reduced with an 8-way transpose butterfly, combined across warps in a fixed order
-//             in shared memory and written once per (gaussian, tile) entry. A per-gaussian pass
-//             (optim.cu) sums a gaussian's entries in order and applies the chain rule, so
-//             gradients are deterministic as well and no global atomics are issued.
+//             are written once per entry. A warp works on 4 pieces at a time, 8 lanes ("octet")
+//             per piece striding over exactly the piece's pixels; pieces are bucketed by their
+//             step count ceil(area / 8) so the 4 pieces of a warp take the same number of steps.
+//             An 8-lane transpose butterfly leaves moment r in lane r of each octet: one 32-byte
+//             store per entry. A per-gaussian pass (optim.cu) sums a gaussian's entries in order
+//             and applies the chain rule: deterministic, no global atomics.
 //   fit       forward -> L2 loss gradient in registers -> backward, in one kernel: the rendered
 //             image and dL/dout never leave the SM.
 //
@@ -27,6 +30,7 @@ namespace rtgs2d {
 namespace {
 
 constexpr int kBatch = 128;
+constexpr int kMaxSteps = kTile * kTile / 8;  // octet steps of a full-tile piece
 
 template <int PPT>
 struct Layout {
@@ -45,7 +49,7 @@ struct RasterArgs {
   const float* weights;       // density variants
   const TileSpan* spans;      // backward: entry index
   const int* offsets;         // backward: entry index
-  const uint32_t* gids;       // sorted gaussian ids
+  const uint64_t* entries;    // sorted (tile key << 32 | gaussian id)
   const int2* ranges;         // per tile
   int height, width, tiles_x, tiles_per_view;
   float cutoff;
@@ -85,6 +89,29 @@ __device__ __forceinline__ float warp_transpose_reduce8(const float (&v)[8], int
   return c;  // sum of v[(lane >> 2) & 7] over the warp
 }
 
+// Transpose butterfly inside each 8-lane octet: returns, in lane r of the octet, the octet-wide sum
+// of v[r].
+__device__ __forceinline__ float octet_transpose_reduce8(const float (&v)[8], int lane) {
+  const bool u4 = lane & 4, u2 = lane & 2, u1 = lane & 1;
+  float a[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float send = u4 ? v[k] : v[k + 4];
+    const float keep = u4 ? v[k + 4] : v[k];
+    a[k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  float b[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const float send = u2 ? a[k] : a[k + 2];
+    const float keep = u2 ? a[k + 2] : a[k];
+    b[k] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  const float send = u1 ? b[0] : b[1];
+  const float keep = u1 ? b[1] : b[0];
+  return keep + __shfl_xor_sync(0xffffffffu, send, 1);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
@@ -108,8 +135,11 @@ raster_kernel(const RasterArgs a) {
   __shared__ uint32_t s_mask[kBatch];
   __shared__ float s_wt[DEN ? kBatch : 1];
   __shared__ int s_entry[kDoBwd ? kBatch : 1];
-  __shared__ float s_part[kDoBwd ? L::kWarps * kAccum : 1][kBatch + 1];
-  __shared__ float s_partd[(kDoBwd && DEN) ? L::kWarps : 1][kBatch + 1];
+  __shared__ int s_piece[kDoBwd ? kBatch : 1];      // rx0 | ry0 << 4 | (pw-1) << 8 | (ph-1) << 12
+  __shared__ float4 s_g[kDoBwd ? kTile * kTile : 1];  // upstream gradient (r, g, b, density) per pixel
+  __shared__ int s_list[kDoBwd ? kBatch : 1];   // batch records sorted by octet steps, descending
+  __shared__ int s_bucket[kMaxSteps + 1];
+  __shared__ int s_next;
   __shared__ double s_loss[L::kWarps][2];
 
   const int tile = blockIdx.x;
@@ -137,7 +167,7 @@ raster_kernel(const RasterArgs a) {
   // Stage records [base, base + n) of this tile's list into shared memory.
   auto stage = [&](int base, int n, bool with_entry) {
     for (int j = threadIdx.x; j < n; j += L::kThreads) {
-      const uint32_t gid = a.gids[base + j];
+      const uint32_t gid = static_cast<uint32_t>(a.entries[base + j]);
       const GaussRecord r = a.records[gid];
       s_geo[j] = r.geo;
       s_app[j] = r.app;
@@ -160,6 +190,9 @@ raster_kernel(const RasterArgs a) {
         if (with_entry) {
           const TileSpan sp = a.spans[gid];
           s_entry[j] = a.offsets[gid] + (tile_y - sp.ty0) * sp.ntx + (tile_x - sp.tx0);
+          const int px0 = max(rx0, 0), px1 = min(rx1, kTile - 1);
+          const int py0 = max(ry0, 0), py1 = min(ry1, kTile - 1);
+          s_piece[j] = px0 | (py0 << 4) | ((px1 - px0) << 8) | ((py1 - py0) << 12);
         }
       }
     }
@@ -173,11 +206,13 @@ raster_kernel(const RasterArgs a) {
     acc[k][0] = acc[k][1] = acc[k][2] = 0.f;
     accd[k] = 0.f;
   }
+  // A list that fits one batch is staged once, with the backward's fields, for both passes.
+  const bool single_batch = range.y - range.x <= kBatch;
   if constexpr (kDoFwd) {
     for (int base = range.x; base < range.y; base += kBatch) {
       const int n = min(kBatch, range.y - base);
       __syncthreads();
-      stage(base, n, false);
+      stage(base, n, kDoBwd && single_batch);
       __syncthreads();
       for (int c = 0; c < n; c += 32) {
         const int j = c + lane;
@@ -298,41 +333,86 @@ raster_kernel(const RasterArgs a) {
 
   if constexpr (kDoBwd) {
     // ---------------------------------------------------------------- backward
+    // Upstream gradient of every tile pixel into shared memory (zeros outside the image).
+#pragma unroll
+    for (int k = 0; k < PPT; ++k) {
+      const int lx = px - ox, ly = py[k] - oy;
+      s_g[ly * kTile + lx] = make_float4(g[k][0], g[k][1], g[k][2], gd[k]);
+    }
+    float* partials_f = reinterpret_cast<float*>(a.partials);
+    const int r8 = lane & 7;
     for (int base = range.x; base < range.y; base += kBatch) {
       const int n = min(kBatch, range.y - base);
       __syncthreads();
-      stage(base, n, true);
+      if (!single_batch || !kDoFwd) stage(base, n, true);
+      for (int i = threadIdx.x; i <= kMaxSteps; i += L::kThreads) s_bucket[i] = 0;
+      if (threadIdx.x == 0) s_next = 0;
       __syncthreads();
-      for (int c = 0; c < n; c += 32) {
-        const int j = c + lane;
-        unsigned bits = __ballot_sync(0xffffffffu, j < n && ((s_mask[j] >> warp) & 1u));
-        while (bits) {
-          const int jj = c + __ffs(bits) - 1;
-          bits &= bits - 1;
-          const float4 geo = s_geo[jj];
-          const float4 app = s_app[jj];
-          const int4 rc = s_rect[jj];
-          float wt = 0.f;
-          if constexpr (DEN) wt = s_wt[jj];
-          float S[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          float Sd = 0.f;
-          bool any = false;
-          const float dx = __fsub_rn(pxc, geo.x);
-          const bool inx = static_cast<unsigned>(px - rc.x) <= static_cast<unsigned>(rc.z);
+      for (int j = threadIdx.x; j < n; j += L::kThreads) {
+        const int pc = s_piece[j];
+        const int area = (((pc >> 8) & 15) + 1) * (((pc >> 12) & 15) + 1);
+        atomicAdd(&s_bucket[(area + 7) >> 3], 1);
+      }
+      __syncthreads();
+      if (warp == 0) {  // list cursors, most steps first: lane l owns step count kMaxSteps - l
+        const int steps = kMaxSteps - lane;
+        const int c = s_bucket[steps];
+        int x = c;
 #pragma unroll
-          for (int k = 0; k < PPT; ++k) {
-            const float dy = __fsub_rn(pyc[k], geo.y);
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, x, o);
+          if (lane >= o) x += y;
+        }
+        s_bucket[steps] = x - c;
+      }
+      __syncthreads();
+      for (int j = threadIdx.x; j < n; j += L::kThreads) {
+        const int pc = s_piece[j];
+        const int area = (((pc >> 8) & 15) + 1) * (((pc >> 12) & 15) + 1);
+        s_list[atomicAdd(&s_bucket[(area + 7) >> 3], 1)] = j;
+      }
+      __syncthreads();
+
+      const int n_tasks = (n + 3) >> 2;
+      while (true) {
+        int task = 0;
+        if (lane == 0) task = atomicAdd(&s_next, 1);
+        task = __shfl_sync(0xffffffffu, task, 0);
+        if (task >= n_tasks) break;
+        const int p = 4 * task + (lane >> 3);
+        const bool valid = p < n;
+        const int j = valid ? s_list[p] : s_list[0];
+        const float4 geo = s_geo[j];
+        const float4 app = s_app[j];
+        const int pc = s_piece[j];
+        const int rx0 = pc & 15, ry0 = (pc >> 4) & 15;
+        const int pw = ((pc >> 8) & 15) + 1, ph = ((pc >> 12) & 15) + 1;
+        const int area = valid ? pw * ph : 0;
+        const int max_steps = static_cast<int>(__reduce_max_sync(0xffffffffu, static_cast<unsigned>((area + 7) >> 3)));
+        const float inv_pw = 1.0f / static_cast<float>(pw);
+        const float pxc0 = static_cast<float>(ox + rx0) + 0.5f;  // integer + 0.5 sums stay exact
+        const float pyc0 = static_cast<float>(oy + ry0) + 0.5f;
+        const int sidx0 = ry0 * kTile + rx0;
+        float wt = 0.f;
+        if constexpr (DEN) wt = s_wt[j];
+        float S[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        float Sd = 0.f;
+        for (int st = 0; st < max_steps; ++st) {
+          const int k = r8 + 8 * st;
+          if (k < area) {
+            // k / pw exactly: (k + 0.5) / pw stays >= 0.5 / pw away from every integer for k < 256.
+            const int yy = __float2int_rz((static_cast<float>(k) + 0.5f) * inv_pw);
+            const int xx = k - yy * pw;
+            const float dx = __fsub_rn(pxc0 + static_cast<float>(xx), geo.x);
+            const float dy = __fsub_rn(pyc0 + static_cast<float>(yy), geo.y);
             const float q = pair_q(dx, dy, geo.z, geo.w, app.x);
-            const bool in = inx &&
-                            static_cast<unsigned>(py[k] - rc.y) <= static_cast<unsigned>(rc.w) &&
-                            q < a.cutoff;
-            if (in) {
-              any = true;
+            if (q < a.cutoff) {
+              const float4 gv = s_g[sidx0 + yy * kTile + xx];
               const float e = __expf(-0.5f * q);
-              float v = g[k][0] * app.y;
-              v = fmaf(g[k][1], app.z, v);
-              v = fmaf(g[k][2], app.w, v);
-              if constexpr (DEN) v = fmaf(gd[k], wt, v);
+              float v = gv.x * app.y;
+              v = fmaf(gv.y, app.z, v);
+              v = fmaf(gv.z, app.w, v);
+              if constexpr (DEN) v = fmaf(gv.w, wt, v);
               const float dq = e * v;
               const float ex = dq * dx;
               const float fy = dq * dy;
@@ -341,41 +421,22 @@ raster_kernel(const RasterArgs a) {
               S[2] = fmaf(ex, dx, S[2]);
               S[3] = fmaf(ex, dy, S[3]);
               S[4] = fmaf(fy, dy, S[4]);
-              S[5] = fmaf(e, g[k][0], S[5]);
-              S[6] = fmaf(e, g[k][1], S[6]);
-              S[7] = fmaf(e, g[k][2], S[7]);
-              if constexpr (DEN) Sd = fmaf(e, gd[k], Sd);
+              S[5] = fmaf(e, gv.x, S[5]);
+              S[6] = fmaf(e, gv.y, S[6]);
+              S[7] = fmaf(e, gv.z, S[7]);
+              if constexpr (DEN) Sd = fmaf(e, gv.w, Sd);
             }
           }
-          float red = 0.f, redd = 0.f;
-          if (__any_sync(0xffffffffu, any)) {
-            red = warp_transpose_reduce8(S, lane);
-            if constexpr (DEN) redd = warp_sum(Sd);
-          }
-          if ((lane & 3) == 0) s_part[warp * kAccum + (lane >> 2)][jj] = red;
-          if constexpr (DEN) {
-            if (lane == 0) s_partd[warp][jj] = redd;
-          }
         }
-      }
-      __syncthreads();
-      // Fixed-order combination across warps, one store per (gaussian, tile) entry.
-      for (int j = threadIdx.x; j < n; j += L::kThreads) {
-        const uint32_t m = s_mask[j];
-        float t[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        float td = 0.f;
-#pragma unroll
-        for (int w = 0; w < L::kWarps; ++w) {
-          if ((m >> w) & 1u) {
-#pragma unroll
-            for (int q = 0; q < 8; ++q) t[q] += s_part[w * kAccum + q][j];
-            if constexpr (DEN) td += s_partd[w][j];
-          }
+        const float red = octet_transpose_reduce8(S, lane);
+        const int64_t e = s_entry[j];
+        if (valid) partials_f[8 * e + r8] = red;
+        if constexpr (DEN) {
+          Sd += __shfl_xor_sync(0xffffffffu, Sd, 4);
+          Sd += __shfl_xor_sync(0xffffffffu, Sd, 2);
+          Sd += __shfl_xor_sync(0xffffffffu, Sd, 1);
+          if (valid && r8 == 0) a.partial_d[e] = Sd;
         }
-        const int e = s_entry[j];
-        a.partials[2 * static_cast<int64_t>(e)] = make_float4(t[0], t[1], t[2], t[3]);
-        a.partials[2 * static_cast<int64_t>(e) + 1] = make_float4(t[4], t[5], t[6], t[7]);
-        if constexpr (DEN) a.partial_d[e] = td;
       }
     }
   }
@@ -416,7 +477,7 @@ RasterArgs base_args(const BinBuffers& bb, const Geometry& g, float cutoff) {
   a.weights = bb.weights.as<float>();
   a.spans = bb.spans.as<TileSpan>();
   a.offsets = bb.offsets.as<int>();
-  a.gids = bb.vals[bb.sorted_sel].as<uint32_t>();
+  a.entries = bb.entries[bb.sorted_sel].as<uint64_t>();
   a.ranges = bb.ranges.as<int2>();
   a.height = g.height;
   a.width = g.width;
@@ -437,10 +498,9 @@ int launch(const RasterArgs& a, const Geometry& g, cudaStream_t s, const char* n
 }
 
 int ensure_partials(BinBuffers& bb, bool den, cudaStream_t s) {
-  const size_t e = static_cast<size_t>(bb.n_entries > 0 ? bb.n_entries : 1);
-  RTGS_TRY(bb.partials.ensure(e * kAccum * sizeof(float), s));
-  if (den) RTGS_TRY(bb.partial_d.ensure(e * sizeof(float), s));
-  return 0;
+  // Entry-sized buffers already hold `capacity` entries; only a first density call allocates.
+  if (bb.partials.ptr && (!den || bb.partial_d.ptr)) return 0;
+  return ensure_entry_capacity(bb, bb.capacity > 0 ? bb.capacity : 1, den, s);
 }
 
 }  // namespace

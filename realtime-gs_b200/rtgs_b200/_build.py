@@ -17,7 +17,7 @@ CSRC = PKG_DIR.parent / "csrc"
 INCLUDE = PKG_DIR.parents[1] / "include"
 LIB_DIR = PKG_DIR / "_lib"
 LIB_PATH = LIB_DIR / "librtgs2d.so"
-SOURCES = ("capi.cu", "project.cu", "binning.cu", "raster.cu", "optim.cu", "fit_engine.cu", "noalloc.cu")
+SOURCES = ("capi.cu", "project.cu", "binning.cu", "raster.cu", "optim.cu", "fit_engine.cu", "noalloc.cu", "sort.cu")
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [

@@ -170,6 +170,17 @@ class FitEngine:
                 )
         return iters, sums
 
+    def reserve(self, entries: int) -> None:
+        """Pre-size the (gaussian, tile) entry capacity of the fit loop."""
+        with torch.cuda.device(self.device):
+            _native.check(self._lib.rtgs2d_fit_reserve(self._h, int(entries), self._stream()))
+
+    def capacity(self) -> tuple[int, int]:
+        """(entry capacity, chunks re-run after a capacity overflow)."""
+        e, r = ctypes.c_int64(), ctypes.c_int64()
+        _native.check(self._lib.rtgs2d_fit_capacity(self._h, ctypes.byref(e), ctypes.byref(r)))
+        return int(e.value), int(r.value)
+
     def set_profiling(self, enable: bool = True) -> None:
         """Record CUDA events around binning, the raster kernel and Adam in every iteration."""
         _native.check(self._lib.rtgs2d_fit_set_profiling(self._h, int(bool(enable))))

@@ -198,3 +198,31 @@ def test_engine_render_matches_renderer_api():
     assert iters.tolist() == [0, 1, 2]
     sse_c = float(((ref[0].clamp(0, 1) - image) ** 2).sum())
     assert abs(sums[0, 1] - sse_c) <= 1e-4 * sse_c
+
+
+def test_entry_capacity_overflow_rolls_back_and_matches_presized_run():
+    """Gaussians that start tiny and grow overflow the initial entry capacity; the engine re-runs
+    the affected chunks and must end bitwise where a run with ample capacity ends."""
+    h, w, n = 96, 128, 400
+    src = synthetic.source_gaussians(5, 30, h, w, (6.0, 20.0))
+    target = (orender.render(src.xy, src.chol, src.color, src.weight, h, w)).clamp(0, 1).to(DEV)
+    init = synthetic.fit_init(5, n, h, w)
+    chol = init.chol.clone()
+    chol[:, 0] = 0.35
+    chol[:, 2] = 0.35
+    chol[:, 1] = 0.0
+    raw = raw_from_gaussians(*(x.to(DEV) for x in (init.xy, chol, init.color, init.weight)), h, w)
+    results = []
+    for presize in (False, True):
+        with FitEngine(1, n, h, w, lr=0.05, iterations=200, log_every=50, device=DEV) as engine:
+            engine.set_targets(target[None])
+            engine.set_raw({k: v[None] for k, v in raw.items()})
+            engine.reserve(2_000_000 if presize else 64)  # 64 entries: the first chunk overflows
+            engine.run(200)
+            cap, retries = engine.capacity()
+            results.append((engine.params(), retries, engine.history()))
+    (p_small, retries_small, h_small), (p_big, retries_big, h_big) = results
+    assert retries_small > 0 and retries_big == 0
+    for a, b in zip(p_small, p_big):
+        assert torch.equal(a, b)
+    assert np.array_equal(h_small[0], h_big[0]) and np.array_equal(h_small[1], h_big[1])
