@@ -1,27 +1,42 @@
 // Tile binning: every gaussian with non-empty support is listed once in each 16x16 tile its
-// support rectangle touches. Entries are emitted gaussian-major (exclusive scan of per-gaussian
-// tile counts) as packed (tile key << 32 | gaussian id) words, then stably radix-sorted by key
-// (sort.cu), so inside each tile the list is in ascending gaussian index -- the order in which
-// the reference's index_add sums a pixel (renderer2d.py:228-253). The reference itself has no
-// binning (one CUDA block per gaussian, renderer2d_ext.cu:26-85); this replaces its per-pair
-// global atomics with per-tile gathers.
+// support rectangle touches, and each tile's list must be read in ascending gaussian index -- the
+// order in which the reference's index_add sums a pixel (renderer2d.py:228-253). The reference
+// itself has no binning (one CUDA block per gaussian, renderer2d_ext.cu:26-85); this replaces its
+// per-pair global atomics with per-tile gathers.
+//
+// Two ways to build the lists, both deterministic in what the raster kernels read:
+//   tile scatter (default)  the projection counts entries per tile; an inclusive scan of the tile
+//                           counts gives every tile's [start, end); each gaussian claims one slot
+//                           per tile by counting that tile's count back down (so the counts are
+//                           zero again for the next projection), and one warp per tile then sorts
+//                           the tile's ids in shared memory (lists up to kSegSortMax).
+//   radix                   entries emitted gaussian-major as (tile key << 32 | id), stable radix
+//                           sort by key (sort.cu), per-tile ranges; used when some tile list is
+//                           longer than kSegSortMax. Emission order must follow the gaussian
+//                           index, so this path first recomputes the entry offsets as an ordered
+//                           exclusive scan of the per-gaussian counts.
+// Entry indices (offsets[g] + local tile index) address the backward's per-(gaussian, tile)
+// gradient moments on both paths.
 #include <cub/device/device_scan.cuh>
 
 #include "internal.h"
+#include "kernels.cuh"
 
 namespace rtgs2d {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kSmallSpan = 16;  // spans above this are emitted by the whole warp
 
 __global__ void __launch_bounds__(kThreads)
 emit_kernel(int64_t m, const int* __restrict__ counts, const int* __restrict__ offsets,
             const TileSpan* __restrict__ spans, int tiles_x, int64_t cap,
             unsigned long long* __restrict__ stats, uint64_t* __restrict__ entries) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
-  const int lane = threadIdx.x & 31;
-  if (i == 0) atomicMax(&stats[kStatMaxEntries], stats[kStatEntries]);
+  if (i == 0) {
+    atomicMax(&stats[kStatMaxEntries], stats[kStatEntries]);
+    stats[kStatLastEntries] = stats[kStatEntries];
+    stats[kStatLastPairs] = stats[kStatPairs];
+  }
   int cnt = 0, off = 0;
   TileSpan sp{0, 0, 1, 0};
   if (i < m) {
@@ -31,32 +46,175 @@ emit_kernel(int64_t m, const int* __restrict__ counts, const int* __restrict__ o
       sp = spans[i];
     }
   }
+  const long long off_l = off;
+  for_each_span_tile(i, cnt, sp, tiles_x, [&](long long g, int j, int key) {
+    // `off` of the span's owner lane: entries of gaussian g are offsets[g] + j.
+    const long long o = g == i ? off_l : static_cast<long long>(offsets[g]);
+    if (o + j < cap) entries[o + j] = (static_cast<uint64_t>(key) << 32) | static_cast<uint64_t>(g);
+  });
+}
+
+// Slot of gaussian g in tile t: tile_end[t] minus the tile count before this gaussian counted it
+// down, i.e. a unique slot of [end - count, end). A lane issues all atomics of its span before it
+// stores, so their round trips overlap. Block 0 also retires the projection's stats slots 0-1
+// (copied to the "last" slots, then zeroed for the next projection).
+constexpr int kScatterUnroll = 4;  // slots in flight per lane on warp-walked spans
+
+__global__ void __launch_bounds__(kThreads)
+scatter_kernel(int64_t m, const int* __restrict__ counts, const TileSpan* __restrict__ spans,
+               int tiles_x, const int* __restrict__ tile_end, int* __restrict__ tile_count,
+               int64_t cap, unsigned long long* __restrict__ stats, uint32_t* __restrict__ list) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  if (i == 0) {
+    const unsigned long long e = stats[kStatEntries];
+    atomicMax(&stats[kStatMaxEntries], e);
+    stats[kStatLastEntries] = e;
+    stats[kStatLastPairs] = stats[kStatPairs];
+    stats[kStatEntries] = 0;
+    stats[kStatPairs] = 0;
+  }
+  int cnt = 0;
+  TileSpan sp{0, 0, 1, 0};
+  if (i < m) {
+    cnt = counts[i];
+    if (cnt > 0) sp = spans[i];
+  }
   if (cnt > 0 && cnt <= kSmallSpan) {
-    for (int j = 0; j < cnt && off + j < cap; ++j) {
-      const int ty = sp.ty0 + j / sp.ntx;
-      const int tx = sp.tx0 + j % sp.ntx;
-      const uint64_t key = static_cast<uint64_t>(sp.key_base + ty * tiles_x + tx);
-      entries[off + j] = (key << 32) | static_cast<uint64_t>(i);
+    int pos[kSmallSpan];
+    int tx = sp.tx0, ty = sp.ty0;
+#pragma unroll
+    for (int j = 0; j < kSmallSpan; ++j) {
+      if (j < cnt) {
+        const int t = sp.key_base + ty * tiles_x + tx;
+        pos[j] = tile_end[t] - atomicSub(&tile_count[t], 1);
+        if (++tx == sp.tx0 + sp.ntx) {
+          tx = sp.tx0;
+          ++ty;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kSmallSpan; ++j) {
+      if (j < cnt && pos[j] >= 0 && pos[j] < cap) list[pos[j]] = static_cast<uint32_t>(i);
     }
   }
+  const int lane = threadIdx.x & 31;
   unsigned big = __ballot_sync(0xffffffffu, cnt > kSmallSpan);
   while (big) {
     const int src = __ffs(big) - 1;
     big &= big - 1;
     const int c = __shfl_sync(0xffffffffu, cnt, src);
-    const int o = __shfl_sync(0xffffffffu, off, src);
     const int tx0 = __shfl_sync(0xffffffffu, sp.tx0, src);
     const int ty0 = __shfl_sync(0xffffffffu, sp.ty0, src);
     const int ntx = __shfl_sync(0xffffffffu, sp.ntx, src);
     const int kb = __shfl_sync(0xffffffffu, sp.key_base, src);
-    const uint64_t gid = static_cast<uint64_t>(blockIdx.x) * kThreads + (threadIdx.x & ~31) + src;
-    for (int j = lane; j < c && o + j < cap; j += 32) {
-      const int ty = ty0 + j / ntx;
-      const int tx = tx0 + j % ntx;
-      const uint64_t key = static_cast<uint64_t>(kb + ty * tiles_x + tx);
-      entries[o + j] = (key << 32) | gid;
+    const uint32_t g = static_cast<uint32_t>(__shfl_sync(0xffffffffu, static_cast<long long>(i), src));
+    for (int j0 = lane; j0 < c; j0 += 32 * kScatterUnroll) {
+      int pos[kScatterUnroll];
+#pragma unroll
+      for (int r = 0; r < kScatterUnroll; ++r) {
+        const int j = j0 + 32 * r;
+        if (j < c) {
+          const int t = kb + (ty0 + j / ntx) * tiles_x + tx0 + j % ntx;
+          pos[r] = tile_end[t] - atomicSub(&tile_count[t], 1);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kScatterUnroll; ++r) {
+        if (j0 + 32 * r < c && pos[r] >= 0 && pos[r] < cap) list[pos[r]] = g;
+      }
     }
   }
+}
+
+// One warp per tile: sort list[start, end) ascending in shared memory (bitonic network over the
+// length padded to a power of two >= 32). Partner strides >= 32 are compare-exchanges in shared
+// memory; strides < 32 run on each 32-element block in registers (shuffles), including the whole
+// first phase (every k <= 32) in one pass. Lists longer than kSegSortMax are left as they are and
+// flagged in stats[kStatLongTile] (the caller re-bins with the radix path).
+constexpr int kTileSortWarps = 4;
+
+__device__ __forceinline__ uint32_t bitonic_shfl(uint32_t v, int i, int k, int j_top) {
+  const bool up = (i & k) == 0;
+#pragma unroll 1
+  for (int j = j_top; j > 0; j >>= 1) {
+    const uint32_t y = __shfl_xor_sync(0xffffffffu, v, j);
+    const bool lower = (i & j) == 0;
+    v = (lower == up) ? min(v, y) : max(v, y);
+  }
+  return v;
+}
+
+__global__ void __launch_bounds__(kTileSortWarps * 32)
+tile_sort_kernel(const int* __restrict__ tile_end, int64_t n_tiles, int64_t cap,
+                 unsigned long long* __restrict__ stats, uint32_t* __restrict__ list) {
+  __shared__ uint32_t s_buf[kTileSortWarps][kSegSortMax];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * kTileSortWarps + warp;
+  if (t >= n_tiles) return;
+  int64_t start = t == 0 ? 0 : tile_end[t - 1];
+  int64_t end = tile_end[t];
+  start = start < cap ? start : cap;
+  end = end < cap ? end : cap;
+  const int len = static_cast<int>(end - start);
+  if (len <= 1) return;
+  if (len > kSegSortMax) {
+    if (lane == 0) atomicMax(&stats[kStatLongTile], static_cast<unsigned long long>(len));
+    return;
+  }
+  uint32_t* seg = list + start;
+  if (len <= 32) {  // one block in registers
+    uint32_t v = lane < len ? seg[lane] : 0xffffffffu;
+#pragma unroll 1
+    for (int k = 2; k <= 32; k <<= 1) v = bitonic_shfl(v, lane, k, k >> 1);
+    if (lane < len) seg[lane] = v;
+    return;
+  }
+  int n_pad = 64;
+  while (n_pad < len) n_pad <<= 1;
+  uint32_t* b = s_buf[warp];
+  for (int c = 0; c < n_pad; c += 32) {  // load + first phase (k <= 32) per 32-element block
+    const int i = c + lane;
+    uint32_t v = i < len ? seg[i] : 0xffffffffu;
+#pragma unroll 1
+    for (int k = 2; k <= 32; k <<= 1) v = bitonic_shfl(v, i, k, k >> 1);
+    b[i] = v;
+  }
+  __syncwarp();
+  for (int k = 64; k <= n_pad; k <<= 1) {
+    for (int j = k >> 1; j >= 32; j >>= 1) {
+      for (int p = lane; p < (n_pad >> 1); p += 32) {  // one compare-exchange per pair
+        const int i = ((p & ~(j - 1)) << 1) | (p & (j - 1));
+        const int ixj = i | j;
+        const uint32_t x = b[i], y = b[ixj];
+        const bool up = (i & k) == 0;
+        if ((x > y) == up) {
+          b[i] = y;
+          b[ixj] = x;
+        }
+      }
+      __syncwarp();
+    }
+    for (int c = 0; c < n_pad; c += 32) {
+      const int i = c + lane;
+      b[i] = bitonic_shfl(b[i], i, k, 16);
+    }
+    __syncwarp();
+  }
+  for (int i = lane; i < len; i += 32) seg[i] = b[i];
+}
+
+// Flag tile lists longer than the raster's shared-memory sort (stats[kStatLongTile] = max length).
+__global__ void __launch_bounds__(kThreads)
+long_tile_kernel(const int* __restrict__ tile_count, int64_t n_tiles,
+                 unsigned long long* __restrict__ stats) {
+  int longest = 0;
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; t < n_tiles;
+       t += static_cast<int64_t>(gridDim.x) * kThreads) {
+    const int c = tile_count[t];
+    longest = c > longest ? c : longest;
+  }
+  if (longest > kSegSortMax) atomicMax(&stats[kStatLongTile], static_cast<unsigned long long>(longest));
 }
 
 __global__ void __launch_bounds__(kThreads)
@@ -71,37 +229,69 @@ ranges_kernel(const uint64_t* __restrict__ entries, const unsigned long long* __
   if (i == n - 1 || static_cast<uint32_t>(entries[i + 1] >> 32) != k) ranges[k].y = static_cast<int>(i + 1);
 }
 
-int scan_counts(BinBuffers& bb, int64_t m, cudaStream_t s) {
-  size_t scan_bytes = 0;
-  RTGS_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, scan_bytes, bb.counts.as<int>(),
-                                          bb.offsets.as<int>(), static_cast<int>(m), s),
-            "scan size query");
-  RTGS_TRY(bb.cub_temp.ensure(scan_bytes, s));
-  RTGS_CUDA(cub::DeviceScan::ExclusiveSum(bb.cub_temp.ptr, scan_bytes, bb.counts.as<int>(),
-                                          bb.offsets.as<int>(), static_cast<int>(m), s),
-            "scan");
+template <bool INCLUSIVE>
+int cub_scan(BinBuffers& bb, const int* in, int* out, int64_t n, cudaStream_t s) {
+  size_t bytes = 0;
+  if constexpr (INCLUSIVE) {
+    RTGS_CUDA(cub::DeviceScan::InclusiveSum(nullptr, bytes, in, out, static_cast<int>(n), s), "scan size query");
+  } else {
+    RTGS_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, bytes, in, out, static_cast<int>(n), s), "scan size query");
+  }
+  RTGS_TRY(bb.cub_temp.ensure(bytes, s));
+  if constexpr (INCLUSIVE) {
+    RTGS_CUDA(cub::DeviceScan::InclusiveSum(bb.cub_temp.ptr, bytes, in, out, static_cast<int>(n), s), "scan");
+  } else {
+    RTGS_CUDA(cub::DeviceScan::ExclusiveSum(bb.cub_temp.ptr, bytes, in, out, static_cast<int>(n), s), "scan");
+  }
   return 0;
 }
 
-int emit_sort_ranges(BinBuffers& bb, const Geometry& g, int64_t m, int64_t launch_entries,
-                     cudaStream_t s) {
+unsigned grid_for(int64_t m) { return static_cast<unsigned>((m + kThreads - 1) / kThreads); }
+
+int bin_radix(BinBuffers& bb, const Geometry& g, int64_t m, int64_t launch_entries, cudaStream_t s) {
   const int64_t n_tiles = g.n_tiles();
   RTGS_TRY(bb.ranges.ensure(static_cast<size_t>(n_tiles > 0 ? n_tiles : 1) * sizeof(int2), s));
   RTGS_CUDA(cudaMemsetAsync(bb.ranges.ptr, 0, static_cast<size_t>(n_tiles) * sizeof(int2), s),
             "memset ranges");
+  bb.presorted = true;
+  bb.counts_cleared = false;
   if (m == 0 || bb.capacity == 0 || launch_entries == 0) return 0;
+  RTGS_TRY(cub_scan<false>(bb, bb.counts.as<int>(), bb.offsets.as<int>(), m, s));
   RTGS_TRY(bb.sort_counts.ensure(sort_counts_bytes(), s));
-  emit_kernel<<<static_cast<unsigned>((m + kThreads - 1) / kThreads), kThreads, 0, s>>>(
+  emit_kernel<<<grid_for(m), kThreads, 0, s>>>(
       m, bb.counts.as<int>(), bb.offsets.as<int>(), bb.spans.as<TileSpan>(), g.tiles_x,
       bb.capacity, bb.stats.as<unsigned long long>(), bb.entries[0].as<uint64_t>());
   RTGS_CUDA(cudaGetLastError(), "emit_kernel");
   RTGS_TRY(radix_sort_entries(bb.entries[0].as<uint64_t>(), bb.entries[1].as<uint64_t>(),
                               bb.stats.as<unsigned long long>() + kStatEntries, bb.capacity,
                               key_bits_for(n_tiles), bb.sort_counts.as<int>(), s, &bb.sorted_sel));
-  ranges_kernel<<<static_cast<unsigned>((launch_entries + kThreads - 1) / kThreads), kThreads, 0, s>>>(
+  ranges_kernel<<<grid_for(launch_entries), kThreads, 0, s>>>(
       bb.entries[bb.sorted_sel].as<uint64_t>(), bb.stats.as<unsigned long long>(), bb.capacity,
       bb.ranges.as<int2>());
   return check_cuda(cudaGetLastError(), "ranges_kernel");
+}
+
+int bin_scatter(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s) {
+  const int64_t n_tiles = g.n_tiles();
+  const size_t tb = static_cast<size_t>(n_tiles > 0 ? n_tiles : 1) * sizeof(int);
+  RTGS_TRY(bb.tile_end.ensure(tb, s));
+  bb.presorted = false;
+  bb.counts_cleared = false;
+  if (n_tiles == 0) return 0;
+  RTGS_TRY(cub_scan<true>(bb, bb.tile_count.as<int>(), bb.tile_end.as<int>(), n_tiles, s));
+  if (m == 0) return 0;
+  scatter_kernel<<<grid_for(m), kThreads, 0, s>>>(
+      m, bb.counts.as<int>(), bb.spans.as<TileSpan>(), g.tiles_x, bb.tile_end.as<int>(),
+      bb.tile_count.as<int>(), bb.capacity, bb.stats.as<unsigned long long>(),
+      bb.list.as<uint32_t>());
+  RTGS_CUDA(cudaGetLastError(), "scatter_kernel");
+  bb.counts_cleared = true;
+  const unsigned blocks = static_cast<unsigned>((n_tiles + kTileSortWarps - 1) / kTileSortWarps);
+  tile_sort_kernel<<<blocks, kTileSortWarps * 32, 0, s>>>(bb.tile_end.as<int>(), n_tiles,
+                                                         bb.capacity,
+                                                         bb.stats.as<unsigned long long>(),
+                                                         bb.list.as<uint32_t>());
+  return check_cuda(cudaGetLastError(), "tile_sort_kernel");
 }
 
 }  // namespace
@@ -123,17 +313,25 @@ Geometry make_geometry(int n_views, int height, int width) {
   return g;
 }
 
+int reset_tile_counts(BinBuffers& bb, const Geometry& g, cudaStream_t s) {
+  const int64_t n_tiles = g.n_tiles();
+  RTGS_TRY(bb.tile_count.ensure(static_cast<size_t>(n_tiles > 0 ? n_tiles : 1) * sizeof(int), s));
+  RTGS_CUDA(cudaMemsetAsync(bb.tile_count.ptr, 0, static_cast<size_t>(n_tiles) * sizeof(int), s),
+            "memset tile counts");
+  return 0;
+}
+
 int ensure_entry_capacity(BinBuffers& bb, int64_t capacity, bool density, cudaStream_t s) {
   const size_t e = static_cast<size_t>(capacity > 0 ? capacity : 1);
+  RTGS_TRY(bb.list.ensure(e * sizeof(uint32_t), s));
   RTGS_TRY(bb.entries[0].ensure(e * sizeof(uint64_t), s));
   RTGS_TRY(bb.entries[1].ensure(e * sizeof(uint64_t), s));
   RTGS_TRY(bb.partials.ensure(e * kAccum * sizeof(float), s));
   if (density) RTGS_TRY(bb.partial_d.ensure(e * sizeof(float), s));
-  const size_t cap_e = bb.entries[0].bytes / sizeof(uint64_t);
-  const size_t cap_e1 = bb.entries[1].bytes / sizeof(uint64_t);
-  const size_t cap_p = bb.partials.bytes / (kAccum * sizeof(float));
-  size_t cap = cap_e < cap_e1 ? cap_e : cap_e1;
-  cap = cap < cap_p ? cap : cap_p;
+  size_t cap = bb.list.bytes / sizeof(uint32_t);
+  const size_t caps[3] = {bb.entries[0].bytes / sizeof(uint64_t), bb.entries[1].bytes / sizeof(uint64_t),
+                          bb.partials.bytes / (kAccum * sizeof(float))};
+  for (size_t c : caps) cap = cap < c ? cap : c;
   if (density) {
     const size_t cap_d = bb.partial_d.bytes / sizeof(float);
     cap = cap < cap_d ? cap : cap_d;
@@ -142,17 +340,27 @@ int ensure_entry_capacity(BinBuffers& bb, int64_t capacity, bool density, cudaSt
   return 0;
 }
 
+int check_long_tiles(BinBuffers& bb, const Geometry& g, cudaStream_t s) {
+  const int64_t n_tiles = g.n_tiles();
+  if (n_tiles == 0) return 0;
+  int64_t blocks = (n_tiles + kThreads - 1) / kThreads;
+  blocks = blocks < 148 ? blocks : 148;
+  long_tile_kernel<<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(
+      bb.tile_count.as<int>(), n_tiles, bb.stats.as<unsigned long long>());
+  return check_cuda(cudaGetLastError(), "long_tile_kernel");
+}
+
 int bin_entries(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s) {
   bb.n_entries = 0;
   bb.n_pairs = 0;
   if (m > INT32_MAX) return set_error(-1, "more than 2^31 gaussians in one call");
-  if (m > 0) RTGS_TRY(scan_counts(bb, m, s));
+  RTGS_TRY(check_long_tiles(bb, g, s));
   if (!bb.host_stats) {
     RTGS_CUDA(cudaMallocHost(reinterpret_cast<void**>(&bb.host_stats),
                              kStatSlots * sizeof(unsigned long long)),
               "pinned stats");
   }
-  RTGS_CUDA(cudaMemcpyAsync(bb.host_stats, bb.stats.ptr, 2 * sizeof(unsigned long long),
+  RTGS_CUDA(cudaMemcpyAsync(bb.host_stats, bb.stats.ptr, kStatSlots * sizeof(unsigned long long),
                             cudaMemcpyDeviceToHost, s),
             "stats readback");
   RTGS_CUDA(cudaStreamSynchronize(s), "stats sync");
@@ -162,16 +370,20 @@ int bin_entries(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s) {
     return set_error(-4, "more than 2^31 (gaussian, tile) entries in one call");
   }
   bb.n_entries = static_cast<int64_t>(entries);
-  if (bb.capacity < bb.n_entries || bb.entries[0].ptr == nullptr) {
+  const bool radix = bb.host_stats[kStatLongTile] > 0;
+  const bool have = radix ? (bb.entries[0].ptr != nullptr && bb.entries[1].ptr != nullptr)
+                          : bb.list.ptr != nullptr;
+  if (bb.capacity < bb.n_entries || !have) {
     RTGS_TRY(ensure_entry_capacity(bb, bb.n_entries, bb.partial_d.ptr != nullptr, s));
   }
-  return emit_sort_ranges(bb, g, m, bb.n_entries, s);
+  if (radix) return bin_radix(bb, g, m, bb.n_entries, s);
+  return bin_scatter(bb, g, m, s);
 }
 
-int bin_entries_async(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s) {
+int bin_entries_async(BinBuffers& bb, const Geometry& g, int64_t m, bool radix, cudaStream_t s) {
   if (m > INT32_MAX) return set_error(-1, "more than 2^31 gaussians in one call");
-  if (m > 0) RTGS_TRY(scan_counts(bb, m, s));
-  return emit_sort_ranges(bb, g, m, bb.capacity, s);
+  if (radix) return bin_radix(bb, g, m, bb.capacity, s);
+  return bin_scatter(bb, g, m, s);  // the tile sort flags a list too long for it
 }
 
 }  // namespace rtgs2d

@@ -3,6 +3,7 @@
 #include <cstdio>
 #include <new>
 #include <string>
+#include <algorithm>
 #include <vector>
 
 #include "../../include/rtgs2d.h"
@@ -52,8 +53,9 @@ void DevBuf::release() {
 }
 
 void BinBuffers::release() {
-  for (DevBuf* b : {&records, &weights, &spans, &counts, &offsets, &entries[0], &entries[1],
-                    &ranges, &partials, &partial_d, &cub_temp, &sort_counts, &stats}) {
+  for (DevBuf* b : {&records, &weights, &spans, &counts, &offsets, &list, &tile_count, &tile_end,
+                    &entries[0], &entries[1], &ranges, &partials, &partial_d, &cub_temp,
+                    &sort_counts, &stats}) {
     b->release();
   }
   if (host_stats) cudaFreeHost(host_stats);
@@ -269,25 +271,56 @@ int rtgs2d_arena_copy_binning(const rtgs2d_arena* arena, int64_t max_entries, ui
                               int64_t* n_tiles, void* stream) {
   RTGS_TRY(check_arena(arena));
   const BinBuffers& bb = arena->bb;
-  if (n_entries) *n_entries = bb.n_entries;
-  if (n_tiles) *n_tiles = arena->n_tiles;
+  const int64_t ne = bb.n_entries < bb.capacity ? bb.n_entries : bb.capacity;
+  const int64_t nt = arena->n_tiles;
+  if (n_entries) *n_entries = ne;
+  if (n_tiles) *n_tiles = nt;
   cudaStream_t s = as_stream(stream);
-  const int64_t ce = bb.n_entries < max_entries ? bb.n_entries : max_entries;
-  const int64_t ct = arena->n_tiles < max_tiles ? arena->n_tiles : max_tiles;
-  std::vector<uint64_t> packed;
-  if (gids && ce > 0) {
-    packed.resize(static_cast<size_t>(ce));
-    RTGS_CUDA(cudaMemcpyAsync(packed.data(), bb.entries[bb.sorted_sel].ptr,
-                              static_cast<size_t>(ce) * sizeof(uint64_t), cudaMemcpyDeviceToHost, s),
-              "copy entries");
+  // Per-tile ranges and the ids in read order (ascending inside each tile), on the host.
+  std::vector<int32_t> rng(static_cast<size_t>(2 * nt), 0);
+  std::vector<uint32_t> ids(static_cast<size_t>(ne), 0);
+  if (bb.presorted) {
+    std::vector<uint64_t> packed(static_cast<size_t>(ne));
+    if (ne > 0) {
+      RTGS_CUDA(cudaMemcpyAsync(packed.data(), bb.entries[bb.sorted_sel].ptr, ne * sizeof(uint64_t),
+                                cudaMemcpyDeviceToHost, s), "copy entries");
+    }
+    if (nt > 0) {
+      RTGS_CUDA(cudaMemcpyAsync(rng.data(), bb.ranges.ptr, nt * 2 * sizeof(int32_t),
+                                cudaMemcpyDeviceToHost, s), "copy ranges");
+    }
+    RTGS_CUDA(cudaStreamSynchronize(s), "copy binning sync");
+    for (int64_t i = 0; i < ne; ++i) ids[static_cast<size_t>(i)] = static_cast<uint32_t>(packed[static_cast<size_t>(i)]);
+  } else {
+    std::vector<int32_t> tend(static_cast<size_t>(nt));
+    if (ne > 0) {
+      RTGS_CUDA(cudaMemcpyAsync(ids.data(), bb.list.ptr, ne * sizeof(uint32_t), cudaMemcpyDeviceToHost, s),
+                "copy list");
+    }
+    if (nt > 0) {
+      RTGS_CUDA(cudaMemcpyAsync(tend.data(), bb.tile_end.ptr, nt * sizeof(int32_t), cudaMemcpyDeviceToHost, s),
+                "copy tile ends");
+    }
+    RTGS_CUDA(cudaStreamSynchronize(s), "copy binning sync");
+    for (int64_t t = 0; t < nt; ++t) {
+      int32_t a = t == 0 ? 0 : tend[static_cast<size_t>(t - 1)];
+      int32_t b = tend[static_cast<size_t>(t)];
+      a = a < ne ? a : static_cast<int32_t>(ne);
+      b = b < ne ? b : static_cast<int32_t>(ne);
+      if (b > a) {  // already ascending inside the tile (the device tile sort)
+        rng[static_cast<size_t>(2 * t)] = a;
+        rng[static_cast<size_t>(2 * t + 1)] = b;
+      }
+    }
   }
-  if (ranges && ct > 0) {
-    RTGS_CUDA(cudaMemcpyAsync(ranges, bb.ranges.ptr, static_cast<size_t>(ct) * 2 * sizeof(int32_t),
-                              cudaMemcpyDeviceToHost, s),
-              "copy ranges");
+  if (gids) {
+    const int64_t c = ne < max_entries ? ne : max_entries;
+    for (int64_t i = 0; i < c; ++i) gids[i] = ids[static_cast<size_t>(i)];
   }
-  RTGS_CUDA(cudaStreamSynchronize(s), "copy binning sync");
-  for (size_t i = 0; i < packed.size(); ++i) gids[i] = static_cast<uint32_t>(packed[i]);
+  if (ranges) {
+    const int64_t c = nt < max_tiles ? nt : max_tiles;
+    for (int64_t i = 0; i < 2 * c; ++i) ranges[i] = rng[static_cast<size_t>(i)];
+  }
   return RTGS2D_OK;
 }
 

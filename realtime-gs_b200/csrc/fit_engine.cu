@@ -44,7 +44,8 @@ struct rtgs2d_fit {
   double lr_current = 0.0;
   double total_pairs = 0.0;
   int64_t last_entries = 0, last_pairs = 0;
-  int64_t retries = 0;  // chunks re-run after an entry-capacity overflow
+  int64_t retries = 0;  // chunks re-run after an entry-capacity overflow or a long tile list
+  bool use_radix = false;  // some tile list exceeded the shared-memory sort: bin by radix sort
   bool have_targets = false, have_raw = false;
   // stage timing (rtgs2d_fit_set_profiling)
   bool profiling = false;
@@ -384,7 +385,7 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
     const size_t logs0 = f->log_iters.size();
     RTGS_TRY(snapshot(f, true, s));
     RTGS_CUDA(cudaMemsetAsync(bb.stats.as<unsigned long long>() + kStatPairsTotal, 0,
-                              2 * sizeof(unsigned long long), s),
+                              3 * sizeof(unsigned long long), s),
               "reset chunk stats");
     if (f->profiling) RTGS_TRY(ensure_events(f, static_cast<size_t>(4 * chunk)));
     // Iteration k: [projection] binning, raster, Adam. The Adam step of iteration k also projects
@@ -395,7 +396,7 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
       const int64_t it = f->step;
       cudaEvent_t* ev = f->profiling ? &f->events[static_cast<size_t>(4 * k)] : nullptr;
       if (ev) RTGS_CUDA(cudaEventRecord(ev[0], s), "event record");
-      RTGS_TRY(bin_entries_async(bb, f->geo, f->m, s));
+      RTGS_TRY(bin_entries_async(bb, f->geo, f->m, f->use_radix, s));
       if (ev) RTGS_CUDA(cudaEventRecord(ev[1], s), "event record");
       RTGS_TRY(launch_raster_fit(bb, f->geo, kCutoff, raster_args(f), true, s));
       if (ev) RTGS_CUDA(cudaEventRecord(ev[2], s), "event record");
@@ -431,7 +432,8 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
               "chunk stats readback");
     RTGS_CUDA(cudaStreamSynchronize(s), "chunk sync");
     const int64_t max_entries = static_cast<int64_t>(bb.host_stats[kStatMaxEntries]);
-    if (max_entries > bb.capacity) {
+    const bool long_tile = !f->use_radix && bb.host_stats[kStatLongTile] > 0;
+    if (max_entries > bb.capacity || long_tile) {
       // Entries were dropped in this chunk: roll back and re-run it with room for them.
       if (max_entries > INT32_MAX) return set_error(RTGS2D_ERR_CAPACITY, "more than 2^31 tile entries");
       RTGS_TRY(snapshot(f, false, s));
@@ -439,11 +441,14 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
       f->lr_current = lr0;
       f->log_iters.resize(logs0);
       f->retries += 1;
-      RTGS_TRY(ensure_entry_capacity(bb, max_entries + max_entries / 2 + 4096, false, s));
+      if (long_tile) f->use_radix = true;  // a tile list too long for the shared-memory sort
+      if (max_entries > bb.capacity) {
+        RTGS_TRY(ensure_entry_capacity(bb, max_entries + max_entries / 2 + 4096, false, s));
+      }
       continue;
     }
-    f->last_entries = static_cast<int64_t>(bb.host_stats[kStatEntries]);
-    f->last_pairs = static_cast<int64_t>(bb.host_stats[kStatPairs]);
+    f->last_entries = static_cast<int64_t>(bb.host_stats[kStatLastEntries]);
+    f->last_pairs = static_cast<int64_t>(bb.host_stats[kStatLastPairs]);
     const double chunk_pairs = static_cast<double>(bb.host_stats[kStatPairsTotal]);
     f->total_pairs += chunk_pairs;
     if (f->profiling) {

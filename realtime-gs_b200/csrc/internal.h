@@ -43,12 +43,19 @@ constexpr int kSortGrid = 592;
 
 // Device statistics slots (unsigned long long each).
 enum StatSlot : int {
-  kStatEntries = 0,     // (gaussian, tile) entries of the current projection
-  kStatPairs = 1,       // (gaussian, pixel-in-rectangle) pairs of the current projection
-  kStatPairsTotal = 2,  // pairs accumulated over projections until reset by the caller
-  kStatMaxEntries = 3,  // largest entry count binned since reset by the caller (capacity check)
-  kStatSlots = 4
+  kStatEntries = 0,      // (gaussian, tile) entries of the current projection
+  kStatPairs = 1,        // (gaussian, pixel-in-rectangle) pairs of the current projection
+  kStatPairsTotal = 2,   // pairs accumulated over projections until reset by the caller
+  kStatMaxEntries = 3,   // largest entry count binned since reset by the caller (capacity check)
+  kStatLongTile = 4,     // largest tile list longer than kSegSortMax since reset (0: none)
+  kStatLastEntries = 5,  // entries of the last binned projection (copied by the binning)
+  kStatLastPairs = 6,    // pairs of the last binned projection
+  kStatSlots = 7
 };
+
+// Tile lists up to this length are sorted by the tile-sort kernel (one warp per tile, in shared
+// memory); a binning with a longer list uses the global radix sort instead.
+constexpr int kSegSortMax = 2048;
 
 // Scratch used by projection + tile binning + raster for one render / one fit iteration.
 struct BinBuffers {
@@ -56,8 +63,12 @@ struct BinBuffers {
   DevBuf weights;     // float[M] (density variants)
   DevBuf spans;       // TileSpan[M]
   DevBuf counts;      // int[M]  tiles per gaussian
-  DevBuf offsets;     // int[M]  exclusive scan of counts (entry index of each gaussian's first tile)
-  DevBuf entries[2];  // uint64[capacity] (tile key << 32 | gaussian id), sort double buffer
+  DevBuf offsets;     // int[M]  entry index of each gaussian's first tile (see bin_entries)
+  DevBuf list;        // uint32[capacity] gaussian ids grouped by tile, ascending inside a tile
+  DevBuf tile_count;  // int[n_tiles] entries per tile (counted up by the projection, back down
+                      //   to zero by the scatter)
+  DevBuf tile_end;    // int[n_tiles] inclusive scan of tile_count
+  DevBuf entries[2];  // uint64[capacity] (tile key << 32 | gaussian id), radix-sort double buffer
   DevBuf ranges;      // int2[n_tiles] [start, end) into the sorted entries
   DevBuf partials;    // float[capacity][8] per (gaussian, tile) gradient moments
   DevBuf partial_d;   // float[capacity]   per (gaussian, tile) density-gradient moment
@@ -66,6 +77,9 @@ struct BinBuffers {
   DevBuf stats;       // unsigned long long[kStatSlots]
   unsigned long long* host_stats = nullptr;  // pinned mirror of `stats`
   int sorted_sel = 0;                         // which entries buffer holds the sorted result
+  bool presorted = false;                     // radix path (entries + ranges) produced the binning
+  bool counts_cleared = false;                // the last binning left tile_count and stats
+                                              //   slots 0-1 at zero (the scatter path does)
   int64_t capacity = 0;                       // entries the entry buffers can hold
   int64_t n_entries = 0;                      // host-known entry count (synchronous binning)
   int64_t n_pairs = 0;
@@ -83,6 +97,7 @@ Geometry make_geometry(int n_views, int height, int width);
 
 // ---- projection (project.cu) --------------------------------------------------------------------
 // All projection launchers zero bb.stats first and fill records/spans/counts (+weights if asked).
+// Projection launchers also count entries per tile into bb.tile_count (zeroed here).
 int launch_project_chol(BinBuffers& bb, const Geometry& g, const float* xy, const float* chol,
                         const float* color, const float* weight, int64_t m, int64_t n_per_view,
                         bool want_weights, cudaStream_t s);
@@ -100,15 +115,22 @@ int launch_build_params(const float* raw, int64_t m, int height, int width, floa
 
 // ---- binning (binning.cu, sort.cu) --------------------------------------------------------------
 // Synchronous binning: scan counts, read the entry count back to the host (synchronises `s`),
-// grow the entry buffers to fit, then bin_entries_async. Requires bb.counts/spans/stats from a
-// projection launcher.
+// grow the entry buffers to fit, then bin asynchronously -- by tile scatter when every tile list
+// fits kSegSortMax, else by the global radix sort. Requires a projection launcher before it.
 int bin_entries(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s);
-// Asynchronous binning into the current capacity (no host synchronisation): scan, emit (entries
-// past the capacity are dropped and show up as stats[kStatMaxEntries] > capacity), stable radix
-// sort with the device-side count, per-tile ranges.
-int bin_entries_async(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s);
-// Allocate the entry-sized buffers (entries, partials[, partial_d]) for `capacity` entries.
+// stats[kStatLongTile] = the longest tile list if any is longer than kSegSortMax (tile counts
+// must be complete, i.e. after the projection).
+int check_long_tiles(BinBuffers& bb, const Geometry& g, cudaStream_t s);
+// Asynchronous binning into the current capacity (no host synchronisation). Tile scatter path:
+// scan of tile counts, atomic-slot scatter of gaussian ids (the raster sorts each tile's list);
+// radix path (radix = true): emit (tile key, id), stable radix sort, tile ranges. Entries past
+// the capacity are dropped and show up as stats[kStatMaxEntries] > capacity; a tile list longer
+// than kSegSortMax on the scatter path is flagged by the raster in stats[kStatLongTile].
+int bin_entries_async(BinBuffers& bb, const Geometry& g, int64_t m, bool radix, cudaStream_t s);
+// Allocate the entry-sized buffers (list, entries, partials[, partial_d]) for `capacity` entries.
 int ensure_entry_capacity(BinBuffers& bb, int64_t capacity, bool density, cudaStream_t s);
+// Zero per-tile counts before a projection (projection launchers call it).
+int reset_tile_counts(BinBuffers& bb, const Geometry& g, cudaStream_t s);
 // Stable LSD radix sort of packed entries by their key bits; the count is read on the device.
 int radix_sort_entries(uint64_t* buf0, uint64_t* buf1, const unsigned long long* d_n, int64_t cap,
                        int key_bits, int* counts, cudaStream_t s, int* result_sel);

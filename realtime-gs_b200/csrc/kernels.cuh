@@ -7,20 +7,72 @@ namespace rtgs2d {
 
 constexpr int kSmallEntries = 32;  // gaussians with more entries are summed by the whole warp
 
+constexpr int kSmallSpan = 16;  // tile spans above this are walked by the whole warp
+
+// Threads per block of every kernel that calls project_tail (its block scan assumes it).
+constexpr int kProjThreads = 256;
+
 struct ProjOut {
   GaussRecord* records;
   float* weights;  // nullable
   TileSpan* spans;
   int* counts;
-  unsigned long long* stats;  // [entries, pairs]
+  int* offsets;               // entry index of each gaussian's first tile
+  int* tile_count;            // entries per tile (atomic)
+  unsigned long long* stats;  // kStat* slots
+  int tiles_x;
 };
 
+// Call f(gaussian id, local tile index j, tile key) for every tile of every active lane's span.
+// Spans up to kSmallSpan tiles are walked by their own lane, longer ones by the whole warp; all
+// lanes of the warp must call this.
+template <typename F>
+__device__ __forceinline__ void for_each_span_tile(int64_t gid, int cnt, const TileSpan& sp,
+                                                   int tiles_x, F&& f) {
+  if (cnt > 0 && cnt <= kSmallSpan) {
+    for (int j = 0; j < cnt; ++j) {
+      const int ty = sp.ty0 + j / sp.ntx;
+      const int tx = sp.tx0 + j % sp.ntx;
+      f(gid, j, sp.key_base + ty * tiles_x + tx);
+    }
+  }
+  const int lane = threadIdx.x & 31;
+  unsigned big = __ballot_sync(0xffffffffu, cnt > kSmallSpan);
+  while (big) {
+    const int src = __ffs(big) - 1;
+    big &= big - 1;
+    const int c = __shfl_sync(0xffffffffu, cnt, src);
+    const int tx0 = __shfl_sync(0xffffffffu, sp.tx0, src);
+    const int ty0 = __shfl_sync(0xffffffffu, sp.ty0, src);
+    const int ntx = __shfl_sync(0xffffffffu, sp.ntx, src);
+    const int kb = __shfl_sync(0xffffffffu, sp.key_base, src);
+    const long long g = __shfl_sync(0xffffffffu, static_cast<long long>(gid), src);
+    for (int j = lane; j < c; j += 32) {
+      const int ty = ty0 + j / ntx;
+      const int tx = tx0 + j % ntx;
+      f(g, j, kb + ty * tiles_x + tx);
+    }
+  }
+}
+
+// Record, span, tile count and entry offset of gaussian i. Must be called by every thread of a
+// kProjThreads block (it contains a block barrier).
+//
+// Entry offsets: a block-wide exclusive scan of the tile counts plus the block's base, reserved
+// with one atomic on stats[kStatEntries]. Blocks reserve in arrival order, so a gaussian's entry
+// index varies from run to run; nothing reads entries in index order (the raster addresses its
+// tile's entries through the gaussian, the gradient gather reads a gaussian's own entries), so no
+// result depends on it.
 __device__ __forceinline__ void project_tail(int64_t i, bool active, float mx, float my, Conic k,
                                              int x0, int x1, int y0, int y1, long long pixels,
                                              float w, float cr, float cg, float cb, int view,
                                              int tiles_x, int tiles_per_view, const ProjOut& o) {
+  constexpr int kWarps = kProjThreads / 32;
+  __shared__ int s_warp_entries[kWarps];
+  __shared__ int s_base;
   int cnt = 0;
   long long pairs = 0;
+  TileSpan sp{0, 0, 1, 0};
   if (active) {
     if (pixels > 0 && isfinite(mx) && isfinite(my)) {
       const int tx0 = x0 / kTile, tx1 = x1 / kTile;
@@ -28,7 +80,6 @@ __device__ __forceinline__ void project_tail(int64_t i, bool active, float mx, f
       const int ntx = tx1 - tx0 + 1;
       cnt = ntx * (ty1 - ty0 + 1);
       pairs = pixels;
-      TileSpan sp;
       sp.tx0 = tx0;
       sp.ty0 = ty0;
       sp.ntx = ntx;
@@ -43,24 +94,47 @@ __device__ __forceinline__ void project_tail(int64_t i, bool active, float mx, f
     if (o.weights) o.weights[i] = w;
     o.counts[i] = cnt;
   }
-  // Warp-aggregated totals (all lanes reach this point).
-  unsigned long long e = static_cast<unsigned long long>(cnt);
+  // Entries per tile for the tile-scatter binning (all lanes reach this point).
+  for_each_span_tile(i, cnt, sp, o.tiles_x, [&](long long, int, int t) {
+    atomicAdd(&o.tile_count[t], 1);  // result unused: a fire-and-forget reduction
+  });
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = cnt;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += y;
+  }
   unsigned long long p = static_cast<unsigned long long>(pairs);
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-    e += __shfl_xor_sync(0xffffffffu, e, off);
-    p += __shfl_xor_sync(0xffffffffu, p, off);
-  }
-  if ((threadIdx.x & 31) == 0 && (e | p)) {
-    atomicAdd(&o.stats[kStatEntries], e);
+  for (int d = 16; d > 0; d >>= 1) p += __shfl_xor_sync(0xffffffffu, p, d);
+  if (lane == 31) s_warp_entries[warp] = incl;
+  if (lane == 0 && p) {
     atomicAdd(&o.stats[kStatPairs], p);
     atomicAdd(&o.stats[kStatPairsTotal], p);
   }
+  __syncthreads();
+  int before = 0, total = 0;
+#pragma unroll
+  for (int w2 = 0; w2 < kWarps; ++w2) {
+    const int v = s_warp_entries[w2];
+    before += w2 < warp ? v : 0;
+    total += v;
+  }
+  if (threadIdx.x == 0) {
+    s_base = total ? static_cast<int>(atomicAdd(&o.stats[kStatEntries],
+                                                static_cast<unsigned long long>(total)))
+                   : 0;
+  }
+  __syncthreads();
+  if (active) o.offsets[i] = s_base + before + incl - cnt;
 }
 
 // Entries at or past the entry capacity were never written (an overflowed binning, whose results
-// the caller discards); never read them.
+// the caller discards); never read them. A negative offset (an entry count past 2^31, which the
+// host rejects after the fact) reads nothing either.
 __device__ __forceinline__ int clamp_to_capacity(int cnt, int off, int64_t cap) {
+  if (off < 0) return 0;
   const int64_t room = cap - off;
   if (room <= 0) return 0;
   return cnt < room ? cnt : static_cast<int>(room);

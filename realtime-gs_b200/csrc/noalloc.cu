@@ -64,6 +64,7 @@ struct BorrowedBins {
   rtgs2d::BinBuffers bb;
   ~BorrowedBins() {
     for (rtgs2d::DevBuf* b : {&bb.records, &bb.weights, &bb.spans, &bb.counts, &bb.offsets,
+                              &bb.list, &bb.tile_count, &bb.tile_end,
                               &bb.entries[0], &bb.entries[1], &bb.ranges, &bb.partials,
                               &bb.partial_d, &bb.cub_temp, &bb.sort_counts, &bb.stats}) {
       b->ptr = nullptr;
@@ -127,17 +128,23 @@ extern "C" int rtgs2d_forward_noalloc(const float* xy, const float* conics, cons
   // Per-gaussian and per-tile buffers (the sizes the projection and binning launchers request).
   const size_t mm = static_cast<size_t>(m > 0 ? m : 1);
   const size_t tiles = static_cast<size_t>(g.n_tiles() > 0 ? g.n_tiles() : 1);
-  size_t scan_bytes = 0;
+  size_t scan_bytes = 0, tile_scan_bytes = 0;
   RTGS_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, scan_bytes, static_cast<int*>(nullptr),
                                           static_cast<int*>(nullptr), static_cast<int>(m), s),
             "scan size query");
+  RTGS_CUDA(cub::DeviceScan::InclusiveSum(nullptr, tile_scan_bytes, static_cast<int*>(nullptr),
+                                          static_cast<int*>(nullptr),
+                                          static_cast<int>(g.n_tiles()), s),
+            "tile scan size query");
+  if (tile_scan_bytes > scan_bytes) scan_bytes = tile_scan_bytes;
   Carver c{base};
   const size_t need_m = mm * (sizeof(GaussRecord) + sizeof(TileSpan) + 3 * sizeof(int)) +
-                        tiles * sizeof(int2) + scan_bytes + sort_counts_bytes();
+                        tiles * (sizeof(int2) + 2 * sizeof(int)) + scan_bytes + sort_counts_bytes();
   if (!c.take(bb.records, mm * sizeof(GaussRecord)) || !c.take(bb.spans, mm * sizeof(TileSpan)) ||
       !c.take(bb.counts, mm * sizeof(int)) || !c.take(bb.offsets, mm * sizeof(int)) ||
       !c.take(bb.stats, kStatSlots * sizeof(unsigned long long)) ||
       !c.take(bb.ranges, tiles * sizeof(int2)) || !c.take(bb.cub_temp, scan_bytes) ||
+      !c.take(bb.tile_count, tiles * sizeof(int)) || !c.take(bb.tile_end, tiles * sizeof(int)) ||
       !c.take(bb.sort_counts, sort_counts_bytes()) ||
       (den != nullptr && !c.take(bb.weights, mm * sizeof(float)))) {
     return too_big(need_m);
@@ -145,17 +152,22 @@ extern "C" int rtgs2d_forward_noalloc(const float* xy, const float* conics, cons
 
   RTGS_TRY(launch_project_conic(bb, g, xy, conics, colors, weights, rects, view_index, m,
                                 den != nullptr, s));
+  RTGS_TRY(check_long_tiles(bb, g, s));
   // Entry count, to size the entry buffers before the binning writes any entry.
-  RTGS_CUDA(cudaMemcpyAsync(g_host_stats, bb.stats.ptr, 2 * sizeof(unsigned long long),
+  RTGS_CUDA(cudaMemcpyAsync(g_host_stats, bb.stats.ptr, kStatSlots * sizeof(unsigned long long),
                             cudaMemcpyDeviceToHost, s),
             "entry count readback");
   RTGS_CUDA(cudaStreamSynchronize(s), "entry count sync");
   const unsigned long long entries = g_host_stats[kStatEntries];
   if (entries > static_cast<unsigned long long>(INT32_MAX)) return too_big(entries * 16);
   const size_t e = static_cast<size_t>(entries > 0 ? entries : 1);
-  if (!c.take(bb.entries[0], e * sizeof(uint64_t)) || !c.take(bb.entries[1], e * sizeof(uint64_t))) {
-    return too_big(c.used + 2 * e * sizeof(uint64_t));
-  }
+  // The tile-scatter binning needs the id list; the radix fallback (a tile list longer than the
+  // shared-memory sort) the entry double buffer.
+  const bool radix = g_host_stats[kStatLongTile] > 0;
+  const bool fits = radix ? (c.take(bb.entries[0], e * sizeof(uint64_t)) &&
+                             c.take(bb.entries[1], e * sizeof(uint64_t)))
+                          : c.take(bb.list, e * sizeof(uint32_t));
+  if (!fits) return too_big(c.used + (radix ? 16 : 4) * e);
   bb.capacity = static_cast<int64_t>(e);  // binning then fits without growing any buffer
   RTGS_TRY(bin_entries(bb, g, m, s));
   return launch_raster_forward(bb, g, static_cast<float>(cutoff), out, den, s);

@@ -18,7 +18,7 @@
 namespace rtgs2d {
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = kProjThreads;
 
 template <bool DEN>
 __global__ void __launch_bounds__(kThreads)
@@ -212,13 +212,20 @@ int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_
   if (m == 0) return 0;
   ProjOut o{};
   if (project_next) {
-    // Same buffers as a projection launcher; stats slots 0-1 restart for the new projection.
+    // Same buffers as a projection launcher; tile counts and stats slots 0-1 restart at zero.
     o.records = bb.records.as<GaussRecord>();
     o.weights = nullptr;
     o.spans = bb.spans.as<TileSpan>();
     o.counts = bb.counts.as<int>();
+    o.offsets = bb.offsets.as<int>();
     o.stats = bb.stats.as<unsigned long long>();
-    RTGS_CUDA(cudaMemsetAsync(bb.stats.ptr, 0, 2 * sizeof(unsigned long long), s), "memset stats");
+    o.tile_count = bb.tile_count.as<int>();
+    o.tiles_x = g.tiles_x;
+    if (!bb.counts_cleared) {  // the scatter binning leaves both at zero; the radix path does not
+      RTGS_TRY(reset_tile_counts(bb, g, s));
+      RTGS_CUDA(cudaMemsetAsync(bb.stats.ptr, 0, 2 * sizeof(unsigned long long), s), "memset stats");
+    }
+    bb.counts_cleared = false;
     adam_fit_kernel<true><<<grid_for(m), kThreads, 0, s>>>(
         m, bb.capacity, bb.counts.as<int>(), bb.offsets.as<int>(), bb.partials.as<float4>(), g.height,
         g.width, raw, m1, m2, a, n_per_view, g.tiles_x, g.tiles_per_view, o);

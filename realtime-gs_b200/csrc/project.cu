@@ -11,7 +11,7 @@
 namespace rtgs2d {
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = kProjThreads;
 
 __global__ void __launch_bounds__(kThreads)
 project_chol_kernel(const float* __restrict__ xy, const float* __restrict__ chol,
@@ -138,7 +138,8 @@ support_rects_kernel(const float* __restrict__ xy, const float* __restrict__ cho
   if (counts) counts[i] = r.pixels;
 }
 
-int prepare(BinBuffers& bb, int64_t m, bool want_weights, cudaStream_t s, ProjOut* o) {
+int prepare(BinBuffers& bb, const Geometry& g, int64_t m, bool want_weights, cudaStream_t s,
+            ProjOut* o) {
   const size_t mm = static_cast<size_t>(m > 0 ? m : 1);
   RTGS_TRY(bb.records.ensure(mm * sizeof(GaussRecord), s));
   RTGS_TRY(bb.spans.ensure(mm * sizeof(TileSpan), s));
@@ -146,12 +147,17 @@ int prepare(BinBuffers& bb, int64_t m, bool want_weights, cudaStream_t s, ProjOu
   RTGS_TRY(bb.offsets.ensure(mm * sizeof(int), s));
   RTGS_TRY(bb.stats.ensure(kStatSlots * sizeof(unsigned long long), s));
   if (want_weights) RTGS_TRY(bb.weights.ensure(mm * sizeof(float), s));
-  RTGS_CUDA(cudaMemsetAsync(bb.stats.ptr, 0, 2 * sizeof(unsigned long long), s), "memset stats");
+  RTGS_CUDA(cudaMemsetAsync(bb.stats.ptr, 0, kStatSlots * sizeof(unsigned long long), s), "memset stats");
   o->records = bb.records.as<GaussRecord>();
   o->weights = want_weights ? bb.weights.as<float>() : nullptr;
   o->spans = bb.spans.as<TileSpan>();
   o->counts = bb.counts.as<int>();
+  o->offsets = bb.offsets.as<int>();
   o->stats = bb.stats.as<unsigned long long>();
+  RTGS_TRY(reset_tile_counts(bb, g, s));
+  bb.counts_cleared = false;  // the projection is about to count
+  o->tile_count = bb.tile_count.as<int>();
+  o->tiles_x = g.tiles_x;
   return 0;
 }
 
@@ -163,7 +169,7 @@ int launch_project_chol(BinBuffers& bb, const Geometry& g, const float* xy, cons
                         const float* color, const float* weight, int64_t m, int64_t n_per_view,
                         bool want_weights, cudaStream_t s) {
   ProjOut o;
-  RTGS_TRY(prepare(bb, m, want_weights, s, &o));
+  RTGS_TRY(prepare(bb, g, m, want_weights, s, &o));
   if (m == 0) return 0;
   project_chol_kernel<<<grid_for(m), kThreads, 0, s>>>(xy, chol, color, weight, m, n_per_view,
                                                        g.height, g.width, g.tiles_x,
@@ -175,7 +181,7 @@ int launch_project_conic(BinBuffers& bb, const Geometry& g, const float* xy, con
                          const float* colors, const float* weights, const int32_t* rects,
                          const int32_t* view_index, int64_t m, bool want_weights, cudaStream_t s) {
   ProjOut o;
-  RTGS_TRY(prepare(bb, m, want_weights, s, &o));
+  RTGS_TRY(prepare(bb, g, m, want_weights, s, &o));
   if (m == 0) return 0;
   project_conic_kernel<<<grid_for(m), kThreads, 0, s>>>(xy, conics, colors, weights, rects,
                                                         view_index, m, g.n_views, g.height,
@@ -186,7 +192,7 @@ int launch_project_conic(BinBuffers& bb, const Geometry& g, const float* xy, con
 int launch_project_raw(BinBuffers& bb, const Geometry& g, const float* raw, int64_t m,
                        int64_t n_per_view, cudaStream_t s) {
   ProjOut o;
-  RTGS_TRY(prepare(bb, m, false, s, &o));
+  RTGS_TRY(prepare(bb, g, m, false, s, &o));
   if (m == 0) return 0;
   project_raw_kernel<<<grid_for(m), kThreads, 0, s>>>(raw, m, n_per_view, g.height, g.width,
                                                       g.tiles_x, g.tiles_per_view, o);

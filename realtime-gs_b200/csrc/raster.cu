@@ -49,8 +49,12 @@ struct RasterArgs {
   const float* weights;       // density variants
   const TileSpan* spans;      // backward: entry index
   const int* offsets;         // backward: entry index
-  const uint64_t* entries;    // sorted (tile key << 32 | gaussian id)
-  const int2* ranges;         // per tile
+  const uint64_t* entries;    // radix path: sorted (tile key << 32 | gaussian id)
+  const int2* ranges;         // radix path: per-tile [start, end)
+  const uint32_t* list;       // scatter path: gaussian ids grouped by tile, ascending in a tile
+  const int* tile_end;        // scatter path: inclusive scan of per-tile counts
+  int64_t cap;                // entry capacity (positions and entry indices at or past it are unused)
+  int presorted;              // 1: radix path, 0: scatter path
   int height, width, tiles_x, tiles_per_view;
   float cutoff;
   // forward outputs
@@ -162,12 +166,21 @@ raster_kernel(const RasterArgs a) {
     inimg[k] = px < a.width && py[k] < a.height;
   }
   const int64_t view_base = static_cast<int64_t>(view) * a.height * a.width;
-  const int2 range = a.ranges[tile];
-
+  int2 range;
+  if (a.presorted) {
+    range = a.ranges[tile];
+  } else {
+    // Scatter path: the tile's ids, sorted by the tile-sort kernel, sit in list[start, end).
+    int64_t start = tile == 0 ? 0 : a.tile_end[tile - 1];
+    int64_t end = a.tile_end[tile];
+    start = start < a.cap ? start : a.cap;
+    end = end < a.cap ? end : a.cap;
+    range = make_int2(static_cast<int>(start), static_cast<int>(end));
+  }
   // Stage records [base, base + n) of this tile's list into shared memory.
   auto stage = [&](int base, int n, bool with_entry) {
     for (int j = threadIdx.x; j < n; j += L::kThreads) {
-      const uint32_t gid = static_cast<uint32_t>(a.entries[base + j]);
+      const uint32_t gid = a.presorted ? static_cast<uint32_t>(a.entries[base + j]) : a.list[base + j];
       const GaussRecord r = a.records[gid];
       s_geo[j] = r.geo;
       s_app[j] = r.app;
@@ -430,12 +443,14 @@ raster_kernel(const RasterArgs a) {
         }
         const float red = octet_transpose_reduce8(S, lane);
         const int64_t e = s_entry[j];
-        if (valid) partials_f[8 * e + r8] = red;
+        // Entries outside [0, capacity) belong to a dropped binning.
+        const bool store = valid && e >= 0 && e < a.cap;
+        if (store) partials_f[8 * e + r8] = red;
         if constexpr (DEN) {
           Sd += __shfl_xor_sync(0xffffffffu, Sd, 4);
           Sd += __shfl_xor_sync(0xffffffffu, Sd, 2);
           Sd += __shfl_xor_sync(0xffffffffu, Sd, 1);
-          if (valid && r8 == 0) a.partial_d[e] = Sd;
+          if (store && r8 == 0) a.partial_d[e] = Sd;
         }
       }
     }
@@ -479,6 +494,10 @@ RasterArgs base_args(const BinBuffers& bb, const Geometry& g, float cutoff) {
   a.offsets = bb.offsets.as<int>();
   a.entries = bb.entries[bb.sorted_sel].as<uint64_t>();
   a.ranges = bb.ranges.as<int2>();
+  a.list = bb.list.as<uint32_t>();
+  a.tile_end = bb.tile_end.as<int>();
+  a.cap = bb.capacity;
+  a.presorted = bb.presorted ? 1 : 0;
   a.height = g.height;
   a.width = g.width;
   a.tiles_x = g.tiles_x;
