@@ -151,10 +151,10 @@ RTGS2D_API int rtgs2d_arena_copy_binning(const rtgs2d_arena* arena, int64_t max_
 
 /*
  * Fit engine: the native Stage-1 fit loop on the device (fit.py:355-554 for one image,
- * batched.py:39-170 for stacked views). Each iteration runs projection from the raw parameters,
- * tile binning, one fused forward + L2-loss-gradient + backward raster kernel and one fused
- * chain-rule + Adam kernel; the host only advances the cosine learning rate
- * (CosineAnnealingLR(T_max=iterations, eta_min=0.1*lr), fit.py:419-422).
+ * batched.py:39-170 for stacked views). Each iteration runs tile binning, one fused forward +
+ * L2-loss-gradient + backward raster kernel and one fused chain-rule + Adam + projection kernel;
+ * the host only advances the cosine learning rate (CosineAnnealingLR(T_max=iterations,
+ * eta_min=0.1*lr), fit.py:419-422) once per chunk of iterations.
  */
 typedef struct rtgs2d_fit rtgs2d_fit;
 
@@ -209,6 +209,14 @@ RTGS2D_API int rtgs2d_fit_capacity(const rtgs2d_fit* fit, int64_t* entries, int6
  * `stream` around projection + binning, the fused raster kernel and the Adam kernel; the
  * accumulated device milliseconds are returned by rtgs2d_fit_stage_times (after a run). */
 RTGS2D_API int rtgs2d_fit_set_profiling(rtgs2d_fit* fit, int32_t enable);
+/* No reference counterpart: CUDA-graph replay of the fit loop. A run proceeds in chunks of 64
+ * iterations with no host synchronisation inside a chunk; once a chunk of a given shape (length,
+ * binning path, buffer layout) has run eagerly, later chunks of that shape are captured into a
+ * CUDA graph once and replayed (same kernels, same results). rtgs2d_fit_set_graphs(fit, 0) runs
+ * every chunk eagerly; rtgs2d_fit_chunk_counts reports how many chunks ran each way. */
+RTGS2D_API int rtgs2d_fit_set_graphs(rtgs2d_fit* fit, int32_t enable);
+RTGS2D_API int rtgs2d_fit_chunk_counts(const rtgs2d_fit* fit, int64_t* graph_chunks,
+                                       int64_t* eager_chunks);
 RTGS2D_API int rtgs2d_fit_stage_times(const rtgs2d_fit* fit, double* bin_ms, double* raster_ms,
                                       double* adam_ms, int64_t* iterations_timed,
                                       double* pairs_timed);

@@ -127,12 +127,62 @@ scatter_kernel(int64_t m, const int* __restrict__ counts, const TileSpan* __rest
   }
 }
 
-// One warp per tile: sort list[start, end) ascending in shared memory (bitonic network over the
-// length padded to a power of two >= 32). Partner strides >= 32 are compare-exchanges in shared
-// memory; strides < 32 run on each 32-element block in registers (shuffles), including the whole
-// first phase (every k <= 32) in one pass. Lists longer than kSegSortMax are left as they are and
-// flagged in stats[kStatLongTile] (the caller re-bins with the radix path).
+// One warp per tile: sort list[start, end) ascending (bitonic network over the length padded to a
+// power of two >= 32, padding = 0xffffffff, which no gaussian id reaches).
+//   len <= 512   in registers: E = n_pad / 32 values per lane in striped order (element
+//                i = e * 32 + lane, coalesced loads and stores); partner strides < 32 are shuffles,
+//                strides >= 32 compare-exchanges inside the lane. Fully unrolled per E.
+//   len <= kSegSortMax  in shared memory (strides >= 32) plus shuffles per 32-element block.
+// Lists longer than kSegSortMax are left as they are and flagged in stats[kStatLongTile] (the
+// caller re-bins with the radix path).
 constexpr int kTileSortWarps = 4;
+constexpr int kRegSortMax = 512;
+
+template <int E>
+__device__ __forceinline__ void warp_sort_striped(uint32_t (&v)[E], int lane) {
+#pragma unroll
+  for (int k = 2; k <= 32 * E; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j >= 32) {
+        const int je = j >> 5;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          if ((e & je) == 0) {
+            const bool up = ((e * 32) & k) == 0;  // k >= 64 here: the lane bits do not matter
+            const uint32_t x = v[e], y = v[e ^ je];
+            v[e] = up ? min(x, y) : max(x, y);
+            v[e ^ je] = up ? max(x, y) : min(x, y);
+          }
+        }
+      } else {
+        const bool lower = (lane & j) == 0;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const bool up = ((e * 32 + lane) & k) == 0;
+          const uint32_t y = __shfl_xor_sync(0xffffffffu, v[e], j);
+          v[e] = (lower == up) ? min(v[e], y) : max(v[e], y);
+        }
+      }
+    }
+  }
+}
+
+template <int E>
+__device__ __forceinline__ void sort_tile_regs(uint32_t* seg, int len, int lane) {
+  uint32_t v[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i = e * 32 + lane;
+    v[e] = i < len ? seg[i] : 0xffffffffu;
+  }
+  warp_sort_striped<E>(v, lane);
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i = e * 32 + lane;
+    if (i < len) seg[i] = v[e];
+  }
+}
 
 __device__ __forceinline__ uint32_t bitonic_shfl(uint32_t v, int i, int k, int j_top) {
   const bool up = (i & k) == 0;
@@ -163,14 +213,12 @@ tile_sort_kernel(const int* __restrict__ tile_end, int64_t n_tiles, int64_t cap,
     return;
   }
   uint32_t* seg = list + start;
-  if (len <= 32) {  // one block in registers
-    uint32_t v = lane < len ? seg[lane] : 0xffffffffu;
-#pragma unroll 1
-    for (int k = 2; k <= 32; k <<= 1) v = bitonic_shfl(v, lane, k, k >> 1);
-    if (lane < len) seg[lane] = v;
-    return;
-  }
-  int n_pad = 64;
+  if (len <= 32) return sort_tile_regs<1>(seg, len, lane);
+  if (len <= 64) return sort_tile_regs<2>(seg, len, lane);
+  if (len <= 128) return sort_tile_regs<4>(seg, len, lane);
+  if (len <= 256) return sort_tile_regs<8>(seg, len, lane);
+  if (len <= kRegSortMax) return sort_tile_regs<16>(seg, len, lane);
+  int n_pad = kRegSortMax * 2;
   while (n_pad < len) n_pad <<= 1;
   uint32_t* b = s_buf[warp];
   for (int c = 0; c < n_pad; c += 32) {  // load + first phase (k <= 32) per 32-element block
@@ -273,8 +321,7 @@ int bin_radix(BinBuffers& bb, const Geometry& g, int64_t m, int64_t launch_entri
 
 int bin_scatter(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s) {
   const int64_t n_tiles = g.n_tiles();
-  const size_t tb = static_cast<size_t>(n_tiles > 0 ? n_tiles : 1) * sizeof(int);
-  RTGS_TRY(bb.tile_end.ensure(tb, s));
+  RTGS_TRY(bb.tile_end.ensure(static_cast<size_t>(n_tiles > 0 ? n_tiles : 1) * sizeof(int), s));
   bb.presorted = false;
   bb.counts_cleared = false;
   if (n_tiles == 0) return 0;

@@ -1,17 +1,20 @@
 // Fit engine: the native Stage-1 fit loop, driven from C++ (no Python per iteration).
 //
 // Per iteration (fit.py:451-482, batched.py:128-145):
-//   project_raw   raw params -> build() -> conic, support rectangle, tile span    (1 kernel)
-//   binning       scan + emit + radix sort with the device-side entry count + tile ranges
+//   binning       tile-count scan, count-down scatter, per-tile sort (or the radix fallback)
 //   raster fit    forward, L2-loss gradient, backward -> per-entry moments   (1 kernel)
-//   loss reduce   only at logging iterations                                  (1 kernel)
-//   adam          entry sums -> chain rule -> Adam on all 9 raw params       (1 kernel)
-// The host advances torch's CosineAnnealingLR recursion in double precision and passes the
-// bias-corrected step size to the Adam kernel. Nothing is read back inside an iteration: the
-// iterations of a chunk are enqueued back to back, and the entry buffers have a fixed capacity.
-// At the end of a chunk the largest entry count of the chunk is read back; if it exceeded the
-// capacity (entries were dropped), the chunk is rolled back to a device snapshot of the raw
-// parameters and Adam moments taken at its start and re-run with a larger capacity.
+//   adam          entry sums -> chain rule -> Adam on all 9 raw params, then the projection
+//                 of the updated parameters for the next iteration; at logging iterations its
+//                 first blocks also reduce the loss                           (1 kernel)
+// The host advances torch's CosineAnnealingLR recursion in double precision and writes every
+// iteration's bias-corrected step size into a small device table once per chunk. Nothing is read
+// back inside a chunk of kChunk iterations, so a chunk is one fixed sequence of launches: after a
+// chunk of the same shape has run once eagerly, it is captured into a CUDA graph and replayed
+// (stage profiling runs eagerly, with events between the stages). At the end of a chunk the
+// largest entry count of the chunk is read back; if it exceeded the capacity (entries were
+// dropped) or a tile list was too long for the tile sort, the chunk is rolled back to a device
+// snapshot of the raw parameters and Adam moments taken at its start and re-run with a larger
+// capacity or the radix binning.
 #include <cmath>
 #include <new>
 #include <vector>
@@ -47,6 +50,18 @@ struct rtgs2d_fit {
   int64_t retries = 0;  // chunks re-run after an entry-capacity overflow or a long tile list
   bool use_radix = false;  // some tile list exceeded the shared-memory sort: bin by radix sort
   bool have_targets = false, have_raw = false;
+  // per-iteration constants of the current chunk, and the replayable chunks
+  DevBuf iter_table;                  // IterScalars[kChunk]
+  IterScalars* host_table = nullptr;  // pinned staging for iter_table
+  cudaStream_t capture_stream = nullptr;
+  struct ChunkGraph {
+    std::vector<uintptr_t> key;
+    cudaGraphExec_t exec = nullptr;
+  };
+  std::vector<ChunkGraph> graphs;        // most recent last
+  std::vector<uintptr_t> last_eager_key;  // layout of the last chunk that ran eagerly and held
+  bool graphs_enabled = true;
+  int64_t graph_chunks = 0, eager_chunks = 0;
   // stage timing (rtgs2d_fit_set_profiling)
   bool profiling = false;
   std::vector<cudaEvent_t> events;  // 4 per iteration of the current run
@@ -55,6 +70,10 @@ struct rtgs2d_fit {
   void release_events() {
     for (cudaEvent_t e : events) cudaEventDestroy(e);
     events.clear();
+  }
+  void release_graphs() {
+    for (ChunkGraph& g : graphs) cudaGraphExecDestroy(g.exec);
+    graphs.clear();
   }
 };
 
@@ -202,6 +221,115 @@ FitRasterArgs raster_args(rtgs2d_fit* f) {
   return fa;
 }
 
+
+// Everything a captured chunk depends on besides the contents of device memory: its length, the
+// binning path and the address and size of every buffer its launches use.
+std::vector<uintptr_t> chunk_key(const rtgs2d_fit* f, int64_t chunk) {
+  const BinBuffers& bb = f->bb;
+  std::vector<uintptr_t> k = {static_cast<uintptr_t>(chunk), static_cast<uintptr_t>(f->use_radix),
+                              static_cast<uintptr_t>(bb.capacity)};
+  for (const DevBuf* b : {&bb.records, &bb.weights, &bb.spans, &bb.counts, &bb.offsets, &bb.list,
+                          &bb.tile_count, &bb.tile_end, &bb.entries[0], &bb.entries[1], &bb.ranges,
+                          &bb.partials, &bb.partial_d, &bb.cub_temp, &bb.sort_counts, &bb.stats,
+                          &f->raw, &f->m1, &f->m2, &f->targets, &f->mask, &f->view_scale,
+                          &f->tile_loss, &f->log, &f->iter_table}) {
+    k.push_back(reinterpret_cast<uintptr_t>(b->ptr));
+    k.push_back(static_cast<uintptr_t>(b->bytes));
+  }
+  return k;
+}
+
+// The launches of one chunk: the chunk's first projection, then per iteration binning, raster and
+// Adam (+ projection of the next iteration, except after the last). With `ev` (profiling), four
+// events per iteration bracket the stages. `capturing`: `s` is in stream capture.
+int enqueue_chunk(rtgs2d_fit* f, int64_t chunk, cudaStream_t s, cudaEvent_t* ev, bool capturing) {
+  BinBuffers& bb = f->bb;
+  const LossLog lg{f->tile_loss.as<double>(), f->log.as<double>(), static_cast<int>(f->n_views),
+                   f->geo.tiles_per_view};
+  const FitRasterArgs fa = raster_args(f);
+  // External records: under stream capture they become event-record nodes of the graph (a plain
+  // record would only order the capture), so the replayed chunk still times its stages.
+  auto record = [s, capturing](cudaEvent_t e) {
+    return capturing ? cudaEventRecordWithFlags(e, s, cudaEventRecordExternal) : cudaEventRecord(e, s);
+  };
+  RTGS_TRY(launch_project_raw(bb, f->geo, f->raw.as<float>(), f->m, f->n, s));
+  for (int64_t k = 0; k < chunk; ++k) {
+    cudaEvent_t* e = ev ? ev + 4 * k : nullptr;
+    if (e) RTGS_CUDA(record(e[0]), "event record");
+    RTGS_TRY(bin_entries_async(bb, f->geo, f->m, f->use_radix, s));
+    if (e) RTGS_CUDA(record(e[1]), "event record");
+    RTGS_TRY(launch_raster_fit(bb, f->geo, kCutoff, fa, true, s));
+    if (e) RTGS_CUDA(record(e[2]), "event record");
+    RTGS_TRY(launch_adam_fit(bb, f->geo, f->m, f->n, f->raw.as<float>(), f->m1.as<float>(),
+                             f->m2.as<float>(), f->iter_table.as<IterScalars>(),
+                             static_cast<int>(k), lg, k + 1 < chunk, s));
+    if (e) RTGS_CUDA(record(e[3]), "event record");
+  }
+  return 0;
+}
+
+// Capture the chunk into a graph (nothing runs). Returns null if capture is not possible (the
+// caller then runs the chunk eagerly); errors of the attempt are cleared.
+cudaGraphExec_t capture_chunk(rtgs2d_fit* f, int64_t chunk, cudaEvent_t* ev) {
+  if (!f->capture_stream &&
+      cudaStreamCreateWithFlags(&f->capture_stream, cudaStreamNonBlocking) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (cudaStreamBeginCapture(f->capture_stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  const int rc = enqueue_chunk(f, chunk, f->capture_stream, ev, true);
+  cudaGraph_t graph = nullptr;
+  const cudaError_t end = cudaStreamEndCapture(f->capture_stream, &graph);
+  cudaGraphExec_t exec = nullptr;
+  if (rc == 0 && end == cudaSuccess && graph) {
+    if (cudaGraphInstantiate(&exec, graph, 0) != cudaSuccess) exec = nullptr;
+  }
+  if (graph) cudaGraphDestroy(graph);
+  cudaGetLastError();
+  return exec;
+}
+
+// Run one chunk: replay its graph when a chunk of the same key has already run eagerly, else run
+// it eagerly. With stage profiling the event records are part of the chunk (and of its graph).
+int run_chunk(rtgs2d_fit* f, int64_t chunk, cudaStream_t s) {
+  cudaEvent_t* ev = nullptr;
+  if (f->profiling) {
+    RTGS_TRY(ensure_events(f, static_cast<size_t>(4 * kChunk)));  // fixed size: a stable address
+    ev = f->events.data();
+  }
+  std::vector<uintptr_t> key = chunk_key(f, chunk);
+  key.push_back(reinterpret_cast<uintptr_t>(ev));
+  if (!f->graphs_enabled) key.clear();  // matches no graph and no eager key
+  for (auto& g : f->graphs) {
+    if (g.key == key) {
+      f->graph_chunks += 1;
+      return check_cuda(cudaGraphLaunch(g.exec, s), "chunk graph launch");
+    }
+  }
+  if (!key.empty() && key == f->last_eager_key) {
+    cudaGraphExec_t exec = capture_chunk(f, chunk, ev);
+    if (exec) {
+      constexpr size_t kMaxGraphs = 4;
+      if (f->graphs.size() == kMaxGraphs) {
+        cudaGraphExecDestroy(f->graphs.front().exec);
+        f->graphs.erase(f->graphs.begin());
+      }
+      f->graphs.push_back({key, exec});
+      f->graph_chunks += 1;
+      return check_cuda(cudaGraphLaunch(exec, s), "chunk graph launch");
+    }
+  }
+  f->eager_chunks += 1;
+  RTGS_TRY(enqueue_chunk(f, chunk, s, ev, false));
+  // The buffers as the next chunk of this shape finds them.
+  f->last_eager_key = chunk_key(f, chunk);
+  f->last_eager_key.push_back(reinterpret_cast<uintptr_t>(ev));
+  return 0;
+}
+
 }  // namespace
 
 extern "C" {
@@ -277,7 +405,11 @@ int rtgs2d_fit_destroy(rtgs2d_fit* fit) {
   fit->log.release();
   fit->eval_sums.release();
   fit->snap.release();
+  fit->iter_table.release();
   fit->release_events();
+  fit->release_graphs();
+  if (fit->capture_stream) cudaStreamDestroy(fit->capture_stream);
+  if (fit->host_table) cudaFreeHost(fit->host_table);
   delete fit;
   if (prev != dev) cudaSetDevice(prev);
   return RTGS2D_OK;
@@ -366,6 +498,11 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
                              kStatSlots * sizeof(unsigned long long)),
               "pinned stats");
   }
+  if (!f->host_table) {
+    RTGS_CUDA(cudaMallocHost(reinterpret_cast<void**>(&f->host_table), kChunk * sizeof(IterScalars)),
+              "pinned iteration table");
+  }
+  RTGS_TRY(f->iter_table.ensure(kChunk * sizeof(IterScalars), s));
   if (!bb.stats.ptr) {
     RTGS_TRY(bb.stats.ensure(kStatSlots * sizeof(unsigned long long), s));
     RTGS_CUDA(cudaMemsetAsync(bb.stats.ptr, 0, kStatSlots * sizeof(unsigned long long), s),
@@ -383,50 +520,41 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
     const int64_t step0 = f->step;
     const double lr0 = f->lr_current;
     const size_t logs0 = f->log_iters.size();
+    // Per-iteration constants: Adam's bias corrections at the current learning rate, the log row.
+    for (int64_t k = 0; k < chunk; ++k) {
+      const int64_t it = f->step;
+      IterScalars& row = f->host_table[k];
+      const double t = static_cast<double>(it + 1);
+      const double bc1 = 1.0 - std::pow(0.9, t);
+      const double bc2 = 1.0 - std::pow(0.999, t);
+      row.adam.neg_step_size = static_cast<float>(-(f->lr_current / bc1));
+      row.adam.bc2_sqrt = static_cast<float>(std::pow(bc2, 0.5));
+      row.adam.beta1 = 0.9f;
+      row.adam.beta2 = 0.999f;
+      row.adam.one_minus_beta1 = static_cast<float>(1.0 - 0.9);
+      row.adam.one_minus_beta2 = static_cast<float>(1.0 - 0.999);
+      row.adam.eps = 1e-8f;
+      row.adam.freeze_geometry = f->opt.freeze_geometry;
+      row.log_slot = -1;
+      if (is_log_iter(f->opt, it)) {
+        const int64_t slot = static_cast<int64_t>(f->log_iters.size());
+        if (slot < f->max_logs) {
+          row.log_slot = static_cast<int>(slot);
+          f->log_iters.push_back(it);
+        }
+      }
+      f->step += 1;
+      f->lr_current = cosine_next_lr(f->lr_current, base_lr, eta_min, f->step, t_max);
+    }
+    RTGS_CUDA(cudaMemcpyAsync(f->iter_table.ptr, f->host_table,
+                              static_cast<size_t>(chunk) * sizeof(IterScalars),
+                              cudaMemcpyHostToDevice, s),
+              "iteration table upload");
     RTGS_TRY(snapshot(f, true, s));
     RTGS_CUDA(cudaMemsetAsync(bb.stats.as<unsigned long long>() + kStatPairsTotal, 0,
                               3 * sizeof(unsigned long long), s),
               "reset chunk stats");
-    if (f->profiling) RTGS_TRY(ensure_events(f, static_cast<size_t>(4 * chunk)));
-    // Iteration k: [projection] binning, raster, Adam. The Adam step of iteration k also projects
-    // the updated parameters for iteration k + 1 (one kernel); only the chunk's first projection
-    // is a separate launch and its last Adam step projects nothing.
-    RTGS_TRY(launch_project_raw(bb, f->geo, f->raw.as<float>(), f->m, f->n, s));
-    for (int64_t k = 0; k < chunk; ++k) {
-      const int64_t it = f->step;
-      cudaEvent_t* ev = f->profiling ? &f->events[static_cast<size_t>(4 * k)] : nullptr;
-      if (ev) RTGS_CUDA(cudaEventRecord(ev[0], s), "event record");
-      RTGS_TRY(bin_entries_async(bb, f->geo, f->m, f->use_radix, s));
-      if (ev) RTGS_CUDA(cudaEventRecord(ev[1], s), "event record");
-      RTGS_TRY(launch_raster_fit(bb, f->geo, kCutoff, raster_args(f), true, s));
-      if (ev) RTGS_CUDA(cudaEventRecord(ev[2], s), "event record");
-      if (is_log_iter(f->opt, it)) {
-        const int64_t slot = static_cast<int64_t>(f->log_iters.size());
-        if (slot < f->max_logs) {
-          RTGS_TRY(launch_loss_reduce(f->tile_loss.as<double>(), f->geo,
-                                      f->log.as<double>() + slot * f->n_views * 2, s));
-          f->log_iters.push_back(it);
-        }
-      }
-      const double t = static_cast<double>(it + 1);
-      const double bc1 = 1.0 - std::pow(0.9, t);
-      const double bc2 = 1.0 - std::pow(0.999, t);
-      const double step_size = f->lr_current / bc1;
-      AdamScalars a;
-      a.neg_step_size = static_cast<float>(-step_size);
-      a.bc2_sqrt = static_cast<float>(std::pow(bc2, 0.5));
-      a.beta1 = 0.9f;
-      a.beta2 = 0.999f;
-      a.one_minus_beta1 = static_cast<float>(1.0 - 0.9);
-      a.one_minus_beta2 = static_cast<float>(1.0 - 0.999);
-      a.eps = 1e-8f;
-      a.freeze_geometry = f->opt.freeze_geometry;
-      RTGS_TRY(launch_adam_fit(bb, f->geo, f->m, f->n, f->raw.as<float>(), f->m1.as<float>(),
-                               f->m2.as<float>(), a, k + 1 < chunk, s));
-      if (ev) RTGS_CUDA(cudaEventRecord(ev[3], s), "event record");
-      f->step += 1;
-      f->lr_current = cosine_next_lr(f->lr_current, base_lr, eta_min, f->step, t_max);
-    }
+    RTGS_TRY(run_chunk(f, chunk, s));
     RTGS_CUDA(cudaMemcpyAsync(bb.host_stats, bb.stats.ptr, kStatSlots * sizeof(unsigned long long),
                               cudaMemcpyDeviceToHost, s),
               "chunk stats readback");
@@ -441,7 +569,7 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
       f->lr_current = lr0;
       f->log_iters.resize(logs0);
       f->retries += 1;
-      if (long_tile) f->use_radix = true;  // a tile list too long for the shared-memory sort
+      if (long_tile) f->use_radix = true;  // a tile list too long for the tile sort
       if (max_entries > bb.capacity) {
         RTGS_TRY(ensure_entry_capacity(bb, max_entries + max_entries / 2 + 4096, false, s));
       }
@@ -489,6 +617,23 @@ int rtgs2d_fit_set_profiling(rtgs2d_fit* f, int32_t enable) {
   f->profiling = enable != 0;
   f->bin_ms = f->raster_ms = f->adam_ms = f->pairs_timed = 0.0;
   f->iterations_timed = 0;
+  return RTGS2D_OK;
+}
+
+int rtgs2d_fit_set_graphs(rtgs2d_fit* f, int32_t enable) {
+  RTGS_TRY(check_fit(f));
+  f->graphs_enabled = enable != 0;
+  if (!f->graphs_enabled) {
+    f->release_graphs();
+    f->last_eager_key.clear();
+  }
+  return RTGS2D_OK;
+}
+
+int rtgs2d_fit_chunk_counts(const rtgs2d_fit* f, int64_t* graph_chunks, int64_t* eager_chunks) {
+  if (!f) return set_error(RTGS2D_ERR_INVALID, "fit is NULL");
+  if (graph_chunks) *graph_chunks = f->graph_chunks;
+  if (eager_chunks) *eager_chunks = f->eager_chunks;
   return RTGS2D_OK;
 }
 

@@ -175,9 +175,23 @@ struct AdamScalars {
   float beta1, beta2, one_minus_beta1, one_minus_beta2, eps;
   int freeze_geometry;
 };
-// Adam step from the last raster's entry moments; with project_next the updated parameters are
-// also projected (records, spans, counts, stats) for the next iteration's binning.
+// Per-iteration constants of a fit chunk, read by the Adam kernel from a device table (so the
+// launches of every chunk are identical and can be replayed from one CUDA graph).
+struct IterScalars {
+  AdamScalars adam;
+  int log_slot;  // >= 0: also reduce this iteration's loss into log row log_slot
+};
+// Where the Adam kernel's loss logging reads and writes.
+struct LossLog {
+  const double* tile_loss;  // (n_tiles, 2) from the raster
+  double* log;              // (rows, n_views, 2)
+  int n_views, tiles_per_view;
+};
+// Adam step from the last raster's entry moments, with the constants of table[k]; with
+// project_next the updated parameters are also projected (records, spans, counts, offsets,
+// stats) for the next iteration's binning.
 int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_view, float* raw,
-                    float* m1, float* m2, const AdamScalars& a, bool project_next, cudaStream_t s);
+                    float* m1, float* m2, const IterScalars* table, int k, const LossLog& lg,
+                    bool project_next, cudaStream_t s);
 
 }  // namespace rtgs2d

@@ -56,7 +56,7 @@ __device__ __forceinline__ void for_each_span_tile(int64_t gid, int cnt, const T
 }
 
 // Record, span, tile count and entry offset of gaussian i. Must be called by every thread of a
-// kProjThreads block (it contains a block barrier).
+// kProjThreads block (it contains block barriers).
 //
 // Entry offsets: a block-wide exclusive scan of the tile counts plus the block's base, reserved
 // with one atomic on stats[kStatEntries]. Blocks reserve in arrival order, so a gaussian's entry
@@ -251,5 +251,36 @@ __device__ __forceinline__ void adam_update(float& p, float& m1, float& m2, floa
   p = __fadd_rn(p, __fmul_rn(a.neg_step_size, __fdiv_rn(m1, denom)));
 }
 
+
+// Loss numerators of one view: the per-tile (squared error, clamped squared error) pairs summed
+// in a fixed order (strided per-thread sums, then a tree), so every caller gets the same bits.
+// Called by all kLossThreads threads of a block.
+constexpr int kLossThreads = 256;
+
+__device__ __forceinline__ void reduce_view_loss(const double* __restrict__ tile_loss,
+                                                 int tiles_per_view, int view, double* dst) {
+  __shared__ double s_loss[2][kLossThreads];
+  double a0 = 0.0, a1 = 0.0;
+  for (int t = threadIdx.x; t < tiles_per_view; t += kLossThreads) {
+    const int64_t idx = static_cast<int64_t>(view) * tiles_per_view + t;
+    a0 += tile_loss[2 * idx];
+    a1 += tile_loss[2 * idx + 1];
+  }
+  s_loss[0][threadIdx.x] = a0;
+  s_loss[1][threadIdx.x] = a1;
+  __syncthreads();
+  for (int stride = kLossThreads / 2; stride > 0; stride >>= 1) {
+    if (threadIdx.x < stride) {
+      s_loss[0][threadIdx.x] += s_loss[0][threadIdx.x + stride];
+      s_loss[1][threadIdx.x] += s_loss[1][threadIdx.x + stride];
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    dst[2 * view] = s_loss[0][0];
+    dst[2 * view + 1] = s_loss[1][0];
+  }
+  __syncthreads();  // s_loss may be reused by a next call
+}
 
 }  // namespace rtgs2d

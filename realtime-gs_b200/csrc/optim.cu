@@ -95,9 +95,18 @@ template <bool PROJECT>
 __global__ void __launch_bounds__(kThreads)
 adam_fit_kernel(int64_t m, int64_t cap, int* counts, const int* __restrict__ offsets,
                 const float4* __restrict__ partials, int height, int width, float* __restrict__ raw,
-                float* __restrict__ m1, float* __restrict__ m2, const AdamScalars a,
-                int64_t n_per_view, int tiles_x, int tiles_per_view, ProjOut o) {
+                float* __restrict__ m1, float* __restrict__ m2,
+                const IterScalars* __restrict__ table, int k_iter, LossLog lg, int64_t n_per_view,
+                int tiles_x, int tiles_per_view, ProjOut o) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  const AdamScalars a = table[k_iter].adam;
+  const int log_slot = table[k_iter].log_slot;
+  if (log_slot >= 0) {  // the first blocks also log this iteration's loss, one view per block
+    for (int v = blockIdx.x; v < lg.n_views; v += gridDim.x) {
+      reduce_view_loss(lg.tile_loss, lg.tiles_per_view, v,
+                       lg.log + static_cast<int64_t>(log_slot) * lg.n_views * 2);
+    }
+  }
   const bool active = i < m;
   float r[kRawSlots], v1[kRawSlots], v2[kRawSlots];
   if (active) {
@@ -208,7 +217,8 @@ int launch_finalize_conic(const BinBuffers& bb, int64_t m, const float* conics,
 }
 
 int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_view, float* raw,
-                    float* m1, float* m2, const AdamScalars& a, bool project_next, cudaStream_t s) {
+                    float* m1, float* m2, const IterScalars* table, int k, const LossLog& lg,
+                    bool project_next, cudaStream_t s) {
   if (m == 0) return 0;
   ProjOut o{};
   if (project_next) {
@@ -228,11 +238,11 @@ int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_
     bb.counts_cleared = false;
     adam_fit_kernel<true><<<grid_for(m), kThreads, 0, s>>>(
         m, bb.capacity, bb.counts.as<int>(), bb.offsets.as<int>(), bb.partials.as<float4>(), g.height,
-        g.width, raw, m1, m2, a, n_per_view, g.tiles_x, g.tiles_per_view, o);
+        g.width, raw, m1, m2, table, k, lg, n_per_view, g.tiles_x, g.tiles_per_view, o);
   } else {
     adam_fit_kernel<false><<<grid_for(m), kThreads, 0, s>>>(
         m, bb.capacity, bb.counts.as<int>(), bb.offsets.as<int>(), bb.partials.as<float4>(), g.height,
-        g.width, raw, m1, m2, a, n_per_view, g.tiles_x, g.tiles_per_view, o);
+        g.width, raw, m1, m2, table, k, lg, n_per_view, g.tiles_x, g.tiles_per_view, o);
   }
   return check_cuda(cudaGetLastError(), "adam_fit_kernel");
 }

@@ -25,6 +25,7 @@
 // Reference semantics: renderer2d_ext.cu:69-84 (forward), :142-171 (backward); parity of the
 // support set with renderer2d.py:233-248.
 #include "internal.h"
+#include "kernels.cuh"
 
 namespace rtgs2d {
 namespace {
@@ -460,28 +461,7 @@ raster_kernel(const RasterArgs a) {
 // Deterministic per-view reduction of tile loss numerators: one block per view.
 __global__ void __launch_bounds__(256)
 loss_reduce_kernel(const double* __restrict__ tile_loss, int tiles_per_view, double* dst) {
-  __shared__ double s[2][256];
-  const int view = blockIdx.x;
-  double a0 = 0.0, a1 = 0.0;
-  for (int t = threadIdx.x; t < tiles_per_view; t += 256) {
-    const int64_t idx = static_cast<int64_t>(view) * tiles_per_view + t;
-    a0 += tile_loss[2 * idx];
-    a1 += tile_loss[2 * idx + 1];
-  }
-  s[0][threadIdx.x] = a0;
-  s[1][threadIdx.x] = a1;
-  __syncthreads();
-  for (int stride = 128; stride > 0; stride >>= 1) {
-    if (threadIdx.x < stride) {
-      s[0][threadIdx.x] += s[0][threadIdx.x + stride];
-      s[1][threadIdx.x] += s[1][threadIdx.x + stride];
-    }
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) {
-    dst[2 * view] = s[0][0];
-    dst[2 * view + 1] = s[1][0];
-  }
+  reduce_view_loss(tile_loss, tiles_per_view, blockIdx.x, dst);
 }
 
 constexpr int kPPT = 2;
@@ -558,7 +538,7 @@ int launch_raster_fit(BinBuffers& bb, const Geometry& g, float cutoff, const Fit
 
 int launch_loss_reduce(const double* tile_loss, const Geometry& g, double* dst, cudaStream_t s) {
   if (g.n_views == 0) return 0;
-  loss_reduce_kernel<<<g.n_views, 256, 0, s>>>(tile_loss, g.tiles_per_view, dst);
+  loss_reduce_kernel<<<g.n_views, kLossThreads, 0, s>>>(tile_loss, g.tiles_per_view, dst);
   return check_cuda(cudaGetLastError(), "loss_reduce_kernel");
 }
 

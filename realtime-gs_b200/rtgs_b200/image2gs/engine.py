@@ -185,6 +185,16 @@ class FitEngine:
         """Record CUDA events around binning, the raster kernel and Adam in every iteration."""
         _native.check(self._lib.rtgs2d_fit_set_profiling(self._h, int(bool(enable))))
 
+    def set_graphs(self, enable: bool = True) -> None:
+        """Replay repeated 64-iteration chunks from a captured CUDA graph (default on)."""
+        _native.check(self._lib.rtgs2d_fit_set_graphs(self._h, int(bool(enable))))
+
+    def chunk_counts(self) -> tuple[int, int]:
+        """(chunks replayed from a CUDA graph, chunks run eagerly) since the engine was created."""
+        g, e = ctypes.c_int64(), ctypes.c_int64()
+        _native.check(self._lib.rtgs2d_fit_chunk_counts(self._h, ctypes.byref(g), ctypes.byref(e)))
+        return int(g.value), int(e.value)
+
     def stage_times(self) -> dict[str, float]:
         b, r, a, p = ctypes.c_double(), ctypes.c_double(), ctypes.c_double(), ctypes.c_double()
         n = ctypes.c_int64()
