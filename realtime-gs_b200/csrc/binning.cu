@@ -5,11 +5,12 @@
 // per-pair global atomics with per-tile gathers.
 //
 // Two ways to build the lists, both deterministic in what the raster kernels read:
-//   tile scatter (default)  the projection counts entries per tile; an inclusive scan of the tile
-//                           counts gives every tile's [start, end); each gaussian claims one slot
-//                           per tile by counting that tile's count back down (so the counts are
-//                           zero again for the next projection), and one warp per tile then sorts
-//                           the tile's ids in shared memory (lists up to kSegSortMax).
+//   tile scatter (default)  the projection counts entries per tile (and in the fit loop emits the
+//                           (tile, id) entries; otherwise emit_kernel does); an inclusive scan of
+//                           the tile counts gives every tile's [start, end); each entry claims a
+//                           slot in its tile by counting that tile's count back down (so the
+//                           counts are zero again for the next projection), and one warp per tile
+//                           then sorts the tile's ids (lists up to kSegSortMax).
 //   radix                   entries emitted gaussian-major as (tile key << 32 | id), stable radix
 //                           sort by key (sort.cu), per-tile ranges; used when some tile list is
 //                           longer than kSegSortMax. Emission order must follow the gaussian
@@ -27,16 +28,28 @@ namespace {
 
 constexpr int kThreads = 256;
 
+// Retire the projection's stats: the largest entry count so far, copies of the entry and pair
+// counts (slots "last"), then slots 0-1 zeroed for the next projection (scatter path only, where
+// nothing later reads them).
+__device__ __forceinline__ void retire_projection_stats(unsigned long long* stats, bool zero) {
+  const unsigned long long e = stats[kStatEntries];
+  atomicMax(&stats[kStatMaxEntries], e);
+  stats[kStatLastEntries] = e;
+  stats[kStatLastPairs] = stats[kStatPairs];
+  if (zero) {
+    stats[kStatEntries] = 0;
+    stats[kStatPairs] = 0;
+  }
+}
+
+// Entries of every gaussian, (tile key << 32 | id) at offsets[g] + j, up to the capacity. With
+// `stats` (radix path) thread 0 also retires the projection's stats (slots 0-1 kept).
 __global__ void __launch_bounds__(kThreads)
 emit_kernel(int64_t m, const int* __restrict__ counts, const int* __restrict__ offsets,
             const TileSpan* __restrict__ spans, int tiles_x, int64_t cap,
             unsigned long long* __restrict__ stats, uint64_t* __restrict__ entries) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
-  if (i == 0) {
-    atomicMax(&stats[kStatMaxEntries], stats[kStatEntries]);
-    stats[kStatLastEntries] = stats[kStatEntries];
-    stats[kStatLastPairs] = stats[kStatPairs];
-  }
+  if (i == 0 && stats) retire_projection_stats(stats, false);
   int cnt = 0, off = 0;
   TileSpan sp{0, 0, 1, 0};
   if (i < m) {
@@ -46,85 +59,29 @@ emit_kernel(int64_t m, const int* __restrict__ counts, const int* __restrict__ o
       sp = spans[i];
     }
   }
-  const long long off_l = off;
-  for_each_span_tile(i, cnt, sp, tiles_x, [&](long long g, int j, int key) {
-    // `off` of the span's owner lane: entries of gaussian g are offsets[g] + j.
-    const long long o = g == i ? off_l : static_cast<long long>(offsets[g]);
-    if (o + j < cap) entries[o + j] = (static_cast<uint64_t>(key) << 32) | static_cast<uint64_t>(g);
+  for_each_span_tile(i, cnt, sp, off, tiles_x, [&](long long g, int j, int key, int g_off) {
+    const int64_t e = static_cast<int64_t>(g_off) + j;
+    if (g_off >= 0 && e < cap) {
+      entries[e] = (static_cast<uint64_t>(key) << 32) | static_cast<uint64_t>(g);
+    }
   });
 }
 
-// Slot of gaussian g in tile t: tile_end[t] minus the tile count before this gaussian counted it
-// down, i.e. a unique slot of [end - count, end). A lane issues all atomics of its span before it
-// stores, so their round trips overlap. Block 0 also retires the projection's stats slots 0-1
-// (copied to the "last" slots, then zeroed for the next projection).
-constexpr int kScatterUnroll = 4;  // slots in flight per lane on warp-walked spans
-
+// One thread per emitted entry: its slot in its tile is tile_end[t] minus the tile count before
+// this entry counted it down, i.e. a unique slot of [end - count, end). The counts end at zero,
+// ready for the next projection.
 __global__ void __launch_bounds__(kThreads)
-scatter_kernel(int64_t m, const int* __restrict__ counts, const TileSpan* __restrict__ spans,
-               int tiles_x, const int* __restrict__ tile_end, int* __restrict__ tile_count,
-               int64_t cap, unsigned long long* __restrict__ stats, uint32_t* __restrict__ list) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
-  if (i == 0) {
-    const unsigned long long e = stats[kStatEntries];
-    atomicMax(&stats[kStatMaxEntries], e);
-    stats[kStatLastEntries] = e;
-    stats[kStatLastPairs] = stats[kStatPairs];
-    stats[kStatEntries] = 0;
-    stats[kStatPairs] = 0;
-  }
-  int cnt = 0;
-  TileSpan sp{0, 0, 1, 0};
-  if (i < m) {
-    cnt = counts[i];
-    if (cnt > 0) sp = spans[i];
-  }
-  if (cnt > 0 && cnt <= kSmallSpan) {
-    int pos[kSmallSpan];
-    int tx = sp.tx0, ty = sp.ty0;
-#pragma unroll
-    for (int j = 0; j < kSmallSpan; ++j) {
-      if (j < cnt) {
-        const int t = sp.key_base + ty * tiles_x + tx;
-        pos[j] = tile_end[t] - atomicSub(&tile_count[t], 1);
-        if (++tx == sp.tx0 + sp.ntx) {
-          tx = sp.tx0;
-          ++ty;
-        }
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < kSmallSpan; ++j) {
-      if (j < cnt && pos[j] >= 0 && pos[j] < cap) list[pos[j]] = static_cast<uint32_t>(i);
-    }
-  }
-  const int lane = threadIdx.x & 31;
-  unsigned big = __ballot_sync(0xffffffffu, cnt > kSmallSpan);
-  while (big) {
-    const int src = __ffs(big) - 1;
-    big &= big - 1;
-    const int c = __shfl_sync(0xffffffffu, cnt, src);
-    const int tx0 = __shfl_sync(0xffffffffu, sp.tx0, src);
-    const int ty0 = __shfl_sync(0xffffffffu, sp.ty0, src);
-    const int ntx = __shfl_sync(0xffffffffu, sp.ntx, src);
-    const int kb = __shfl_sync(0xffffffffu, sp.key_base, src);
-    const uint32_t g = static_cast<uint32_t>(__shfl_sync(0xffffffffu, static_cast<long long>(i), src));
-    for (int j0 = lane; j0 < c; j0 += 32 * kScatterUnroll) {
-      int pos[kScatterUnroll];
-#pragma unroll
-      for (int r = 0; r < kScatterUnroll; ++r) {
-        const int j = j0 + 32 * r;
-        if (j < c) {
-          const int t = kb + (ty0 + j / ntx) * tiles_x + tx0 + j % ntx;
-          pos[r] = tile_end[t] - atomicSub(&tile_count[t], 1);
-        }
-      }
-#pragma unroll
-      for (int r = 0; r < kScatterUnroll; ++r) {
-        if (j0 + 32 * r < c && pos[r] >= 0 && pos[r] < cap) list[pos[r]] = g;
-      }
-    }
-  }
+scatter_kernel(const uint64_t* __restrict__ entries, const unsigned long long* __restrict__ stats,
+               int64_t cap, const int* __restrict__ tile_end, int* __restrict__ tile_count,
+               uint32_t* __restrict__ list) {
+  const int64_t e = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  const int64_t n_all = static_cast<int64_t>(stats[kStatEntries]);
+  const int64_t n = n_all < cap ? n_all : cap;
+  if (e >= n) return;
+  const uint64_t v = entries[e];
+  const int t = static_cast<int>(v >> 32);
+  const int pos = tile_end[t] - atomicSub(&tile_count[t], 1);
+  if (pos >= 0 && pos < cap) list[pos] = static_cast<uint32_t>(v);
 }
 
 // One warp per tile: sort list[start, end) ascending (bitonic network over the length padded to a
@@ -199,6 +156,7 @@ __global__ void __launch_bounds__(kTileSortWarps * 32)
 tile_sort_kernel(const int* __restrict__ tile_end, int64_t n_tiles, int64_t cap,
                  unsigned long long* __restrict__ stats, uint32_t* __restrict__ list) {
   __shared__ uint32_t s_buf[kTileSortWarps][kSegSortMax];
+  if (blockIdx.x == 0 && threadIdx.x == 0) retire_projection_stats(stats, true);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * kTileSortWarps + warp;
   if (t >= n_tiles) return;
@@ -306,9 +264,10 @@ int bin_radix(BinBuffers& bb, const Geometry& g, int64_t m, int64_t launch_entri
   if (m == 0 || bb.capacity == 0 || launch_entries == 0) return 0;
   RTGS_TRY(cub_scan<false>(bb, bb.counts.as<int>(), bb.offsets.as<int>(), m, s));
   RTGS_TRY(bb.sort_counts.ensure(sort_counts_bytes(), s));
-  emit_kernel<<<grid_for(m), kThreads, 0, s>>>(
-      m, bb.counts.as<int>(), bb.offsets.as<int>(), bb.spans.as<TileSpan>(), g.tiles_x,
-      bb.capacity, bb.stats.as<unsigned long long>(), bb.entries[0].as<uint64_t>());
+  emit_kernel<<<grid_for(m), kThreads, 0, s>>>(m, bb.counts.as<int>(), bb.offsets.as<int>(),
+                                                bb.spans.as<TileSpan>(), g.tiles_x, bb.capacity,
+                                                bb.stats.as<unsigned long long>(),
+                                                bb.entries[0].as<uint64_t>());
   RTGS_CUDA(cudaGetLastError(), "emit_kernel");
   RTGS_TRY(radix_sort_entries(bb.entries[0].as<uint64_t>(), bb.entries[1].as<uint64_t>(),
                               bb.stats.as<unsigned long long>() + kStatEntries, bb.capacity,
@@ -325,13 +284,19 @@ int bin_scatter(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s) {
   bb.presorted = false;
   bb.counts_cleared = false;
   if (n_tiles == 0) return 0;
+  if (m > 0 && !bb.entries_emitted && bb.capacity > 0) {
+    emit_kernel<<<grid_for(m), kThreads, 0, s>>>(m, bb.counts.as<int>(), bb.offsets.as<int>(),
+                                                  bb.spans.as<TileSpan>(), g.tiles_x, bb.capacity,
+                                                  nullptr, bb.entries[0].as<uint64_t>());
+    RTGS_CUDA(cudaGetLastError(), "emit_kernel");
+  }
   RTGS_TRY(cub_scan<true>(bb, bb.tile_count.as<int>(), bb.tile_end.as<int>(), n_tiles, s));
-  if (m == 0) return 0;
-  scatter_kernel<<<grid_for(m), kThreads, 0, s>>>(
-      m, bb.counts.as<int>(), bb.spans.as<TileSpan>(), g.tiles_x, bb.tile_end.as<int>(),
-      bb.tile_count.as<int>(), bb.capacity, bb.stats.as<unsigned long long>(),
-      bb.list.as<uint32_t>());
-  RTGS_CUDA(cudaGetLastError(), "scatter_kernel");
+  if (m > 0 && bb.capacity > 0) {
+    scatter_kernel<<<grid_for(bb.capacity), kThreads, 0, s>>>(
+        bb.entries[0].as<uint64_t>(), bb.stats.as<unsigned long long>(), bb.capacity,
+        bb.tile_end.as<int>(), bb.tile_count.as<int>(), bb.list.as<uint32_t>());
+    RTGS_CUDA(cudaGetLastError(), "scatter_kernel");
+  }
   bb.counts_cleared = true;
   const unsigned blocks = static_cast<unsigned>((n_tiles + kTileSortWarps - 1) / kTileSortWarps);
   tile_sort_kernel<<<blocks, kTileSortWarps * 32, 0, s>>>(bb.tile_end.as<int>(), n_tiles,
@@ -418,8 +383,8 @@ int bin_entries(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s) {
   }
   bb.n_entries = static_cast<int64_t>(entries);
   const bool radix = bb.host_stats[kStatLongTile] > 0;
-  const bool have = radix ? (bb.entries[0].ptr != nullptr && bb.entries[1].ptr != nullptr)
-                          : bb.list.ptr != nullptr;
+  const bool have = bb.entries[0].ptr != nullptr &&
+                    (radix ? bb.entries[1].ptr != nullptr : bb.list.ptr != nullptr);
   if (bb.capacity < bb.n_entries || !have) {
     RTGS_TRY(ensure_entry_capacity(bb, bb.n_entries, bb.partial_d.ptr != nullptr, s));
   }

@@ -186,7 +186,7 @@ int ensure_events(rtgs2d_fit* f, size_t need) {
 
 // Projection + synchronous binning (exact entry count; used outside the iteration loop).
 int project_and_bin(rtgs2d_fit* f, cudaStream_t s) {
-  RTGS_TRY(launch_project_raw(f->bb, f->geo, f->raw.as<float>(), f->m, f->n, s));
+  RTGS_TRY(launch_project_raw(f->bb, f->geo, f->raw.as<float>(), f->m, f->n, false, s));
   RTGS_TRY(bin_entries(f->bb, f->geo, f->m, s));
   f->last_entries = f->bb.n_entries;
   f->last_pairs = f->bb.n_pairs;
@@ -252,7 +252,7 @@ int enqueue_chunk(rtgs2d_fit* f, int64_t chunk, cudaStream_t s, cudaEvent_t* ev,
   auto record = [s, capturing](cudaEvent_t e) {
     return capturing ? cudaEventRecordWithFlags(e, s, cudaEventRecordExternal) : cudaEventRecord(e, s);
   };
-  RTGS_TRY(launch_project_raw(bb, f->geo, f->raw.as<float>(), f->m, f->n, s));
+  RTGS_TRY(launch_project_raw(bb, f->geo, f->raw.as<float>(), f->m, f->n, true, s));
   for (int64_t k = 0; k < chunk; ++k) {
     cudaEvent_t* e = ev ? ev + 4 * k : nullptr;
     if (e) RTGS_CUDA(record(e[0]), "event record");

@@ -80,6 +80,7 @@ struct BinBuffers {
   bool presorted = false;                     // radix path (entries + ranges) produced the binning
   bool counts_cleared = false;                // the last binning left tile_count and stats
                                               //   slots 0-1 at zero (the scatter path does)
+  bool entries_emitted = false;               // the last projection emitted the entries
   int64_t capacity = 0;                       // entries the entry buffers can hold
   int64_t n_entries = 0;                      // host-known entry count (synchronous binning)
   int64_t n_pairs = 0;
@@ -96,8 +97,10 @@ struct Geometry {
 Geometry make_geometry(int n_views, int height, int width);
 
 // ---- projection (project.cu) --------------------------------------------------------------------
-// All projection launchers zero bb.stats first and fill records/spans/counts (+weights if asked).
-// Projection launchers also count entries per tile into bb.tile_count (zeroed here).
+// All projection launchers zero bb.stats first and fill records/spans/counts/offsets (+weights
+// if asked), and count entries per tile into bb.tile_count (zeroed here). With `emit`
+// (launch_project_raw) they also write the entries themselves into bb.entries[0], up to the
+// current capacity (see project_tail); otherwise the binning emits them.
 int launch_project_chol(BinBuffers& bb, const Geometry& g, const float* xy, const float* chol,
                         const float* color, const float* weight, int64_t m, int64_t n_per_view,
                         bool want_weights, cudaStream_t s);
@@ -105,7 +108,7 @@ int launch_project_conic(BinBuffers& bb, const Geometry& g, const float* xy, con
                          const float* colors, const float* weights, const int32_t* rects,
                          const int32_t* view_index, int64_t m, bool want_weights, cudaStream_t s);
 int launch_project_raw(BinBuffers& bb, const Geometry& g, const float* raw, int64_t m,
-                       int64_t n_per_view, cudaStream_t s);
+                       int64_t n_per_view, bool emit, cudaStream_t s);
 // Bit-exact support rectangles only: rects (M,4) (x0, x1, y0, y1; x1 = x0 - 1 if empty), counts (M,).
 int launch_support_rects(const float* xy, const float* chol, int64_t m, int height, int width,
                          int32_t* rects, int64_t* counts, cudaStream_t s);

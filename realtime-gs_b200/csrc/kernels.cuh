@@ -18,22 +18,28 @@ struct ProjOut {
   TileSpan* spans;
   int* counts;
   int* offsets;               // entry index of each gaussian's first tile
-  int* tile_count;            // entries per tile (atomic)
+  int* tile_count;            // entries per tile (atomic; emitted entries only)
+  uint64_t* entries;          // null: count every entry; else emit (tile key << 32 | id) at
+  int64_t cap;                //   each entry index below cap and count only those
   unsigned long long* stats;  // kStat* slots
   int tiles_x;
 };
 
-// Call f(gaussian id, local tile index j, tile key) for every tile of every active lane's span.
-// Spans up to kSmallSpan tiles are walked by their own lane, longer ones by the whole warp; all
-// lanes of the warp must call this.
+// Call f(gaussian id, local tile index j, tile key, payload of that gaussian) for every tile of
+// every active lane's span. Spans up to kSmallSpan tiles are walked by their own lane, longer ones
+// by the whole warp (the owner's payload travels with its span); all lanes of the warp must call
+// this.
 template <typename F>
 __device__ __forceinline__ void for_each_span_tile(int64_t gid, int cnt, const TileSpan& sp,
-                                                   int tiles_x, F&& f) {
+                                                   int payload, int tiles_x, F&& f) {
   if (cnt > 0 && cnt <= kSmallSpan) {
+    int tx = sp.tx0, ty = sp.ty0;
     for (int j = 0; j < cnt; ++j) {
-      const int ty = sp.ty0 + j / sp.ntx;
-      const int tx = sp.tx0 + j % sp.ntx;
-      f(gid, j, sp.key_base + ty * tiles_x + tx);
+      f(gid, j, sp.key_base + ty * tiles_x + tx, payload);
+      if (++tx == sp.tx0 + sp.ntx) {
+        tx = sp.tx0;
+        ++ty;
+      }
     }
   }
   const int lane = threadIdx.x & 31;
@@ -46,11 +52,12 @@ __device__ __forceinline__ void for_each_span_tile(int64_t gid, int cnt, const T
     const int ty0 = __shfl_sync(0xffffffffu, sp.ty0, src);
     const int ntx = __shfl_sync(0xffffffffu, sp.ntx, src);
     const int kb = __shfl_sync(0xffffffffu, sp.key_base, src);
+    const int pl = __shfl_sync(0xffffffffu, payload, src);
     const long long g = __shfl_sync(0xffffffffu, static_cast<long long>(gid), src);
     for (int j = lane; j < c; j += 32) {
       const int ty = ty0 + j / ntx;
       const int tx = tx0 + j % ntx;
-      f(g, j, kb + ty * tiles_x + tx);
+      f(g, j, kb + ty * tiles_x + tx, pl);
     }
   }
 }
@@ -94,10 +101,6 @@ __device__ __forceinline__ void project_tail(int64_t i, bool active, float mx, f
     if (o.weights) o.weights[i] = w;
     o.counts[i] = cnt;
   }
-  // Entries per tile for the tile-scatter binning (all lanes reach this point).
-  for_each_span_tile(i, cnt, sp, o.tiles_x, [&](long long, int, int t) {
-    atomicAdd(&o.tile_count[t], 1);  // result unused: a fire-and-forget reduction
-  });
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int incl = cnt;
 #pragma unroll
@@ -127,7 +130,22 @@ __device__ __forceinline__ void project_tail(int64_t i, bool active, float mx, f
                    : 0;
   }
   __syncthreads();
-  if (active) o.offsets[i] = s_base + before + incl - cnt;
+  const int off = s_base + before + incl - cnt;
+  if (active) o.offsets[i] = off;
+  // Tile counts, and with o.entries the entries themselves (all lanes reach this point). Emitted,
+  // only entries that fit the capacity are emitted and counted: the binning stays consistent, and
+  // stats[kStatEntries] (all entries) tells the caller it overflowed.
+  for_each_span_tile(i, cnt, sp, off, o.tiles_x, [&](long long g, int j, int t, int g_off) {
+    if (!o.entries) {
+      atomicAdd(&o.tile_count[t], 1);  // result unused: a fire-and-forget reduction
+      return;
+    }
+    const int64_t e = static_cast<int64_t>(g_off) + j;
+    if (g_off >= 0 && e < o.cap) {
+      atomicAdd(&o.tile_count[t], 1);
+      o.entries[e] = (static_cast<uint64_t>(t) << 32) | static_cast<uint64_t>(g);
+    }
+  });
 }
 
 // Entries at or past the entry capacity were never written (an overflowed binning, whose results

@@ -161,13 +161,13 @@ extern "C" int rtgs2d_forward_noalloc(const float* xy, const float* conics, cons
   const unsigned long long entries = g_host_stats[kStatEntries];
   if (entries > static_cast<unsigned long long>(INT32_MAX)) return too_big(entries * 16);
   const size_t e = static_cast<size_t>(entries > 0 ? entries : 1);
-  // The tile-scatter binning needs the id list; the radix fallback (a tile list longer than the
-  // shared-memory sort) the entry double buffer.
+  // Both binnings need the entries; the tile scatter also the id list, the radix fallback (a
+  // tile list longer than the tile sort) the entry double buffer.
   const bool radix = g_host_stats[kStatLongTile] > 0;
-  const bool fits = radix ? (c.take(bb.entries[0], e * sizeof(uint64_t)) &&
-                             c.take(bb.entries[1], e * sizeof(uint64_t)))
-                          : c.take(bb.list, e * sizeof(uint32_t));
-  if (!fits) return too_big(c.used + (radix ? 16 : 4) * e);
+  const bool fits = c.take(bb.entries[0], e * sizeof(uint64_t)) &&
+                    (radix ? c.take(bb.entries[1], e * sizeof(uint64_t))
+                           : c.take(bb.list, e * sizeof(uint32_t)));
+  if (!fits) return too_big(c.used + (radix ? 16 : 12) * e);
   bb.capacity = static_cast<int64_t>(e);  // binning then fits without growing any buffer
   RTGS_TRY(bin_entries(bb, g, m, s));
   return launch_raster_forward(bb, g, static_cast<float>(cutoff), out, den, s);

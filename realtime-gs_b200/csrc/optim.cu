@@ -230,12 +230,15 @@ int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_
     o.offsets = bb.offsets.as<int>();
     o.stats = bb.stats.as<unsigned long long>();
     o.tile_count = bb.tile_count.as<int>();
+    o.entries = bb.entries[0].as<uint64_t>();
+    o.cap = bb.capacity;
     o.tiles_x = g.tiles_x;
     if (!bb.counts_cleared) {  // the scatter binning leaves both at zero; the radix path does not
       RTGS_TRY(reset_tile_counts(bb, g, s));
       RTGS_CUDA(cudaMemsetAsync(bb.stats.ptr, 0, 2 * sizeof(unsigned long long), s), "memset stats");
     }
     bb.counts_cleared = false;
+    bb.entries_emitted = true;
     adam_fit_kernel<true><<<grid_for(m), kThreads, 0, s>>>(
         m, bb.capacity, bb.counts.as<int>(), bb.offsets.as<int>(), bb.partials.as<float4>(), g.height,
         g.width, raw, m1, m2, table, k, lg, n_per_view, g.tiles_x, g.tiles_per_view, o);

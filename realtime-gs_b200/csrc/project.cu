@@ -157,6 +157,9 @@ int prepare(BinBuffers& bb, const Geometry& g, int64_t m, bool want_weights, cud
   RTGS_TRY(reset_tile_counts(bb, g, s));
   bb.counts_cleared = false;  // the projection is about to count
   o->tile_count = bb.tile_count.as<int>();
+  o->entries = nullptr;  // count only; a launcher that emits sets entries and cap
+  o->cap = 0;
+  bb.entries_emitted = false;
   o->tiles_x = g.tiles_x;
   return 0;
 }
@@ -190,9 +193,14 @@ int launch_project_conic(BinBuffers& bb, const Geometry& g, const float* xy, con
 }
 
 int launch_project_raw(BinBuffers& bb, const Geometry& g, const float* raw, int64_t m,
-                       int64_t n_per_view, cudaStream_t s) {
+                       int64_t n_per_view, bool emit, cudaStream_t s) {
   ProjOut o;
   RTGS_TRY(prepare(bb, g, m, false, s, &o));
+  if (emit && bb.entries[0].ptr) {
+    o.entries = bb.entries[0].as<uint64_t>();
+    o.cap = bb.capacity;
+    bb.entries_emitted = true;
+  }
   if (m == 0) return 0;
   project_raw_kernel<<<grid_for(m), kThreads, 0, s>>>(raw, m, n_per_view, g.height, g.width,
                                                       g.tiles_x, g.tiles_per_view, o);
