@@ -102,6 +102,16 @@ __device__ __forceinline__ float pair_q(float dx, float dy, float i00, float i01
   return __fadd_rn(__fadd_rn(t0, t1), t2);
 }
 
+// Gaussian falloff exp(-q / 2) = 2^(q * (-log2(e) / 2)): one multiply and the hardware base-2
+// exponential (ex2.approx, relative error ~2^-22, flushes denormal results to zero, which only
+// happens for q > 250, far outside the q < 12 support).
+__device__ __forceinline__ float falloff(float q) {
+  constexpr float kNegHalfLog2e = -0.72134752044448170368f;  // -log2(e) / 2
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(q * kNegHalfLog2e));
+  return r;
+}
+
 // ---------------------------------------------------------------------------------------------
 // Raw-parameter transforms of the native fit, fit.py:402-417.
 

@@ -137,7 +137,6 @@ raster_kernel(const RasterArgs a) {
   __shared__ float4 s_geo[kBatch];
   __shared__ float4 s_app[kBatch];
   __shared__ int4 s_rect[kBatch];
-  __shared__ uint32_t s_mask[kBatch];
   __shared__ float s_wt[DEN ? kBatch : 1];
   __shared__ int s_entry[kDoBwd ? kBatch : 1];
   __shared__ int s_piece[kDoBwd ? kBatch : 1];      // rx0 | ry0 << 4 | (pw-1) << 8 | (ph-1) << 12
@@ -166,6 +165,8 @@ raster_kernel(const RasterArgs a) {
     pyc[k] = static_cast<float>(py[k]) + 0.5f;
     inimg[k] = px < a.width && py[k] < a.height;
   }
+  const int sx0 = ox + sbx * L::kSubW, sy0 = oy + sby * L::kSubH;  // this warp's sub-block
+  const int sub_col = lane & 7, sub_row0 = lane >> 3;
   const int64_t view_base = static_cast<int64_t>(view) * a.height * a.width;
   int2 range;
   if (a.presorted) {
@@ -188,17 +189,6 @@ raster_kernel(const RasterArgs a) {
       s_rect[j] = r.rect;
       const int rx0 = r.rect.x - ox, rx1 = rx0 + r.rect.z;
       const int ry0 = r.rect.y - oy, ry1 = ry0 + r.rect.w;
-      uint32_t m = 0;
-#pragma unroll
-      for (int sy = 0; sy < L::kSubY; ++sy) {
-#pragma unroll
-        for (int sx = 0; sx < L::kSubX; ++sx) {
-          const bool hit = rx0 <= sx * L::kSubW + L::kSubW - 1 && rx1 >= sx * L::kSubW &&
-                           ry0 <= sy * L::kSubH + L::kSubH - 1 && ry1 >= sy * L::kSubH;
-          m |= static_cast<uint32_t>(hit) << (sy * L::kSubX + sx);
-        }
-      }
-      s_mask[j] = m;
       if constexpr (DEN) s_wt[j] = a.weights[gid];
       if constexpr (kDoBwd) {
         if (with_entry) {
@@ -228,30 +218,64 @@ raster_kernel(const RasterArgs a) {
       __syncthreads();
       stage(base, n, kDoBwd && single_batch);
       __syncthreads();
+      // 32 records at a time: each lane learns which of them cover each of its pixels (support
+      // rectangle only; the ellipse test stays per pair) from 16 ballots, then walks exactly those,
+      // in list order. Pixels outside the image are in no rectangle.
       for (int c = 0; c < n; c += 32) {
-        const int j = c + lane;
-        unsigned bits = __ballot_sync(0xffffffffu, j < n && ((s_mask[j] >> warp) & 1u));
-        while (bits) {
-          const int jj = c + __ffs(bits) - 1;
-          bits &= bits - 1;
+        unsigned cbits = 0, rbits = 0;  // record c + lane: covered columns / rows of this sub-block
+        if (c + lane < n) {
+          const int4 rc = s_rect[c + lane];
+          const int clo = max(rc.x - sx0, 0), chi = min(rc.x + rc.z - sx0, L::kSubW - 1);
+          const int rlo = max(rc.y - sy0, 0), rhi = min(rc.y + rc.w - sy0, L::kSubH - 1);
+          if (clo <= chi && rlo <= rhi) {
+            cbits = (0xffu >> (L::kSubW - 1 - chi)) & (0xffu << clo);
+            rbits = ((2u << rhi) - 1u) & ~((1u << rlo) - 1u);
+          }
+        }
+        unsigned mcol = 0;
+#pragma unroll
+        for (int b = 0; b < L::kSubW; ++b) {
+          const unsigned v = __ballot_sync(0xffffffffu, (cbits >> b) & 1u);
+          mcol = sub_col == b ? v : mcol;
+        }
+        unsigned mpix[PPT];
+#pragma unroll
+        for (int k = 0; k < PPT; ++k) mpix[k] = 0;
+#pragma unroll
+        for (int b = 0; b < L::kSubH; ++b) {
+          const unsigned v = __ballot_sync(0xffffffffu, (rbits >> b) & 1u);
+#pragma unroll
+          for (int k = 0; k < PPT; ++k) mpix[k] = sub_row0 + 4 * k == b ? v : mpix[k];
+        }
+        unsigned walk = 0;
+#pragma unroll
+        for (int k = 0; k < PPT; ++k) {
+          mpix[k] &= mcol;
+          walk |= mpix[k];
+        }
+        while (walk) {
+          const int jb = __ffs(walk) - 1;
+          walk &= walk - 1;
+          const int jj = c + jb;
           const float4 geo = s_geo[jj];
           const float4 app = s_app[jj];
-          const int4 rc = s_rect[jj];
           const float dx = __fsub_rn(pxc, geo.x);
-          const bool inx = static_cast<unsigned>(px - rc.x) <= static_cast<unsigned>(rc.z);
+          float wt = 0.f;
+          if constexpr (DEN) wt = s_wt[jj];
 #pragma unroll
           for (int k = 0; k < PPT; ++k) {
+            // One flat predicate (rectangle bit and ellipse), no nested branches. The sums are
+            // guarded rather than multiplied by zero, so a non-finite colour outside the support
+            // leaves a pixel untouched.
             const float dy = __fsub_rn(pyc[k], geo.y);
             const float q = pair_q(dx, dy, geo.z, geo.w, app.x);
-            const bool in = inx &&
-                            static_cast<unsigned>(py[k] - rc.y) <= static_cast<unsigned>(rc.w) &&
-                            q < a.cutoff;
+            const bool in = ((mpix[k] >> jb) & 1u) && q < a.cutoff;
             if (in) {
-              const float e = __expf(-0.5f * q);
+              const float e = falloff(q);
               acc[k][0] = fmaf(e, app.y, acc[k][0]);
               acc[k][1] = fmaf(e, app.z, acc[k][1]);
               acc[k][2] = fmaf(e, app.w, acc[k][2]);
-              if constexpr (DEN) accd[k] = fmaf(e, s_wt[jj], accd[k]);
+              if constexpr (DEN) accd[k] = fmaf(e, wt, accd[k]);
             }
           }
         }
@@ -422,7 +446,7 @@ raster_kernel(const RasterArgs a) {
             const float q = pair_q(dx, dy, geo.z, geo.w, app.x);
             if (q < a.cutoff) {
               const float4 gv = s_g[sidx0 + yy * kTile + xx];
-              const float e = __expf(-0.5f * q);
+              const float e = falloff(q);
               float v = gv.x * app.y;
               v = fmaf(gv.y, app.z, v);
               v = fmaf(gv.z, app.w, v);
