@@ -427,43 +427,62 @@ raster_kernel(const RasterArgs a) {
         const int pw = ((pc >> 8) & 15) + 1, ph = ((pc >> 12) & 15) + 1;
         const int area = valid ? pw * ph : 0;
         const int max_steps = static_cast<int>(__reduce_max_sync(0xffffffffu, static_cast<unsigned>((area + 7) >> 3)));
-        const float inv_pw = 1.0f / static_cast<float>(pw);
         const float pxc0 = static_cast<float>(ox + rx0) + 0.5f;  // integer + 0.5 sums stay exact
         const float pyc0 = static_cast<float>(oy + ry0) + 0.5f;
-        const int sidx0 = ry0 * kTile + rx0;
         float wt = 0.f;
         if constexpr (DEN) wt = s_wt[j];
+        // Lane r8 visits piece pixels k = r8, r8 + 8, ... (row-major, width pw): start at
+        // (r8 % pw, r8 / pw), then advance by (8 % pw, 8 / pw) with one carry per step. The pixel
+        // centres are carried as floats (integers + 0.5, exact), so dx and dy round exactly as
+        // the reference's.
+        const int adv_y = pw > 8 ? 0 : 8 / pw;
+        const int adv_x = 8 - adv_y * pw;
+        int yy = r8 / pw;
+        int xx = r8 - yy * pw;
+        float fx = pxc0 + static_cast<float>(xx);
+        float fy = pyc0 + static_cast<float>(yy);
+        int sidx = (ry0 + yy) * kTile + rx0 + xx;
+        const float fadv_x = static_cast<float>(adv_x), fadv_y = static_cast<float>(adv_y);
+        const float fpw = static_cast<float>(pw);
         float S[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         float Sd = 0.f;
+        int k = r8;
+#pragma unroll 2
         for (int st = 0; st < max_steps; ++st) {
-          const int k = r8 + 8 * st;
-          if (k < area) {
-            // k / pw exactly: (k + 0.5) / pw stays >= 0.5 / pw away from every integer for k < 256.
-            const int yy = __float2int_rz((static_cast<float>(k) + 0.5f) * inv_pw);
-            const int xx = k - yy * pw;
-            const float dx = __fsub_rn(pxc0 + static_cast<float>(xx), geo.x);
-            const float dy = __fsub_rn(pyc0 + static_cast<float>(yy), geo.y);
-            const float q = pair_q(dx, dy, geo.z, geo.w, app.x);
-            if (q < a.cutoff) {
-              const float4 gv = s_g[sidx0 + yy * kTile + xx];
-              const float e = falloff(q);
-              float v = gv.x * app.y;
-              v = fmaf(gv.y, app.z, v);
-              v = fmaf(gv.z, app.w, v);
-              if constexpr (DEN) v = fmaf(gv.w, wt, v);
-              const float dq = e * v;
-              const float ex = dq * dx;
-              const float fy = dq * dy;
-              S[0] += ex;
-              S[1] += fy;
-              S[2] = fmaf(ex, dx, S[2]);
-              S[3] = fmaf(ex, dy, S[3]);
-              S[4] = fmaf(fy, dy, S[4]);
-              S[5] = fmaf(e, gv.x, S[5]);
-              S[6] = fmaf(e, gv.y, S[6]);
-              S[7] = fmaf(e, gv.z, S[7]);
-              if constexpr (DEN) Sd = fmaf(e, gv.w, Sd);
-            }
+          const float dx = __fsub_rn(fx, geo.x);
+          const float dy = __fsub_rn(fy, geo.y);
+          const float dxdx = __fmul_rn(dx, dx), dxdy = __fmul_rn(dx, dy), dydy = __fmul_rn(dy, dy);
+          // pair_q with the products shared: ((dx^2 i00 + dx dy 2 i01) + dy^2 i11)
+          const float q = __fadd_rn(__fadd_rn(__fmul_rn(dxdx, geo.z), __fmul_rn(dxdy, geo.w)),
+                                    __fmul_rn(dydy, app.x));
+          if (k < area && q < a.cutoff) {
+            const float4 gv = s_g[sidx];
+            const float e = falloff(q);
+            float v = gv.x * app.y;
+            v = fmaf(gv.y, app.z, v);
+            v = fmaf(gv.z, app.w, v);
+            if constexpr (DEN) v = fmaf(gv.w, wt, v);
+            const float dq = e * v;
+            S[0] = fmaf(dq, dx, S[0]);
+            S[1] = fmaf(dq, dy, S[1]);
+            S[2] = fmaf(dq, dxdx, S[2]);
+            S[3] = fmaf(dq, dxdy, S[3]);
+            S[4] = fmaf(dq, dydy, S[4]);
+            S[5] = fmaf(e, gv.x, S[5]);
+            S[6] = fmaf(e, gv.y, S[6]);
+            S[7] = fmaf(e, gv.z, S[7]);
+            if constexpr (DEN) Sd = fmaf(e, gv.w, Sd);
+          }
+          k += 8;
+          xx += adv_x;
+          fx += fadv_x;
+          fy += fadv_y;
+          sidx += adv_y * kTile + adv_x;
+          if (xx >= pw) {
+            xx -= pw;
+            fx -= fpw;
+            fy += 1.f;
+            sidx += kTile - pw;
           }
         }
         const float red = octet_transpose_reduce8(S, lane);
