@@ -19,7 +19,7 @@ import torch
 from rtgs_b200 import _native
 from rtgs_b200.core.gaussians2d import Gaussians2D
 from rtgs_b200.core.metrics import masked_psnr, psnr
-from rtgs_b200.image2gs.engine import FitEngine, pack_mask_bits, psnr_values
+from rtgs_b200.image2gs.engine import acquire_engine, pack_mask_bits, psnr_values, release_engine
 from rtgs_b200.image2gs.fit import (
     FitConfig,
     _history_from_engine,
@@ -84,11 +84,12 @@ def fit_stacked(
     raw = raw_from_gaussians(xy0, chol0, color0, weight0, height, width)
     _validate_raw_parameters(raw)
     loss_mode = _native.LOSS_MSE if masks is None else _native.LOSS_MASK_ONLY
-    engine = FitEngine(
+    engine = acquire_engine(
         n_views, xy0.shape[1], height, width, lr=config.lr, iterations=config.iterations,
         log_every=config.log_every, freeze_geometry=config.freeze_geometry, loss_mode=loss_mode,
         device=targets.device,
     )
+    ok = False
     try:
         mask_bits = None if masks is None else pack_mask_bits(masks)
         engine.set_targets(targets, mask_bits)
@@ -101,8 +102,9 @@ def fit_stacked(
         histories = _history_from_engine(engine, config, counts)
         xy, chol, color, weight = engine.params()
         final, _ = engine.evaluate(want_render=True)
+        ok = True
     finally:
-        engine.close()
+        release_engine(engine, reusable=ok)
     for b in range(n_views):
         pred = final[b].clamp(0, 1)
         if masks is None:

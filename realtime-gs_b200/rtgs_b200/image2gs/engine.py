@@ -5,8 +5,10 @@ The whole iteration loop runs in C++/CUDA; Python only moves tensors in and out.
 
 from __future__ import annotations
 
+import collections
 import ctypes
 import math
+import threading
 
 import numpy as np
 import torch
@@ -218,3 +220,67 @@ def psnr_values(sums: np.ndarray, counts: np.ndarray) -> list[float]:
         mse = max(float(s) / float(c), 1e-12) if c > 0 else 1e-12
         out.append(-10.0 * math.log10(mse))
     return out
+
+
+# ---------------------------------------------------------------------------------------------
+# Engine pool. Creating an engine allocates its device buffers and its first run captures the
+# CUDA graphs of its chunks; destroying it frees them (cudaFree synchronises the device). Fits that
+# repeat one configuration -- the common case when many images are fitted with one FitConfig --
+# take an idle engine of that configuration instead, keeping buffers and graphs. A pooled engine
+# is reset by set_targets / set_raw, so results do not depend on its history.
+
+_POOL_LOCK = threading.Lock()
+_POOL: "collections.OrderedDict[tuple, list[FitEngine]]" = collections.OrderedDict()
+_POOL_MAX_IDLE = 4  # idle engines kept per process, least recently released closed first
+
+
+def acquire_engine(n_views: int, n: int, height: int, width: int, *, lr: float, iterations: int,
+                   log_every: int, check_every: int = 0, freeze_geometry: bool = False,
+                   loss_mode: int = _native.LOSS_MSE, device: torch.device | None = None) -> FitEngine:
+    """An idle pooled engine of exactly this configuration, else a new one."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    if dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    key = (dev.index, int(n_views), int(n), int(height), int(width), float(lr), int(iterations),
+           int(log_every), int(check_every), bool(freeze_geometry), int(loss_mode))
+    with _POOL_LOCK:
+        idle = _POOL.get(key)
+        if idle:
+            engine = idle.pop()
+            if not idle:
+                del _POOL[key]
+            return engine
+    engine = FitEngine(n_views, n, height, width, lr=lr, iterations=iterations, log_every=log_every,
+                       check_every=check_every, freeze_geometry=freeze_geometry, loss_mode=loss_mode,
+                       device=dev)
+    engine._pool_key = key
+    return engine
+
+
+def release_engine(engine: FitEngine, reusable: bool = True) -> None:
+    """Return an engine from acquire_engine; `reusable=False` (after an error) destroys it."""
+    key = getattr(engine, "_pool_key", None)
+    if not reusable or key is None or not getattr(engine, "_h", None):
+        engine.close()
+        return
+    evicted = []
+    with _POOL_LOCK:
+        _POOL.setdefault(key, []).append(engine)
+        _POOL.move_to_end(key)
+        while sum(len(v) for v in _POOL.values()) > _POOL_MAX_IDLE:
+            old_key, old = next(iter(_POOL.items()))
+            evicted.append(old.pop(0))
+            if not old:
+                del _POOL[old_key]
+    for e in evicted:
+        e.close()
+
+
+def clear_engine_pool() -> None:
+    """Destroy every idle pooled engine (frees their device memory)."""
+    with _POOL_LOCK:
+        engines = [e for v in _POOL.values() for e in v]
+        _POOL.clear()
+    for e in engines:
+        e.close()
+

@@ -24,7 +24,7 @@ import torch
 from rtgs_b200 import _native
 from rtgs_b200.core.gaussians2d import Gaussians2D
 from rtgs_b200.core.metrics import masked_psnr, psnr
-from rtgs_b200.image2gs.engine import FitEngine, pack_mask_bits, psnr_values
+from rtgs_b200.image2gs.engine import FitEngine, acquire_engine, pack_mask_bits, psnr_values, release_engine
 
 _MIN_DIAG = 0.3
 _CURRENT_APPEARANCE = "weight_color_9p"
@@ -252,11 +252,12 @@ def _fit_native_from_initialization(
     loss_mode = _native.LOSS_MSE if mask is None else _native.LOSS_MASK_WEIGHTED
     patience = int(config.convergence_patience)
     check_every = int(config.convergence_check_every) if patience else 0
-    engine = FitEngine(
+    engine = acquire_engine(
         1, g0.n, h, w, lr=config.lr, iterations=config.iterations, log_every=config.log_every,
         check_every=check_every, freeze_geometry=config.freeze_geometry, loss_mode=loss_mode,
         device=image.device,
     )
+    ok = False
     try:
         mask_bits = None if mask is None else pack_mask_bits(mask[None])
         engine.set_targets(target[None], mask_bits)
@@ -289,8 +290,9 @@ def _fit_native_from_initialization(
             history["stopped_iter"] = stopped
         xy, chol, color, weight = (t[0] for t in engine.params())
         final, _ = engine.evaluate(want_render=True)
+        ok = True
     finally:
-        engine.close()
+        release_engine(engine, reusable=ok)
     result = Gaussians2D(xy=xy, chol=chol, color=color, weight=weight)
     pred = final[0].clamp(0, 1)
     history["final_psnr_full"] = psnr(pred, target)

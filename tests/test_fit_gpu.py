@@ -253,3 +253,30 @@ def test_graph_replay_matches_eager_chunks_bitwise():
         for a, b in zip(p_e, other_p):
             assert torch.equal(a, b)
         assert np.array_equal(h_e[0], other_h[0]) and np.array_equal(h_e[1], other_h[1])
+
+
+def test_pooled_engine_reuse_is_stateless():
+    """Fits that repeat a configuration reuse a pooled engine (buffers and captured graphs); a fit
+    run on a reused engine, after a fit of another image, ends bitwise where a fresh engine ends."""
+    from rtgs_b200.image2gs import engine as eng_mod
+
+    h, w, n = 64, 96, 300
+    cfg = FitConfig(n_gaussians=n, iterations=150, log_every=50)
+    images, inits = [], []
+    for seed in (21, 22):
+        src = synthetic.source_gaussians(seed, 30, h, w, (2.0, 8.0))
+        images.append(orender.render(src.xy, src.chol, src.color, src.weight, h, w).clamp(0, 1).to(DEV))
+        i0 = synthetic.fit_init(seed, n, h, w)
+        inits.append(Gaussians2D(*(x.to(DEV) for x in (i0.xy, i0.chol, i0.color, i0.weight))))
+    eng_mod.clear_engine_pool()
+    fresh, fresh_h = fit_image_from_initialization(images[0], inits[0], cfg)
+    assert sum(len(v) for v in eng_mod._POOL.values()) == 1
+    pooled_engine = next(iter(eng_mod._POOL.values()))[0]
+    fit_image_from_initialization(images[1], inits[1], cfg)
+    again, again_h = fit_image_from_initialization(images[0], inits[0], cfg)
+    assert next(iter(eng_mod._POOL.values()))[0] is pooled_engine  # the same engine served all three
+    for a, b in ((fresh.xy, again.xy), (fresh.chol, again.chol), (fresh.color, again.color), (fresh.weight, again.weight)):
+        assert torch.equal(a, b)
+    assert fresh_h["psnr"] == again_h["psnr"] and fresh_h["final_psnr"] == again_h["final_psnr"]
+    eng_mod.clear_engine_pool()
+    assert not eng_mod._POOL
