@@ -115,18 +115,21 @@ __device__ __forceinline__ float falloff(float q) {
 // ---------------------------------------------------------------------------------------------
 // Raw-parameter transforms of the native fit, fit.py:402-417.
 
-__device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+// The transforms only shape parameters and gradients (never the bit-exact support tests), so they
+// use the hardware exponential (__expf, ~2 ulp) and fast division (__fdividef, ~2 ulp; 0 for a
+// denominator above 2^126, where the exact quotient is below 2^-126 anyway): they sit on the
+// latency-bound Adam kernel's critical path.
+__device__ __forceinline__ float sigmoid_f(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 // torch.nn.functional.softplus with beta = 1, threshold = 20.
-__device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+__device__ __forceinline__ float softplus_f(float x) { return x > 20.0f ? x : log1pf(__expf(x)); }
 
 // d softplus / dx (torch softplus_backward: z / (z + 1), z = exp(x); 1 above the threshold).
 __device__ __forceinline__ float softplus_grad_f(float x) {
   if (x > 20.0f) return 1.0f;
-  const float z = expf(x);
-  return z / (z + 1.0f);
+  const float z = __expf(x);
+  return __fdividef(z, z + 1.0f);
 }
-
 // Planar raw-parameter slots (each slot is an array of M floats).
 enum RawSlot : int {
   kXr = 0, kYr = 1, kD0 = 2, kD1 = 3, kOff = 4, kCr = 5, kCg = 6, kCb = 7, kWr = 8, kRawSlots = 9

@@ -9,8 +9,9 @@ constexpr int kSmallEntries = 32;  // gaussians with more entries are summed by 
 
 constexpr int kSmallSpan = 16;  // tile spans above this are walked by the whole warp
 
-// Threads per block of every kernel that calls project_tail (its block scan assumes it).
-constexpr int kProjThreads = 256;
+// Threads per block of every kernel that calls project_tail (its block scan assumes it). 128
+// spreads the per-gaussian kernels over the SMs in more, smaller blocks (they are latency bound).
+constexpr int kProjThreads = 128;
 
 struct ProjOut {
   GaussRecord* records;
@@ -272,8 +273,9 @@ __device__ __forceinline__ void adam_update(float& p, float& m1, float& m2, floa
 
 // Loss numerators of one view: the per-tile (squared error, clamped squared error) pairs summed
 // in a fixed order (strided per-thread sums, then a tree), so every caller gets the same bits.
-// Called by all kLossThreads threads of a block.
-constexpr int kLossThreads = 256;
+// Called by all kLossThreads threads of a block (the per-gaussian kernels' block size, so that the
+// Adam kernel's logging and the evaluation kernel reduce in the same order).
+constexpr int kLossThreads = kProjThreads;
 
 __device__ __forceinline__ void reduce_view_loss(const double* __restrict__ tile_loss,
                                                  int tiles_per_view, int view, double* dst) {

@@ -502,7 +502,7 @@ raster_kernel(const RasterArgs a) {
 }
 
 // Deterministic per-view reduction of tile loss numerators: one block per view.
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kLossThreads)
 loss_reduce_kernel(const double* __restrict__ tile_loss, int tiles_per_view, double* dst) {
   reduce_view_loss(tile_loss, tiles_per_view, blockIdx.x, dst);
 }
