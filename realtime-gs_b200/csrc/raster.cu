@@ -31,7 +31,7 @@ namespace rtgs2d {
 namespace {
 
 constexpr int kBatch = 128;
-constexpr int kMaxSteps = kTile * kTile / 8;  // octet steps of a full-tile piece
+constexpr int kBuckets = 2 * kTile;  // backward work-list buckets: (orientation, steps)
 
 template <int PPT>
 struct Layout {
@@ -127,6 +127,82 @@ __device__ __forceinline__ bool mask_bit(const uint8_t* bits, int64_t idx) {
   return (bits[idx >> 3] >> (idx & 7)) & 1;
 }
 
+// Backward piece = a gaussian's support rectangle clipped to the tile, packed as
+// rx0 | ry0 << 4 | (pw - 1) << 8 | (ph - 1) << 12. Its bucket orders the backward's work list:
+// row-wise pieces (pw >= ph) first, then column-wise ones, each by descending step count (the
+// other side), so the 4 pieces of a warp task share an orientation and a step count.
+__device__ __forceinline__ int piece_bucket(int pc) {
+  const int pw = ((pc >> 8) & 15) + 1, ph = ((pc >> 12) & 15) + 1;
+  return pw >= ph ? kTile - ph : 2 * kTile - pw;
+}
+
+// One octet lane's part of a backward piece: up to two pixels per step along the lane axis
+// (a = r8 and r8 + 8), max_steps steps along the other axis (rows when ROW, columns otherwise).
+// The fixed coordinate's terms are computed once; q keeps the reference's rounding order
+// ((dx^2 i00 + dx dy 2 i01) + dy^2 i11), and pixel centres are exact (integers + 0.5).
+// Moments: S0 = sum dq dx, S1 = sum dq dy, S2 = sum dq dx^2, S3 = sum dq dx dy, S4 = sum dq dy^2,
+// S5..S7 = sum e g_rgb, Sd = sum e g_den, with e = exp(-q/2) and dq = e (g . w c).
+template <bool ROW, bool DEN>
+__device__ __forceinline__ void backward_piece(const float4& geo, const float4& app, float wt,
+                                               float pxc0, float pyc0, int sidx0, int r8,
+                                               int lim_a, int lim_b, bool any_b, int max_steps,
+                                               float cutoff, const float4* s_g, float (&S)[8],
+                                               float& Sd) {
+  // Lane-axis (fixed) coordinate of pixels A and B, and its squared term.
+  const float fix_a = (ROW ? pxc0 : pyc0) + static_cast<float>(r8);
+  const float fix_b = fix_a + 8.f;
+  const float da = __fsub_rn(fix_a, ROW ? geo.x : geo.y);
+  const float db = __fsub_rn(fix_b, ROW ? geo.x : geo.y);
+  const float sq_a = __fmul_rn(da, da), sq_b = __fmul_rn(db, db);
+  const float coef_fix = ROW ? geo.z : app.x;  // i00 for x, i11 for y
+  const float coef_var = ROW ? app.x : geo.z;
+  const float t_a = __fmul_rn(sq_a, coef_fix), t_b = __fmul_rn(sq_b, coef_fix);
+  constexpr int kStep = ROW ? kTile : 1;        // shared-memory stride of one step
+  constexpr int kLaneStride = ROW ? 1 : kTile;  // and of one lane-axis pixel
+  int sidx_a = sidx0 + r8 * kLaneStride;
+  float fvar = ROW ? pyc0 : pxc0;
+  auto accumulate = [&](int sidx, float d_fix, float sq_fix, float cross, float d_var, float sq_var,
+                        float q) {
+    const float4 gv = s_g[sidx];
+    const float e = falloff(q);
+    float v = gv.x * app.y;
+    v = fmaf(gv.y, app.z, v);
+    v = fmaf(gv.z, app.w, v);
+    if constexpr (DEN) v = fmaf(gv.w, wt, v);
+    const float dq = e * v;
+    const float dx = ROW ? d_fix : d_var, dy = ROW ? d_var : d_fix;
+    const float dxdx = ROW ? sq_fix : sq_var, dydy = ROW ? sq_var : sq_fix;
+    S[0] = fmaf(dq, dx, S[0]);
+    S[1] = fmaf(dq, dy, S[1]);
+    S[2] = fmaf(dq, dxdx, S[2]);
+    S[3] = fmaf(dq, cross, S[3]);
+    S[4] = fmaf(dq, dydy, S[4]);
+    S[5] = fmaf(e, gv.x, S[5]);
+    S[6] = fmaf(e, gv.y, S[6]);
+    S[7] = fmaf(e, gv.z, S[7]);
+    if constexpr (DEN) Sd = fmaf(e, gv.w, Sd);
+  };
+  for (int st = 0; st < max_steps; ++st) {
+    const float dv = __fsub_rn(fvar, ROW ? geo.y : geo.x);
+    const float sq_v = __fmul_rn(dv, dv);
+    const float t_v = __fmul_rn(sq_v, coef_var);
+    {
+      const float cross = __fmul_rn(da, dv);  // dx dy (multiplication commutes exactly)
+      const float t1 = __fmul_rn(cross, geo.w);
+      const float q = ROW ? __fadd_rn(__fadd_rn(t_a, t1), t_v) : __fadd_rn(__fadd_rn(t_v, t1), t_a);
+      if (st < lim_a && q < cutoff) accumulate(sidx_a, da, sq_a, cross, dv, sq_v, q);
+    }
+    if (any_b) {
+      const float cross = __fmul_rn(db, dv);
+      const float t1 = __fmul_rn(cross, geo.w);
+      const float q = ROW ? __fadd_rn(__fadd_rn(t_b, t1), t_v) : __fadd_rn(__fadd_rn(t_v, t1), t_b);
+      if (st < lim_b && q < cutoff) accumulate(sidx_a + 8 * kLaneStride, db, sq_b, cross, dv, sq_v, q);
+    }
+    fvar += 1.f;
+    sidx_a += kStep;
+  }
+}
+
 template <int PPT, int MODE, bool DEN>
 __global__ void __launch_bounds__(Layout<PPT>::kThreads)
 raster_kernel(const RasterArgs a) {
@@ -142,7 +218,9 @@ raster_kernel(const RasterArgs a) {
   __shared__ int s_piece[kDoBwd ? kBatch : 1];      // rx0 | ry0 << 4 | (pw-1) << 8 | (ph-1) << 12
   __shared__ float4 s_g[kDoBwd ? kTile * kTile : 1];  // upstream gradient (r, g, b, density) per pixel
   __shared__ int s_list[kDoBwd ? kBatch : 1];   // batch records sorted by octet steps, descending
-  __shared__ int s_bucket[kMaxSteps + 1];
+  __shared__ int s_wcount[kDoBwd ? L::kWarps : 1][kBuckets];  // per-warp bucket counts, then starts
+  static_assert(kBatch == L::kThreads, "the backward work list assigns one piece per thread");
+  static_assert(kBuckets == 32, "warp 0 scans one bucket per lane");
   __shared__ int s_next;
   __shared__ double s_loss[L::kWarps][2];
 
@@ -383,32 +461,39 @@ raster_kernel(const RasterArgs a) {
       const int n = min(kBatch, range.y - base);
       __syncthreads();
       if (!single_batch || !kDoFwd) stage(base, n, true);
-      for (int i = threadIdx.x; i <= kMaxSteps; i += L::kThreads) s_bucket[i] = 0;
+      // Work list: the batch's pieces ordered by bucket, stably (by index inside a bucket), so
+      // the 4 pieces of every task -- and the orientation each is traversed in -- depend only on
+      // the input. One piece per thread (kBatch == block size); ranks from match_any within a warp,
+      // per-warp bucket counts for the order across warps.
+      const int jb = threadIdx.x;
+      const int bucket = jb < n ? piece_bucket(s_piece[jb]) : kBuckets;
+      for (int i = threadIdx.x; i < L::kWarps * kBuckets; i += L::kThreads) (&s_wcount[0][0])[i] = 0;
       if (threadIdx.x == 0) s_next = 0;
       __syncthreads();
-      for (int j = threadIdx.x; j < n; j += L::kThreads) {
-        const int pc = s_piece[j];
-        const int area = (((pc >> 8) & 15) + 1) * (((pc >> 12) & 15) + 1);
-        atomicAdd(&s_bucket[(area + 7) >> 3], 1);
-      }
+      const unsigned peers = __match_any_sync(0xffffffffu, bucket);
+      const int rank = __popc(peers & ((1u << lane) - 1u));
+      if (bucket < kBuckets && rank == 0) s_wcount[warp][bucket] = __popc(peers);
       __syncthreads();
-      if (warp == 0) {  // list cursors, most steps first: lane l owns step count kMaxSteps - l
-        const int steps = kMaxSteps - lane;
-        const int c = s_bucket[steps];
-        int x = c;
+      if (warp == 0) {  // lane l owns bucket l: start of each (warp, bucket) run
+        int total = 0;
+#pragma unroll
+        for (int w = 0; w < L::kWarps; ++w) total += s_wcount[w][lane];
+        int x = total;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
           const int y = __shfl_up_sync(0xffffffffu, x, o);
           if (lane >= o) x += y;
         }
-        s_bucket[steps] = x - c;
+        int run = x - total;
+#pragma unroll
+        for (int w = 0; w < L::kWarps; ++w) {
+          const int c = s_wcount[w][lane];
+          s_wcount[w][lane] = run;
+          run += c;
+        }
       }
       __syncthreads();
-      for (int j = threadIdx.x; j < n; j += L::kThreads) {
-        const int pc = s_piece[j];
-        const int area = (((pc >> 8) & 15) + 1) * (((pc >> 12) & 15) + 1);
-        s_list[atomicAdd(&s_bucket[(area + 7) >> 3], 1)] = j;
-      }
+      if (bucket < kBuckets) s_list[s_wcount[warp][bucket] + rank] = jb;
       __syncthreads();
 
       const int n_tasks = (n + 3) >> 2;
@@ -425,65 +510,29 @@ raster_kernel(const RasterArgs a) {
         const int pc = s_piece[j];
         const int rx0 = pc & 15, ry0 = (pc >> 4) & 15;
         const int pw = ((pc >> 8) & 15) + 1, ph = ((pc >> 12) & 15) + 1;
-        const int area = valid ? pw * ph : 0;
-        const int max_steps = static_cast<int>(__reduce_max_sync(0xffffffffu, static_cast<unsigned>((area + 7) >> 3)));
+        // The task runs in the orientation of its first piece (the bucket order groups pieces of
+        // one orientation): row-wise, each octet lane owns columns r8 and r8 + 8 of its piece and
+        // steps down the rows; column-wise, rows r8 and r8 + 8, stepping across the columns. Any
+        // piece is correct in either orientation.
+        const bool row = __shfl_sync(0xffffffffu, pw >= ph, 0);
+        const int lane_dim = row ? pw : ph, step_dim = row ? ph : pw;
+        const int my_steps = valid ? step_dim : 0;
+        const int max_steps = static_cast<int>(__reduce_max_sync(0xffffffffu, static_cast<unsigned>(my_steps)));
+        const int lim_a = r8 < lane_dim ? my_steps : 0;      // steps of lane pixel A (axis r8)
+        const int lim_b = r8 + 8 < lane_dim ? my_steps : 0;  // and of pixel B (axis r8 + 8)
+        const bool any_b = __any_sync(0xffffffffu, lim_b > 0);
         const float pxc0 = static_cast<float>(ox + rx0) + 0.5f;  // integer + 0.5 sums stay exact
         const float pyc0 = static_cast<float>(oy + ry0) + 0.5f;
         float wt = 0.f;
         if constexpr (DEN) wt = s_wt[j];
-        // Lane r8 visits piece pixels k = r8, r8 + 8, ... (row-major, width pw): start at
-        // (r8 % pw, r8 / pw), then advance by (8 % pw, 8 / pw) with one carry per step. The pixel
-        // centres are carried as floats (integers + 0.5, exact), so dx and dy round exactly as
-        // the reference's.
-        const int adv_y = pw > 8 ? 0 : 8 / pw;
-        const int adv_x = 8 - adv_y * pw;
-        int yy = r8 / pw;
-        int xx = r8 - yy * pw;
-        float fx = pxc0 + static_cast<float>(xx);
-        float fy = pyc0 + static_cast<float>(yy);
-        int sidx = (ry0 + yy) * kTile + rx0 + xx;
-        const float fadv_x = static_cast<float>(adv_x), fadv_y = static_cast<float>(adv_y);
-        const float fpw = static_cast<float>(pw);
         float S[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         float Sd = 0.f;
-        int k = r8;
-#pragma unroll 2
-        for (int st = 0; st < max_steps; ++st) {
-          const float dx = __fsub_rn(fx, geo.x);
-          const float dy = __fsub_rn(fy, geo.y);
-          const float dxdx = __fmul_rn(dx, dx), dxdy = __fmul_rn(dx, dy), dydy = __fmul_rn(dy, dy);
-          // pair_q with the products shared: ((dx^2 i00 + dx dy 2 i01) + dy^2 i11)
-          const float q = __fadd_rn(__fadd_rn(__fmul_rn(dxdx, geo.z), __fmul_rn(dxdy, geo.w)),
-                                    __fmul_rn(dydy, app.x));
-          if (k < area && q < a.cutoff) {
-            const float4 gv = s_g[sidx];
-            const float e = falloff(q);
-            float v = gv.x * app.y;
-            v = fmaf(gv.y, app.z, v);
-            v = fmaf(gv.z, app.w, v);
-            if constexpr (DEN) v = fmaf(gv.w, wt, v);
-            const float dq = e * v;
-            S[0] = fmaf(dq, dx, S[0]);
-            S[1] = fmaf(dq, dy, S[1]);
-            S[2] = fmaf(dq, dxdx, S[2]);
-            S[3] = fmaf(dq, dxdy, S[3]);
-            S[4] = fmaf(dq, dydy, S[4]);
-            S[5] = fmaf(e, gv.x, S[5]);
-            S[6] = fmaf(e, gv.y, S[6]);
-            S[7] = fmaf(e, gv.z, S[7]);
-            if constexpr (DEN) Sd = fmaf(e, gv.w, Sd);
-          }
-          k += 8;
-          xx += adv_x;
-          fx += fadv_x;
-          fy += fadv_y;
-          sidx += adv_y * kTile + adv_x;
-          if (xx >= pw) {
-            xx -= pw;
-            fx -= fpw;
-            fy += 1.f;
-            sidx += kTile - pw;
-          }
+        if (row) {
+          backward_piece<true, DEN>(geo, app, wt, pxc0, pyc0, ry0 * kTile + rx0, r8, lim_a, lim_b,
+                                    any_b, max_steps, a.cutoff, s_g, S, Sd);
+        } else {
+          backward_piece<false, DEN>(geo, app, wt, pxc0, pyc0, ry0 * kTile + rx0, r8, lim_a, lim_b,
+                                     any_b, max_steps, a.cutoff, s_g, S, Sd);
         }
         const float red = octet_transpose_reduce8(S, lane);
         const int64_t e = s_entry[j];
