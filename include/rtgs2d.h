@@ -209,6 +209,18 @@ RTGS2D_API int rtgs2d_fit_capacity(const rtgs2d_fit* fit, int64_t* entries, int6
  * `stream` around projection + binning, the fused raster kernel and the Adam kernel; the
  * accumulated device milliseconds are returned by rtgs2d_fit_stage_times (after a run). */
 RTGS2D_API int rtgs2d_fit_set_profiling(rtgs2d_fit* fit, int32_t enable);
+/* Pool rows (image2gs/pool.py:55-151: GaussianPool2D's active mask, park, activate and the
+ * per-row Adam moment reset). rtgs2d_fit_set_active copies a device mask of M = n_views * n
+ * bytes (0 = parked: the row is not rendered, so it has no contribution and no gradient; with
+ * zero Adam moments it then stays unchanged); NULL makes every row live. rtgs2d_fit_write_rows
+ * writes raw parameters (the layouts of rtgs2d_fit_set_raw, n_rows rows each; all five NULL keeps
+ * the values) into the rows listed in the device array `rows` (indices into M; others skipped)
+ * and zeroes both Adam moments of those rows. Both are ordered on `stream`. */
+RTGS2D_API int rtgs2d_fit_set_active(rtgs2d_fit* fit, const uint8_t* active, void* stream);
+RTGS2D_API int rtgs2d_fit_write_rows(rtgs2d_fit* fit, const int64_t* rows, int64_t n_rows,
+                                     const float* xy_raw, const float* diag_raw,
+                                     const float* off_raw, const float* color_raw,
+                                     const float* weight_raw, void* stream);
 /* No reference counterpart: CUDA-graph replay of the fit loop. A run proceeds in chunks of 64
  * iterations with no host synchronisation inside a chunk; once a chunk of a given shape (length,
  * binning path, buffer layout) has run eagerly, later chunks of that shape are captured into a

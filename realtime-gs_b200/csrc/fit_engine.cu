@@ -41,6 +41,8 @@ struct rtgs2d_fit {
   DevBuf tile_loss;    // (n_tiles, 2) double
   DevBuf log;          // (max_logs, B, 2) double
   DevBuf eval_sums;    // (B, 2) double
+  DevBuf active;       // (M,) uint8: 0 = parked row (rtgs2d_fit_set_active); unused until set
+  bool use_active = false;
   int64_t max_logs = 0;
   std::vector<int64_t> log_iters;
   int64_t step = 0;
@@ -184,9 +186,43 @@ int ensure_events(rtgs2d_fit* f, size_t need) {
   return 0;
 }
 
+const uint8_t* active_rows(const rtgs2d_fit* f) {
+  return f->use_active ? f->active.as<uint8_t>() : nullptr;
+}
+
+// Rows `rows[0..n)` of the planar raw parameters: write the given values (reference layouts, like
+// rtgs2d_fit_set_raw; all null = keep the values) and zero both Adam moments. Indices outside
+// [0, m) are skipped.
+__global__ void write_rows_kernel(int64_t m, const int64_t* __restrict__ rows, int64_t n,
+                                  const float* __restrict__ xy, const float* __restrict__ diag,
+                                  const float* __restrict__ off, const float* __restrict__ color,
+                                  const float* __restrict__ weight, float* __restrict__ raw,
+                                  float* __restrict__ m1, float* __restrict__ m2) {
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  if (r >= n) return;
+  const int64_t i = rows[r];
+  if (i < 0 || i >= m) return;
+  if (xy) {
+    raw[kXr * m + i] = xy[2 * r];
+    raw[kYr * m + i] = xy[2 * r + 1];
+    raw[kD0 * m + i] = diag[2 * r];
+    raw[kD1 * m + i] = diag[2 * r + 1];
+    raw[kOff * m + i] = off[r];
+    raw[kCr * m + i] = color[3 * r];
+    raw[kCg * m + i] = color[3 * r + 1];
+    raw[kCb * m + i] = color[3 * r + 2];
+    raw[kWr * m + i] = weight[r];
+  }
+#pragma unroll
+  for (int k = 0; k < kRawSlots; ++k) {
+    m1[k * m + i] = 0.f;
+    m2[k * m + i] = 0.f;
+  }
+}
+
 // Projection + synchronous binning (exact entry count; used outside the iteration loop).
 int project_and_bin(rtgs2d_fit* f, cudaStream_t s) {
-  RTGS_TRY(launch_project_raw(f->bb, f->geo, f->raw.as<float>(), f->m, f->n, false, s));
+  RTGS_TRY(launch_project_raw(f->bb, f->geo, f->raw.as<float>(), f->m, f->n, false, active_rows(f), s));
   RTGS_TRY(bin_entries(f->bb, f->geo, f->m, s));
   f->last_entries = f->bb.n_entries;
   f->last_pairs = f->bb.n_pairs;
@@ -227,12 +263,12 @@ FitRasterArgs raster_args(rtgs2d_fit* f) {
 std::vector<uintptr_t> chunk_key(const rtgs2d_fit* f, int64_t chunk) {
   const BinBuffers& bb = f->bb;
   std::vector<uintptr_t> k = {static_cast<uintptr_t>(chunk), static_cast<uintptr_t>(f->use_radix),
-                              static_cast<uintptr_t>(bb.capacity)};
+                              static_cast<uintptr_t>(bb.capacity), static_cast<uintptr_t>(f->use_active)};
   for (const DevBuf* b : {&bb.records, &bb.weights, &bb.spans, &bb.counts, &bb.offsets, &bb.list,
                           &bb.tile_count, &bb.tile_end, &bb.entries[0], &bb.entries[1], &bb.ranges,
                           &bb.partials, &bb.partial_d, &bb.cub_temp, &bb.sort_counts, &bb.stats,
                           &f->raw, &f->m1, &f->m2, &f->targets, &f->mask, &f->view_scale,
-                          &f->tile_loss, &f->log, &f->iter_table}) {
+                          &f->tile_loss, &f->log, &f->iter_table, &f->active}) {
     k.push_back(reinterpret_cast<uintptr_t>(b->ptr));
     k.push_back(static_cast<uintptr_t>(b->bytes));
   }
@@ -252,7 +288,7 @@ int enqueue_chunk(rtgs2d_fit* f, int64_t chunk, cudaStream_t s, cudaEvent_t* ev,
   auto record = [s, capturing](cudaEvent_t e) {
     return capturing ? cudaEventRecordWithFlags(e, s, cudaEventRecordExternal) : cudaEventRecord(e, s);
   };
-  RTGS_TRY(launch_project_raw(bb, f->geo, f->raw.as<float>(), f->m, f->n, true, s));
+  RTGS_TRY(launch_project_raw(bb, f->geo, f->raw.as<float>(), f->m, f->n, true, active_rows(f), s));
   for (int64_t k = 0; k < chunk; ++k) {
     cudaEvent_t* e = ev ? ev + 4 * k : nullptr;
     if (e) RTGS_CUDA(record(e[0]), "event record");
@@ -262,7 +298,7 @@ int enqueue_chunk(rtgs2d_fit* f, int64_t chunk, cudaStream_t s, cudaEvent_t* ev,
     if (e) RTGS_CUDA(record(e[2]), "event record");
     RTGS_TRY(launch_adam_fit(bb, f->geo, f->m, f->n, f->raw.as<float>(), f->m1.as<float>(),
                              f->m2.as<float>(), f->iter_table.as<IterScalars>(),
-                             static_cast<int>(k), lg, k + 1 < chunk, s));
+                             static_cast<int>(k), lg, k + 1 < chunk, active_rows(f), s));
     if (e) RTGS_CUDA(record(e[3]), "event record");
   }
   return 0;
@@ -404,6 +440,7 @@ int rtgs2d_fit_destroy(rtgs2d_fit* fit) {
   fit->tile_loss.release();
   fit->log.release();
   fit->eval_sums.release();
+  fit->active.release();
   fit->snap.release();
   fit->iter_table.release();
   fit->release_events();
@@ -618,6 +655,40 @@ int rtgs2d_fit_set_profiling(rtgs2d_fit* f, int32_t enable) {
   f->bin_ms = f->raster_ms = f->adam_ms = f->pairs_timed = 0.0;
   f->iterations_timed = 0;
   return RTGS2D_OK;
+}
+
+int rtgs2d_fit_set_active(rtgs2d_fit* f, const uint8_t* active, void* stream) {
+  RTGS_TRY(check_fit(f));
+  if (!active) {
+    f->use_active = false;
+    return RTGS2D_OK;
+  }
+  cudaStream_t s = as_stream(stream);
+  RTGS_TRY(f->active.ensure(static_cast<size_t>(f->m > 0 ? f->m : 1), s));
+  if (f->m > 0) {
+    RTGS_CUDA(cudaMemcpyAsync(f->active.ptr, active, static_cast<size_t>(f->m), cudaMemcpyDeviceToDevice, s),
+              "copy active rows");
+  }
+  f->use_active = true;
+  return RTGS2D_OK;
+}
+
+int rtgs2d_fit_write_rows(rtgs2d_fit* f, const int64_t* rows, int64_t n_rows, const float* xy_raw,
+                          const float* diag_raw, const float* off_raw, const float* color_raw,
+                          const float* weight_raw, void* stream) {
+  RTGS_TRY(check_fit(f));
+  if (n_rows < 0) return set_error(RTGS2D_ERR_INVALID, "n_rows must be >= 0");
+  if (n_rows == 0 || f->m == 0) return RTGS2D_OK;
+  if (!rows) return set_error(RTGS2D_ERR_INVALID, "rows is NULL");
+  const int given = (xy_raw != nullptr) + (diag_raw != nullptr) + (off_raw != nullptr) +
+                    (color_raw != nullptr) + (weight_raw != nullptr);
+  if (given != 0 && given != 5) {
+    return set_error(RTGS2D_ERR_INVALID, "give all five raw parameter arrays or none");
+  }
+  write_rows_kernel<<<grid_for(n_rows), kThreads, 0, as_stream(stream)>>>(
+      f->m, rows, n_rows, xy_raw, diag_raw, off_raw, color_raw, weight_raw, f->raw.as<float>(),
+      f->m1.as<float>(), f->m2.as<float>());
+  return check_cuda(cudaGetLastError(), "write_rows_kernel");
 }
 
 int rtgs2d_fit_set_graphs(rtgs2d_fit* f, int32_t enable) {

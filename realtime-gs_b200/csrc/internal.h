@@ -100,7 +100,8 @@ Geometry make_geometry(int n_views, int height, int width);
 // All projection launchers zero bb.stats first and fill records/spans/counts/offsets (+weights
 // if asked), and count entries per tile into bb.tile_count (zeroed here). With `emit`
 // (launch_project_raw) they also write the entries themselves into bb.entries[0], up to the
-// current capacity (see project_tail); otherwise the binning emits them.
+// current capacity (see project_tail); otherwise the binning emits them. `active` (nullable, one
+// byte per gaussian): rows with 0 are parked -- no entries, so no contribution and no gradient.
 int launch_project_chol(BinBuffers& bb, const Geometry& g, const float* xy, const float* chol,
                         const float* color, const float* weight, int64_t m, int64_t n_per_view,
                         bool want_weights, cudaStream_t s);
@@ -108,7 +109,7 @@ int launch_project_conic(BinBuffers& bb, const Geometry& g, const float* xy, con
                          const float* colors, const float* weights, const int32_t* rects,
                          const int32_t* view_index, int64_t m, bool want_weights, cudaStream_t s);
 int launch_project_raw(BinBuffers& bb, const Geometry& g, const float* raw, int64_t m,
-                       int64_t n_per_view, bool emit, cudaStream_t s);
+                       int64_t n_per_view, bool emit, const uint8_t* active, cudaStream_t s);
 // Bit-exact support rectangles only: rects (M,4) (x0, x1, y0, y1; x1 = x0 - 1 if empty), counts (M,).
 int launch_support_rects(const float* xy, const float* chol, int64_t m, int height, int width,
                          int32_t* rects, int64_t* counts, cudaStream_t s);
@@ -195,6 +196,6 @@ struct LossLog {
 // stats) for the next iteration's binning.
 int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_view, float* raw,
                     float* m1, float* m2, const IterScalars* table, int k, const LossLog& lg,
-                    bool project_next, cudaStream_t s);
+                    bool project_next, const uint8_t* active, cudaStream_t s);
 
 }  // namespace rtgs2d

@@ -22,6 +22,7 @@ struct ProjOut {
   int* tile_count;            // entries per tile (atomic; emitted entries only)
   uint64_t* entries;          // null: count every entry; else emit (tile key << 32 | id) at
   int64_t cap;                //   each entry index below cap and count only those
+  const uint8_t* active;      // null: every gaussian is live; else 0 = parked (not rendered)
   unsigned long long* stats;  // kStat* slots
   int tiles_x;
 };
@@ -82,7 +83,7 @@ __device__ __forceinline__ void project_tail(int64_t i, bool active, float mx, f
   long long pairs = 0;
   TileSpan sp{0, 0, 1, 0};
   if (active) {
-    if (pixels > 0 && isfinite(mx) && isfinite(my)) {
+    if (pixels > 0 && isfinite(mx) && isfinite(my) && (!o.active || o.active[i])) {
       const int tx0 = x0 / kTile, tx1 = x1 / kTile;
       const int ty0 = y0 / kTile, ty1 = y1 / kTile;
       const int ntx = tx1 - tx0 + 1;

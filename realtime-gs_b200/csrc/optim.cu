@@ -218,7 +218,7 @@ int launch_finalize_conic(const BinBuffers& bb, int64_t m, const float* conics,
 
 int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_view, float* raw,
                     float* m1, float* m2, const IterScalars* table, int k, const LossLog& lg,
-                    bool project_next, cudaStream_t s) {
+                    bool project_next, const uint8_t* active, cudaStream_t s) {
   if (m == 0) return 0;
   ProjOut o{};
   if (project_next) {
@@ -232,6 +232,7 @@ int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_
     o.tile_count = bb.tile_count.as<int>();
     o.entries = bb.entries[0].as<uint64_t>();
     o.cap = bb.capacity;
+    o.active = active;
     o.tiles_x = g.tiles_x;
     if (!bb.counts_cleared) {  // the scatter binning leaves both at zero; the radix path does not
       RTGS_TRY(reset_tile_counts(bb, g, s));

@@ -159,6 +159,7 @@ int prepare(BinBuffers& bb, const Geometry& g, int64_t m, bool want_weights, cud
   o->tile_count = bb.tile_count.as<int>();
   o->entries = nullptr;  // count only; a launcher that emits sets entries and cap
   o->cap = 0;
+  o->active = nullptr;
   bb.entries_emitted = false;
   o->tiles_x = g.tiles_x;
   return 0;
@@ -193,9 +194,10 @@ int launch_project_conic(BinBuffers& bb, const Geometry& g, const float* xy, con
 }
 
 int launch_project_raw(BinBuffers& bb, const Geometry& g, const float* raw, int64_t m,
-                       int64_t n_per_view, bool emit, cudaStream_t s) {
+                       int64_t n_per_view, bool emit, const uint8_t* active, cudaStream_t s) {
   ProjOut o;
   RTGS_TRY(prepare(bb, g, m, false, s, &o));
+  o.active = active;
   if (emit && bb.entries[0].ptr) {
     o.entries = bb.entries[0].as<uint64_t>();
     o.cap = bb.capacity;

@@ -187,6 +187,37 @@ class FitEngine:
         """Record CUDA events around binning, the raster kernel and Adam in every iteration."""
         _native.check(self._lib.rtgs2d_fit_set_profiling(self._h, int(bool(enable))))
 
+    def set_active(self, active: torch.Tensor | None) -> None:
+        """(n_views, n) bool/uint8 CUDA mask of live rows (parked rows are not rendered); None = all."""
+        with torch.cuda.device(self.device):
+            if active is None:
+                _native.check(self._lib.rtgs2d_fit_set_active(self._h, None, self._stream()))
+                return
+            if active.shape != (self.n_views, self.n) or active.device != self.device:
+                raise ValueError("active mask must be a (n_views, n) tensor on the engine's device")
+            a = active.to(torch.uint8).contiguous()
+            # `a` is freed on return; the caching allocator reuses it only after the copy queued on
+            # the same stream.
+            _native.check(self._lib.rtgs2d_fit_set_active(self._h, a.data_ptr(), self._stream()))
+
+    def write_rows(self, rows: torch.Tensor, raw: dict[str, torch.Tensor] | None = None) -> None:
+        """Write raw parameters into flat rows (indices into n_views * n) and zero their Adam
+        moments; raw = None zeroes the moments only."""
+        rows = rows.to(self.device, torch.int64).contiguous()
+        n_rows = rows.numel()
+        if n_rows == 0:
+            return
+        ptrs = [None] * 5
+        keep = []
+        if raw is not None:
+            shapes = {"xy_raw": 2, "diag_raw": 2, "off_raw": 1, "color_raw": 3, "weight_raw": 1}
+            for k, name in enumerate(("xy_raw", "diag_raw", "off_raw", "color_raw", "weight_raw")):
+                t = raw[name].to(self.device, torch.float32).reshape(n_rows, shapes[name]).contiguous()
+                keep.append(t)
+                ptrs[k] = t.data_ptr()
+        with torch.cuda.device(self.device):
+            _native.check(self._lib.rtgs2d_fit_write_rows(self._h, rows.data_ptr(), n_rows, *ptrs, self._stream()))
+
     def set_graphs(self, enable: bool = True) -> None:
         """Replay repeated 64-iteration chunks from a captured CUDA graph (default on)."""
         _native.check(self._lib.rtgs2d_fit_set_graphs(self._h, int(bool(enable))))

@@ -190,8 +190,18 @@ def _validate_fit_controls(config: FitConfig, diagnostic_callback=None, diagnost
         raise ValueError("init_strategy='structure_tensor' is not implemented by rtgs_b200")
     if config.appearance_parameterization != _CURRENT_APPEARANCE:
         raise ValueError("only the weight_color_9p appearance parameterization is implemented")
-    if config.pool:
-        raise ValueError("pool fitting is not implemented by rtgs_b200")
+    if config.pool:  # fit.py:600-616
+        if config.freeze_geometry:
+            raise ValueError("pool fitting is incompatible with freeze_geometry")
+        if diagnostic_callback is not None or tuple(diagnostic_steps):
+            raise ValueError("pool fitting does not support native fit diagnostics")
+        if config.pool_capacity is not None and config.pool_capacity < config.n_gaussians:
+            raise ValueError("pool_capacity must be at least n_gaussians")
+        if config.pool_min_live < 1:
+            raise ValueError("pool_min_live must be at least 1")
+        for name in ("pool_triage_every", "pool_prune_count", "pool_spawn_count"):
+            if getattr(config, name) < 0:
+                raise ValueError(f"{name} must be non-negative")
     if config.mask_coverage_weight > 0.0:
         raise ValueError("mask_coverage_weight is not implemented by rtgs_b200")
     if diagnostic_callback is not None or tuple(diagnostic_steps):
@@ -328,6 +338,10 @@ def fit_image(
     if seed is not None:
         gen = torch.Generator(device=image.device).manual_seed(seed)
     g0 = init_gaussians_2d(target, config.n_gaussians, config.grad_init_mix, gen)
+    if config.pool:
+        from rtgs_b200.image2gs.pool import fit_pooled_from_initialization
+
+        return fit_pooled_from_initialization(image, target, g0, config, mask, xy_offset)
     return _fit_native_from_initialization(image, target, g0, config, mask, xy_offset)
 
 
@@ -351,6 +365,10 @@ def fit_image_from_initialization(
     if mask is not None:
         target = image * mask.to(image).clamp(0, 1)[..., None]
     g0 = initial_gaussians.to(image.device)
+    if config.pool:
+        from rtgs_b200.image2gs.pool import fit_pooled_from_initialization
+
+        return fit_pooled_from_initialization(image, target, g0, config, mask, xy_offset)
     return _fit_native_from_initialization(image, target, g0, config, mask, xy_offset)
 
 

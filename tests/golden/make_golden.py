@@ -163,5 +163,36 @@ def main(ref_src: str) -> None:
     _save("single", image=render_gaussians_2d(single, 17, 17))
 
 
+def pool_fixture(ref_src: str) -> None:
+    """8. Pooled fit with triage (pool.py:210-291) from a fixed initialisation of the scene image."""
+    sys.path.insert(0, ref_src)
+    from rtgs.data.synthetic import make_synthetic_scene
+    from rtgs.image2gs.fit import FitConfig, init_gaussians_2d
+    from rtgs.image2gs.pool import fit_pooled_from_initialization
+
+    torch.manual_seed(0)
+    scene = make_synthetic_scene(n_gaussians=25, n_cameras=8, image_size=32, seed=0)
+    image = scene.images[0]
+    g_init = init_gaussians_2d(image, 40, 0.7, torch.Generator().manual_seed(3))
+    cfg = FitConfig(n_gaussians=40, iterations=60, log_every=10, pool=True, pool_capacity=64,
+                    pool_triage_every=15, pool_prune_count=3, pool_spawn_count=6)
+    fitted, hist = fit_pooled_from_initialization(image, image, g_init, cfg, None, image.new_zeros(2))
+    _save("fit_pool", image=image, init_xy=g_init.xy, init_chol=g_init.chol,
+          init_color=g_init.color, init_weight=g_init.weight,
+          iterations=cfg.iterations, log_every=cfg.log_every, lr=cfg.lr, capacity=cfg.pool_capacity,
+          triage_every=cfg.pool_triage_every, prune=cfg.pool_prune_count, spawn=cfg.pool_spawn_count,
+          out_xy=fitted.xy, out_chol=fitted.chol, out_color=fitted.color, out_weight=fitted.weight,
+          psnr_iters=np.array([i for i, _ in hist["psnr"]]),
+          psnr_vals=np.array([v for _, v in hist["psnr"]]),
+          final_psnr=hist["final_psnr"], live_count=hist["live_count"])
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src")
+    # make_golden.py [REF_SRC] [--only pool]
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    ref = args[0] if args and args[0] != "pool" else "/root/reference/src"
+    if "--only" in sys.argv:
+        pool_fixture(ref)
+    else:
+        main(ref)
+        pool_fixture(ref)

@@ -73,8 +73,12 @@ def test_fit_rejects_cpu_images_and_unsupported_modes():
     img = torch.rand(16, 16, 3)
     with pytest.raises(RuntimeError, match="CUDA tensors"):
         fit_image(img, FitConfig(n_gaussians=8, iterations=2), seed=0)
-    for bad in (dict(backend="structsplat"), dict(pool=True), dict(init_strategy="structure_tensor"),
-                dict(mask_coverage_weight=0.5), dict(native_renderer="bogus")):
+    for bad in (dict(backend="structsplat"), dict(init_strategy="structure_tensor"),
+                dict(mask_coverage_weight=0.5), dict(native_renderer="bogus"),
+                # the reference's pool validation (fit.py:600-616)
+                dict(pool=True, freeze_geometry=True), dict(pool=True, pool_capacity=4),
+                dict(pool=True, pool_min_live=0), dict(pool=True, pool_triage_every=-1),
+                dict(pool=True, pool_prune_count=-1), dict(pool=True, pool_spawn_count=-1)):
         with pytest.raises(ValueError):
             fit_image(img, replace(FitConfig(n_gaussians=8, iterations=2), **bad), seed=0)
 
@@ -131,3 +135,23 @@ def test_synthetic_workloads_are_deterministic_and_in_range():
     sc = synthetic.splat_scene(0, n=20_000, height=216, width=384)
     sig = torch.linalg.eigvalsh(chol_covariance(sc.chol.double())).sqrt()
     assert float(sig.min()) >= 0.34 and float(sig.max()) <= 64.5
+
+
+def test_pool_row_store_without_rendering():
+    """The reference's pool tests that need no renderer (tests/test_image2gs_pool.py)."""
+    from rtgs_b200.image2gs.pool import GaussianPool2D
+
+    g0 = Gaussians2D(xy=torch.rand(4, 2) * 20, chol=torch.tensor([[2.0, 0.0, 2.0]]).repeat(4, 1),
+                     color=torch.rand(4, 3), weight=torch.full((4,), 0.5))
+    with pytest.raises(ValueError, match="capacity"):
+        GaussianPool2D(g0, torch.tensor([24.0, 24.0]), 2)
+    pool = GaussianPool2D(g0, torch.tensor([24.0, 24.0]), 6)
+    optimizer = torch.optim.Adam(pool.params(), lr=1e-2)
+    ids = [id(p) for p in pool.params()]
+    assert pool.live_count == 4 and pool.free_rows().tolist() == [4, 5]
+    pool.park(torch.tensor([0]), optimizer)
+    assert pool.live_count == 3 and pool.free_rows().tolist() == [0, 4, 5]
+    pool.activate(pool.free_rows()[:1], Gaussians2D(g0.xy[:1], g0.chol[:1], g0.color[:1], g0.weight[:1]), optimizer)
+    assert pool.live_count == 4 and pool.free_rows().tolist() == [4, 5]
+    assert [id(p) for p in pool.params()] == ids
+    assert FitConfig().pool is False
