@@ -32,7 +32,7 @@ extern "C" {
 #define RTGS2D_API
 #endif
 
-#define RTGS2D_ABI_VERSION 1
+#define RTGS2D_ABI_VERSION 2
 
 #define RTGS2D_OK 0
 #define RTGS2D_ERR_INVALID (-1)  /* bad argument (shape, size, null pointer, wrong device) */
@@ -169,6 +169,9 @@ typedef struct rtgs2d_fit_options {
   int64_t check_every;     /* also record at (it + 1) % check_every == 0 (0: never) */
   int32_t freeze_geometry; /* nonzero: only color/weight are optimised (FitConfig.freeze_geometry) */
   int32_t loss_mode;       /* RTGS2D_LOSS_* */
+  double mask_coverage_weight; /* > 0: add weight * mean(coverage * (1 - mask)) to the loss, coverage
+                                  = 1 - exp(-sum weight_i G_i) (fit.py:457-459,566-572); needs a
+                                  mask loss mode */
 } rtgs2d_fit_options;
 
 RTGS2D_API int rtgs2d_fit_create(int64_t n_views, int64_t n, int64_t height, int64_t width,

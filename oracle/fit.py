@@ -9,6 +9,7 @@ Restated reference behaviour (paths relative to the reference project):
   - loop: zero_grad, build, render, MSE, backward, step, sched, PSNR log   fit.py:451-540
   - final render and PSNR                    src/rtgs/image2gs/fit.py:542-554
   - stacked multi-view loop, loss = sum_b mean_b   src/rtgs/image2gs/batched.py:79-170
+  - serial masked loss + mask coverage penalty  src/rtgs/image2gs/fit.py:457-459,557-572
   - psnr                                     src/rtgs/core/metrics.py:12-15
 The renderer is ``oracle.render2d`` (the reference's pure-PyTorch scatter renderer, restated).
 A mask-restricted loss (mean over mask pixels x 3 channels, the denominator of
@@ -125,6 +126,46 @@ def fit_views(
             hist[b]["final_psnr_full"] = full
             hist[b]["final_psnr"] = full if masks is None else masked_psnr(pred, targets[b], masks[b])
     return (xy, chol, color, weight), hist
+
+
+def fit_serial(target, init, iterations, lr=1e-2, log_every=50, mask=None, coverage_weight=0.0):
+    """The serial native fit loop (fit.py:451-554) of one (H, W, 3) target, with the serial loss
+    (fit.py:557-563: MSE, or (0.1 + 0.9 mask)-weighted MSE with a mask) and the optional mask
+    coverage penalty weight * mean(coverage * (1 - mask)), coverage = 1 - exp(-density)
+    (fit.py:457-459, 566-572; renderer2d.py:128-140). Returns ((xy, chol, color, weight), history).
+    """
+    height, width = target.shape[:2]
+    raw = to_raw(*init, height, width)
+    for value in raw.values():
+        value.requires_grad_(True)
+    opt = torch.optim.Adam(list(raw.values()), lr=lr)
+    sched = torch.optim.lr_scheduler.CosineAnnealingLR(opt, T_max=iterations, eta_min=lr * 0.1)
+    hist = {"psnr": [], "stopped_iter": iterations - 1}
+    for it in range(iterations):
+        opt.zero_grad()
+        xy, chol, color, weight = build(raw, height, width)
+        rendered, density = render2d.render_batched(xy[None], chol[None], color[None], weight[None],
+                                                    height, width, with_density=True)
+        rendered, density = rendered[0], density[0]
+        if mask is None:
+            loss = torch.nn.functional.mse_loss(rendered, target)
+        else:
+            wts = 0.1 + 0.9 * mask.to(rendered).clamp(0, 1)
+            loss = (((rendered - target) ** 2) * wts[..., None]).mean()
+            if coverage_weight > 0.0:
+                coverage = 1.0 - torch.exp(-density)
+                loss = loss + coverage_weight * (coverage * (1.0 - mask.to(coverage).clamp(0, 1))).mean()
+        loss.backward()
+        opt.step()
+        sched.step()
+        if it % log_every == 0 or it == iterations - 1:
+            with torch.no_grad():
+                hist["psnr"].append((it, psnr(rendered.clamp(0, 1), target)))
+    with torch.no_grad():
+        params = build(raw, height, width)
+        final = render2d.render(*params, height, width)
+    hist["final_psnr"] = psnr(final.clamp(0, 1), target)
+    return tuple(p.detach() for p in params), hist
 
 
 def adam_first_step(raw: torch.Tensor, grad: torch.Tensor, lr: float) -> torch.Tensor:

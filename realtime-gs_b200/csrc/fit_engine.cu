@@ -186,6 +186,8 @@ int ensure_events(rtgs2d_fit* f, size_t need) {
   return 0;
 }
 
+bool coverage(const rtgs2d_fit* f) { return f->opt.mask_coverage_weight > 0.0; }
+
 const uint8_t* active_rows(const rtgs2d_fit* f) {
   return f->use_active ? f->active.as<uint8_t>() : nullptr;
 }
@@ -222,7 +224,8 @@ __global__ void write_rows_kernel(int64_t m, const int64_t* __restrict__ rows, i
 
 // Projection + synchronous binning (exact entry count; used outside the iteration loop).
 int project_and_bin(rtgs2d_fit* f, cudaStream_t s) {
-  RTGS_TRY(launch_project_raw(f->bb, f->geo, f->raw.as<float>(), f->m, f->n, false, active_rows(f), s));
+  RTGS_TRY(launch_project_raw(f->bb, f->geo, f->raw.as<float>(), f->m, f->n, false, active_rows(f),
+                              coverage(f), s));
   RTGS_TRY(bin_entries(f->bb, f->geo, f->m, s));
   f->last_entries = f->bb.n_entries;
   f->last_pairs = f->bb.n_pairs;
@@ -254,6 +257,9 @@ FitRasterArgs raster_args(rtgs2d_fit* f) {
   fa.loss_mode = f->opt.loss_mode;
   fa.tile_loss = f->tile_loss.as<double>();
   fa.render_out = nullptr;
+  // mean over the H x W pixels of coverage * (1 - mask), times the weight (fit.py:566-572)
+  fa.coverage_coef = static_cast<float>(f->opt.mask_coverage_weight /
+                                        (static_cast<double>(f->height) * f->width));
   return fa;
 }
 
@@ -288,7 +294,8 @@ int enqueue_chunk(rtgs2d_fit* f, int64_t chunk, cudaStream_t s, cudaEvent_t* ev,
   auto record = [s, capturing](cudaEvent_t e) {
     return capturing ? cudaEventRecordWithFlags(e, s, cudaEventRecordExternal) : cudaEventRecord(e, s);
   };
-  RTGS_TRY(launch_project_raw(bb, f->geo, f->raw.as<float>(), f->m, f->n, true, active_rows(f), s));
+  RTGS_TRY(launch_project_raw(bb, f->geo, f->raw.as<float>(), f->m, f->n, true, active_rows(f),
+                              coverage(f), s));
   for (int64_t k = 0; k < chunk; ++k) {
     cudaEvent_t* e = ev ? ev + 4 * k : nullptr;
     if (e) RTGS_CUDA(record(e[0]), "event record");
@@ -298,7 +305,8 @@ int enqueue_chunk(rtgs2d_fit* f, int64_t chunk, cudaStream_t s, cudaEvent_t* ev,
     if (e) RTGS_CUDA(record(e[2]), "event record");
     RTGS_TRY(launch_adam_fit(bb, f->geo, f->m, f->n, f->raw.as<float>(), f->m1.as<float>(),
                              f->m2.as<float>(), f->iter_table.as<IterScalars>(),
-                             static_cast<int>(k), lg, k + 1 < chunk, active_rows(f), s));
+                             static_cast<int>(k), lg, k + 1 < chunk, active_rows(f), coverage(f),
+                             s));
     if (e) RTGS_CUDA(record(e[3]), "event record");
   }
   return 0;
@@ -385,6 +393,12 @@ int rtgs2d_fit_create(int64_t n_views, int64_t n, int64_t height, int64_t width,
   }
   if (options->loss_mode < RTGS2D_LOSS_MSE || options->loss_mode > RTGS2D_LOSS_MASK_ONLY) {
     return set_error(RTGS2D_ERR_INVALID, "unknown loss_mode");
+  }
+  if (!(options->mask_coverage_weight >= 0.0)) {
+    return set_error(RTGS2D_ERR_INVALID, "mask_coverage_weight must be non-negative");
+  }
+  if (options->mask_coverage_weight > 0.0 && options->loss_mode == RTGS2D_LOSS_MSE) {
+    return set_error(RTGS2D_ERR_INVALID, "mask_coverage_weight requires a mask");
   }
   rtgs2d_fit* f = new (std::nothrow) rtgs2d_fit();
   if (!f) return set_error(RTGS2D_ERR_ALLOC, "host allocation failed");
@@ -548,7 +562,7 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
   // Initial capacity: the current entry count with headroom (gaussians grow and shrink).
   if (bb.capacity == 0) {
     RTGS_TRY(project_and_bin(f, s));
-    RTGS_TRY(ensure_entry_capacity(bb, f->last_entries + f->last_entries / 2 + 4096, false, s));
+    RTGS_TRY(ensure_entry_capacity(bb, f->last_entries + f->last_entries / 2 + 4096, coverage(f), s));
   }
   int64_t remaining = t_max - f->step < n_iterations ? t_max - f->step : n_iterations;
   while (remaining > 0) {
@@ -608,7 +622,7 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
       f->retries += 1;
       if (long_tile) f->use_radix = true;  // a tile list too long for the tile sort
       if (max_entries > bb.capacity) {
-        RTGS_TRY(ensure_entry_capacity(bb, max_entries + max_entries / 2 + 4096, false, s));
+        RTGS_TRY(ensure_entry_capacity(bb, max_entries + max_entries / 2 + 4096, coverage(f), s));
       }
       continue;
     }
@@ -639,7 +653,7 @@ int rtgs2d_fit_reserve(rtgs2d_fit* f, int64_t entries, void* stream) {
   RTGS_TRY(check_fit(f));
   if (entries < 0 || entries > INT32_MAX) return set_error(RTGS2D_ERR_CAPACITY, "entries out of range");
   if (entries <= f->bb.capacity) return RTGS2D_OK;
-  return ensure_entry_capacity(f->bb, entries, false, as_stream(stream));
+  return ensure_entry_capacity(f->bb, entries, coverage(f), as_stream(stream));
 }
 
 int rtgs2d_fit_capacity(const rtgs2d_fit* f, int64_t* entries, int64_t* retries) {

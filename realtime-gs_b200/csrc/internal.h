@@ -109,7 +109,8 @@ int launch_project_conic(BinBuffers& bb, const Geometry& g, const float* xy, con
                          const float* colors, const float* weights, const int32_t* rects,
                          const int32_t* view_index, int64_t m, bool want_weights, cudaStream_t s);
 int launch_project_raw(BinBuffers& bb, const Geometry& g, const float* raw, int64_t m,
-                       int64_t n_per_view, bool emit, const uint8_t* active, cudaStream_t s);
+                       int64_t n_per_view, bool emit, const uint8_t* active, bool want_weights,
+                       cudaStream_t s);
 // Bit-exact support rectangles only: rects (M,4) (x0, x1, y0, y1; x1 = x0 - 1 if empty), counts (M,).
 int launch_support_rects(const float* xy, const float* chol, int64_t m, int height, int width,
                          int32_t* rects, int64_t* counts, cudaStream_t s);
@@ -153,6 +154,7 @@ struct FitRasterArgs {
   int loss_mode = kLossMse;
   double* tile_loss = nullptr;        // (n_tiles, 2): loss numerator, clamped PSNR numerator
   float* render_out = nullptr;        // optional (B, H, W, 3)
+  float coverage_coef = 0.f;          // > 0: mask coverage penalty weight / (H * W) (density pass)
 };
 
 int launch_raster_forward(const BinBuffers& bb, const Geometry& g, float cutoff, float* out,
@@ -196,6 +198,6 @@ struct LossLog {
 // stats) for the next iteration's binning.
 int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_view, float* raw,
                     float* m1, float* m2, const IterScalars* table, int k, const LossLog& lg,
-                    bool project_next, const uint8_t* active, cudaStream_t s);
+                    bool project_next, const uint8_t* active, bool density, cudaStream_t s);
 
 }  // namespace rtgs2d

@@ -91,10 +91,11 @@ finalize_conic_kernel(int64_t m, int64_t cap, const int* __restrict__ counts, co
 // parameters are projected for the next iteration in the same pass (the projection of
 // project_raw_kernel), which saves a launch and a re-read of the raw parameters per iteration.
 // `counts` is read (previous binning) before the projection rewrites it, by the same thread.
-template <bool PROJECT>
+template <bool PROJECT, bool DEN>
 __global__ void __launch_bounds__(kThreads)
 adam_fit_kernel(int64_t m, int64_t cap, int* counts, const int* __restrict__ offsets,
-                const float4* __restrict__ partials, int height, int width, float* __restrict__ raw,
+                const float4* __restrict__ partials, const float* __restrict__ partial_d,
+                int height, int width, float* __restrict__ raw,
                 float* __restrict__ m1, float* __restrict__ m2,
                 const IterScalars* __restrict__ table, int k_iter, LossLog lg, int64_t n_per_view,
                 int tiles_x, int tiles_per_view, ProjOut o) {
@@ -120,7 +121,7 @@ adam_fit_kernel(int64_t m, int64_t cap, int* counts, const int* __restrict__ off
   int cnt = active ? counts[i] : 0;
   const int off = cnt > 0 ? offsets[i] : 0;
   cnt = clamp_to_capacity(cnt, off, cap);
-  const Moments mo = gather_moments<false>(partials, nullptr, cnt, off);
+  const Moments mo = gather_moments<DEN>(partials, partial_d, cnt, off);
 
   if (active) {
     const float sx = sigmoid_f(r[kXr]), sy = sigmoid_f(r[kYr]);
@@ -141,7 +142,9 @@ adam_fit_kernel(int64_t m, int64_t cap, int* counts, const int* __restrict__ off
     grad[kCr] = w * mo.s[5] * (1.0f - cr) * cr;
     grad[kCg] = w * mo.s[6] * (1.0f - cg) * cg;
     grad[kCb] = w * mo.s[7] * (1.0f - cb) * cb;
-    grad[kWr] = fmaf(cr, mo.s[5], fmaf(cg, mo.s[6], cb * mo.s[7])) * (1.0f - w) * w;
+    // dL/dweight = sum_k color_k S_k (+ the density moment of the mask coverage penalty)
+    grad[kWr] = (fmaf(cr, mo.s[5], fmaf(cg, mo.s[6], cb * mo.s[7])) + (DEN ? mo.sd : 0.f)) *
+                (1.0f - w) * w;
 
     const int first = a.freeze_geometry ? kCr : 0;
 #pragma unroll
@@ -218,13 +221,14 @@ int launch_finalize_conic(const BinBuffers& bb, int64_t m, const float* conics,
 
 int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_view, float* raw,
                     float* m1, float* m2, const IterScalars* table, int k, const LossLog& lg,
-                    bool project_next, const uint8_t* active, cudaStream_t s) {
+                    bool project_next, const uint8_t* active, bool density, cudaStream_t s) {
   if (m == 0) return 0;
   ProjOut o{};
+  const float* pd = density ? bb.partial_d.as<float>() : nullptr;
   if (project_next) {
     // Same buffers as a projection launcher; tile counts and stats slots 0-1 restart at zero.
     o.records = bb.records.as<GaussRecord>();
-    o.weights = nullptr;
+    o.weights = density ? bb.weights.as<float>() : nullptr;
     o.spans = bb.spans.as<TileSpan>();
     o.counts = bb.counts.as<int>();
     o.offsets = bb.offsets.as<int>();
@@ -240,14 +244,19 @@ int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_
     }
     bb.counts_cleared = false;
     bb.entries_emitted = true;
-    adam_fit_kernel<true><<<grid_for(m), kThreads, 0, s>>>(
-        m, bb.capacity, bb.counts.as<int>(), bb.offsets.as<int>(), bb.partials.as<float4>(), g.height,
-        g.width, raw, m1, m2, table, k, lg, n_per_view, g.tiles_x, g.tiles_per_view, o);
-  } else {
-    adam_fit_kernel<false><<<grid_for(m), kThreads, 0, s>>>(
-        m, bb.capacity, bb.counts.as<int>(), bb.offsets.as<int>(), bb.partials.as<float4>(), g.height,
-        g.width, raw, m1, m2, table, k, lg, n_per_view, g.tiles_x, g.tiles_per_view, o);
   }
+  const unsigned grid = grid_for(m);
+#define RTGS_ADAM(P, D)                                                                            \
+  adam_fit_kernel<P, D><<<grid, kThreads, 0, s>>>(m, bb.capacity, bb.counts.as<int>(),             \
+                                                  bb.offsets.as<int>(), bb.partials.as<float4>(),  \
+                                                  pd, g.height, g.width, raw, m1, m2, table, k, lg, \
+                                                  n_per_view, g.tiles_x, g.tiles_per_view, o)
+  if (project_next) {
+    if (density) RTGS_ADAM(true, true); else RTGS_ADAM(true, false);
+  } else {
+    if (density) RTGS_ADAM(false, true); else RTGS_ADAM(false, false);
+  }
+#undef RTGS_ADAM
   return check_cuda(cudaGetLastError(), "adam_fit_kernel");
 }
 

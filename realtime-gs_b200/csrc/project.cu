@@ -194,9 +194,10 @@ int launch_project_conic(BinBuffers& bb, const Geometry& g, const float* xy, con
 }
 
 int launch_project_raw(BinBuffers& bb, const Geometry& g, const float* raw, int64_t m,
-                       int64_t n_per_view, bool emit, const uint8_t* active, cudaStream_t s) {
+                       int64_t n_per_view, bool emit, const uint8_t* active, bool want_weights,
+                       cudaStream_t s) {
   ProjOut o;
-  RTGS_TRY(prepare(bb, g, m, false, s, &o));
+  RTGS_TRY(prepare(bb, g, m, want_weights, s, &o));
   o.active = active;
   if (emit && bb.entries[0].ptr) {
     o.entries = bb.entries[0].as<uint64_t>();

@@ -409,6 +409,9 @@ raster_kernel(const RasterArgs a) {
       if (f.loss_mode != kLossMse) {
         const bool mb = mask_bit(f.mask_bits + static_cast<int64_t>(view) * f.mask_bytes_per_view,
                                  static_cast<int64_t>(py[k]) * a.width + px);
+        // Mask coverage penalty coef * mean(coverage * (1 - mask)), coverage = 1 - exp(-density):
+        // its gradient reaches the backward as an upstream gradient on the density channel.
+        if constexpr (MODE == kFit && DEN) gd[k] = mb ? 0.f : f.coverage_coef * __expf(-accd[k]);
         if (f.loss_mode == kLossMaskWeighted) {
           wpix = mb ? 1.0f : 0.1f;  // 0.1 + 0.9 * mask (fit.py:562)
         } else {
@@ -620,10 +623,14 @@ int launch_raster_backward(BinBuffers& bb, const Geometry& g, float cutoff, cons
 
 int launch_raster_fit(BinBuffers& bb, const Geometry& g, float cutoff, const FitRasterArgs& fa,
                       bool backward, cudaStream_t s) {
-  RTGS_TRY(ensure_partials(bb, false, s));
+  RTGS_TRY(ensure_partials(bb, backward && fa.coverage_coef > 0.f, s));
   RasterArgs a = base_args(bb, g, cutoff);
   a.partials = bb.partials.as<float4>();
   a.fit = fa;
+  if (backward && fa.coverage_coef > 0.f) {
+    a.partial_d = bb.partial_d.as<float>();
+    return launch<kFit, true>(a, g, s, "raster fit (coverage)");
+  }
   if (backward) return launch<kFit, false>(a, g, s, "raster fit");
   return launch<kEval, false>(a, g, s, "raster eval");
 }

@@ -32,6 +32,7 @@ class FitOptions(ctypes.Structure):
         ("check_every", ctypes.c_int64),
         ("freeze_geometry", ctypes.c_int32),
         ("loss_mode", ctypes.c_int32),
+        ("mask_coverage_weight", ctypes.c_double),
     ]
 
 

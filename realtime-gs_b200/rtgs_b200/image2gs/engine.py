@@ -50,6 +50,7 @@ class FitEngine:
         freeze_geometry: bool = False,
         loss_mode: int = _native.LOSS_MSE,
         device: torch.device | None = None,
+        mask_coverage_weight: float = 0.0,
     ) -> None:
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         if self.device.index is None:
@@ -59,7 +60,7 @@ class FitEngine:
         opts = _native.FitOptions(
             lr=float(lr), iterations=int(iterations), log_every=int(log_every),
             check_every=int(check_every), freeze_geometry=int(bool(freeze_geometry)),
-            loss_mode=int(loss_mode),
+            loss_mode=int(loss_mode), mask_coverage_weight=float(mask_coverage_weight),
         )
         self._lib = _native.lib()
         handle = ctypes.c_void_p()
@@ -267,13 +268,15 @@ _POOL_MAX_IDLE = 4  # idle engines kept per process, least recently released clo
 
 def acquire_engine(n_views: int, n: int, height: int, width: int, *, lr: float, iterations: int,
                    log_every: int, check_every: int = 0, freeze_geometry: bool = False,
-                   loss_mode: int = _native.LOSS_MSE, device: torch.device | None = None) -> FitEngine:
+                   loss_mode: int = _native.LOSS_MSE, device: torch.device | None = None,
+                   mask_coverage_weight: float = 0.0) -> FitEngine:
     """An idle pooled engine of exactly this configuration, else a new one."""
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
     if dev.index is None:
         dev = torch.device("cuda", torch.cuda.current_device())
     key = (dev.index, int(n_views), int(n), int(height), int(width), float(lr), int(iterations),
-           int(log_every), int(check_every), bool(freeze_geometry), int(loss_mode))
+           int(log_every), int(check_every), bool(freeze_geometry), int(loss_mode),
+           float(mask_coverage_weight))
     with _POOL_LOCK:
         idle = _POOL.get(key)
         if idle:
@@ -283,7 +286,7 @@ def acquire_engine(n_views: int, n: int, height: int, width: int, *, lr: float, 
             return engine
     engine = FitEngine(n_views, n, height, width, lr=lr, iterations=iterations, log_every=log_every,
                        check_every=check_every, freeze_geometry=freeze_geometry, loss_mode=loss_mode,
-                       device=dev)
+                       device=dev, mask_coverage_weight=mask_coverage_weight)
     engine._pool_key = key
     return engine
 

@@ -202,8 +202,8 @@ def _validate_fit_controls(config: FitConfig, diagnostic_callback=None, diagnost
         for name in ("pool_triage_every", "pool_prune_count", "pool_spawn_count"):
             if getattr(config, name) < 0:
                 raise ValueError(f"{name} must be non-negative")
-    if config.mask_coverage_weight > 0.0:
-        raise ValueError("mask_coverage_weight is not implemented by rtgs_b200")
+    if config.mask_coverage_weight > 0.0 and (config.batch_views or config.pool):  # fit.py:618-622
+        raise ValueError("mask_coverage_weight is not supported with batch_views or the pool")
     if diagnostic_callback is not None or tuple(diagnostic_steps):
         raise ValueError("native fit diagnostics are not implemented by rtgs_b200")
     if config.iterations < 1:
@@ -257,6 +257,8 @@ def _fit_native_from_initialization(
     _require_cuda(image)
     h, w = image.shape[:2]
     _validate_initial_gaussians(g0, h, w)
+    if config.mask_coverage_weight > 0.0 and mask is None:  # fit.py:371-372
+        raise ValueError("mask_coverage_weight requires a mask")
     raw = raw_from_gaussians(g0.xy, g0.chol, g0.color, g0.weight, h, w)
     _validate_raw_parameters(raw)
     loss_mode = _native.LOSS_MSE if mask is None else _native.LOSS_MASK_WEIGHTED
@@ -265,7 +267,7 @@ def _fit_native_from_initialization(
     engine = acquire_engine(
         1, g0.n, h, w, lr=config.lr, iterations=config.iterations, log_every=config.log_every,
         check_every=check_every, freeze_geometry=config.freeze_geometry, loss_mode=loss_mode,
-        device=image.device,
+        device=image.device, mask_coverage_weight=config.mask_coverage_weight if mask is not None else 0.0,
     )
     ok = False
     try:

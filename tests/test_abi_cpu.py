@@ -44,7 +44,7 @@ def test_build_targets_sm_100a_only():
 
 def test_version_and_error_string_need_no_gpu():
     lib = _native.lib()
-    assert lib.rtgs2d_abi_version() == 1
+    assert lib.rtgs2d_abi_version() == 2
     assert isinstance(lib.rtgs2d_last_error(), bytes)
 
 

@@ -74,7 +74,10 @@ def test_fit_rejects_cpu_images_and_unsupported_modes():
     with pytest.raises(RuntimeError, match="CUDA tensors"):
         fit_image(img, FitConfig(n_gaussians=8, iterations=2), seed=0)
     for bad in (dict(backend="structsplat"), dict(init_strategy="structure_tensor"),
-                dict(mask_coverage_weight=0.5), dict(native_renderer="bogus"),
+                dict(native_renderer="bogus"),
+                # the reference's mask containment validation (fit.py:616-622)
+                dict(mask_coverage_weight=-1.0), dict(mask_coverage_weight=1.0, batch_views=True),
+                dict(mask_coverage_weight=1.0, pool=True),
                 # the reference's pool validation (fit.py:600-616)
                 dict(pool=True, freeze_geometry=True), dict(pool=True, pool_capacity=4),
                 dict(pool=True, pool_min_live=0), dict(pool=True, pool_triage_every=-1),
