@@ -182,9 +182,10 @@ def splat_microbench(device, steps: int, warmup: int) -> dict:
     def step():
         _native.check(lib.rtgs2d_render_forward(arena, xy.data_ptr(), chol.data_ptr(), color.data_ptr(),
                                                 weight.data_ptr(), 1, m, h, w, out.data_ptr(), None, stream))
-        _native.check(lib.rtgs2d_render_backward(arena, up.data_ptr(), None, xy.data_ptr(), chol.data_ptr(),
-                                                 color.data_ptr(), weight.data_ptr(), 1, m, h, w,
-                                                 *(g.data_ptr() for g in grads), stream))
+        # The backward of an autograd step: it reuses the forward's projection and binning.
+        _native.check(lib.rtgs2d_render_backward_after_forward(
+            arena, up.data_ptr(), None, xy.data_ptr(), chol.data_ptr(), color.data_ptr(), weight.data_ptr(),
+            1, m, h, w, *(g.data_ptr() for g in grads), stream))
 
     for _ in range(warmup):
         step()

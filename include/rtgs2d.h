@@ -131,6 +131,23 @@ RTGS2D_API int rtgs2d_render_backward(rtgs2d_arena* arena, const float* grad_out
                            float* grad_weight, void* stream);
 
 /*
+ * rtgs2d_render_backward for the backward pass of an autograd graph (cuda_backend.py:87-124):
+ * when the arena's last binning came from rtgs2d_render_forward with the same xy / chol / color /
+ * weight pointers and sizes (and, if grad_den is given, that forward wrote the density), that
+ * projection and binning are reused instead of recomputed; otherwise it is rtgs2d_render_backward.
+ * The caller guarantees the inputs were not modified since that forward (autograd does: saved
+ * tensors are kept alive and in-place changes to them are rejected). Any other binning on the
+ * arena (every forward / backward entry point) ends the reuse.
+ */
+RTGS2D_API int rtgs2d_render_backward_after_forward(rtgs2d_arena* arena, const float* grad_out,
+                                                    const float* grad_den, const float* xy,
+                                                    const float* chol, const float* color,
+                                                    const float* weight, int64_t n_views, int64_t n,
+                                                    int64_t height, int64_t width, float* grad_xy,
+                                                    float* grad_chol, float* grad_color,
+                                                    float* grad_weight, void* stream);
+
+/*
  * Support rectangles on the device, bit-exact with src/rtgs/image2gs/renderer2d.py:156-181 and in
  * the rectangle convention of src/rtgs/image2gs/cuda_backend.py:153-158: rects (M,4) int32
  * (x0, x1, y0, y1) with x1 = x0 - 1 when the support is empty, counts (M,) int64 pixels inside.

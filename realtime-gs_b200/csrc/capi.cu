@@ -72,6 +72,14 @@ struct rtgs2d_arena {
   int device = 0;
   BinBuffers bb;
   int64_t n_tiles = 0;  // tiles of the last binning
+  // Inputs of the last binning if it came from rtgs2d_render_forward (valid = true); any other
+  // binning on the arena clears it. rtgs2d_render_backward_after_forward reuses that binning.
+  struct ForwardKey {
+    const float *xy, *chol, *color, *weight;
+    int64_t n_views, n, height, width;
+    bool weights_written;
+  } last_forward{};
+  bool last_forward_valid = false;
 };
 
 namespace {
@@ -107,6 +115,44 @@ int check_dims(int64_t m, int64_t n_views, int64_t height, int64_t width) {
 int require(const void* p, const char* name) {
   if (p == nullptr) return set_error(RTGS2D_ERR_INVALID, std::string(name) + " is NULL");
   return 0;
+}
+
+}  // namespace
+
+namespace {
+
+int render_backward(rtgs2d_arena* arena, const float* grad_out, const float* grad_den,
+                    const float* xy, const float* chol, const float* color, const float* weight,
+                    int64_t n_views, int64_t n, int64_t height, int64_t width, float* grad_xy,
+                    float* grad_chol, float* grad_color, float* grad_weight, bool reuse,
+                    void* stream) {
+  RTGS_TRY(check_arena(arena));
+  if (n < 0) return set_error(RTGS2D_ERR_INVALID, "n must be non-negative");
+  const int64_t m = n_views * n;
+  RTGS_TRY(check_dims(m, n_views, height, width));
+  if (m == 0) return RTGS2D_OK;
+  RTGS_TRY(require(xy, "xy"));
+  RTGS_TRY(require(chol, "chol"));
+  RTGS_TRY(require(color, "color"));
+  RTGS_TRY(require(weight, "weight"));
+  cudaStream_t s = as_stream(stream);
+  const Geometry g = make_geometry(static_cast<int>(n_views), static_cast<int>(height),
+                                   static_cast<int>(width));
+  BinBuffers& bb = arena->bb;
+  const bool den = grad_den != nullptr;
+  const rtgs2d_arena::ForwardKey& k = arena->last_forward;
+  const bool same = reuse && arena->last_forward_valid && k.xy == xy && k.chol == chol &&
+                    k.color == color && k.weight == weight && k.n_views == n_views && k.n == n &&
+                    k.height == height && k.width == width && (k.weights_written || !den);
+  if (!same) {
+    arena->last_forward_valid = false;
+    RTGS_TRY(launch_project_chol(bb, g, xy, chol, color, weight, m, n, den, s));
+    RTGS_TRY(bin_entries(bb, g, m, s));
+    arena->n_tiles = g.n_tiles();
+  }
+  RTGS_TRY(launch_raster_backward(bb, g, kCutoff, grad_out, grad_den, s));
+  return launch_finalize_chol(bb, m, chol, color, weight, den, grad_xy, grad_chol, grad_color,
+                              grad_weight, s);
 }
 
 }  // namespace
@@ -152,6 +198,7 @@ int rtgs2d_forward(rtgs2d_arena* arena, const float* xy, const float* conics, co
                    int64_t m, int64_t n_views, int64_t height, int64_t width, double cutoff,
                    float* out, float* den, void* stream) {
   RTGS_TRY(check_arena(arena));
+  arena->last_forward_valid = false;
   RTGS_TRY(check_dims(m, n_views, height, width));
   RTGS_TRY(require(out, "out"));
   if (m > 0) {
@@ -180,6 +227,7 @@ int rtgs2d_backward(rtgs2d_arena* arena, const float* grad_out, const float* gra
                     float* grad_xy, float* grad_conics, float* grad_colors, float* grad_weights,
                     void* stream) {
   RTGS_TRY(check_arena(arena));
+  arena->last_forward_valid = false;
   RTGS_TRY(check_dims(m, n_views, height, width));
   if (m == 0) return RTGS2D_OK;
   RTGS_TRY(require(xy, "xy"));
@@ -223,9 +271,12 @@ int rtgs2d_render_forward(rtgs2d_arena* arena, const float* xy, const float* cho
   const Geometry g = make_geometry(static_cast<int>(n_views), static_cast<int>(height),
                                    static_cast<int>(width));
   BinBuffers& bb = arena->bb;
+  arena->last_forward_valid = false;
   RTGS_TRY(launch_project_chol(bb, g, xy, chol, color, weight, m, n > 0 ? n : 1, den != nullptr, s));
   RTGS_TRY(bin_entries(bb, g, m, s));
   arena->n_tiles = g.n_tiles();
+  arena->last_forward = {xy, chol, color, weight, n_views, n, height, width, den != nullptr};
+  arena->last_forward_valid = true;
   return launch_raster_forward(bb, g, kCutoff, out, den, s);
 }
 
@@ -234,27 +285,21 @@ int rtgs2d_render_backward(rtgs2d_arena* arena, const float* grad_out, const flo
                            const float* weight, int64_t n_views, int64_t n, int64_t height,
                            int64_t width, float* grad_xy, float* grad_chol, float* grad_color,
                            float* grad_weight, void* stream) {
-  RTGS_TRY(check_arena(arena));
-  if (n < 0) return set_error(RTGS2D_ERR_INVALID, "n must be non-negative");
-  const int64_t m = n_views * n;
-  RTGS_TRY(check_dims(m, n_views, height, width));
-  if (m == 0) return RTGS2D_OK;
-  RTGS_TRY(require(xy, "xy"));
-  RTGS_TRY(require(chol, "chol"));
-  RTGS_TRY(require(color, "color"));
-  RTGS_TRY(require(weight, "weight"));
-  cudaStream_t s = as_stream(stream);
-  const Geometry g = make_geometry(static_cast<int>(n_views), static_cast<int>(height),
-                                   static_cast<int>(width));
-  BinBuffers& bb = arena->bb;
-  const bool den = grad_den != nullptr;
-  RTGS_TRY(launch_project_chol(bb, g, xy, chol, color, weight, m, n, den, s));
-  RTGS_TRY(bin_entries(bb, g, m, s));
-  arena->n_tiles = g.n_tiles();
-  RTGS_TRY(launch_raster_backward(bb, g, kCutoff, grad_out, grad_den, s));
-  return launch_finalize_chol(bb, m, chol, color, weight, den, grad_xy, grad_chol, grad_color,
-                              grad_weight, s);
+  return render_backward(arena, grad_out, grad_den, xy, chol, color, weight, n_views, n, height,
+                         width, grad_xy, grad_chol, grad_color, grad_weight, false, stream);
 }
+
+int rtgs2d_render_backward_after_forward(rtgs2d_arena* arena, const float* grad_out,
+                                         const float* grad_den, const float* xy,
+                                         const float* chol, const float* color,
+                                         const float* weight, int64_t n_views, int64_t n,
+                                         int64_t height, int64_t width, float* grad_xy,
+                                         float* grad_chol, float* grad_color, float* grad_weight,
+                                         void* stream) {
+  return render_backward(arena, grad_out, grad_den, xy, chol, color, weight, n_views, n, height,
+                         width, grad_xy, grad_chol, grad_color, grad_weight, true, stream);
+}
+
 
 int rtgs2d_support_rects(const float* xy, const float* chol, int64_t m, int64_t height,
                          int64_t width, int32_t* rects, int64_t* counts, void* stream) {

@@ -63,6 +63,10 @@ _SIGNATURES = {
         [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_int64, _c_int64, _c_int64, _c_int64, _vp, _vp, _vp, _vp, _vp],
         ctypes.c_int,
     ),
+    "rtgs2d_render_backward_after_forward": (
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_int64, _c_int64, _c_int64, _c_int64, _vp, _vp, _vp, _vp, _vp],
+        ctypes.c_int,
+    ),
     "rtgs2d_support_rects": ([_vp, _vp, _c_int64, _c_int64, _c_int64, _vp, _vp, _vp], ctypes.c_int),
     "rtgs2d_arena_copy_binning": (
         [_vp, _c_int64, _vp, _c_int64, _vp, ctypes.POINTER(_c_int64), ctypes.POINTER(_c_int64), _vp],

@@ -63,8 +63,10 @@ def _backward(ctx, grad_out, grad_den):
     gd = grad_den.contiguous() if grad_den is not None else None
     L = _native.lib()
     with torch.cuda.device(device):
+        # Saved tensors are alive and unmodified (autograd enforces it), so the forward's
+        # binning is reused when nothing else has binned on the arena since.
         _native.check(
-            L.rtgs2d_render_backward(
+            L.rtgs2d_render_backward_after_forward(
                 _native.arena(device), _native.ptr(go), _native.ptr(gd), xy.data_ptr(),
                 chol.data_ptr(), color.data_ptr(), weight.data_ptr(), n_views, n, height, width,
                 *(_native.ptr(g) for g in grads), _native.stream_ptr(device),

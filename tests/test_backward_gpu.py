@@ -146,3 +146,37 @@ def test_reference_abi_rejects_bad_arguments():
     assert rc == -1
     e = ctypes.c_int64()
     assert lib.rtgs2d_arena_last_stats(arena, ctypes.byref(e), None) == 0
+
+
+def test_backward_after_forward_reuses_binning_only_when_valid():
+    """rtgs2d_render_backward_after_forward equals rtgs2d_render_backward bit for bit, both when it
+    reuses the forward's binning and when another binning intervened (it then recomputes)."""
+    from rtgs_b200 import _native
+
+    xy, chol, color, weight = cuda(*stacked(12, 2, 300, 48, 40))
+    other = cuda(*stacked(13, 2, 200, 48, 40))
+    up = torch.randn(2, 48, 40, 3, generator=torch.Generator().manual_seed(3)).to(DEV)
+    lib, dev = _native.lib(), xy.device
+    arena, st = _native.arena(dev), _native.stream_ptr(dev)
+    n = xy.shape[1]
+
+    def fwd(args):
+        out = torch.empty(2, 48, 40, 3, device=DEV)
+        _native.check(lib.rtgs2d_render_forward(arena, *(t.data_ptr() for t in args), 2, args[0].shape[1], 48, 40,
+                                                out.data_ptr(), None, st))
+
+    def bwd(fn):
+        grads = [torch.empty_like(t) for t in (xy, chol, color, weight)]
+        _native.check(fn(arena, up.data_ptr(), None, xy.data_ptr(), chol.data_ptr(), color.data_ptr(),
+                         weight.data_ptr(), 2, n, 48, 40, *(g.data_ptr() for g in grads), st))
+        torch.cuda.synchronize()
+        return grads
+
+    ref = bwd(lib.rtgs2d_render_backward)
+    fwd((xy, chol, color, weight))
+    reused = bwd(lib.rtgs2d_render_backward_after_forward)
+    fwd((xy, chol, color, weight))
+    fwd(other)  # another binning in between: must recompute
+    recomputed = bwd(lib.rtgs2d_render_backward_after_forward)
+    for a, b, c in zip(ref, reused, recomputed):
+        assert torch.equal(a, b) and torch.equal(a, c)
