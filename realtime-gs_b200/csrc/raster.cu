@@ -161,15 +161,24 @@ __device__ __forceinline__ void backward_piece(const float4& geo, const float4& 
   constexpr int kLaneStride = ROW ? 1 : kTile;  // and of one lane-axis pixel
   int sidx_a = sidx0 + r8 * kLaneStride;
   float fvar = ROW ? pyc0 : pxc0;
-  auto accumulate = [&](int sidx, float d_fix, float sq_fix, float cross, float d_var, float sq_var,
-                        float q) {
-    const float4 gv = s_g[sidx];
-    const float e = falloff(q);
-    float v = gv.x * app.y;
-    v = fmaf(gv.y, app.z, v);
-    v = fmaf(gv.z, app.w, v);
-    if constexpr (DEN) v = fmaf(gv.w, wt, v);
-    const float dq = e * v;
+  // Only the shared-memory load, the falloff and the weighted upstream gradient sit under the
+  // support predicate (short enough to be predicated rather than branched); the moment updates
+  // run unconditionally with dq = e = 0 and g = 0 outside the support, which adds exact zeros
+  // (the offsets and their products are finite), so a non-finite colour or gradient still only
+  // reaches pixels inside the support.
+  auto accumulate = [&](bool in, int sidx, float d_fix, float sq_fix, float cross, float d_var,
+                        float sq_var, float q) {
+    float4 gv = make_float4(0.f, 0.f, 0.f, 0.f);
+    float e = 0.f, dq = 0.f;
+    if (in) {
+      gv = s_g[sidx];
+      e = falloff(q);
+      float v = gv.x * app.y;
+      v = fmaf(gv.y, app.z, v);
+      v = fmaf(gv.z, app.w, v);
+      if constexpr (DEN) v = fmaf(gv.w, wt, v);
+      dq = e * v;
+    }
     const float dx = ROW ? d_fix : d_var, dy = ROW ? d_var : d_fix;
     const float dxdx = ROW ? sq_fix : sq_var, dydy = ROW ? sq_var : sq_fix;
     S[0] = fmaf(dq, dx, S[0]);
@@ -190,13 +199,13 @@ __device__ __forceinline__ void backward_piece(const float4& geo, const float4& 
       const float cross = __fmul_rn(da, dv);  // dx dy (multiplication commutes exactly)
       const float t1 = __fmul_rn(cross, geo.w);
       const float q = ROW ? __fadd_rn(__fadd_rn(t_a, t1), t_v) : __fadd_rn(__fadd_rn(t_v, t1), t_a);
-      if (st < lim_a && q < cutoff) accumulate(sidx_a, da, sq_a, cross, dv, sq_v, q);
+      accumulate(st < lim_a && q < cutoff, sidx_a, da, sq_a, cross, dv, sq_v, q);
     }
     if (any_b) {
       const float cross = __fmul_rn(db, dv);
       const float t1 = __fmul_rn(cross, geo.w);
       const float q = ROW ? __fadd_rn(__fadd_rn(t_b, t1), t_v) : __fadd_rn(__fadd_rn(t_v, t1), t_b);
-      if (st < lim_b && q < cutoff) accumulate(sidx_a + 8 * kLaneStride, db, sq_b, cross, dv, sq_v, q);
+      accumulate(st < lim_b && q < cutoff, sidx_a + 8 * kLaneStride, db, sq_b, cross, dv, sq_v, q);
     }
     fvar += 1.f;
     sidx_a += kStep;
