@@ -235,6 +235,46 @@ ranges_kernel(const uint64_t* __restrict__ entries, const unsigned long long* __
   if (i == n - 1 || static_cast<uint32_t>(entries[i + 1] >> 32) != k) ranges[k].y = static_cast<int>(i + 1);
 }
 
+// Inclusive scan of up to kSmallScanMax ints by one block (tile counts -> tile ends): one launch
+// instead of the device-wide scan's two for the tile counts of ordinary frames.
+constexpr int kSmallScanThreads = 1024;
+constexpr int kSmallScanMax = 8 * kSmallScanThreads;
+
+__global__ void __launch_bounds__(kSmallScanThreads)
+small_inclusive_scan_kernel(const int* __restrict__ in, int* __restrict__ out, int n) {
+  __shared__ int s_warp[kSmallScanThreads / 32];
+  const int per = (n + kSmallScanThreads - 1) / kSmallScanThreads;
+  const int i0 = threadIdx.x * per;
+  const int i1 = min(i0 + per, n);
+  int sum = 0;
+  for (int i = i0; i < i1; ++i) sum += in[i];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = sum;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += y;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int v = s_warp[lane];
+    int x = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, d);
+      if (lane >= d) x += y;
+    }
+    s_warp[lane] = x - v;  // exclusive prefix of the warp totals
+  }
+  __syncthreads();
+  int run = s_warp[warp] + incl - sum;
+  for (int i = i0; i < i1; ++i) {
+    run += in[i];
+    out[i] = run;
+  }
+}
+
 template <bool INCLUSIVE>
 int cub_scan(BinBuffers& bb, const int* in, int* out, int64_t n, cudaStream_t s) {
   size_t bytes = 0;
@@ -290,7 +330,14 @@ int bin_scatter(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s) {
                                                   nullptr, bb.entries[0].as<uint64_t>());
     RTGS_CUDA(cudaGetLastError(), "emit_kernel");
   }
-  RTGS_TRY(cub_scan<true>(bb, bb.tile_count.as<int>(), bb.tile_end.as<int>(), n_tiles, s));
+  if (n_tiles <= kSmallScanMax) {
+    small_inclusive_scan_kernel<<<1, kSmallScanThreads, 0, s>>>(bb.tile_count.as<int>(),
+                                                                bb.tile_end.as<int>(),
+                                                                static_cast<int>(n_tiles));
+    RTGS_CUDA(cudaGetLastError(), "small_inclusive_scan_kernel");
+  } else {
+    RTGS_TRY(cub_scan<true>(bb, bb.tile_count.as<int>(), bb.tile_end.as<int>(), n_tiles, s));
+  }
   if (m > 0 && bb.capacity > 0) {
     scatter_kernel<<<grid_for(bb.capacity), kThreads, 0, s>>>(
         bb.entries[0].as<uint64_t>(), bb.stats.as<unsigned long long>(), bb.capacity,
