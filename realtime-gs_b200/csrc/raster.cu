@@ -1,24 +1,27 @@
 // Per-tile raster kernels for the accumulated 2D splatting renderer (sm_100a).
 //
-// One CTA per 16x16 tile. Each warp owns an 8 x (4*PPT) pixel sub-block and each lane PPT
-// pixels of one column (rows r, r+4, ...). The tile's gaussian list (ascending gaussian index,
-// from the binning step) is staged through shared memory in batches; while staging, every
-// record gets a bit mask of the warps whose sub-block its support rectangle touches, so a warp
-// walks only the records that can reach its pixels (ballot + ffs), with no per-record test in
-// the inner loop.
+// One CTA per 16x16 tile, 4 warps. Each warp owns an 8 x (4*PPT) pixel sub-block and each lane PPT
+// adjacent pixels of one column (rows PPT*r .. PPT*r + PPT-1, so that a small gaussian usually
+// covers all of them). The tile's gaussian list (ascending gaussian index, from the binning step)
+// is staged through shared memory in batches of 128 records.
 //
-//   forward   pixel accumulators live in registers; the list order is the reference's
-//             summation order, so a render is deterministic and no atomics are used.
-//   backward  the tile's upstream gradients are staged in shared memory; for every (gaussian,
-//             tile) entry the exact piece = support rectangle x tile is evaluated and 8 moments
+//   forward   per 32 staged records, 16 ballots give every lane a 32-bit mask of the records whose
+//             support rectangle covers each of its pixels; the lane walks exactly those, in list
+//             order, accumulating in registers (flat predicate for the ellipse test q < cutoff,
+//             exp(-q/2) as one multiply + ex2). The list order is the reference's summation
+//             order, so a render is deterministic and no atomics are used.
+//   backward  the tile's upstream gradients are staged in shared memory; every (gaussian, tile)
+//             entry's piece = support rectangle x tile is evaluated over exactly its pixels and
+//             8 moments
 //               Sdx = sum dq*dx, Sdy = sum dq*dy, Sxx = sum dq*dx^2, Sxy = sum dq*dx*dy,
 //               Syy = sum dq*dy^2, Sr/Sg/Sb = sum e*g_rgb       (e = exp(-q/2), dq = e * g.A)
-//             are written once per entry. A warp works on 4 pieces at a time, 8 lanes ("octet")
-//             per piece striding over exactly the piece's pixels; pieces are bucketed by their
-//             step count ceil(area / 8) so the 4 pieces of a warp take the same number of steps.
-//             An 8-lane transpose butterfly leaves moment r in lane r of each octet: one 32-byte
-//             store per entry. A per-gaussian pass (optim.cu) sums a gaussian's entries in order
-//             and applies the chain rule: deterministic, no global atomics.
+//             are written once per entry. Pieces are ordered by (orientation, step count) with a
+//             stable counting sort; a warp takes 4 pieces at a time, 8 lanes ("octet") per piece,
+//             each lane owning up to two columns (wide pieces, stepping down the rows) or two rows
+//             (tall pieces, stepping across the columns). An 8-lane transpose butterfly leaves
+//             moment r in lane r of each octet: one 32-byte store per entry. A per-gaussian pass
+//             (optim.cu) sums a gaussian's entries in order and applies the chain rule:
+//             deterministic, no global atomics.
 //   fit       forward -> L2 loss gradient in registers -> backward, in one kernel: the rendered
 //             image and dL/dout never leave the SM.
 //
@@ -248,12 +251,12 @@ raster_kernel(const RasterArgs a) {
   bool inimg[PPT];
 #pragma unroll
   for (int k = 0; k < PPT; ++k) {
-    py[k] = oy + sby * L::kSubH + (lane >> 3) + 4 * k;
+    py[k] = oy + sby * L::kSubH + PPT * (lane >> 3) + k;
     pyc[k] = static_cast<float>(py[k]) + 0.5f;
     inimg[k] = px < a.width && py[k] < a.height;
   }
   const int sx0 = ox + sbx * L::kSubW, sy0 = oy + sby * L::kSubH;  // this warp's sub-block
-  const int sub_col = lane & 7, sub_row0 = lane >> 3;
+  const int sub_col = lane & 7, sub_row0 = PPT * (lane >> 3);
   const int64_t view_base = static_cast<int64_t>(view) * a.height * a.width;
   int2 range;
   if (a.presorted) {
@@ -332,7 +335,7 @@ raster_kernel(const RasterArgs a) {
         for (int b = 0; b < L::kSubH; ++b) {
           const unsigned v = __ballot_sync(0xffffffffu, (rbits >> b) & 1u);
 #pragma unroll
-          for (int k = 0; k < PPT; ++k) mpix[k] = sub_row0 + 4 * k == b ? v : mpix[k];
+          for (int k = 0; k < PPT; ++k) mpix[k] = sub_row0 + k == b ? v : mpix[k];
         }
         unsigned walk = 0;
 #pragma unroll
