@@ -40,6 +40,7 @@ for _p in (str(ROOT), str(ROOT / "realtime-gs_b200")):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
+import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 FLOP_PER_PAIR = 68.0  # 20 forward + 48 backward FP32 flop per pair (FMA = 2)
@@ -53,6 +54,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("native", "reference"), default="native")
     ap.add_argument("--workload", default="single_large")
+    ap.add_argument("--views", type=int, default=1,
+                    help="images fitted together in one engine per GPU and step (batched fit); value counts images")
     ap.add_argument("--no-splat", action="store_true", help="skip the 4K splat micro-benchmark")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--cpu-iters", type=int, default=2, help="oracle iterations per CPU sample step")
@@ -243,22 +246,25 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
             print(json.dumps({"splat_fwd_bwd": res}), flush=True)
         return
     h, w, n, iters = wl["height"], wl["width"], wl["n_fit"], wl["iterations"]
-    seed = 1000 + rank
-    target = synthetic.make_target(seed, wl, render_gaussians_2d_batched, device)
-    init = synthetic.fit_init(seed, n, h, w)
-    init_dev = tuple(x.to(device) for x in (init.xy, init.chol, init.color, init.weight))
-    raw = {k: v[None].contiguous() for k, v in raw_from_gaussians(*init_dev, h, w).items()}
-    engine = FitEngine(1, n, h, w, lr=1e-2, iterations=iters, log_every=50, device=device)
-    engine.set_targets(target[None])
+    views = max(1, int(args.views))
+    # Image v of rank r is global image r * views + v (its seeds do not depend on the GPU count).
+    seeds = [1000 + rank * views + v for v in range(views)]
+    targets = torch.stack([synthetic.make_target(sd, wl, render_gaussians_2d_batched, device) for sd in seeds])
+    inits = [synthetic.fit_init(sd, n, h, w) for sd in seeds]
+    init_dev = tuple(torch.stack([getattr(g, f) for g in inits]).to(device) for f in ("xy", "chol", "color", "weight"))
+    raw = {k: v.contiguous() for k, v in raw_from_gaussians(*init_dev, h, w).items()}
+    engine = FitEngine(views, n, h, w, lr=1e-2, iterations=iters, log_every=50, device=device)
+    engine.set_targets(targets)
+    target, init = targets[0], inits[0]  # the e2e and CPU legs use the rank's first image
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)  # > 126 MB L2
-    gathered = torch.empty(world, n, 9, device=device) if world > 1 else None
+    gathered = torch.empty(world, views * n, 9, device=device) if world > 1 else None
 
     def one_fit():
         engine.set_raw(raw)
         engine.run(iters)
         if world > 1:  # the single collective of the job: gather every rank's fitted parameters
-            xy, chol, color, weight = engine.params()
-            packed = torch.cat([xy[0], chol[0], color[0], weight[0][:, None]], dim=1).contiguous()
+            xy, chol, color, weight = (t.reshape(views * n, -1) for t in engine.params())
+            packed = torch.cat([xy, chol, color, weight], dim=1).contiguous()
             dist.all_gather_into_tensor(gathered, packed)
 
     for _ in range(args.warmup):
@@ -283,7 +289,7 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
     wall_s = time.perf_counter() - t_wall
     clocks = sampler.stop()
     _, sums = engine.evaluate(want_render=False)
-    final_psnr = -10.0 * math.log10(max(sums[0, 1] / (3.0 * h * w), 1e-12))
+    final_psnr = float(np.mean([-10.0 * math.log10(max(sums[b, 1] / (3.0 * h * w), 1e-12)) for b in range(views)]))
     # Stage split and the raster kernel's duration: one more fit of the same workload with CUDA
     # events around every stage of every iteration (recorded inside the replayed graphs). Kept out
     # of the timed fits because the event records themselves lengthen an iteration.
@@ -298,14 +304,14 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
     if world > 1:
         dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
     total_ms = float(total_ms.item())
-    value = world * args.steps / (total_ms / 1e3)
+    value = world * views * args.steps / (total_ms / 1e3)
 
     # e2e through the public API with host buffers (all ranks concurrently).
     target_host = target.cpu().pin_memory()
     init_host = tuple(x.pin_memory() for x in (init.xy, init.chol, init.color, init.weight))
     del engine
     e2e_value, h2d, d2h = None, 0, 0
-    if not args.no_e2e:
+    if not args.no_e2e and views == 1:  # the public API's single-image fit
         e2e_s, h2d, d2h = e2e_fit(device, wl, target_host, init_host, steps=2)
         e2e_t = torch.tensor([e2e_s], dtype=torch.float64, device=device)
         if world > 1:
@@ -336,10 +342,13 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
     if world == 1 and not args.no_cpu:
         res = cpu_fit_sample(wl, seed, args.cpu_iters, steps=1, warmup=1)
         cpu = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")}
-    # Own kernels per fit: one projection per 64-iteration chunk, then per iteration scatter, tile
-    # sort, raster fit and Adam (+ projection, + loss logging); CUB's tile-count scan (2 kernels per
-    # iteration) is a library launch and counted apart.
+    # Own kernels per fit: one projection per 64-iteration chunk, then per iteration Adam (+
+    # projection, + loss logging), the tile-count scan (own single-block kernel up to 8192 tiles,
+    # else CUB's two kernels, counted as library launches), scatter, tile sort and raster fit.
     chunks_per_fit = (iters + 63) // 64
+    n_tiles = views * ((h + 15) // 16) * ((w + 15) // 16)
+    own_per_iter = 5 if n_tiles <= 8192 else 4
+    lib_per_iter = 0 if n_tiles <= 8192 else 2
     line = {
         "metric": "2D-gaussian image fits/sec",
         "value": value,
@@ -355,7 +364,7 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
         "data": "synthetic",
         "config": {
             "workload": args.workload, "height": h, "width": w, "gaussians": n, "iterations": iters,
-            "source_gaussians": wl["n_sources"], "images_per_gpu_per_step": 1, "parallelism": f"dp{world} (whole images)",
+            "source_gaussians": wl["n_sources"], "images_per_gpu_per_step": views, "parallelism": f"dp{world} (whole images)",
             "l2": "256 MB buffer written between timed fits; a fit's own 1000 iterations run L2-warm",
             "final_psnr_db": final_psnr,
         },
@@ -374,8 +383,8 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
                                        "adam": stages["adam_ms"] / its},
         },
         "cpu_baseline": cpu,
-        "gpu_launches": args.steps * (chunks_per_fit + 4 * iters),
-        "library_launches": args.steps * 2 * iters,
+        "gpu_launches": args.steps * (chunks_per_fit + own_per_iter * iters),
+        "library_launches": args.steps * lib_per_iter * iters,
         "clocks": clocks,
         "wall_s_timed_region": wall_s,
     }
