@@ -3,16 +3,18 @@
 
 Workload (default ``single_large``): a 1024x768 RGB fp32 target made of 5,000 random anisotropic
 gaussians + N(0, 0.01) noise, fitted with 50,000 gaussians, L2 loss, Adam lr 1e-2 with the cosine
-schedule, 1,000 iterations. One step = one complete fit of one image per GPU (weak scaling: rank r
-fits its own image, seed 1000 + r), followed for N > 1 by the one gather of fitted parameters to
-all ranks (NCCL). ``value`` = fits completed by all ranks / max-over-ranks device time.
+schedule, 1,000 iterations. One step = one complete fit of one image per GPU (``--views V``: V
+images fitted together in one engine; weak scaling: rank r fits its own images, seeds
+1000 + r * V + v), followed for N > 1 by the one gather of fitted parameters to all ranks (NCCL).
+``value`` = images fitted by all ranks / max-over-ranks device time.
 
 Also measured in the same run:
   e2e       the same fit through the public API (fit_image_from_initialization) with the target and
             the initial parameters in pinned host memory and the fitted parameters read back.
   roofline  the fused raster kernel (forward + loss gradient + backward), timed with CUDA events
-            on its launch stream inside the timed fits; algorithmic work = 68 FP32 flop per
-            (gaussian, pixel-in-support-rectangle) pair.
+            on its launch stream around every raster launch of one extra fit of the same workload
+            run right after the timed fits; algorithmic work = 68 FP32 flop per (gaussian,
+            pixel-in-support-rectangle) pair.
   splat     the 4K micro-benchmark: 1,000,000 fixed gaussians on 3840x2160, forward + backward
             through the renderer C ABI with an N(0,1) upstream gradient (Gpixel.gauss/s).
   cpu_baseline  the CPU oracle (restatement of the reference's pure-PyTorch fit) on the host
@@ -340,7 +342,7 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
         traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
     cpu = None
     if world == 1 and not args.no_cpu:
-        res = cpu_fit_sample(wl, seed, args.cpu_iters, steps=1, warmup=1)
+        res = cpu_fit_sample(wl, seeds[0], args.cpu_iters, steps=1, warmup=1)
         cpu = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")}
     # Own kernels per fit: one projection per 64-iteration chunk, then per iteration Adam (+
     # projection, + loss logging), the tile-count scan (own single-block kernel up to 8192 tiles,
