@@ -9,8 +9,8 @@ constexpr int kSmallEntries = 32;  // gaussians with more entries are summed by 
 
 constexpr int kSmallSpan = 16;  // tile spans above this are walked by the whole warp
 
-// Threads per block of every kernel that calls project_tail (its block scan assumes it). 128
-// spreads the per-gaussian kernels over the SMs in more, smaller blocks (they are latency bound).
+// Threads per block of the per-gaussian kernels (projection, finalisation, Adam) and of the loss
+// reduction: 128 spreads the latency-bound per-gaussian kernels over the SMs in smaller blocks.
 constexpr int kProjThreads = 128;
 
 struct ProjOut {
@@ -64,21 +64,17 @@ __device__ __forceinline__ void for_each_span_tile(int64_t gid, int cnt, const T
   }
 }
 
-// Record, span, tile count and entry offset of gaussian i. Must be called by every thread of a
-// kProjThreads block (it contains block barriers).
+// Record, span, tile count and entry offset of gaussian i. Must be called by every lane of a warp.
 //
-// Entry offsets: a block-wide exclusive scan of the tile counts plus the block's base, reserved
-// with one atomic on stats[kStatEntries]. Blocks reserve in arrival order, so a gaussian's entry
-// index varies from run to run; nothing reads entries in index order (the raster addresses its
-// tile's entries through the gaussian, the gradient gather reads a gaussian's own entries), so no
-// result depends on it.
+// Entry offsets: a warp-wide exclusive scan of the tile counts plus the warp's base, reserved with
+// one atomic on stats[kStatEntries]. Warps reserve in arrival order, so a gaussian's entry index
+// varies from run to run; nothing reads entries in index order (the raster addresses its tile's
+// entries through the gaussian, the gradient gather reads a gaussian's own entries), so no result
+// depends on it.
 __device__ __forceinline__ void project_tail(int64_t i, bool active, float mx, float my, Conic k,
                                              int x0, int x1, int y0, int y1, long long pixels,
                                              float w, float cr, float cg, float cb, int view,
                                              int tiles_x, int tiles_per_view, const ProjOut& o) {
-  constexpr int kWarps = kProjThreads / 32;
-  __shared__ int s_warp_entries[kWarps];
-  __shared__ int s_base;
   int cnt = 0;
   long long pairs = 0;
   TileSpan sp{0, 0, 1, 0};
@@ -103,7 +99,7 @@ __device__ __forceinline__ void project_tail(int64_t i, bool active, float mx, f
     if (o.weights) o.weights[i] = w;
     o.counts[i] = cnt;
   }
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
   int incl = cnt;
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) {
@@ -113,26 +109,16 @@ __device__ __forceinline__ void project_tail(int64_t i, bool active, float mx, f
   unsigned long long p = static_cast<unsigned long long>(pairs);
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) p += __shfl_xor_sync(0xffffffffu, p, d);
-  if (lane == 31) s_warp_entries[warp] = incl;
   if (lane == 0 && p) {
     atomicAdd(&o.stats[kStatPairs], p);
     atomicAdd(&o.stats[kStatPairsTotal], p);
   }
-  __syncthreads();
-  int before = 0, total = 0;
-#pragma unroll
-  for (int w2 = 0; w2 < kWarps; ++w2) {
-    const int v = s_warp_entries[w2];
-    before += w2 < warp ? v : 0;
-    total += v;
+  int wbase = 0;
+  if (lane == 31 && incl) {
+    wbase = static_cast<int>(atomicAdd(&o.stats[kStatEntries], static_cast<unsigned long long>(incl)));
   }
-  if (threadIdx.x == 0) {
-    s_base = total ? static_cast<int>(atomicAdd(&o.stats[kStatEntries],
-                                                static_cast<unsigned long long>(total)))
-                   : 0;
-  }
-  __syncthreads();
-  const int off = s_base + before + incl - cnt;
+  wbase = __shfl_sync(0xffffffffu, wbase, 31);
+  const int off = wbase + incl - cnt;
   if (active) o.offsets[i] = off;
   // Tile counts, and with o.entries the entries themselves (all lanes reach this point). Emitted,
   // only entries that fit the capacity are emitted and counted: the binning stays consistent, and

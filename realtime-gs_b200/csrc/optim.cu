@@ -119,7 +119,8 @@ adam_fit_kernel(int64_t m, int64_t cap, int* counts, const int* __restrict__ off
     }
   }
   int cnt = active ? counts[i] : 0;
-  const int off = cnt > 0 ? offsets[i] : 0;
+  const int off_any = active ? offsets[i] : 0;  // loaded together with counts[i], not after it
+  const int off = cnt > 0 ? off_any : 0;
   cnt = clamp_to_capacity(cnt, off, cap);
   const Moments mo = gather_moments<DEN>(partials, partial_d, cnt, off);
 
