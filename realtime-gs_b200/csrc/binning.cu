@@ -153,17 +153,28 @@ __device__ __forceinline__ uint32_t bitonic_shfl(uint32_t v, int i, int k, int j
 }
 
 __global__ void __launch_bounds__(kTileSortWarps * 32)
-tile_sort_kernel(const int* __restrict__ tile_end, int64_t n_tiles, int64_t cap,
-                 unsigned long long* __restrict__ stats, uint32_t* __restrict__ list) {
+tile_sort_kernel(const int* __restrict__ tile_end, const int2* __restrict__ tile_seg,
+                 const int* __restrict__ fill, int64_t n_tiles, int64_t cap,
+                 unsigned long long* __restrict__ stats, uint32_t* __restrict__ list,
+                 int2* __restrict__ ranges) {
   __shared__ uint32_t s_buf[kTileSortWarps][kSegSortMax];
   if (blockIdx.x == 0 && threadIdx.x == 0) retire_projection_stats(stats, true);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * kTileSortWarps + warp;
   if (t >= n_tiles) return;
-  int64_t start = t == 0 ? 0 : tile_end[t - 1];
-  int64_t end = tile_end[t];
+  int64_t start, end;
+  if (tile_seg) {  // direct placement: the tile's segment and how much of it the projection filled
+    const int2 sg = tile_seg[t];
+    const int filled = fill[t];
+    start = sg.x;
+    end = start + (filled < sg.y ? filled : sg.y);
+  } else {    // scatter: inclusive scan of the tile counts
+    start = t == 0 ? 0 : tile_end[t - 1];
+    end = tile_end[t];
+  }
   start = start < cap ? start : cap;
   end = end < cap ? end : cap;
+  if (lane == 0) ranges[t] = make_int2(static_cast<int>(start), static_cast<int>(end));
   const int len = static_cast<int>(end - start);
   if (len <= 1) return;
   if (len > kSegSortMax) {
@@ -275,6 +286,53 @@ small_inclusive_scan_kernel(const int* __restrict__ in, int* __restrict__ out, i
   }
 }
 
+// Direct placement layout for the next binning: tile t gets a segment of count + 8 + count / 4
+// slots (count = this binning's entries of the tile), segments packed in tile order and clipped to
+// the list capacity. Counts come from the scan (tile_end, after a scatter) or from the fill
+// counters of a direct placement, which are then zeroed for the next one. One block.
+__global__ void __launch_bounds__(kSmallScanThreads)
+layout_kernel(const int* __restrict__ tile_end, int* __restrict__ fill, int n_tiles,
+              int list_cap, int2* __restrict__ seg) {
+  __shared__ int s_warp[kSmallScanThreads / 32];
+  const int per = (n_tiles + kSmallScanThreads - 1) / kSmallScanThreads;
+  const int i0 = threadIdx.x * per;
+  const int i1 = min(i0 + per, n_tiles);
+  auto count = [&](int t) {
+    return tile_end ? tile_end[t] - (t > 0 ? tile_end[t - 1] : 0) : fill[t];
+  };
+  auto seg_cap = [](int c) { return c + 8 + (c >> 2); };
+  int sum = 0;
+  for (int t = i0; t < i1; ++t) sum += seg_cap(count(t));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = sum;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += y;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int v = s_warp[lane];
+    int x = v;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, d);
+      if (lane >= d) x += y;
+    }
+    s_warp[lane] = x - v;
+  }
+  __syncthreads();
+  int start = s_warp[warp] + incl - sum;
+  for (int t = i0; t < i1; ++t) {
+    const int c = seg_cap(count(t));
+    const int room = list_cap - start;
+    seg[t] = make_int2(start, c < room ? c : (room > 0 ? room : 0));
+    if (!tile_end) fill[t] = 0;
+    start += c;
+  }
+}
+
 template <bool INCLUSIVE>
 int cub_scan(BinBuffers& bb, const int* in, int* out, int64_t n, cudaStream_t s) {
   size_t bytes = 0;
@@ -346,14 +404,43 @@ int bin_scatter(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s) {
   }
   bb.counts_cleared = true;
   const unsigned blocks = static_cast<unsigned>((n_tiles + kTileSortWarps - 1) / kTileSortWarps);
-  tile_sort_kernel<<<blocks, kTileSortWarps * 32, 0, s>>>(bb.tile_end.as<int>(), n_tiles,
-                                                         bb.capacity,
-                                                         bb.stats.as<unsigned long long>(),
-                                                         bb.list.as<uint32_t>());
+  RTGS_TRY(bb.ranges.ensure(static_cast<size_t>(n_tiles) * sizeof(int2), s));
+  tile_sort_kernel<<<blocks, kTileSortWarps * 32, 0, s>>>(
+      bb.tile_end.as<int>(), nullptr, nullptr, n_tiles, bb.capacity,
+      bb.stats.as<unsigned long long>(), bb.list.as<uint32_t>(), bb.ranges.as<int2>());
   return check_cuda(cudaGetLastError(), "tile_sort_kernel");
 }
 
 }  // namespace
+
+bool direct_binning_supported(const Geometry& g) {
+  return g.n_tiles() > 0 && g.n_tiles() <= kSmallScanMax;
+}
+
+int direct_layout(BinBuffers& bb, const Geometry& g, bool after_scatter, cudaStream_t s) {
+  const int64_t n_tiles = g.n_tiles();
+  if (!direct_binning_supported(g)) return set_error(-1, "direct binning needs at most 8192 tiles");
+  RTGS_TRY(bb.seg.ensure(static_cast<size_t>(n_tiles) * sizeof(int2), s));
+  const int64_t list_cap = static_cast<int64_t>(bb.list.bytes / sizeof(uint32_t));
+  layout_kernel<<<1, kSmallScanThreads, 0, s>>>(
+      after_scatter ? bb.tile_end.as<int>() : nullptr, bb.tile_count.as<int>(),
+      static_cast<int>(n_tiles), static_cast<int>(list_cap < INT32_MAX ? list_cap : INT32_MAX),
+      bb.seg.as<int2>());
+  if (!after_scatter) bb.counts_cleared = true;  // the kernel zeroes the fill counters
+  return check_cuda(cudaGetLastError(), "layout_kernel");
+}
+
+int direct_sort(BinBuffers& bb, const Geometry& g, cudaStream_t s) {
+  const int64_t n_tiles = g.n_tiles();
+  RTGS_TRY(bb.ranges.ensure(static_cast<size_t>(n_tiles) * sizeof(int2), s));
+  bb.presorted = false;
+  const unsigned blocks = static_cast<unsigned>((n_tiles + kTileSortWarps - 1) / kTileSortWarps);
+  tile_sort_kernel<<<blocks, kTileSortWarps * 32, 0, s>>>(
+      nullptr, bb.seg.as<int2>(), bb.tile_count.as<int>(), n_tiles,
+      static_cast<int64_t>(bb.list.bytes / sizeof(uint32_t)), bb.stats.as<unsigned long long>(),
+      bb.list.as<uint32_t>(), bb.ranges.as<int2>());
+  return check_cuda(cudaGetLastError(), "tile_sort_kernel");
+}
 
 int key_bits_for(int64_t n_tiles) {
   int b = 1;

@@ -54,7 +54,7 @@ void DevBuf::release() {
 
 void BinBuffers::release() {
   for (DevBuf* b : {&records, &weights, &spans, &counts, &offsets, &list, &tile_count, &tile_end,
-                    &entries[0], &entries[1], &ranges, &partials, &partial_d, &cub_temp,
+                    &entries[0], &entries[1], &ranges, &seg, &partials, &partial_d, &cub_temp,
                     &sort_counts, &stats}) {
     b->release();
   }
@@ -337,25 +337,26 @@ int rtgs2d_arena_copy_binning(const rtgs2d_arena* arena, int64_t max_entries, ui
     RTGS_CUDA(cudaStreamSynchronize(s), "copy binning sync");
     for (int64_t i = 0; i < ne; ++i) ids[static_cast<size_t>(i)] = static_cast<uint32_t>(packed[static_cast<size_t>(i)]);
   } else {
-    std::vector<int32_t> tend(static_cast<size_t>(nt));
+    // List path: each tile's ids sit in list[ranges[t]) in ascending order (the tile sort).
+    std::vector<uint32_t> list(static_cast<size_t>(ne), 0);
     if (ne > 0) {
-      RTGS_CUDA(cudaMemcpyAsync(ids.data(), bb.list.ptr, ne * sizeof(uint32_t), cudaMemcpyDeviceToHost, s),
+      RTGS_CUDA(cudaMemcpyAsync(list.data(), bb.list.ptr, ne * sizeof(uint32_t), cudaMemcpyDeviceToHost, s),
                 "copy list");
     }
+    std::vector<int32_t> r(static_cast<size_t>(2 * nt), 0);
     if (nt > 0) {
-      RTGS_CUDA(cudaMemcpyAsync(tend.data(), bb.tile_end.ptr, nt * sizeof(int32_t), cudaMemcpyDeviceToHost, s),
-                "copy tile ends");
+      RTGS_CUDA(cudaMemcpyAsync(r.data(), bb.ranges.ptr, nt * 2 * sizeof(int32_t), cudaMemcpyDeviceToHost, s),
+                "copy ranges");
     }
     RTGS_CUDA(cudaStreamSynchronize(s), "copy binning sync");
+    int64_t at = 0;  // repack tile by tile, so ranges index the returned ids
     for (int64_t t = 0; t < nt; ++t) {
-      int32_t a = t == 0 ? 0 : tend[static_cast<size_t>(t - 1)];
-      int32_t b = tend[static_cast<size_t>(t)];
-      a = a < ne ? a : static_cast<int32_t>(ne);
-      b = b < ne ? b : static_cast<int32_t>(ne);
-      if (b > a) {  // already ascending inside the tile (the device tile sort)
-        rng[static_cast<size_t>(2 * t)] = a;
-        rng[static_cast<size_t>(2 * t + 1)] = b;
-      }
+      int32_t a0 = r[static_cast<size_t>(2 * t)], a1 = r[static_cast<size_t>(2 * t + 1)];
+      a0 = a0 < ne ? a0 : static_cast<int32_t>(ne);
+      a1 = a1 < ne ? a1 : static_cast<int32_t>(ne);
+      rng[static_cast<size_t>(2 * t)] = static_cast<int32_t>(at);
+      for (int32_t k = a0; k < a1 && at < ne; ++k) ids[static_cast<size_t>(at++)] = list[static_cast<size_t>(k)];
+      rng[static_cast<size_t>(2 * t + 1)] = static_cast<int32_t>(at);
     }
   }
   if (gids) {

@@ -51,6 +51,13 @@ struct rtgs2d_fit {
   int64_t last_entries = 0, last_pairs = 0;
   int64_t retries = 0;  // chunks re-run after an entry-capacity overflow or a long tile list
   bool use_radix = false;  // some tile list exceeded the shared-memory sort: bin by radix sort
+  bool direct_enabled = true;  // direct placement of later iterations' ids (rtgs2d_fit_set_graphs off
+                               //   does not change it; see direct_chunk)
+  bool direct_retry = false;   // the current chunk overflowed a segment: re-run it by scatter
+  int64_t segment_retries = 0;
+  cudaStream_t side_stream = nullptr;  // segment layout beside the raster
+  cudaEvent_t fork_event = nullptr;
+  cudaEvent_t join_event = nullptr;
   bool have_targets = false, have_raw = false;
   // per-iteration constants of the current chunk, and the replayable chunks
   DevBuf iter_table;                  // IterScalars[kChunk]
@@ -188,6 +195,31 @@ int ensure_events(rtgs2d_fit* f, size_t need) {
 
 bool coverage(const rtgs2d_fit* f) { return f->opt.mask_coverage_weight > 0.0; }
 
+// Direct placement for this chunk: not on the radix path, at most 8192 tiles, and not right after
+// a chunk that overflowed a tile segment (that chunk re-runs with the scatter binning).
+bool direct_chunk(const rtgs2d_fit* f) {
+  return f->direct_enabled && !f->direct_retry && !f->use_radix && direct_binning_supported(f->geo);
+}
+
+// The stream and events that run the segment layout beside the raster.
+int ensure_side_stream(rtgs2d_fit* f) {
+  if (!f->side_stream) {
+    RTGS_CUDA(cudaStreamCreateWithFlags(&f->side_stream, cudaStreamNonBlocking), "side stream");
+  }
+  if (!f->fork_event) RTGS_CUDA(cudaEventCreateWithFlags(&f->fork_event, cudaEventDisableTiming), "fork event");
+  if (!f->join_event) RTGS_CUDA(cudaEventCreateWithFlags(&f->join_event, cudaEventDisableTiming), "join event");
+  return 0;
+}
+
+// The list holds the direct segments: entries + a quarter + 8 slots per tile, with headroom.
+int ensure_segment_room(rtgs2d_fit* f, cudaStream_t s) {
+  if (!direct_binning_supported(f->geo)) return 0;
+  const int64_t cap = f->bb.capacity;
+  const size_t want = static_cast<size_t>(cap + cap / 4 + 16 * f->geo.n_tiles()) * sizeof(uint32_t);
+  RTGS_TRY(f->bb.seg.ensure(static_cast<size_t>(f->geo.n_tiles()) * sizeof(int2), s));
+  return f->bb.list.ensure(want, s);
+}
+
 const uint8_t* active_rows(const rtgs2d_fit* f) {
   return f->use_active ? f->active.as<uint8_t>() : nullptr;
 }
@@ -269,9 +301,10 @@ FitRasterArgs raster_args(rtgs2d_fit* f) {
 std::vector<uintptr_t> chunk_key(const rtgs2d_fit* f, int64_t chunk) {
   const BinBuffers& bb = f->bb;
   std::vector<uintptr_t> k = {static_cast<uintptr_t>(chunk), static_cast<uintptr_t>(f->use_radix),
-                              static_cast<uintptr_t>(bb.capacity), static_cast<uintptr_t>(f->use_active)};
+                              static_cast<uintptr_t>(bb.capacity), static_cast<uintptr_t>(f->use_active),
+                              static_cast<uintptr_t>(direct_chunk(f))};
   for (const DevBuf* b : {&bb.records, &bb.weights, &bb.spans, &bb.counts, &bb.offsets, &bb.list,
-                          &bb.tile_count, &bb.tile_end, &bb.entries[0], &bb.entries[1], &bb.ranges,
+                          &bb.tile_count, &bb.tile_end, &bb.seg, &bb.entries[0], &bb.entries[1], &bb.ranges,
                           &bb.partials, &bb.partial_d, &bb.cub_temp, &bb.sort_counts, &bb.stats,
                           &f->raw, &f->m1, &f->m2, &f->targets, &f->mask, &f->view_scale,
                           &f->tile_loss, &f->log, &f->iter_table, &f->active}) {
@@ -296,17 +329,36 @@ int enqueue_chunk(rtgs2d_fit* f, int64_t chunk, cudaStream_t s, cudaEvent_t* ev,
   };
   RTGS_TRY(launch_project_raw(bb, f->geo, f->raw.as<float>(), f->m, f->n, true, active_rows(f),
                               coverage(f), s));
+  // Binning: the chunk's first iteration scatters the projection's entries; with direct placement
+  // (direct_chunk), every later projection (fused into Adam) writes its ids straight into tile
+  // segments sized from the previous binning, and the binning is just the tile sort.
+  // The layout of the next segments runs on the side stream beside the raster and joins before
+  // Adam (the projection that fills them).
+  const bool direct = direct_chunk(f);
+  if (direct) RTGS_TRY(ensure_side_stream(f));
   for (int64_t k = 0; k < chunk; ++k) {
     cudaEvent_t* e = ev ? ev + 4 * k : nullptr;
     if (e) RTGS_CUDA(record(e[0]), "event record");
-    RTGS_TRY(bin_entries_async(bb, f->geo, f->m, f->use_radix, s));
+    if (direct && k > 0) {
+      RTGS_TRY(direct_sort(bb, f->geo, s));
+    } else {
+      RTGS_TRY(bin_entries_async(bb, f->geo, f->m, f->use_radix, s));
+    }
+    const bool layout = direct && k + 1 < chunk;
+    if (layout) {
+      RTGS_CUDA(cudaEventRecord(f->fork_event, s), "fork record");
+      RTGS_CUDA(cudaStreamWaitEvent(f->side_stream, f->fork_event, 0), "fork wait");
+      RTGS_TRY(direct_layout(bb, f->geo, k == 0, f->side_stream));
+      RTGS_CUDA(cudaEventRecord(f->join_event, f->side_stream), "join record");
+    }
     if (e) RTGS_CUDA(record(e[1]), "event record");
     RTGS_TRY(launch_raster_fit(bb, f->geo, kCutoff, fa, true, s));
     if (e) RTGS_CUDA(record(e[2]), "event record");
+    if (layout) RTGS_CUDA(cudaStreamWaitEvent(s, f->join_event, 0), "join wait");
     RTGS_TRY(launch_adam_fit(bb, f->geo, f->m, f->n, f->raw.as<float>(), f->m1.as<float>(),
                              f->m2.as<float>(), f->iter_table.as<IterScalars>(),
                              static_cast<int>(k), lg, k + 1 < chunk, active_rows(f), coverage(f),
-                             s));
+                             layout ? bb.seg.as<int2>() : nullptr, s));
     if (e) RTGS_CUDA(record(e[3]), "event record");
   }
   return 0;
@@ -460,6 +512,9 @@ int rtgs2d_fit_destroy(rtgs2d_fit* fit) {
   fit->release_events();
   fit->release_graphs();
   if (fit->capture_stream) cudaStreamDestroy(fit->capture_stream);
+  if (fit->side_stream) cudaStreamDestroy(fit->side_stream);
+  if (fit->fork_event) cudaEventDestroy(fit->fork_event);
+  if (fit->join_event) cudaEventDestroy(fit->join_event);
   if (fit->host_table) cudaFreeHost(fit->host_table);
   delete fit;
   if (prev != dev) cudaSetDevice(prev);
@@ -564,6 +619,7 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
     RTGS_TRY(project_and_bin(f, s));
     RTGS_TRY(ensure_entry_capacity(bb, f->last_entries + f->last_entries / 2 + 4096, coverage(f), s));
   }
+  RTGS_TRY(ensure_segment_room(f, s));
   int64_t remaining = t_max - f->step < n_iterations ? t_max - f->step : n_iterations;
   while (remaining > 0) {
     const int64_t chunk = remaining < kChunk ? remaining : kChunk;
@@ -603,7 +659,7 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
               "iteration table upload");
     RTGS_TRY(snapshot(f, true, s));
     RTGS_CUDA(cudaMemsetAsync(bb.stats.as<unsigned long long>() + kStatPairsTotal, 0,
-                              3 * sizeof(unsigned long long), s),
+                              (kStatSlots - kStatPairsTotal) * sizeof(unsigned long long), s),
               "reset chunk stats");
     RTGS_TRY(run_chunk(f, chunk, s));
     RTGS_CUDA(cudaMemcpyAsync(bb.host_stats, bb.stats.ptr, kStatSlots * sizeof(unsigned long long),
@@ -612,7 +668,8 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
     RTGS_CUDA(cudaStreamSynchronize(s), "chunk sync");
     const int64_t max_entries = static_cast<int64_t>(bb.host_stats[kStatMaxEntries]);
     const bool long_tile = !f->use_radix && bb.host_stats[kStatLongTile] > 0;
-    if (max_entries > bb.capacity || long_tile) {
+    const bool seg_full = bb.host_stats[kStatSegOverflow] > 0;
+    if (max_entries > bb.capacity || long_tile || seg_full) {
       // Entries were dropped in this chunk: roll back and re-run it with room for them.
       if (max_entries > INT32_MAX) return set_error(RTGS2D_ERR_CAPACITY, "more than 2^31 tile entries");
       RTGS_TRY(snapshot(f, false, s));
@@ -621,11 +678,17 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
       f->log_iters.resize(logs0);
       f->retries += 1;
       if (long_tile) f->use_radix = true;  // a tile list too long for the tile sort
+      if (seg_full) {                      // a tile segment too short: this chunk bins by scatter
+        f->direct_retry = true;
+        f->segment_retries += 1;
+      }
       if (max_entries > bb.capacity) {
         RTGS_TRY(ensure_entry_capacity(bb, max_entries + max_entries / 2 + 4096, coverage(f), s));
+        RTGS_TRY(ensure_segment_room(f, s));
       }
       continue;
     }
+    f->direct_retry = false;
     f->last_entries = static_cast<int64_t>(bb.host_stats[kStatLastEntries]);
     f->last_pairs = static_cast<int64_t>(bb.host_stats[kStatLastPairs]);
     const double chunk_pairs = static_cast<double>(bb.host_stats[kStatPairsTotal]);

@@ -50,7 +50,8 @@ enum StatSlot : int {
   kStatLongTile = 4,     // largest tile list longer than kSegSortMax since reset (0: none)
   kStatLastEntries = 5,  // entries of the last binned projection (copied by the binning)
   kStatLastPairs = 6,    // pairs of the last binned projection
-  kStatSlots = 7
+  kStatSegOverflow = 7,  // a direct placement found a tile segment full (its binning is invalid)
+  kStatSlots = 8
 };
 
 // Tile lists up to this length are sorted by the tile-sort kernel (one warp per tile, in shared
@@ -69,7 +70,8 @@ struct BinBuffers {
                       //   to zero by the scatter)
   DevBuf tile_end;    // int[n_tiles] inclusive scan of tile_count
   DevBuf entries[2];  // uint64[capacity] (tile key << 32 | gaussian id), radix-sort double buffer
-  DevBuf ranges;      // int2[n_tiles] [start, end) into the sorted entries
+  DevBuf ranges;      // int2[n_tiles] [start, end) of every tile in the list (or sorted entries)
+  DevBuf seg;         // int2[n_tiles] direct placement: (start, slots) of each tile's segment
   DevBuf partials;    // float[capacity][8] per (gaussian, tile) gradient moments
   DevBuf partial_d;   // float[capacity]   per (gaussian, tile) density-gradient moment
   DevBuf cub_temp;    // exclusive-scan temporaries
@@ -132,6 +134,16 @@ int check_long_tiles(BinBuffers& bb, const Geometry& g, cudaStream_t s);
 // the capacity are dropped and show up as stats[kStatMaxEntries] > capacity; a tile list longer
 // than kSegSortMax on the scatter path is flagged by the raster in stats[kStatLongTile].
 int bin_entries_async(BinBuffers& bb, const Geometry& g, int64_t m, bool radix, cudaStream_t s);
+// Direct placement (fit loop): a projection with ProjOut::seg set writes each gaussian id straight
+// into its tile's segment (slot from the tile's fill counter, bb.tile_count), sized from the
+// previous binning's counts with slack; a full segment sets stats[kStatSegOverflow].
+// direct_layout computes the segments from the last binning (after_scatter: from tile_end; else
+// from the fill counters, which it zeroes); direct_sort sorts the filled segments into
+// bb.ranges. Nothing but the next projection reads the layout, so it can run beside the raster.
+// Up to kSmallScanMax (8192) tiles.
+bool direct_binning_supported(const Geometry& g);
+int direct_layout(BinBuffers& bb, const Geometry& g, bool after_scatter, cudaStream_t s);
+int direct_sort(BinBuffers& bb, const Geometry& g, cudaStream_t s);
 // Allocate the entry-sized buffers (list, entries, partials[, partial_d]) for `capacity` entries.
 int ensure_entry_capacity(BinBuffers& bb, int64_t capacity, bool density, cudaStream_t s);
 // Zero per-tile counts before a projection (projection launchers call it).
@@ -195,9 +207,11 @@ struct LossLog {
 };
 // Adam step from the last raster's entry moments, with the constants of table[k]; with
 // project_next the updated parameters are also projected (records, spans, counts, offsets,
-// stats) for the next iteration's binning.
+// stats) for the next iteration's binning: entries for the scatter path, or with `seg` the ids
+// placed directly into the tile segments (see direct_layout).
 int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_view, float* raw,
                     float* m1, float* m2, const IterScalars* table, int k, const LossLog& lg,
-                    bool project_next, const uint8_t* active, bool density, cudaStream_t s);
+                    bool project_next, const uint8_t* active, bool density, const int2* seg,
+                    cudaStream_t s);
 
 }  // namespace rtgs2d

@@ -23,6 +23,8 @@ struct ProjOut {
   uint64_t* entries;          // null: count every entry; else emit (tile key << 32 | id) at
   int64_t cap;                //   each entry index below cap and count only those
   const uint8_t* active;      // null: every gaussian is live; else 0 = parked (not rendered)
+  const int2* seg;            // non-null: direct placement into tile segments (start, slots); the
+  uint32_t* list;             //   ids go to list, tile_count is the fill counter
   unsigned long long* stats;  // kStat* slots
   int tiles_x;
 };
@@ -60,6 +62,68 @@ __device__ __forceinline__ void for_each_span_tile(int64_t gid, int cnt, const T
       const int ty = ty0 + j / ntx;
       const int tx = tx0 + j % ntx;
       f(g, j, kb + ty * tiles_x + tx, pl);
+    }
+  }
+}
+
+// Direct placement of gaussian gid into the segments of the tiles of its span: slot = the tile's
+// fill counter before this entry, position = segment start + slot; a slot past the segment sets
+// stats[kStatSegOverflow] (the binning is then invalid and the caller re-bins). Small spans issue
+// all of a lane's counter atomics before any store, so their round trips overlap; longer spans
+// are walked by the whole warp. All lanes of the warp must call this.
+__device__ __forceinline__ void direct_place(int64_t gid, int cnt, const TileSpan& sp,
+                                             const ProjOut& o) {
+  if (cnt > 0 && cnt <= kSmallSpan) {
+    int slot[kSmallSpan];
+    int tx = sp.tx0, ty = sp.ty0;
+#pragma unroll
+    for (int j = 0; j < kSmallSpan; ++j) {
+      if (j < cnt) {
+        slot[j] = atomicAdd(&o.tile_count[sp.key_base + ty * o.tiles_x + tx], 1);
+        if (++tx == sp.tx0 + sp.ntx) {
+          tx = sp.tx0;
+          ++ty;
+        }
+      }
+    }
+    tx = sp.tx0;
+    ty = sp.ty0;
+#pragma unroll
+    for (int j = 0; j < kSmallSpan; ++j) {
+      if (j < cnt) {
+        const int2 sg = o.seg[sp.key_base + ty * o.tiles_x + tx];
+        if (slot[j] < sg.y) {
+          o.list[sg.x + slot[j]] = static_cast<uint32_t>(gid);
+        } else {
+          atomicMax(&o.stats[kStatSegOverflow], 1ull);
+        }
+        if (++tx == sp.tx0 + sp.ntx) {
+          tx = sp.tx0;
+          ++ty;
+        }
+      }
+    }
+  }
+  const int lane = threadIdx.x & 31;
+  unsigned big = __ballot_sync(0xffffffffu, cnt > kSmallSpan);
+  while (big) {
+    const int src = __ffs(big) - 1;
+    big &= big - 1;
+    const int c = __shfl_sync(0xffffffffu, cnt, src);
+    const int tx0 = __shfl_sync(0xffffffffu, sp.tx0, src);
+    const int ty0 = __shfl_sync(0xffffffffu, sp.ty0, src);
+    const int ntx = __shfl_sync(0xffffffffu, sp.ntx, src);
+    const int kb = __shfl_sync(0xffffffffu, sp.key_base, src);
+    const uint32_t g = static_cast<uint32_t>(__shfl_sync(0xffffffffu, static_cast<long long>(gid), src));
+    for (int j = lane; j < c; j += 32) {
+      const int t = kb + (ty0 + j / ntx) * o.tiles_x + tx0 + j % ntx;
+      const int sl = atomicAdd(&o.tile_count[t], 1);
+      const int2 sg = o.seg[t];
+      if (sl < sg.y) {
+        o.list[sg.x + sl] = g;
+      } else {
+        atomicMax(&o.stats[kStatSegOverflow], 1ull);
+      }
     }
   }
 }
@@ -120,6 +184,10 @@ __device__ __forceinline__ void project_tail(int64_t i, bool active, float mx, f
   wbase = __shfl_sync(0xffffffffu, wbase, 31);
   const int off = wbase + incl - cnt;
   if (active) o.offsets[i] = off;
+  if (o.seg) {  // direct placement (warp-uniform choice; all lanes reach this point)
+    direct_place(i, cnt, sp, o);
+    return;
+  }
   // Tile counts, and with o.entries the entries themselves (all lanes reach this point). Emitted,
   // only entries that fit the capacity are emitted and counted: the binning stays consistent, and
   // stats[kStatEntries] (all entries) tells the caller it overflowed.

@@ -222,7 +222,8 @@ int launch_finalize_conic(const BinBuffers& bb, int64_t m, const float* conics,
 
 int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_view, float* raw,
                     float* m1, float* m2, const IterScalars* table, int k, const LossLog& lg,
-                    bool project_next, const uint8_t* active, bool density, cudaStream_t s) {
+                    bool project_next, const uint8_t* active, bool density, const int2* seg,
+                    cudaStream_t s) {
   if (m == 0) return 0;
   ProjOut o{};
   const float* pd = density ? bb.partial_d.as<float>() : nullptr;
@@ -238,6 +239,8 @@ int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_
     o.entries = bb.entries[0].as<uint64_t>();
     o.cap = bb.capacity;
     o.active = active;
+    o.seg = seg;  // direct placement into the tile segments laid out by direct_layout
+    o.list = seg ? bb.list.as<uint32_t>() : nullptr;
     o.tiles_x = g.tiles_x;
     if (!bb.counts_cleared) {  // the scatter binning leaves both at zero; the radix path does not
       RTGS_TRY(reset_tile_counts(bb, g, s));

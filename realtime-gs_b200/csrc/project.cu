@@ -160,6 +160,8 @@ int prepare(BinBuffers& bb, const Geometry& g, int64_t m, bool want_weights, cud
   o->entries = nullptr;  // count only; a launcher that emits sets entries and cap
   o->cap = 0;
   o->active = nullptr;
+  o->seg = nullptr;  // direct placement is set up by the fit loop's Adam launcher only
+  o->list = nullptr;
   bb.entries_emitted = false;
   o->tiles_x = g.tiles_x;
   return 0;

@@ -54,9 +54,8 @@ struct RasterArgs {
   const TileSpan* spans;      // backward: entry index
   const int* offsets;         // backward: entry index
   const uint64_t* entries;    // radix path: sorted (tile key << 32 | gaussian id)
-  const int2* ranges;         // radix path: per-tile [start, end)
-  const uint32_t* list;       // scatter path: gaussian ids grouped by tile, ascending in a tile
-  const int* tile_end;        // scatter path: inclusive scan of per-tile counts
+  const int2* ranges;         // per-tile [start, end) into list (or entries on the radix path)
+  const uint32_t* list;       // list paths: gaussian ids grouped by tile, ascending in a tile
   int64_t cap;                // entry capacity (positions and entry indices at or past it are unused)
   int presorted;              // 1: radix path, 0: scatter path
   int height, width, tiles_x, tiles_per_view;
@@ -258,17 +257,8 @@ raster_kernel(const RasterArgs a) {
   const int sx0 = ox + sbx * L::kSubW, sy0 = oy + sby * L::kSubH;  // this warp's sub-block
   const int sub_col = lane & 7, sub_row0 = PPT * (lane >> 3);
   const int64_t view_base = static_cast<int64_t>(view) * a.height * a.width;
-  int2 range;
-  if (a.presorted) {
-    range = a.ranges[tile];
-  } else {
-    // Scatter path: the tile's ids, sorted by the tile-sort kernel, sit in list[start, end).
-    int64_t start = tile == 0 ? 0 : a.tile_end[tile - 1];
-    int64_t end = a.tile_end[tile];
-    start = start < a.cap ? start : a.cap;
-    end = end < a.cap ? end : a.cap;
-    range = make_int2(static_cast<int>(start), static_cast<int>(end));
-  }
+  // The tile's ids in ascending order: list[range) (tile sort) or the sorted entries (radix path).
+  const int2 range = a.ranges[tile];
   // Stage records [base, base + n) of this tile's list into shared memory.
   auto stage = [&](int base, int n, bool with_entry) {
     for (int j = threadIdx.x; j < n; j += L::kThreads) {
@@ -582,7 +572,6 @@ RasterArgs base_args(const BinBuffers& bb, const Geometry& g, float cutoff) {
   a.entries = bb.entries[bb.sorted_sel].as<uint64_t>();
   a.ranges = bb.ranges.as<int2>();
   a.list = bb.list.as<uint32_t>();
-  a.tile_end = bb.tile_end.as<int>();
   a.cap = bb.capacity;
   a.presorted = bb.presorted ? 1 : 0;
   a.height = g.height;
