@@ -249,6 +249,24 @@ RTGS2D_API int rtgs2d_fit_write_rows(rtgs2d_fit* fit, const int64_t* rows, int64
 RTGS2D_API int rtgs2d_fit_set_graphs(rtgs2d_fit* fit, int32_t enable);
 RTGS2D_API int rtgs2d_fit_chunk_counts(const rtgs2d_fit* fit, int64_t* graph_chunks,
                                        int64_t* eager_chunks);
+/* No reference counterpart: how the fit loop bins (gaussian, tile) entries. Every mode gives the
+ * same per-tile lists, so the same results bit for bit.
+ *   RTGS2D_BINNING_AUTO     the first iteration of a chunk scatters its entries into tile lists;
+ *                           each later projection writes its ids straight into per-tile segments
+ *                           sized from the previous binning with slack (count + count/4 + 8), and
+ *                           the binning is the per-tile sort. A segment that fills up invalidates
+ *                           the chunk, which re-runs with SCATTER. Frames of up to 8192 tiles;
+ *                           larger ones use SCATTER.
+ *   RTGS2D_BINNING_SCATTER  every iteration: entries, tile-count scan, scatter, per-tile sort.
+ *   RTGS2D_BINNING_RADIX    every iteration: entries, radix sort by (tile, id), tile ranges.
+ *   RTGS2D_BINNING_TIGHT    AUTO with segments of exactly the previous counts (no slack): any tile
+ *                           that gains an entry overflows. Exercises the overflow re-run.
+ * Re-runs after an overflow count in rtgs2d_fit_capacity's `retries`. */
+#define RTGS2D_BINNING_AUTO 0
+#define RTGS2D_BINNING_SCATTER 1
+#define RTGS2D_BINNING_RADIX 2
+#define RTGS2D_BINNING_TIGHT 3
+RTGS2D_API int rtgs2d_fit_set_binning(rtgs2d_fit* fit, int32_t mode);
 RTGS2D_API int rtgs2d_fit_stage_times(const rtgs2d_fit* fit, double* bin_ms, double* raster_ms,
                                       double* adam_ms, int64_t* iterations_timed,
                                       double* pairs_timed);

@@ -287,12 +287,13 @@ small_inclusive_scan_kernel(const int* __restrict__ in, int* __restrict__ out, i
 }
 
 // Direct placement layout for the next binning: tile t gets a segment of count + 8 + count / 4
-// slots (count = this binning's entries of the tile), segments packed in tile order and clipped to
-// the list capacity. Counts come from the scan (tile_end, after a scatter) or from the fill
-// counters of a direct placement, which are then zeroed for the next one. One block.
+// slots (count = this binning's entries of the tile; exactly count without slack), segments packed
+// in tile order and clipped to the list capacity. Counts come from the scan (tile_end, after a
+// scatter) or from the fill counters of a direct placement, which are then zeroed for the next
+// one. One block.
 __global__ void __launch_bounds__(kSmallScanThreads)
 layout_kernel(const int* __restrict__ tile_end, int* __restrict__ fill, int n_tiles,
-              int list_cap, int2* __restrict__ seg) {
+              int list_cap, bool slack, int2* __restrict__ seg) {
   __shared__ int s_warp[kSmallScanThreads / 32];
   const int per = (n_tiles + kSmallScanThreads - 1) / kSmallScanThreads;
   const int i0 = threadIdx.x * per;
@@ -300,7 +301,7 @@ layout_kernel(const int* __restrict__ tile_end, int* __restrict__ fill, int n_ti
   auto count = [&](int t) {
     return tile_end ? tile_end[t] - (t > 0 ? tile_end[t - 1] : 0) : fill[t];
   };
-  auto seg_cap = [](int c) { return c + 8 + (c >> 2); };
+  auto seg_cap = [slack](int c) { return slack ? c + 8 + (c >> 2) : c; };
   int sum = 0;
   for (int t = i0; t < i1; ++t) sum += seg_cap(count(t));
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -417,14 +418,14 @@ bool direct_binning_supported(const Geometry& g) {
   return g.n_tiles() > 0 && g.n_tiles() <= kSmallScanMax;
 }
 
-int direct_layout(BinBuffers& bb, const Geometry& g, bool after_scatter, cudaStream_t s) {
+int direct_layout(BinBuffers& bb, const Geometry& g, bool after_scatter, bool slack, cudaStream_t s) {
   const int64_t n_tiles = g.n_tiles();
   if (!direct_binning_supported(g)) return set_error(-1, "direct binning needs at most 8192 tiles");
   RTGS_TRY(bb.seg.ensure(static_cast<size_t>(n_tiles) * sizeof(int2), s));
   const int64_t list_cap = static_cast<int64_t>(bb.list.bytes / sizeof(uint32_t));
   layout_kernel<<<1, kSmallScanThreads, 0, s>>>(
       after_scatter ? bb.tile_end.as<int>() : nullptr, bb.tile_count.as<int>(),
-      static_cast<int>(n_tiles), static_cast<int>(list_cap < INT32_MAX ? list_cap : INT32_MAX),
+      static_cast<int>(n_tiles), static_cast<int>(list_cap < INT32_MAX ? list_cap : INT32_MAX), slack,
       bb.seg.as<int2>());
   if (!after_scatter) bb.counts_cleared = true;  // the kernel zeroes the fill counters
   return check_cuda(cudaGetLastError(), "layout_kernel");

@@ -51,8 +51,7 @@ struct rtgs2d_fit {
   int64_t last_entries = 0, last_pairs = 0;
   int64_t retries = 0;  // chunks re-run after an entry-capacity overflow or a long tile list
   bool use_radix = false;  // some tile list exceeded the shared-memory sort: bin by radix sort
-  bool direct_enabled = true;  // direct placement of later iterations' ids (rtgs2d_fit_set_graphs off
-                               //   does not change it; see direct_chunk)
+  int32_t binning = RTGS2D_BINNING_AUTO;  // rtgs2d_fit_set_binning
   bool direct_retry = false;   // the current chunk overflowed a segment: re-run it by scatter
   int64_t segment_retries = 0;
   cudaStream_t side_stream = nullptr;  // segment layout beside the raster
@@ -195,10 +194,14 @@ int ensure_events(rtgs2d_fit* f, size_t need) {
 
 bool coverage(const rtgs2d_fit* f) { return f->opt.mask_coverage_weight > 0.0; }
 
+// Bin by radix sort: chosen by the caller, or after a tile list too long for the tile sort.
+bool radix(const rtgs2d_fit* f) { return f->use_radix || f->binning == RTGS2D_BINNING_RADIX; }
+
 // Direct placement for this chunk: not on the radix path, at most 8192 tiles, and not right after
 // a chunk that overflowed a tile segment (that chunk re-runs with the scatter binning).
 bool direct_chunk(const rtgs2d_fit* f) {
-  return f->direct_enabled && !f->direct_retry && !f->use_radix && direct_binning_supported(f->geo);
+  const bool mode = f->binning == RTGS2D_BINNING_AUTO || f->binning == RTGS2D_BINNING_TIGHT;
+  return mode && !f->direct_retry && !radix(f) && direct_binning_supported(f->geo);
 }
 
 // The stream and events that run the segment layout beside the raster.
@@ -300,7 +303,7 @@ FitRasterArgs raster_args(rtgs2d_fit* f) {
 // binning path and the address and size of every buffer its launches use.
 std::vector<uintptr_t> chunk_key(const rtgs2d_fit* f, int64_t chunk) {
   const BinBuffers& bb = f->bb;
-  std::vector<uintptr_t> k = {static_cast<uintptr_t>(chunk), static_cast<uintptr_t>(f->use_radix),
+  std::vector<uintptr_t> k = {static_cast<uintptr_t>(chunk), static_cast<uintptr_t>(radix(f)),
                               static_cast<uintptr_t>(bb.capacity), static_cast<uintptr_t>(f->use_active),
                               static_cast<uintptr_t>(direct_chunk(f))};
   for (const DevBuf* b : {&bb.records, &bb.weights, &bb.spans, &bb.counts, &bb.offsets, &bb.list,
@@ -342,13 +345,13 @@ int enqueue_chunk(rtgs2d_fit* f, int64_t chunk, cudaStream_t s, cudaEvent_t* ev,
     if (direct && k > 0) {
       RTGS_TRY(direct_sort(bb, f->geo, s));
     } else {
-      RTGS_TRY(bin_entries_async(bb, f->geo, f->m, f->use_radix, s));
+      RTGS_TRY(bin_entries_async(bb, f->geo, f->m, radix(f), s));
     }
     const bool layout = direct && k + 1 < chunk;
     if (layout) {
       RTGS_CUDA(cudaEventRecord(f->fork_event, s), "fork record");
       RTGS_CUDA(cudaStreamWaitEvent(f->side_stream, f->fork_event, 0), "fork wait");
-      RTGS_TRY(direct_layout(bb, f->geo, k == 0, f->side_stream));
+      RTGS_TRY(direct_layout(bb, f->geo, k == 0, f->binning != RTGS2D_BINNING_TIGHT, f->side_stream));
       RTGS_CUDA(cudaEventRecord(f->join_event, f->side_stream), "join record");
     }
     if (e) RTGS_CUDA(record(e[1]), "event record");
@@ -667,7 +670,7 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
               "chunk stats readback");
     RTGS_CUDA(cudaStreamSynchronize(s), "chunk sync");
     const int64_t max_entries = static_cast<int64_t>(bb.host_stats[kStatMaxEntries]);
-    const bool long_tile = !f->use_radix && bb.host_stats[kStatLongTile] > 0;
+    const bool long_tile = !radix(f) && bb.host_stats[kStatLongTile] > 0;
     const bool seg_full = bb.host_stats[kStatSegOverflow] > 0;
     if (max_entries > bb.capacity || long_tile || seg_full) {
       // Entries were dropped in this chunk: roll back and re-run it with room for them.
@@ -766,6 +769,15 @@ int rtgs2d_fit_write_rows(rtgs2d_fit* f, const int64_t* rows, int64_t n_rows, co
       f->m, rows, n_rows, xy_raw, diag_raw, off_raw, color_raw, weight_raw, f->raw.as<float>(),
       f->m1.as<float>(), f->m2.as<float>());
   return check_cuda(cudaGetLastError(), "write_rows_kernel");
+}
+
+int rtgs2d_fit_set_binning(rtgs2d_fit* f, int32_t mode) {
+  RTGS_TRY(check_fit(f));
+  if (mode < RTGS2D_BINNING_AUTO || mode > RTGS2D_BINNING_TIGHT) {
+    return set_error(RTGS2D_ERR_INVALID, "unknown binning mode");
+  }
+  f->binning = mode;
+  return RTGS2D_OK;
 }
 
 int rtgs2d_fit_set_graphs(rtgs2d_fit* f, int32_t enable) {

@@ -138,11 +138,11 @@ int bin_entries_async(BinBuffers& bb, const Geometry& g, int64_t m, bool radix, 
 // into its tile's segment (slot from the tile's fill counter, bb.tile_count), sized from the
 // previous binning's counts with slack; a full segment sets stats[kStatSegOverflow].
 // direct_layout computes the segments from the last binning (after_scatter: from tile_end; else
-// from the fill counters, which it zeroes); direct_sort sorts the filled segments into
-// bb.ranges. Nothing but the next projection reads the layout, so it can run beside the raster.
-// Up to kSmallScanMax (8192) tiles.
+// from the fill counters, which it zeroes; slack: count + count/4 + 8 slots, else count);
+// direct_sort sorts the filled segments into bb.ranges. Nothing but the next projection reads the
+// layout, so it can run beside the raster. Up to kSmallScanMax (8192) tiles.
 bool direct_binning_supported(const Geometry& g);
-int direct_layout(BinBuffers& bb, const Geometry& g, bool after_scatter, cudaStream_t s);
+int direct_layout(BinBuffers& bb, const Geometry& g, bool after_scatter, bool slack, cudaStream_t s);
 int direct_sort(BinBuffers& bb, const Geometry& g, cudaStream_t s);
 // Allocate the entry-sized buffers (list, entries, partials[, partial_d]) for `capacity` entries.
 int ensure_entry_capacity(BinBuffers& bb, int64_t capacity, bool density, cudaStream_t s);

@@ -86,6 +86,7 @@ _SIGNATURES = {
     "rtgs2d_fit_history": ([_vp, _c_int64, _vp, _vp, ctypes.POINTER(_c_int64)], ctypes.c_int),
     "rtgs2d_fit_set_profiling": ([_vp, ctypes.c_int32], ctypes.c_int),
     "rtgs2d_fit_set_graphs": ([_vp, ctypes.c_int32], ctypes.c_int),
+    "rtgs2d_fit_set_binning": ([_vp, ctypes.c_int32], ctypes.c_int),
     "rtgs2d_fit_set_active": ([_vp, _vp, _vp], ctypes.c_int),
     "rtgs2d_fit_write_rows": ([_vp, _vp, _c_int64, _vp, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
     "rtgs2d_fit_chunk_counts": ([_vp, ctypes.POINTER(_c_int64), ctypes.POINTER(_c_int64)], ctypes.c_int),

@@ -255,6 +255,36 @@ def test_graph_replay_matches_eager_chunks_bitwise():
         assert np.array_equal(h_e[0], other_h[0]) and np.array_equal(h_e[1], other_h[1])
 
 
+def test_binning_modes_give_identical_fits():
+    """Direct placement into per-tile segments, scatter and radix binning build the same sorted
+    tile lists, so fits end bitwise equal (history included). Tight segments (no slack) overflow
+    as soon as a tile gains an entry: those chunks re-run with scatter binning and still end equal;
+    a multi-view engine (two views' tiles in one binning) covers the view offsets of the segments."""
+    h, w, n, iters = 96, 128, 600, 200
+    src = synthetic.source_gaussians(12, 40, h, w, (3.0, 12.0))
+    target = (orender.render(src.xy, src.chol, src.color, src.weight, h, w)).clamp(0, 1).to(DEV)
+    init = synthetic.fit_init(12, n, h, w)
+    raw = raw_from_gaussians(*(x.to(DEV) for x in (init.xy, init.chol, init.color, init.weight)), h, w)
+    for views in (1, 2):
+        targets = torch.stack([target, target.flip(1)][:views])
+        raws = {k: torch.stack([v] * views) for k, v in raw.items()}
+        results = {}
+        for mode in ("auto", "scatter", "radix", "tight"):
+            with FitEngine(views, n, h, w, lr=1e-2, iterations=iters, log_every=25, device=DEV) as engine:
+                engine.set_binning(mode)
+                engine.set_targets(targets)
+                engine.set_raw(raws)
+                engine.run(iters)
+                results[mode] = (engine.params(), engine.history(), engine.capacity()[1])
+        p_a, h_a, _ = results["auto"]
+        assert results["tight"][2] > 0  # overflowing segments re-ran chunks
+        for mode in ("scatter", "radix", "tight"):
+            p_m, h_m, _ = results[mode]
+            for a, b in zip(p_a, p_m):
+                assert torch.equal(a, b), mode
+            assert np.array_equal(h_a[0], h_m[0]) and np.array_equal(h_a[1], h_m[1]), mode
+
+
 def test_pooled_engine_reuse_is_stateless():
     """Fits that repeat a configuration reuse a pooled engine (buffers and captured graphs); a fit
     run on a reused engine, after a fit of another image, ends bitwise where a fresh engine ends."""
