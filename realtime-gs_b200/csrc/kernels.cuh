@@ -68,38 +68,43 @@ __device__ __forceinline__ void for_each_span_tile(int64_t gid, int cnt, const T
 
 // Direct placement of gaussian gid into the segments of the tiles of its span: slot = the tile's
 // fill counter before this entry, position = segment start + slot; a slot past the segment sets
-// stats[kStatSegOverflow] (the binning is then invalid and the caller re-bins). Small spans issue
-// all of a lane's counter atomics before any store, so their round trips overlap; longer spans
-// are walked by the whole warp. All lanes of the warp must call this.
-__device__ __forceinline__ void direct_place(int64_t gid, int cnt, const TileSpan& sp,
-                                             const ProjOut& o) {
-  if (cnt > 0 && cnt <= kSmallSpan) {
-    int slot[kSmallSpan];
-    int tx = sp.tx0, ty = sp.ty0;
+// stats[kStatSegOverflow] (the binning is then invalid and the caller re-bins). Two halves, so the
+// caller can overlap their round trips with its own: direct_reserve issues a small span's counter
+// atomics and segment loads (nothing waits on them yet); direct_commit stores the ids, and walks
+// spans longer than kSmallSpan with the whole warp (all lanes of the warp must call it).
+struct DirectSlots {
+  int slot[kSmallSpan];
+  int2 seg[kSmallSpan];
+};
+
+__device__ __forceinline__ void direct_reserve(int cnt, const TileSpan& sp, const ProjOut& o,
+                                               DirectSlots& d) {
+  if (cnt <= 0 || cnt > kSmallSpan) return;
+  int tx = sp.tx0, ty = sp.ty0;
 #pragma unroll
-    for (int j = 0; j < kSmallSpan; ++j) {
-      if (j < cnt) {
-        slot[j] = atomicAdd(&o.tile_count[sp.key_base + ty * o.tiles_x + tx], 1);
-        if (++tx == sp.tx0 + sp.ntx) {
-          tx = sp.tx0;
-          ++ty;
-        }
+  for (int j = 0; j < kSmallSpan; ++j) {
+    if (j < cnt) {
+      const int t = sp.key_base + ty * o.tiles_x + tx;
+      d.slot[j] = atomicAdd(&o.tile_count[t], 1);
+      d.seg[j] = o.seg[t];
+      if (++tx == sp.tx0 + sp.ntx) {
+        tx = sp.tx0;
+        ++ty;
       }
     }
-    tx = sp.tx0;
-    ty = sp.ty0;
+  }
+}
+
+__device__ __forceinline__ void direct_commit(int64_t gid, int cnt, const TileSpan& sp,
+                                              const ProjOut& o, const DirectSlots& d) {
+  if (cnt > 0 && cnt <= kSmallSpan) {
 #pragma unroll
     for (int j = 0; j < kSmallSpan; ++j) {
       if (j < cnt) {
-        const int2 sg = o.seg[sp.key_base + ty * o.tiles_x + tx];
-        if (slot[j] < sg.y) {
-          o.list[sg.x + slot[j]] = static_cast<uint32_t>(gid);
+        if (d.slot[j] < d.seg[j].y) {
+          o.list[d.seg[j].x + d.slot[j]] = static_cast<uint32_t>(gid);
         } else {
           atomicMax(&o.stats[kStatSegOverflow], 1ull);
-        }
-        if (++tx == sp.tx0 + sp.ntx) {
-          tx = sp.tx0;
-          ++ty;
         }
       }
     }
@@ -163,6 +168,8 @@ __device__ __forceinline__ void project_tail(int64_t i, bool active, float mx, f
     if (o.weights) o.weights[i] = w;
     o.counts[i] = cnt;
   }
+  DirectSlots dslots;  // with direct placement its round trips overlap the offset reservation's
+  if (o.seg) direct_reserve(cnt, sp, o, dslots);
   const int lane = threadIdx.x & 31;
   int incl = cnt;
 #pragma unroll
@@ -185,7 +192,7 @@ __device__ __forceinline__ void project_tail(int64_t i, bool active, float mx, f
   const int off = wbase + incl - cnt;
   if (active) o.offsets[i] = off;
   if (o.seg) {  // direct placement (warp-uniform choice; all lanes reach this point)
-    direct_place(i, cnt, sp, o);
+    direct_commit(i, cnt, sp, o, dslots);
     return;
   }
   // Tile counts, and with o.entries the entries themselves (all lanes reach this point). Emitted,
