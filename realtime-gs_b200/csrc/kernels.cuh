@@ -239,28 +239,27 @@ __device__ __forceinline__ Moments gather_moments(const float4* __restrict__ par
   mo.sd = 0.f;
   if (cnt > 0 && cnt <= kSmallEntries) {
     const float4* p = partials + 2 * static_cast<int64_t>(off);
-    int j = 0;
-    // Four entries' loads in flight at a time; the additions keep the sequential entry order.
-    for (; j + 4 <= cnt; j += 4) {
+    // Four entries' loads in flight at a time (predicated past the count, so a gaussian with 1..4
+    // entries waits for one round trip); the additions keep the sequential entry order.
+    for (int j = 0; j < cnt; j += 4) {
       float4 v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = p[2 * j + u];
+      float vd[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        mo.s[0] += v[2 * u].x; mo.s[1] += v[2 * u].y; mo.s[2] += v[2 * u].z; mo.s[3] += v[2 * u].w;
-        mo.s[4] += v[2 * u + 1].x; mo.s[5] += v[2 * u + 1].y; mo.s[6] += v[2 * u + 1].z;
-        mo.s[7] += v[2 * u + 1].w;
+        const bool in = j + u < cnt;
+        v[2 * u] = in ? p[2 * (j + u)] : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[2 * u + 1] = in ? p[2 * (j + u) + 1] : make_float4(0.f, 0.f, 0.f, 0.f);
+        if constexpr (DEN) vd[u] = in ? partial_d[off + j + u] : 0.f;
       }
-      if constexpr (DEN) {
-        for (int u = 0; u < 4; ++u) mo.sd += partial_d[off + j + u];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (j + u < cnt) {
+          mo.s[0] += v[2 * u].x; mo.s[1] += v[2 * u].y; mo.s[2] += v[2 * u].z; mo.s[3] += v[2 * u].w;
+          mo.s[4] += v[2 * u + 1].x; mo.s[5] += v[2 * u + 1].y; mo.s[6] += v[2 * u + 1].z;
+          mo.s[7] += v[2 * u + 1].w;
+          if constexpr (DEN) mo.sd += vd[u];
+        }
       }
-    }
-    for (; j < cnt; ++j) {
-      const float4 p0 = p[2 * j];
-      const float4 p1 = p[2 * j + 1];
-      mo.s[0] += p0.x; mo.s[1] += p0.y; mo.s[2] += p0.z; mo.s[3] += p0.w;
-      mo.s[4] += p1.x; mo.s[5] += p1.y; mo.s[6] += p1.z; mo.s[7] += p1.w;
-      if constexpr (DEN) mo.sd += partial_d[off + j];
     }
   }
   const int lane = threadIdx.x & 31;
