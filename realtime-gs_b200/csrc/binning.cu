@@ -286,51 +286,86 @@ small_inclusive_scan_kernel(const int* __restrict__ in, int* __restrict__ out, i
   }
 }
 
-// Direct placement layout for the next binning: tile t gets a segment of count + 8 + count / 4
-// slots (count = this binning's entries of the tile; exactly count without slack), segments packed
-// in tile order and clipped to the list capacity. Counts come from the scan (tile_end, after a
-// scatter) or from the fill counters of a direct placement, which are then zeroed for the next
-// one. One block.
-__global__ void __launch_bounds__(kSmallScanThreads)
-layout_kernel(const int* __restrict__ tile_end, int* __restrict__ fill, int n_tiles,
-              int list_cap, bool slack, int2* __restrict__ seg) {
-  __shared__ int s_warp[kSmallScanThreads / 32];
-  const int per = (n_tiles + kSmallScanThreads - 1) / kSmallScanThreads;
-  const int i0 = threadIdx.x * per;
-  const int i1 = min(i0 + per, n_tiles);
-  auto count = [&](int t) {
-    return tile_end ? tile_end[t] - (t > 0 ? tile_end[t - 1] : 0) : fill[t];
-  };
-  auto seg_cap = [slack](int c) { return slack ? c + 8 + (c >> 2) : c; };
-  int sum = 0;
-  for (int t = i0; t < i1; ++t) sum += seg_cap(count(t));
+// Exclusive prefix of v over the block (kSmallScanThreads threads); *total gets the block sum.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int incl = sum;
+  int incl = v;
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) {
     const int y = __shfl_up_sync(0xffffffffu, incl, d);
     if (lane >= d) incl += y;
   }
+  __syncthreads();  // s_warp may still be read by a previous scan
   if (lane == 31) s_warp[warp] = incl;
   __syncthreads();
   if (warp == 0) {
-    const int v = s_warp[lane];
-    int x = v;
+    const int w = s_warp[lane];
+    int x = w;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
       const int y = __shfl_up_sync(0xffffffffu, x, d);
       if (lane >= d) x += y;
     }
-    s_warp[lane] = x - v;
+    s_warp[lane] = x - w;
+    if (lane == 31) s_warp[32] = x;
   }
   __syncthreads();
-  int start = s_warp[warp] + incl - sum;
-  for (int t = i0; t < i1; ++t) {
-    const int c = seg_cap(count(t));
-    const int room = list_cap - start;
-    seg[t] = make_int2(start, c < room ? c : (room > 0 ? room : 0));
-    if (!tile_end) fill[t] = 0;
-    start += c;
+  if (total) *total = s_warp[32];
+  return s_warp[warp] + incl - v;
+}
+
+// Direct placement layout for the next binning: tile t gets a segment of count + 8 + count / 4
+// slots (count = this binning's entries of the tile; exactly count without slack), segments packed
+// in tile order and clipped to the list capacity. Counts come from the scan (tile_end, after a
+// scatter) or from the fill counters of a direct placement, which are then zeroed for the next
+// one. With `order`, the tiles are also counting-sorted by descending count (capped at 1023) into
+// order[]: the next raster's block order. One block; each thread owns up to 8 consecutive tiles.
+__global__ void __launch_bounds__(kSmallScanThreads)
+layout_kernel(const int* __restrict__ tile_end, int* __restrict__ fill, int n_tiles,
+              int list_cap, bool slack, int2* __restrict__ seg, int* __restrict__ order) {
+  constexpr int kPer = kSmallScanMax / kSmallScanThreads;
+  __shared__ int s_warp[kSmallScanThreads / 32 + 1];
+  __shared__ int s_bin[kSmallScanThreads];
+  const int per = (n_tiles + kSmallScanThreads - 1) / kSmallScanThreads;
+  const int i0 = threadIdx.x * per;
+  int c[kPer];
+  int sum = 0;
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) {
+    const int t = i0 + u;
+    c[u] = 0;
+    if (u < per && t < n_tiles) {
+      c[u] = tile_end ? tile_end[t] - (t > 0 ? tile_end[t - 1] : 0) : fill[t];
+      sum += slack ? c[u] + 8 + (c[u] >> 2) : c[u];
+    }
+  }
+  int start = block_exclusive_scan(sum, s_warp, nullptr);
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) {
+    const int t = i0 + u;
+    if (u < per && t < n_tiles) {
+      const int sc = slack ? c[u] + 8 + (c[u] >> 2) : c[u];
+      const int room = list_cap - start;
+      seg[t] = make_int2(start, sc < room ? sc : (room > 0 ? room : 0));
+      if (!tile_end) fill[t] = 0;
+      start += sc;
+    }
+  }
+  if (!order) return;
+  auto bin = [](int cnt) { return kSmallScanThreads - 1 - min(cnt, kSmallScanThreads - 1); };
+  s_bin[threadIdx.x] = 0;
+  __syncthreads();
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) {
+    if (u < per && i0 + u < n_tiles) atomicAdd(&s_bin[bin(c[u])], 1);
+  }
+  __syncthreads();
+  const int first = block_exclusive_scan(s_bin[threadIdx.x], s_warp, nullptr);
+  s_bin[threadIdx.x] = first;  // every thread read its own bin before the scan's barriers
+  __syncthreads();
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) {
+    if (u < per && i0 + u < n_tiles) order[atomicAdd(&s_bin[bin(c[u])], 1)] = i0 + u;
   }
 }
 
@@ -418,7 +453,8 @@ bool direct_binning_supported(const Geometry& g) {
   return g.n_tiles() > 0 && g.n_tiles() <= kSmallScanMax;
 }
 
-int direct_layout(BinBuffers& bb, const Geometry& g, bool after_scatter, bool slack, cudaStream_t s) {
+int direct_layout(BinBuffers& bb, const Geometry& g, bool after_scatter, bool slack, int* order,
+                  cudaStream_t s) {
   const int64_t n_tiles = g.n_tiles();
   if (!direct_binning_supported(g)) return set_error(-1, "direct binning needs at most 8192 tiles");
   RTGS_TRY(bb.seg.ensure(static_cast<size_t>(n_tiles) * sizeof(int2), s));
@@ -426,7 +462,7 @@ int direct_layout(BinBuffers& bb, const Geometry& g, bool after_scatter, bool sl
   layout_kernel<<<1, kSmallScanThreads, 0, s>>>(
       after_scatter ? bb.tile_end.as<int>() : nullptr, bb.tile_count.as<int>(),
       static_cast<int>(n_tiles), static_cast<int>(list_cap < INT32_MAX ? list_cap : INT32_MAX), slack,
-      bb.seg.as<int2>());
+      bb.seg.as<int2>(), order);
   if (!after_scatter) bb.counts_cleared = true;  // the kernel zeroes the fill counters
   return check_cuda(cudaGetLastError(), "layout_kernel");
 }

@@ -220,6 +220,7 @@ int ensure_segment_room(rtgs2d_fit* f, cudaStream_t s) {
   const int64_t cap = f->bb.capacity;
   const size_t want = static_cast<size_t>(cap + cap / 4 + 16 * f->geo.n_tiles()) * sizeof(uint32_t);
   RTGS_TRY(f->bb.seg.ensure(static_cast<size_t>(f->geo.n_tiles()) * sizeof(int2), s));
+  RTGS_TRY(f->bb.tile_order.ensure(static_cast<size_t>(2 * f->geo.n_tiles()) * sizeof(int), s));
   return f->bb.list.ensure(want, s);
 }
 
@@ -307,7 +308,7 @@ std::vector<uintptr_t> chunk_key(const rtgs2d_fit* f, int64_t chunk) {
                               static_cast<uintptr_t>(bb.capacity), static_cast<uintptr_t>(f->use_active),
                               static_cast<uintptr_t>(direct_chunk(f))};
   for (const DevBuf* b : {&bb.records, &bb.weights, &bb.spans, &bb.counts, &bb.offsets, &bb.list,
-                          &bb.tile_count, &bb.tile_end, &bb.seg, &bb.entries[0], &bb.entries[1], &bb.ranges,
+                          &bb.tile_count, &bb.tile_end, &bb.seg, &bb.tile_order, &bb.entries[0], &bb.entries[1], &bb.ranges,
                           &bb.partials, &bb.partial_d, &bb.cub_temp, &bb.sort_counts, &bb.stats,
                           &f->raw, &f->m1, &f->m2, &f->targets, &f->mask, &f->view_scale,
                           &f->tile_loss, &f->log, &f->iter_table, &f->active}) {
@@ -347,15 +348,22 @@ int enqueue_chunk(rtgs2d_fit* f, int64_t chunk, cudaStream_t s, cudaEvent_t* ev,
     } else {
       RTGS_TRY(bin_entries_async(bb, f->geo, f->m, radix(f), s));
     }
+    // Tile orders alternate between two buffers: the layout of iteration k writes the order of
+    // raster k + 1 while raster k reads the one written beside raster k - 1.
     const bool layout = direct && k + 1 < chunk;
+    int* orders = bb.tile_order.as<int>();
+    const int64_t n_tiles = f->geo.n_tiles();
     if (layout) {
       RTGS_CUDA(cudaEventRecord(f->fork_event, s), "fork record");
       RTGS_CUDA(cudaStreamWaitEvent(f->side_stream, f->fork_event, 0), "fork wait");
-      RTGS_TRY(direct_layout(bb, f->geo, k == 0, f->binning != RTGS2D_BINNING_TIGHT, f->side_stream));
+      RTGS_TRY(direct_layout(bb, f->geo, k == 0, f->binning != RTGS2D_BINNING_TIGHT,
+                             orders + ((k + 1) & 1) * n_tiles, f->side_stream));
       RTGS_CUDA(cudaEventRecord(f->join_event, f->side_stream), "join record");
     }
     if (e) RTGS_CUDA(record(e[1]), "event record");
-    RTGS_TRY(launch_raster_fit(bb, f->geo, kCutoff, fa, true, s));
+    FitRasterArgs fk = fa;
+    if (direct && k > 0) fk.tile_order = orders + (k & 1) * n_tiles;
+    RTGS_TRY(launch_raster_fit(bb, f->geo, kCutoff, fk, true, s));
     if (e) RTGS_CUDA(record(e[2]), "event record");
     if (layout) RTGS_CUDA(cudaStreamWaitEvent(s, f->join_event, 0), "join wait");
     RTGS_TRY(launch_adam_fit(bb, f->geo, f->m, f->n, f->raw.as<float>(), f->m1.as<float>(),

@@ -72,6 +72,7 @@ struct BinBuffers {
   DevBuf entries[2];  // uint64[capacity] (tile key << 32 | gaussian id), radix-sort double buffer
   DevBuf ranges;      // int2[n_tiles] [start, end) of every tile in the list (or sorted entries)
   DevBuf seg;         // int2[n_tiles] direct placement: (start, slots) of each tile's segment
+  DevBuf tile_order;  // int[2][n_tiles] raster block order (tiles by descending entry count)
   DevBuf partials;    // float[capacity][8] per (gaussian, tile) gradient moments
   DevBuf partial_d;   // float[capacity]   per (gaussian, tile) density-gradient moment
   DevBuf cub_temp;    // exclusive-scan temporaries
@@ -140,9 +141,12 @@ int bin_entries_async(BinBuffers& bb, const Geometry& g, int64_t m, bool radix, 
 // direct_layout computes the segments from the last binning (after_scatter: from tile_end; else
 // from the fill counters, which it zeroes; slack: count + count/4 + 8 slots, else count);
 // direct_sort sorts the filled segments into bb.ranges. Nothing but the next projection reads the
-// layout, so it can run beside the raster. Up to kSmallScanMax (8192) tiles.
+// layout, so it can run beside the raster. With `order`, direct_layout also writes the tiles in
+// descending order of their entry count (a permutation of the tiles, ties in any order) for the
+// next raster: heaviest tiles first shortens the launch's tail. Up to kSmallScanMax (8192) tiles.
 bool direct_binning_supported(const Geometry& g);
-int direct_layout(BinBuffers& bb, const Geometry& g, bool after_scatter, bool slack, cudaStream_t s);
+int direct_layout(BinBuffers& bb, const Geometry& g, bool after_scatter, bool slack, int* order,
+                  cudaStream_t s);
 int direct_sort(BinBuffers& bb, const Geometry& g, cudaStream_t s);
 // Allocate the entry-sized buffers (list, entries, partials[, partial_d]) for `capacity` entries.
 int ensure_entry_capacity(BinBuffers& bb, int64_t capacity, bool density, cudaStream_t s);
@@ -167,6 +171,7 @@ struct FitRasterArgs {
   double* tile_loss = nullptr;        // (n_tiles, 2): loss numerator, clamped PSNR numerator
   float* render_out = nullptr;        // optional (B, H, W, 3)
   float coverage_coef = 0.f;          // > 0: mask coverage penalty weight / (H * W) (density pass)
+  const int* tile_order = nullptr;    // optional: block b rasterises tile tile_order[b]
 };
 
 int launch_raster_forward(const BinBuffers& bb, const Geometry& g, float cutoff, float* out,

@@ -235,7 +235,7 @@ raster_kernel(const RasterArgs a) {
   __shared__ int s_next;
   __shared__ double s_loss[L::kWarps][2];
 
-  const int tile = blockIdx.x;
+  const int tile = a.fit.tile_order ? a.fit.tile_order[blockIdx.x] : static_cast<int>(blockIdx.x);
   const int view = tile / a.tiles_per_view;
   const int tin = tile - view * a.tiles_per_view;
   const int tile_y = tin / a.tiles_x;
