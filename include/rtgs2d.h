@@ -255,8 +255,9 @@ RTGS2D_API int rtgs2d_fit_chunk_counts(const rtgs2d_fit* fit, int64_t* graph_chu
  *                           each later projection writes its ids straight into per-tile segments
  *                           sized from the previous binning with slack (count + count/4 + 8), and
  *                           the binning is the per-tile sort. A segment that fills up invalidates
- *                           the chunk, which re-runs with SCATTER. Frames of up to 8192 tiles;
- *                           larger ones use SCATTER.
+ *                           the chunk, which re-runs with SCATTER. The rasters of later
+ *                           iterations take their tiles heaviest first. Up to 2^20 tiles (all
+ *                           views); more use SCATTER.
  *   RTGS2D_BINNING_SCATTER  every iteration: entries, tile-count scan, scatter, per-tile sort.
  *   RTGS2D_BINNING_RADIX    every iteration: entries, radix sort by (tile, id), tile ranges.
  *   RTGS2D_BINNING_TIGHT    AUTO with segments of exactly the previous counts (no slack): any tile

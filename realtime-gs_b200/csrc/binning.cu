@@ -319,53 +319,45 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int* tot
 // in tile order and clipped to the list capacity. Counts come from the scan (tile_end, after a
 // scatter) or from the fill counters of a direct placement, which are then zeroed for the next
 // one. With `order`, the tiles are also counting-sorted by descending count (capped at 1023) into
-// order[]: the next raster's block order. One block; each thread owns up to 8 consecutive tiles.
+// order[]: the next raster's block order. One block (it runs beside the raster, off the critical
+// path); each thread owns a run of consecutive tiles and reads their counts once per pass.
 __global__ void __launch_bounds__(kSmallScanThreads)
 layout_kernel(const int* __restrict__ tile_end, int* __restrict__ fill, int n_tiles,
               int list_cap, bool slack, int2* __restrict__ seg, int* __restrict__ order) {
-  constexpr int kPer = kSmallScanMax / kSmallScanThreads;
   __shared__ int s_warp[kSmallScanThreads / 32 + 1];
   __shared__ int s_bin[kSmallScanThreads];
   const int per = (n_tiles + kSmallScanThreads - 1) / kSmallScanThreads;
-  const int i0 = threadIdx.x * per;
-  int c[kPer];
+  const int i0 = min(static_cast<int>(threadIdx.x) * per, n_tiles);
+  const int i1 = min(i0 + per, n_tiles);
+  auto count = [&](int t) { return tile_end ? tile_end[t] - (t > 0 ? tile_end[t - 1] : 0) : fill[t]; };
+  auto seg_cap = [slack](int c) { return slack ? c + 8 + (c >> 2) : c; };
+  auto bin = [](int c) { return kSmallScanThreads - 1 - min(c, kSmallScanThreads - 1); };
+  if (order) s_bin[threadIdx.x] = 0;
+  __syncthreads();
   int sum = 0;
-#pragma unroll
-  for (int u = 0; u < kPer; ++u) {
-    const int t = i0 + u;
-    c[u] = 0;
-    if (u < per && t < n_tiles) {
-      c[u] = tile_end ? tile_end[t] - (t > 0 ? tile_end[t - 1] : 0) : fill[t];
-      sum += slack ? c[u] + 8 + (c[u] >> 2) : c[u];
-    }
+  for (int t = i0; t < i1; ++t) {
+    const int c = count(t);
+    sum += seg_cap(c);
+    if (order) atomicAdd(&s_bin[bin(c)], 1);
   }
   int start = block_exclusive_scan(sum, s_warp, nullptr);
-#pragma unroll
-  for (int u = 0; u < kPer; ++u) {
-    const int t = i0 + u;
-    if (u < per && t < n_tiles) {
-      const int sc = slack ? c[u] + 8 + (c[u] >> 2) : c[u];
-      const int room = list_cap - start;
-      seg[t] = make_int2(start, sc < room ? sc : (room > 0 ? room : 0));
-      if (!tile_end) fill[t] = 0;
-      start += sc;
-    }
+  const bool zero_here = !tile_end && !order;  // else the order pass zeroes the fill counters
+  for (int t = i0; t < i1; ++t) {
+    const int c = count(t);
+    const int sc = seg_cap(c);
+    const int room = list_cap - start;
+    seg[t] = make_int2(start, sc < room ? sc : (room > 0 ? room : 0));
+    if (zero_here) fill[t] = 0;
+    start += sc;
   }
   if (!order) return;
-  auto bin = [](int cnt) { return kSmallScanThreads - 1 - min(cnt, kSmallScanThreads - 1); };
-  s_bin[threadIdx.x] = 0;
-  __syncthreads();
-#pragma unroll
-  for (int u = 0; u < kPer; ++u) {
-    if (u < per && i0 + u < n_tiles) atomicAdd(&s_bin[bin(c[u])], 1);
-  }
-  __syncthreads();
   const int first = block_exclusive_scan(s_bin[threadIdx.x], s_warp, nullptr);
   s_bin[threadIdx.x] = first;  // every thread read its own bin before the scan's barriers
   __syncthreads();
-#pragma unroll
-  for (int u = 0; u < kPer; ++u) {
-    if (u < per && i0 + u < n_tiles) order[atomicAdd(&s_bin[bin(c[u])], 1)] = i0 + u;
+  for (int t = i0; t < i1; ++t) {
+    const int c = count(t);
+    order[atomicAdd(&s_bin[bin(c)], 1)] = t;
+    if (!tile_end) fill[t] = 0;
   }
 }
 
@@ -450,13 +442,13 @@ int bin_scatter(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s) {
 }  // namespace
 
 bool direct_binning_supported(const Geometry& g) {
-  return g.n_tiles() > 0 && g.n_tiles() <= kSmallScanMax;
+  return g.n_tiles() > 0 && g.n_tiles() <= kDirectMaxTiles;
 }
 
 int direct_layout(BinBuffers& bb, const Geometry& g, bool after_scatter, bool slack, int* order,
                   cudaStream_t s) {
   const int64_t n_tiles = g.n_tiles();
-  if (!direct_binning_supported(g)) return set_error(-1, "direct binning needs at most 8192 tiles");
+  if (!direct_binning_supported(g)) return set_error(-1, "direct binning: too many tiles");
   RTGS_TRY(bb.seg.ensure(static_cast<size_t>(n_tiles) * sizeof(int2), s));
   const int64_t list_cap = static_cast<int64_t>(bb.list.bytes / sizeof(uint32_t));
   layout_kernel<<<1, kSmallScanThreads, 0, s>>>(

@@ -197,7 +197,7 @@ bool coverage(const rtgs2d_fit* f) { return f->opt.mask_coverage_weight > 0.0; }
 // Bin by radix sort: chosen by the caller, or after a tile list too long for the tile sort.
 bool radix(const rtgs2d_fit* f) { return f->use_radix || f->binning == RTGS2D_BINNING_RADIX; }
 
-// Direct placement for this chunk: not on the radix path, at most 8192 tiles, and not right after
+// Direct placement for this chunk: not on the radix path, at most 2^20 tiles, and not right after
 // a chunk that overflowed a tile segment (that chunk re-runs with the scatter binning).
 bool direct_chunk(const rtgs2d_fit* f) {
   const bool mode = f->binning == RTGS2D_BINNING_AUTO || f->binning == RTGS2D_BINNING_TIGHT;

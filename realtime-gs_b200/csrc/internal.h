@@ -143,7 +143,8 @@ int bin_entries_async(BinBuffers& bb, const Geometry& g, int64_t m, bool radix, 
 // direct_sort sorts the filled segments into bb.ranges. Nothing but the next projection reads the
 // layout, so it can run beside the raster. With `order`, direct_layout also writes the tiles in
 // descending order of their entry count (a permutation of the tiles, ties in any order) for the
-// next raster: heaviest tiles first shortens the launch's tail. Up to kSmallScanMax (8192) tiles.
+// next raster: heaviest tiles first shortens the launch's tail. Up to kDirectMaxTiles tiles.
+constexpr int64_t kDirectMaxTiles = int64_t{1} << 20;
 bool direct_binning_supported(const Geometry& g);
 int direct_layout(BinBuffers& bb, const Geometry& g, bool after_scatter, bool slack, int* order,
                   cudaStream_t s);
