@@ -217,13 +217,16 @@ def e2e_fit(device, wl, target_host, init_host, steps: int) -> tuple[float, int,
     h2d = target_host.numel() * 4 + sum(x.numel() * 4 for x in init_host)
     times = []
     d2h = 0
+    # Fitted parameters come back into pinned host buffers (asynchronous copies, one wait).
+    out = [torch.empty(x.shape, dtype=torch.float32, pin_memory=True) for x in init_host]
     for k in range(steps + 1):
         torch.cuda.synchronize(device)
         t0 = time.perf_counter()
         image = target_host.to(device, non_blocking=True)
         g0 = Gaussians2D(*(x.to(device, non_blocking=True) for x in init_host))
         fitted, _hist = fit_image_from_initialization(image, g0, cfg)
-        out = [x.to("cpu") for x in (fitted.xy, fitted.chol, fitted.color, fitted.weight)]
+        for dst, src in zip(out, (fitted.xy, fitted.chol, fitted.color, fitted.weight)):
+            dst.copy_(src, non_blocking=True)
         torch.cuda.synchronize(device)
         dt = time.perf_counter() - t0
         d2h = sum(x.numel() * 4 for x in out)

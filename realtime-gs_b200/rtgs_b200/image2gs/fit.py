@@ -131,16 +131,24 @@ def raw_from_gaussians(xy, chol, color, weight, height: int, width: int) -> dict
 
 
 def _validate_raw_parameters(raw_parameters: dict[str, torch.Tensor]) -> None:
+    # One host synchronisation for all fields; the failing rows are gathered only on error.
+    finite = {name: torch.isfinite(value) for name, value in raw_parameters.items()}
+    if not finite or all(torch.stack([f.all() for f in finite.values()]).tolist()):
+        return
     for name, value in raw_parameters.items():
-        finite = torch.isfinite(value)
-        if bool(finite.all()):
+        if bool(finite[name].all()):
             continue
-        rows = torch.nonzero(~finite.reshape(value.shape[0], -1).all(dim=1)).flatten().tolist()
+        rows = torch.nonzero(~finite[name].reshape(value.shape[0], -1).all(dim=1)).flatten().tolist()
         raise NonFiniteRawParameterError(name, rows, value)
 
 
 def _validate_initial_gaussians(g0: Gaussians2D, height: int, width: int) -> None:
-    """Reject malformed initialiser fields (fit.py:634-676)."""
+    """Reject malformed initialiser fields (fit.py:634-676).
+
+    Shapes and dtypes are checked on the host; the value checks run on the device and are read
+    back with one synchronisation, and only a failing check gathers its rows, in the reference's
+    order of checks (finiteness per field, bounds, Cholesky diagonal, colour / weight range).
+    """
     expected = {"xy": (g0.n, 2), "chol": (g0.n, 3), "color": (g0.n, 3), "weight": (g0.n,)}
     for name, shape in expected.items():
         value = getattr(g0, name)
@@ -149,21 +157,25 @@ def _validate_initial_gaussians(g0: Gaussians2D, height: int, width: int) -> Non
             raise ValueError(f"initial Gaussians2D {name} shape must be {shape}, got {actual}")
         if not value.is_floating_point():
             raise ValueError(f"initial Gaussians2D {name} must be floating point")
-        finite = torch.isfinite(value)
-        if not bool(finite.all()):
-            rows = torch.nonzero(~finite.reshape(g0.n, -1).all(dim=1)).flatten().tolist()
-            raise ValueError(f"non-finite initial rows in {name}: {rows}")
+    finite = {name: torch.isfinite(getattr(g0, name)).reshape(g0.n, -1).all(dim=1) for name in expected}
     inside = (g0.xy[:, 0] >= 0) & (g0.xy[:, 0] < width) & (g0.xy[:, 1] >= 0) & (g0.xy[:, 1] < height)
+    diag_ok = (g0.chol[:, 0] > _MIN_DIAG) & (g0.chol[:, 2] > _MIN_DIAG)
+    unit = {name: ((getattr(g0, name) >= 0) & (getattr(g0, name) <= 1)).reshape(g0.n, -1).all(dim=1)
+            for name in ("color", "weight")}
+    checks = [*finite.values(), inside, diag_ok, *unit.values()]
+    if all(torch.stack([c.all() for c in checks]).tolist()):
+        return
+    for name in expected:
+        if not bool(finite[name].all()):
+            rows = torch.nonzero(~finite[name]).flatten().tolist()
+            raise ValueError(f"non-finite initial rows in {name}: {rows}")
     if not bool(inside.all()):
         rows = torch.nonzero(~inside).flatten().tolist()
         raise ValueError(f"initial Gaussians2D xy rows outside image bounds: {rows}")
-    diag_ok = (g0.chol[:, 0] > _MIN_DIAG) & (g0.chol[:, 2] > _MIN_DIAG)
     if not bool(diag_ok.all()):
         rows = torch.nonzero(~diag_ok).flatten().tolist()
         raise ValueError(f"initial Gaussians2D Cholesky diagonal must exceed {_MIN_DIAG}: rows {rows}")
-    for name in ("color", "weight"):
-        value = getattr(g0, name)
-        ok = ((value >= 0) & (value <= 1)).reshape(g0.n, -1).all(dim=1)
+    for name, ok in unit.items():
         if not bool(ok.all()):
             rows = torch.nonzero(~ok).flatten().tolist()
             raise ValueError(f"initial Gaussians2D {name} rows outside [0,1]: {rows}")
