@@ -144,6 +144,9 @@ __device__ __forceinline__ int piece_bucket(int pc) {
 // ((dx^2 i00 + dx dy 2 i01) + dy^2 i11), and pixel centres are exact (integers + 0.5).
 // Moments: S0 = sum dq dx, S1 = sum dq dy, S2 = sum dq dx^2, S3 = sum dq dx dy, S4 = sum dq dy^2,
 // S5..S7 = sum e g_rgb, Sd = sum e g_den, with e = exp(-q/2) and dq = e (g . w c).
+// A lane's pixel keeps its fixed-axis offset f for the whole piece, so the dq moments factor:
+// per pixel only P0 = sum dq, P1 = sum dq v and P2 = sum dq v^2 (v = varying-axis offset) are
+// accumulated, and f, f^2 are applied once at the end (S for dx-dy = f P1, for f^2 = f^2 P0, ...).
 template <bool ROW, bool DEN>
 __device__ __forceinline__ void backward_piece(const float4& geo, const float4& app, float wt,
                                                float pxc0, float pyc0, int sidx0, int r8,
@@ -163,13 +166,13 @@ __device__ __forceinline__ void backward_piece(const float4& geo, const float4& 
   constexpr int kLaneStride = ROW ? 1 : kTile;  // and of one lane-axis pixel
   int sidx_a = sidx0 + r8 * kLaneStride;
   float fvar = ROW ? pyc0 : pxc0;
+  float pa[3] = {0.f, 0.f, 0.f}, pb[3] = {0.f, 0.f, 0.f};
   // Only the shared-memory load, the falloff and the weighted upstream gradient sit under the
   // support predicate (short enough to be predicated rather than branched); the moment updates
   // run unconditionally with dq = e = 0 and g = 0 outside the support, which adds exact zeros
   // (the offsets and their products are finite), so a non-finite colour or gradient still only
   // reaches pixels inside the support.
-  auto accumulate = [&](bool in, int sidx, float d_fix, float sq_fix, float cross, float d_var,
-                        float sq_var, float q) {
+  auto accumulate = [&](bool in, int sidx, float d_var, float sq_var, float q, float (&p)[3]) {
     float4 gv = make_float4(0.f, 0.f, 0.f, 0.f);
     float e = 0.f, dq = 0.f;
     if (in) {
@@ -181,13 +184,9 @@ __device__ __forceinline__ void backward_piece(const float4& geo, const float4& 
       if constexpr (DEN) v = fmaf(gv.w, wt, v);
       dq = e * v;
     }
-    const float dx = ROW ? d_fix : d_var, dy = ROW ? d_var : d_fix;
-    const float dxdx = ROW ? sq_fix : sq_var, dydy = ROW ? sq_var : sq_fix;
-    S[0] = fmaf(dq, dx, S[0]);
-    S[1] = fmaf(dq, dy, S[1]);
-    S[2] = fmaf(dq, dxdx, S[2]);
-    S[3] = fmaf(dq, cross, S[3]);
-    S[4] = fmaf(dq, dydy, S[4]);
+    p[0] += dq;
+    p[1] = fmaf(dq, d_var, p[1]);
+    p[2] = fmaf(dq, sq_var, p[2]);
     S[5] = fmaf(e, gv.x, S[5]);
     S[6] = fmaf(e, gv.y, S[6]);
     S[7] = fmaf(e, gv.z, S[7]);
@@ -198,20 +197,30 @@ __device__ __forceinline__ void backward_piece(const float4& geo, const float4& 
     const float sq_v = __fmul_rn(dv, dv);
     const float t_v = __fmul_rn(sq_v, coef_var);
     {
-      const float cross = __fmul_rn(da, dv);  // dx dy (multiplication commutes exactly)
-      const float t1 = __fmul_rn(cross, geo.w);
+      const float t1 = __fmul_rn(__fmul_rn(da, dv), geo.w);  // dx dy (multiplication commutes)
       const float q = ROW ? __fadd_rn(__fadd_rn(t_a, t1), t_v) : __fadd_rn(__fadd_rn(t_v, t1), t_a);
-      accumulate(st < lim_a && q < cutoff, sidx_a, da, sq_a, cross, dv, sq_v, q);
+      accumulate(st < lim_a && q < cutoff, sidx_a, dv, sq_v, q, pa);
     }
     if (any_b) {
-      const float cross = __fmul_rn(db, dv);
-      const float t1 = __fmul_rn(cross, geo.w);
+      const float t1 = __fmul_rn(__fmul_rn(db, dv), geo.w);
       const float q = ROW ? __fadd_rn(__fadd_rn(t_b, t1), t_v) : __fadd_rn(__fadd_rn(t_v, t1), t_b);
-      accumulate(st < lim_b && q < cutoff, sidx_a + 8 * kLaneStride, db, sq_b, cross, dv, sq_v, q);
+      accumulate(st < lim_b && q < cutoff, sidx_a + 8 * kLaneStride, dv, sq_v, q, pb);
     }
     fvar += 1.f;
     sidx_a += kStep;
   }
+  // Fixed-axis factors: f P0 (first moment), P1 (varying first moment), f P1 (cross), f^2 P0 and
+  // P2 (second moments), summed over the lane's pixels A and B.
+  const float m_f = fmaf(da, pa[0], db * pb[0]);
+  const float m_v = pa[1] + pb[1];
+  const float m_ff = fmaf(sq_a, pa[0], sq_b * pb[0]);
+  const float m_fv = fmaf(da, pa[1], db * pb[1]);
+  const float m_vv = pa[2] + pb[2];
+  S[0] = ROW ? m_f : m_v;    // sum dq dx
+  S[1] = ROW ? m_v : m_f;    // sum dq dy
+  S[2] = ROW ? m_ff : m_vv;  // sum dq dx^2
+  S[3] = m_fv;               // sum dq dx dy
+  S[4] = ROW ? m_vv : m_ff;  // sum dq dy^2
 }
 
 template <int PPT, int MODE, bool DEN>
