@@ -285,6 +285,33 @@ def test_binning_modes_give_identical_fits():
             assert np.array_equal(h_a[0], h_m[0]) and np.array_equal(h_a[1], h_m[1]), mode
 
 
+def test_binning_modes_agree_above_single_block_scan_size():
+    """More than 8192 tiles in one engine (three 720p views, 10,800 tiles): the first iteration of a
+    chunk scans the tile counts with the device-wide scan, the segment layout and tile order run
+    with several tiles per thread. Direct placement and scatter binning end bitwise equal."""
+    h, w, n, iters = 720, 1280, 500, 70  # a full chunk of 64 and a tail of 6
+    views = 3
+    targets, raws = [], []
+    for v in range(views):
+        src = synthetic.source_gaussians(30 + v, 60, h, w, (2.0, 20.0))
+        targets.append(orender.render(src.xy, src.chol, src.color, src.weight, h, w).clamp(0, 1).to(DEV))
+        init = synthetic.fit_init(30 + v, n, h, w)
+        raws.append(raw_from_gaussians(*(x.to(DEV) for x in (init.xy, init.chol, init.color, init.weight)), h, w))
+    raw = {k: torch.stack([r[k] for r in raws]) for k in raws[0]}
+    results = {}
+    for mode in ("auto", "scatter"):
+        with FitEngine(views, n, h, w, lr=1e-2, iterations=iters, log_every=10, device=DEV) as engine:
+            engine.set_binning(mode)
+            engine.set_targets(torch.stack(targets))
+            engine.set_raw(raw)
+            engine.run(iters)
+            results[mode] = (engine.params(), engine.history())
+    (p_a, h_a), (p_s, h_s) = results["auto"], results["scatter"]
+    for a, b in zip(p_a, p_s):
+        assert torch.equal(a, b)
+    assert np.array_equal(h_a[0], h_s[0]) and np.array_equal(h_a[1], h_s[1])
+
+
 def test_pooled_engine_reuse_is_stateless():
     """Fits that repeat a configuration reuse a pooled engine (buffers and captured graphs); a fit
     run on a reused engine, after a fit of another image, ends bitwise where a fresh engine ends."""
