@@ -6,11 +6,15 @@ gaussians + N(0, 0.01) noise, fitted with 50,000 gaussians, L2 loss, Adam lr 1e-
 schedule, 1,000 iterations. One step = one complete fit of one image per GPU (``--views V``: V
 images fitted together in one engine; weak scaling: rank r fits its own images, seeds
 1000 + r * V + v), followed for N > 1 by the one gather of fitted parameters to all ranks (NCCL).
-``value`` = images fitted by all ranks / max-over-ranks device time.
+``value`` = images fitted by all ranks / max-over-ranks device time. Other workloads
+(``--workload``): ``batched_720p`` (1280x720, 70,000 gaussians, 1,000 iterations) and
+``masked_540p`` (960x540, 30,000 gaussians initialised inside a binary ellipse-union mask, 600
+iterations, L2 over the mask pixels read from bit-packed masks).
 
 Also measured in the same run:
-  e2e       the same fit through the public API (fit_image_from_initialization) with the target and
-            the initial parameters in pinned host memory and the fitted parameters read back.
+  e2e       the same fit through the public API (fit_image_from_initialization; several images:
+            the batched fit; masked workloads: fit_views_batched_masked) with the targets, masks
+            and initial parameters in pinned host memory and the fitted parameters read back.
   roofline  the fused raster kernel (forward + loss gradient + backward), timed with CUDA events
             on its launch stream around every raster launch of one extra fit of the same workload
             run right after the timed fits; algorithmic work = 68 FP32 flop per (gaussian,
@@ -132,12 +136,18 @@ def cpu_fit_sample(wl: dict, seed: int, iters: int, steps: int, warmup: int) -> 
     with torch.no_grad():
         target = (orender.render(src.xy, src.chol, src.color, src.weight, h, w)
                   + synthetic.noise(seed, h, w, wl["noise"])).clamp(0, 1)
-    init = synthetic.fit_init(seed, wl["n_fit"], h, w)
+    mask = None
+    if wl.get("masked"):
+        mask = synthetic.ellipse_mask(seed, h, w)
+        init = synthetic.masked_fit_init(seed, wl["n_fit"], mask)
+        mask = mask[None]
+    else:
+        init = synthetic.fit_init(seed, wl["n_fit"], h, w)
     init = tuple(x[None] for x in (init.xy, init.chol, init.color, init.weight))
     times = []
     for k in range(warmup + steps):
         t0 = time.perf_counter()
-        ofit.fit_views(target[None], init, iters, lr=1e-2, log_every=10**9)
+        ofit.fit_views(target[None], init, iters, lr=1e-2, log_every=10**9, masks=mask)
         dt = time.perf_counter() - t0
         if k >= warmup:
             times.append(dt)
@@ -145,7 +155,8 @@ def cpu_fit_sample(wl: dict, seed: int, iters: int, steps: int, warmup: int) -> 
     per_iter = statistics.median(times) / (iters + 1)
     fits_per_s = 1.0 / (per_iter * wl["iterations"])
     return {"value": fits_per_s, "unit": "fits/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{wl['height']}x{wl['width']} target, {wl['n_fit']} gaussians: {iters} oracle iterations "
+            "sample": f"{wl['height']}x{wl['width']} target{' (masked loss)' if mask is not None else ''}, "
+                      f"{wl['n_fit']} gaussians: {iters} oracle iterations "
                       f"(+1 final render) per step, median of {steps} steps after {warmup} warm-up, "
                       f"scaled to {wl['iterations']} iterations",
             "s_per_iteration": per_iter}
@@ -184,9 +195,11 @@ def splat_microbench(device, steps: int, warmup: int) -> dict:
     stream = _native.stream_ptr(device)
     m = xy.shape[0]
 
-    def step():
+    def step(mid=None):
         _native.check(lib.rtgs2d_render_forward(arena, xy.data_ptr(), chol.data_ptr(), color.data_ptr(),
                                                 weight.data_ptr(), 1, m, h, w, out.data_ptr(), None, stream))
+        if mid is not None:
+            mid.record()
         # The backward of an autograd step: it reuses the forward's projection and binning.
         _native.check(lib.rtgs2d_render_backward_after_forward(
             arena, up.data_ptr(), None, xy.data_ptr(), chol.data_ptr(), color.data_ptr(), weight.data_ptr(),
@@ -195,51 +208,75 @@ def splat_microbench(device, steps: int, warmup: int) -> dict:
     for _ in range(warmup):
         step()
     torch.cuda.synchronize(device)
-    times = []
+    times, fwd = [], []
     for _ in range(steps):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0, em, e1 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record()
-        step()
+        step(em)
         e1.record()
         e1.synchronize()
         times.append(e0.elapsed_time(e1))
+        fwd.append(e0.elapsed_time(em))
     entries, pairs = _native.arena_last_stats(device)
     ms = statistics.median(times)
-    return {"pairs": pairs, "entries": entries, "ms": ms, "gpairs_per_s": pairs / (ms * 1e-3) / 1e9}
+    fwd_ms = statistics.median(fwd)
+    return {"pairs": pairs, "entries": entries, "ms": ms, "forward_ms": fwd_ms, "backward_ms": ms - fwd_ms,
+            "gpairs_per_s": pairs / (ms * 1e-3) / 1e9}
 
 
-def e2e_fit(device, wl, target_host, init_host, steps: int) -> tuple[float, int, int]:
-    """Public-API fit with host inputs; returns (median seconds per fit, h2d bytes, d2h bytes)."""
+def e2e_fit(device, wl, targets_host, init_host, masks_host, steps: int) -> tuple[float, int, int, str]:
+    """Public-API fit of the rank's images with host inputs.
+
+    One image without a mask: ``fit_image_from_initialization``; several images: the batched fit
+    (``fit_stacked``, the engine call behind ``fit_views_batched``); masked images:
+    ``fit_views_batched_masked`` with boolean masks. Returns (median seconds per step, h2d bytes,
+    d2h bytes, API name).
+    """
     from rtgs_b200.core.gaussians2d import Gaussians2D
+    from rtgs_b200.image2gs.batched import fit_stacked, fit_views_batched_masked
     from rtgs_b200.image2gs.fit import FitConfig, fit_image_from_initialization
 
+    views = targets_host.shape[0]
     cfg = FitConfig(n_gaussians=wl["n_fit"], iterations=wl["iterations"], log_every=50)
-    h2d = target_host.numel() * 4 + sum(x.numel() * 4 for x in init_host)
+    h2d = targets_host.numel() * 4 + sum(x.numel() * 4 for x in init_host)
+    if masks_host is not None:
+        h2d += masks_host.numel() * masks_host.element_size()
+        api = "fit_views_batched_masked"
+    else:
+        api = "fit_image_from_initialization" if views == 1 else "fit_stacked (fit_views_batched)"
     times = []
-    d2h = 0
     # Fitted parameters come back into pinned host buffers (asynchronous copies, one wait).
     out = [torch.empty(x.shape, dtype=torch.float32, pin_memory=True) for x in init_host]
+    d2h = sum(x.numel() * 4 for x in out)
     for k in range(steps + 1):
         torch.cuda.synchronize(device)
         t0 = time.perf_counter()
-        image = target_host.to(device, non_blocking=True)
-        g0 = Gaussians2D(*(x.to(device, non_blocking=True) for x in init_host))
-        fitted, _hist = fit_image_from_initialization(image, g0, cfg)
-        for dst, src in zip(out, (fitted.xy, fitted.chol, fitted.color, fitted.weight)):
+        images = targets_host.to(device, non_blocking=True)
+        init = tuple(x.to(device, non_blocking=True) for x in init_host)
+        if masks_host is not None:
+            masks = masks_host.to(device, non_blocking=True)
+            fitted, _hist = fit_views_batched_masked(list(images), list(masks), init, cfg)
+        elif views == 1:
+            fitted, _hist = fit_image_from_initialization(images[0], Gaussians2D(*(x[0] for x in init)), cfg)
+            fitted = [fitted]
+        else:
+            fitted, _hist = fit_stacked(images, init, cfg)
+        for i, dst in enumerate(out):
+            src = torch.stack([(g.xy, g.chol, g.color, g.weight)[i] for g in fitted])
             dst.copy_(src, non_blocking=True)
         torch.cuda.synchronize(device)
         dt = time.perf_counter() - t0
-        d2h = sum(x.numel() * 4 for x in out)
         if k > 0:  # the first call is a warm-up
             times.append(dt)
-    return statistics.median(times), h2d, d2h
+    return statistics.median(times), h2d, d2h, api
 
 
 def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
     import torch.distributed as dist
 
     from rtgs_b200.image2gs import synthetic
-    from rtgs_b200.image2gs.engine import FitEngine
+    from rtgs_b200 import _native
+    from rtgs_b200.image2gs.engine import FitEngine, pack_mask_bits
     from rtgs_b200.image2gs.fit import raw_from_gaussians
     from rtgs_b200.image2gs.renderer2d import render_gaussians_2d_batched
 
@@ -252,15 +289,23 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
         return
     h, w, n, iters = wl["height"], wl["width"], wl["n_fit"], wl["iterations"]
     views = max(1, int(args.views))
+    masked = bool(wl.get("masked"))
     # Image v of rank r is global image r * views + v (its seeds do not depend on the GPU count).
     seeds = [1000 + rank * views + v for v in range(views)]
     targets = torch.stack([synthetic.make_target(sd, wl, render_gaussians_2d_batched, device) for sd in seeds])
-    inits = [synthetic.fit_init(sd, n, h, w) for sd in seeds]
-    init_dev = tuple(torch.stack([getattr(g, f) for g in inits]).to(device) for f in ("xy", "chol", "color", "weight"))
+    masks = None
+    if masked:  # binary ellipse-union masks, loss restricted to them, means initialised inside them
+        masks = torch.stack([synthetic.ellipse_mask(sd, h, w) for sd in seeds])
+        inits = [synthetic.masked_fit_init(sd, n, m) for sd, m in zip(seeds, masks)]
+    else:
+        inits = [synthetic.fit_init(sd, n, h, w) for sd in seeds]
+    init_stack = tuple(torch.stack([getattr(g, f) for g in inits]) for f in ("xy", "chol", "color", "weight"))
+    init_dev = tuple(x.to(device) for x in init_stack)
     raw = {k: v.contiguous() for k, v in raw_from_gaussians(*init_dev, h, w).items()}
-    engine = FitEngine(views, n, h, w, lr=1e-2, iterations=iters, log_every=50, device=device)
-    engine.set_targets(targets)
-    target, init = targets[0], inits[0]  # the e2e and CPU legs use the rank's first image
+    engine = FitEngine(views, n, h, w, lr=1e-2, iterations=iters, log_every=50, device=device,
+                       loss_mode=_native.LOSS_MASK_ONLY if masked else _native.LOSS_MSE)
+    engine.set_targets(targets, pack_mask_bits(masks.to(device)) if masked else None)
+    mask_px = (masks.reshape(views, -1) > 0.5).sum(1).double().numpy() if masked else np.full(views, float(h * w))
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)  # > 126 MB L2
     gathered = torch.empty(world, views * n, 9, device=device) if world > 1 else None
 
@@ -294,7 +339,7 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
     wall_s = time.perf_counter() - t_wall
     clocks = sampler.stop()
     _, sums = engine.evaluate(want_render=False)
-    final_psnr = float(np.mean([-10.0 * math.log10(max(sums[b, 1] / (3.0 * h * w), 1e-12)) for b in range(views)]))
+    final_psnr = float(np.mean([-10.0 * math.log10(max(sums[b, 1] / (3.0 * mask_px[b]), 1e-12)) for b in range(views)]))
     # Stage split and the raster kernel's duration: one more fit of the same workload with CUDA
     # events around every stage of every iteration (recorded inside the replayed graphs). Kept out
     # of the timed fits because the event records themselves lengthen an iteration.
@@ -312,16 +357,17 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
     value = world * views * args.steps / (total_ms / 1e3)
 
     # e2e through the public API with host buffers (all ranks concurrently).
-    target_host = target.cpu().pin_memory()
-    init_host = tuple(x.pin_memory() for x in (init.xy, init.chol, init.color, init.weight))
+    targets_host = targets.cpu().pin_memory()
+    init_host = tuple(x.pin_memory() for x in init_stack)
+    masks_host = (masks > 0.5).pin_memory() if masked else None
     del engine
-    e2e_value, h2d, d2h = None, 0, 0
-    if not args.no_e2e and views == 1:  # the public API's single-image fit
-        e2e_s, h2d, d2h = e2e_fit(device, wl, target_host, init_host, steps=2)
+    e2e_value, h2d, d2h, e2e_api = None, 0, 0, None
+    if not args.no_e2e:
+        e2e_s, h2d, d2h, e2e_api = e2e_fit(device, wl, targets_host, init_host, masks_host, steps=2)
         e2e_t = torch.tensor([e2e_s], dtype=torch.float64, device=device)
         if world > 1:
             dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
-        e2e_value = world / float(e2e_t.item())
+        e2e_value = world * views / float(e2e_t.item())
 
     splat = None
     if not args.no_splat:
@@ -373,11 +419,12 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
         "config": {
             "workload": args.workload, "height": h, "width": w, "gaussians": n, "iterations": iters,
             "source_gaussians": wl["n_sources"], "images_per_gpu_per_step": views, "parallelism": f"dp{world} (whole images)",
-            "l2": "256 MB buffer written between timed fits; a fit's own 1000 iterations run L2-warm",
+            "l2": f"256 MB buffer written between timed fits; a fit's own {iters} iterations run L2-warm",
+            "loss": "L2 over mask pixels (bit-packed masks)" if masked else "L2",
             "final_psnr_db": final_psnr,
         },
         "e2e": {"value": e2e_value, "unit": "fits/s", "h2d_bytes_per_step": int(h2d * world),
-                "d2h_bytes_per_step": int(d2h * world), "api": "fit_image_from_initialization"},
+                "d2h_bytes_per_step": int(d2h * world), "api": e2e_api},
         "roofline": {
             "bound": "fp32", "kernel": "raster_kernel<2,kFit> (fused forward + L2 gradient + backward)",
             "achieved": achieved, "peak": fp32_peak, "unit": "TFLOP/s",
@@ -400,6 +447,7 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
         line["splat_fwd_bwd"] = {
             "workload": "splat_4k: 3840x2160, 1,000,000 gaussians, fixed parameters, N(0,1) upstream grad",
             "value": splat["aggregate_gpairs_per_s"], "unit": "Gpixel.gauss/s", "ms": splat["ms"],
+            "forward_ms": splat["forward_ms"], "backward_ms": splat["backward_ms"],
             "pairs": splat["pairs"], "entries": splat["entries"],
             "achieved_tflops": FLOP_PER_PAIR * splat["pairs"] / (splat["ms"] * 1e-3) / 1e12,
             "frac_fp32": FLOP_PER_PAIR * splat["pairs"] / (splat["ms"] * 1e-3) / 1e12 / fp32_peak,

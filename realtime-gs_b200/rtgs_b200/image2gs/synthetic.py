@@ -35,7 +35,7 @@ WORKLOADS = {
     "batched_720p": dict(height=720, width=1280, n_sources=8_000, sigma=(0.5, 40.0), noise=0.005,
                          n_fit=70_000, iterations=1_000, n_views=64),
     "masked_540p": dict(height=540, width=960, n_sources=8_000, sigma=(0.5, 40.0), noise=0.005,
-                        n_fit=30_000, iterations=600, n_views=256),
+                        n_fit=30_000, iterations=600, n_views=256, masked=True),
 }
 
 

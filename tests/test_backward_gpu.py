@@ -180,3 +180,41 @@ def test_backward_after_forward_reuses_binning_only_when_valid():
     recomputed = bwd(lib.rtgs2d_render_backward_after_forward)
     for a, b, c in zip(ref, reused, recomputed):
         assert torch.equal(a, b) and torch.equal(a, c)
+
+
+def test_backward_line_spans_keep_every_support_pixel():
+    """Elongated, rotated, large gaussians (one per view) with the upstream gradient non-zero only
+    in a band around each support boundary (9 < q < 13): the renderer backward walks only the
+    ellipse's line spans, and a support pixel missed at the boundary would move the colour gradient
+    (a sum over about a hundred band pixels) by far more than the tolerance."""
+    from rtgs_b200.image2gs.synthetic import _chol_from_sigmas
+
+    views, h, w = 16, 160, 160
+    gen = torch.Generator().manual_seed(11)
+    s1 = torch.exp(torch.rand(views, generator=gen, dtype=torch.float64) * (torch.log(torch.tensor(40.0)) - 0.7) + 0.7)
+    aspect = torch.exp(torch.rand(views, generator=gen, dtype=torch.float64) * torch.log(torch.tensor(60.0)))
+    theta = torch.rand(views, generator=gen, dtype=torch.float64) * torch.pi
+    chol = _chol_from_sigmas(s1, (s1 / aspect).clamp(min=0.8), theta).reshape(views, 1, 3)
+    xy = (torch.rand(views, 1, 2, generator=gen) * 100 + 30).float()
+    color = torch.rand(views, 1, 3, generator=gen)
+    weight = 0.2 + 0.8 * torch.rand(views, 1, generator=gen)
+    # q of every pixel centre in float64, band 9 < q < 13 per view
+    l11, l21, l22 = (chol[:, 0, k].double() for k in range(3))
+    s00, s01, s11 = l11 * l11, l11 * l21, l21 * l21 + l22 * l22
+    det = s00 * s11 - s01 * s01
+    i00, i01, i11 = s11 / det, -s01 / det, s00 / det
+    px = torch.arange(w, dtype=torch.float64) + 0.5
+    py = torch.arange(h, dtype=torch.float64) + 0.5
+    dx = px[None, None, :] - xy[:, 0, 0].double()[:, None, None]
+    dy = py[None, :, None] - xy[:, 0, 1].double()[:, None, None]
+    q = i00[:, None, None] * dx * dx + 2 * i01[:, None, None] * dx * dy + i11[:, None, None] * dy * dy
+    band = ((q > 9.0) & (q < 13.0)).float()
+    up = (torch.randn(views, h, w, 3, generator=gen) * band[..., None]).float()
+    assert band.sum(dim=(1, 2)).min() > 20
+    args = (xy, chol, color, weight)
+    ours = _ours(args, h, w, lambda im: (im * up.to(DEV)).sum())
+    ref = oracle_grads(*args, h, w, up)
+    for name, a, b in zip(NAMES, ours, ref):
+        for v in range(views):  # per view: each view's gradient is one gaussian's band sum
+            assert rel_err(a[v], b[v]) <= GRAD_TOL, (name, v)
+        assert torch.allclose(a, b, atol=3e-4, rtol=3e-4), name
