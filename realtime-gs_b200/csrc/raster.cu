@@ -335,9 +335,12 @@ __device__ __forceinline__ void backward_piece(const float4& geo, const float4& 
   S[4] = ROW ? m_vv : m_ff;  // sum dq dy^2
 }
 
-// The renderer backward (with line spans) is held to 56 registers: 9 blocks of 128 threads per SM.
+// Register caps (measured on B200): the renderer backward (with line spans) is held to 56
+// registers, 9 blocks of 128 threads per SM; the fit kernel without the density channel to 48,
+// 10 blocks (no spills; 76.7 -> 76.2 ms per 1024x768 / 50k-gaussian fit; 12 blocks spill and are
+// slower).
 template <int PPT, int MODE, bool DEN>
-__global__ void __launch_bounds__(Layout<PPT>::kThreads, MODE == kBwd ? 9 : 0)
+__global__ void __launch_bounds__(Layout<PPT>::kThreads, MODE == kBwd ? 9 : (MODE == kFit && !DEN ? 10 : 0))
 raster_kernel(const RasterArgs a) {
   using L = Layout<PPT>;
   constexpr bool kDoFwd = MODE != kBwd;
