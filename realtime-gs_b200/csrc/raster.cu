@@ -1,11 +1,12 @@
 // Per-tile raster kernels for the accumulated 2D splatting renderer (sm_100a).
 //
-// One CTA per 16x16 tile, 4 warps. Each warp owns an 8 x (4*PPT) pixel sub-block and each lane PPT
-// adjacent pixels of one column (rows PPT*r .. PPT*r + PPT-1, so that a small gaussian usually
-// covers all of them). The tile's gaussian list (ascending gaussian index, from the binning step)
-// is staged through shared memory in batches of 128 records.
+// One CTA per 16x16 tile, 16 / (4*PPT) * 2 warps (PPT pixels per lane: 4 in the renderer forward,
+// 2 elsewhere, see kPPT). Each warp owns an 8 x (4*PPT) pixel sub-block and each lane PPT adjacent
+// pixels of one column (rows PPT*r .. PPT*r + PPT-1, so that a small gaussian usually covers all
+// of them). The tile's gaussian list (ascending gaussian index, from the binning step) is staged
+// through shared memory in batches of one record per thread.
 //
-//   forward   per 32 staged records, 16 ballots give every lane a 32-bit mask of the records whose
+//   forward   per 32 staged records, 8 + 4*PPT ballots give every lane a 32-bit mask of the records whose
 //             support rectangle covers each of its pixels; the lane walks exactly those, in list
 //             order, accumulating in registers (flat predicate for the ellipse test q < cutoff,
 //             exp(-q/2) as one multiply + ex2). The list order is the reference's summation
@@ -36,7 +37,6 @@
 namespace rtgs2d {
 namespace {
 
-constexpr int kBatch = 128;
 constexpr int kBuckets = 2 * kTile;  // backward work-list buckets: (orientation, steps)
 
 template <int PPT>
@@ -47,6 +47,7 @@ struct Layout {
   static constexpr int kSubY = kTile / kSubH;
   static constexpr int kWarps = kSubX * kSubY;
   static constexpr int kThreads = kWarps * 32;
+  static constexpr int kBatch = kThreads;  // records staged per batch: one per thread
 };
 
 enum Mode : int { kFwd = 0, kBwd = 1, kFit = 2, kEval = 3 };
@@ -346,6 +347,7 @@ raster_kernel(const RasterArgs a) {
   constexpr bool kDoFwd = MODE != kBwd;
   constexpr bool kDoBwd = MODE == kBwd || MODE == kFit;
 
+  constexpr int kBatch = L::kBatch;
   __shared__ float4 s_geo[kBatch];
   __shared__ float4 s_app[kBatch];
   __shared__ int4 s_rect[kBatch];
@@ -714,7 +716,13 @@ loss_reduce_kernel(const double* __restrict__ tile_loss, int tiles_per_view, dou
   reduce_view_loss(tile_loss, tiles_per_view, blockIdx.x, dst);
 }
 
-constexpr int kPPT = 2;
+// Pixels per lane: the renderer forward walks each record for a column of 4 pixels (2 warps per
+// tile), which halves the per-record walk cost per pixel (4K frame, 1M gaussians: forward call
+// 2.28 -> 1.94 ms); the backward variants and the fused fit kernel keep 2 (4 warps per tile: with 4
+// they are slower, the backward's octet tasks having fewer warps per tile and the fit's small
+// gaussians covering fewer of a lane's 4 rows).
+template <int MODE>
+constexpr int kPPT = MODE == kFwd ? 4 : 2;
 
 RasterArgs base_args(const BinBuffers& bb, const Geometry& g, float cutoff) {
   RasterArgs a{};
@@ -740,8 +748,8 @@ int launch(const RasterArgs& a, const Geometry& g, cudaStream_t s, const char* n
   const int64_t n_tiles = g.n_tiles();
   if (n_tiles == 0) return 0;
   if (n_tiles > INT32_MAX) return set_error(-1, "too many tiles");
-  raster_kernel<kPPT, MODE, DEN>
-      <<<static_cast<unsigned>(n_tiles), Layout<kPPT>::kThreads, 0, s>>>(a);
+  raster_kernel<kPPT<MODE>, MODE, DEN>
+      <<<static_cast<unsigned>(n_tiles), Layout<kPPT<MODE>>::kThreads, 0, s>>>(a);
   return check_cuda(cudaGetLastError(), name);
 }
 
