@@ -6,9 +6,11 @@
 // of them). The tile's gaussian list (ascending gaussian index, from the binning step) is staged
 // through shared memory in batches of one record per thread.
 //
-//   forward   per 32 staged records, 8 + 4*PPT ballots give every lane a 32-bit mask of the records whose
-//             support rectangle covers each of its pixels; the lane walks exactly those, in list
-//             order, accumulating in registers (flat predicate for the ellipse test q < cutoff,
+//   forward   per 32 staged records, 8 + 4*PPT ballots give every lane a 32-bit mask of the
+//             records whose support rectangle covers each of its pixels (in the renderer forward
+//             narrowed to the records whose ellipse can reach them: reach masks); the lane walks
+//             exactly those, in list order, accumulating in registers (flat predicate for the
+//             ellipse test q < cutoff,
 //             exp(-q/2) as one multiply + ex2). The list order is the reference's summation
 //             order, so a render is deterministic and no atomics are used.
 //   backward  the tile's upstream gradients are staged in shared memory; every (gaussian, tile)
@@ -121,6 +123,20 @@ __device__ __forceinline__ float octet_transpose_reduce8(const float (&v)[8], in
   const float send = u1 ? b[0] : b[1];
   const float keep = u1 ? b[1] : b[0];
   return keep + __shfl_xor_sync(0xffffffffu, send, 1);
+}
+
+// 32 x 32 bit-matrix transpose across the warp: lane i returns the word whose bit j is bit i of
+// lane j's x (off-diagonal blocks swapped at every scale, 5 shuffle rounds).
+__device__ __forceinline__ uint32_t warp_transpose32(uint32_t x, int lane) {
+  constexpr uint32_t kLow[5] = {0x0000ffffu, 0x00ff00ffu, 0x0f0f0f0fu, 0x33333333u, 0x55555555u};
+#pragma unroll
+  for (int r = 0; r < 5; ++r) {
+    const int s = 16 >> r;
+    const uint32_t m = kLow[r];
+    const uint32_t y = __shfl_xor_sync(0xffffffffu, x, s);
+    x = (lane & s) ? ((x & ~m) | ((y >> s) & m)) : ((x & m) | ((y << s) & ~m));
+  }
+  return x;
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -339,9 +355,11 @@ __device__ __forceinline__ void backward_piece(const float4& geo, const float4& 
 // Register caps (measured on B200): the renderer backward (with line spans) is held to 56
 // registers, 9 blocks of 128 threads per SM; the fit kernel without the density channel to 48,
 // 10 blocks (no spills; 76.7 -> 76.2 ms per 1024x768 / 50k-gaussian fit; 12 blocks spill and are
-// slower).
+// slower); the renderer forward without density to 48, 20 blocks of 64 threads (the reach masks
+// would take it to 64 registers; 1.73 -> 1.68 ms per 4K forward call with the cap).
 template <int PPT, int MODE, bool DEN>
-__global__ void __launch_bounds__(Layout<PPT>::kThreads, MODE == kBwd ? 9 : (MODE == kFit && !DEN ? 10 : 0))
+__global__ void __launch_bounds__(Layout<PPT>::kThreads,
+                                  MODE == kBwd ? 9 : (MODE == kFit && !DEN ? 10 : (MODE == kFwd && !DEN ? 20 : 0)))
 raster_kernel(const RasterArgs a) {
   using L = Layout<PPT>;
   constexpr bool kDoFwd = MODE != kBwd;
@@ -363,6 +381,12 @@ raster_kernel(const RasterArgs a) {
   static_assert(kBatch == L::kThreads, "the backward work list assigns one piece per thread");
   static_assert(kBuckets == 32, "warp 0 scans one bucket per lane");
   __shared__ int s_next;
+  // Renderer forward: the walk is pruned to records whose support ellipse can reach a lane's
+  // pixels (line spans along the sub-block's columns, in groups of 4 rows, one word per record,
+  // transposed across the warp); the rectangle bit and the exact q test stay per pixel. 4K frame,
+  // 1M gaussians (59% of rectangle pixels outside their ellipse): forward call 1.94 -> 1.68 ms.
+  // With 2 pixels per lane the same masks cost as much as they saved.
+  constexpr bool kEllMask = MODE == kFwd && PPT == 4;
   __shared__ double s_loss[L::kWarps][2];
 
   const int tile = a.fit.tile_order ? a.fit.tile_order[blockIdx.x] : static_cast<int>(blockIdx.x);
@@ -442,6 +466,32 @@ raster_kernel(const RasterArgs a) {
             rbits = ((2u << rhi) - 1u) & ~((1u << rlo) - 1u);
           }
         }
+        // Bit g*8 + col of record c + lane: its ellipse's span along sub-block column col meets
+        // rows 4g .. 4g+3 (a superset: line_span); with lane = g*8 + col that is lane g*8+col's
+        // pixel column, so a bit transpose gives each lane its mask over the 32 records.
+        uint32_t reach = 0xffffffffu;
+        if constexpr (kEllMask) {
+          static_assert(L::kSubW == 8 && L::kSubH == 16, "4 groups of 4 rows x 8 columns");
+          if (cbits != 0) {
+            const float4 geo = s_geo[c + lane];
+            const float4 app = s_app[c + lane];
+            const LineCoef lc = line_coef(geo.z, app.x, geo.w, geo.y, static_cast<float>(sy0) + 0.5f, a.cutoff);
+            if (lc.pd) {
+              reach = 0;
+#pragma unroll
+              for (int b = 0; b < L::kSubW; ++b) {
+                const float d = __fsub_rn(static_cast<float>(sx0 + b) + 0.5f, geo.x);
+                int lo = 0, hi = L::kSubH - 1;
+                line_span(lc, d, __fmul_rn(d, d), L::kSubH, lo, hi);
+                if (lo <= hi) {
+                  const uint32_t groups = ((2u << (hi >> 2)) - 1u) & ~((1u << (lo >> 2)) - 1u);
+                  reach |= ((groups * 0x00204081u) & 0x01010101u) << b;  // group g -> bit 8g
+                }
+              }
+            }
+          }
+          reach = warp_transpose32(reach, lane);
+        }
         unsigned mcol = 0;
 #pragma unroll
         for (int b = 0; b < L::kSubW; ++b) {
@@ -463,6 +513,7 @@ raster_kernel(const RasterArgs a) {
           mpix[k] &= mcol;
           walk |= mpix[k];
         }
+        if constexpr (kEllMask) walk &= reach;
         while (walk) {
           const int jb = __ffs(walk) - 1;
           walk &= walk - 1;

@@ -185,7 +185,8 @@ def test_backward_after_forward_reuses_binning_only_when_valid():
 def test_backward_line_spans_keep_every_support_pixel():
     """Elongated, rotated, large gaussians (one per view) with the upstream gradient non-zero only
     in a band around each support boundary (9 < q < 13): the renderer backward walks only the
-    ellipse's line spans, and a support pixel missed at the boundary would move the colour gradient
+    ellipse's line spans and the forward only the records whose ellipse reaches a lane, and a
+    support pixel missed at the boundary would move the render (per view) or the colour gradient
     (a sum over about a hundred band pixels) by far more than the tolerance."""
     from rtgs_b200.image2gs.synthetic import _chol_from_sigmas
 
@@ -212,6 +213,12 @@ def test_backward_line_spans_keep_every_support_pixel():
     up = (torch.randn(views, h, w, 3, generator=gen) * band[..., None]).float()
     assert band.sum(dim=(1, 2)).min() > 20
     args = (xy, chol, color, weight)
+    # The renderer forward skips records whose ellipse cannot reach a lane's pixels: a support
+    # pixel skipped there would change its view's render by ~exp(-6) of the view's peak.
+    img = render_gaussians_2d_batched(*cuda(*args), h, w, renderer="cuda").cpu()
+    ref_img = orender.render_batched(*args, h, w)
+    for v in range(views):
+        assert rel_err(img[v], ref_img[v]) <= 1e-5, ("render", v)
     ours = _ours(args, h, w, lambda im: (im * up.to(DEV)).sum())
     ref = oracle_grads(*args, h, w, up)
     for name, a, b in zip(NAMES, ours, ref):
