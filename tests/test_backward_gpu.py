@@ -136,6 +136,56 @@ def test_reference_abi_forward_and_backward_match_oracle():
         assert rel_err(ours, leaf.grad) <= GRAD_TOL, name
 
 
+
+def test_reference_abi_with_conics_that_are_not_positive_definite():
+    """The reference ABI takes any conic. The renderer's reach masks (forward) and line spans
+    (backward) only narrow the walk for positive definite conics; indefinite, degenerate, negative
+    and NaN-free extreme conics must walk their whole rectangles, exactly like the oracle."""
+    h, w = 48, 64
+    gen = torch.Generator().manual_seed(21)
+    conics = torch.tensor([
+        [0.05, 0.0, 0.02],      # positive definite, wide
+        [0.5, 0.0, -0.02],      # indefinite: q < cutoff on a hyperbolic band
+        [0.0, 0.0, 0.08],       # degenerate: no x dependence
+        [-0.01, 0.0, 0.3],      # negative along x
+        [0.1, 0.2, 0.1],        # det < 0
+        [0.2, 0.09, 0.05],      # positive definite, strongly correlated
+        [0.0, 0.0, 0.0],        # zero: every rectangle pixel has q = 0
+        [1e-8, 0.0, 1e-8],      # nearly zero
+    ], dtype=torch.float32)
+    m = conics.shape[0]
+    xy = torch.rand(m, 2, generator=gen) * torch.tensor([w - 20.0, h - 20.0]) + 10.0
+    x0 = (xy[:, 0] - 9).floor().clamp(0, w - 1).int()
+    y0 = (xy[:, 1] - 7).floor().clamp(0, h - 1).int()
+    rects = torch.stack([x0, (x0 + 18).clamp(max=w - 1), y0, (y0 + 14).clamp(max=h - 1)], dim=1).int()
+    colors = torch.rand(m, 3, generator=gen)
+    weights = 0.2 + 0.8 * torch.rand(m, generator=gen)
+    view = torch.zeros(m, dtype=torch.int32)
+    d = cuda(xy, conics, colors, weights, rects, view)
+    lib = _native.lib()
+    arena = _native.arena(DEV)
+    out = torch.empty(1, h, w, 3, device=DEV)
+    den = torch.empty(1, h, w, device=DEV)
+    _native.check(lib.rtgs2d_forward(arena, *(x.data_ptr() for x in d), m, 1, h, w, 12.0,
+                                     out.data_ptr(), den.data_ptr(), None))
+    leaves = [x.clone().requires_grad_(True) for x in (xy, conics, colors, weights)]
+    rimg, rden = orender.accumulate(leaves[0], leaves[1], leaves[2], leaves[3], rects, view, 1, h, w)
+    assert rel_err(out, rimg.reshape(1, h, w, 3)) <= 1e-5
+    assert rel_err(den, rden.reshape(1, h, w)) <= 1e-5
+    up = torch.randn(1, h, w, 3, generator=gen)
+    up_d = torch.randn(1, h, w, generator=gen)
+    ((rimg * up.reshape(-1, 3)).sum() + (rden * up_d.reshape(-1)).sum()).backward()
+    grads = [torch.empty_like(x) for x in (d[0], d[1], d[2], d[3])]
+    up_dev, up_d_dev = up.to(DEV), up_d.to(DEV)
+    _native.check(lib.rtgs2d_backward(arena, up_dev.data_ptr(), up_d_dev.data_ptr(),
+                                      *(x.data_ptr() for x in d), m, 1, h, w, 12.0,
+                                      *(g.data_ptr() for g in grads), None))
+    torch.cuda.synchronize()
+    for name, ours, leaf in zip(("xy", "conics", "colors", "weights"), grads, leaves):
+        for i in range(m):  # per gaussian: each one's gradient is its own rectangle's sum
+            assert rel_err(ours[i], leaf.grad[i]) <= GRAD_TOL, (name, i)
+
+
 def test_reference_abi_rejects_bad_arguments():
     lib = _native.lib()
     arena = _native.arena(DEV)
