@@ -10,9 +10,8 @@
 //             records whose support rectangle covers each of its pixels (in the renderer forward
 //             narrowed to the records whose ellipse can reach them: reach masks); the lane walks
 //             exactly those, in list order, accumulating in registers (flat predicate for the
-//             ellipse test q < cutoff,
-//             exp(-q/2) as one multiply + ex2). The list order is the reference's summation
-//             order, so a render is deterministic and no atomics are used.
+//             ellipse test q < cutoff, exp(-q/2) as one multiply + ex2). The list order is the
+//             reference's summation order, so a render is deterministic and no atomics are used.
 //   backward  the tile's upstream gradients are staged in shared memory; every (gaussian, tile)
 //             entry's piece = support rectangle x tile is evaluated over exactly its pixels and
 //             8 moments
@@ -291,7 +290,11 @@ __device__ __forceinline__ void backward_piece(const float4& geo, const float4& 
   const float t_a = __fmul_rn(sq_a, coef_fix), t_b = __fmul_rn(sq_b, coef_fix);
   constexpr int kStep = ROW ? kTile : 1;        // shared-memory stride of one step
   constexpr int kLaneStride = ROW ? 1 : kTile;  // and of one lane-axis pixel
-  // Pixel A is on at steps st with st - a_first in [0, a_len) (one unsigned compare); B alike.
+  // The lane's steps [0, count) are the union of pixel A's span (from a_first, a_len steps) and
+  // B's; a step inside the union but outside one pixel's own span is still inside the piece, where
+  // that pixel's rounded q >= cutoff (line_span), so only the union bound is tested per step.
+  const int count = static_cast<int>(max(a_first + a_len, b_first + b_len));
+  const bool has_a = a_len > 0, has_b = b_len > 0;
   int sidx_a = sidx0 + r8 * kLaneStride + start * kStep;
   float fvar = (ROW ? pyc0 : pxc0) + static_cast<float>(start);  // integer + 0.5: exact
   float pa[3] = {0.f, 0.f, 0.f}, pb[3] = {0.f, 0.f, 0.f};
@@ -324,16 +327,16 @@ __device__ __forceinline__ void backward_piece(const float4& geo, const float4& 
     const float dv = __fsub_rn(fvar, ROW ? geo.y : geo.x);
     const float sq_v = __fmul_rn(dv, dv);
     const float t_v = __fmul_rn(sq_v, coef_var);
+    const bool on = st < count;
     {
       const float t1 = __fmul_rn(__fmul_rn(da, dv), geo.w);  // dx dy (multiplication commutes)
       const float q = ROW ? __fadd_rn(__fadd_rn(t_a, t1), t_v) : __fadd_rn(__fadd_rn(t_v, t1), t_a);
-      accumulate(static_cast<unsigned>(st) - a_first < a_len && q < cutoff, sidx_a, dv, sq_v, q, pa);
+      accumulate(on && has_a && q < cutoff, sidx_a, dv, sq_v, q, pa);
     }
     if (any_b) {
       const float t1 = __fmul_rn(__fmul_rn(db, dv), geo.w);
       const float q = ROW ? __fadd_rn(__fadd_rn(t_b, t1), t_v) : __fadd_rn(__fadd_rn(t_v, t1), t_b);
-      accumulate(static_cast<unsigned>(st) - b_first < b_len && q < cutoff, sidx_a + 8 * kLaneStride,
-                 dv, sq_v, q, pb);
+      accumulate(on && has_b && q < cutoff, sidx_a + 8 * kLaneStride, dv, sq_v, q, pb);
     }
     fvar += 1.f;
     sidx_a += kStep;
