@@ -38,7 +38,8 @@ extern "C" {
 #define RTGS2D_ERR_INVALID (-1)  /* bad argument (shape, size, null pointer, wrong device) */
 #define RTGS2D_ERR_CUDA (-2)     /* a CUDA runtime call or kernel launch failed */
 #define RTGS2D_ERR_ALLOC (-3)    /* device or pinned allocation failed */
-#define RTGS2D_ERR_CAPACITY (-4) /* problem larger than the 32-bit entry indexing supports */
+#define RTGS2D_ERR_CAPACITY (-4) /* problem larger than the 32-bit entry indexing supports, or (the
+                                    allocation-free entry point) than its static scratch */
 
 /* No reference counterpart: version and error string of this library. */
 RTGS2D_API int rtgs2d_abi_version(void);
@@ -47,9 +48,16 @@ RTGS2D_API const char* rtgs2d_last_error(void);
 /*
  * Scratch arena: owns the growable device buffers that projection, tile binning and the raster
  * kernels need (records, tile entries, sort buffers, per-entry gradient moments). One arena
- * serves one device; it grows on demand (cudaMalloc) and is reused across calls. Not safe for
- * concurrent use from two host threads. Replaces the per-call torch::zeros allocations of the
- * reference extension (src/rtgs/image2gs/cuda/renderer2d_ext.cu:198-199,234-237).
+ * serves one device; it grows on demand (cudaMalloc) and is reused across calls. Replaces the
+ * per-call torch::zeros allocations of the reference extension
+ * (src/rtgs/image2gs/cuda/renderer2d_ext.cu:198-199,234-237).
+ *   - Streams: calls on one arena may use different streams without ordering them: each call's
+ *     stream first waits (cudaStreamWaitEvent) for the end of the previous call's work on the
+ *     arena, whatever stream that was, so their kernels never overlap on the arena's buffers. The
+ *     price is that renders on two streams sharing one arena run one after the other on the
+ *     device; give each stream its own arena for overlap.
+ *   - Host threads: not safe for concurrent calls from two host threads (use one arena per
+ *     thread, or a lock).
  */
 typedef struct rtgs2d_arena rtgs2d_arena;
 RTGS2D_API int rtgs2d_arena_create(rtgs2d_arena** out);
@@ -96,9 +104,14 @@ RTGS2D_API int rtgs2d_backward(rtgs2d_arena* arena, const float* grad_out, const
  *     (gaussian, 16x16 tile) entry, 8 bytes per tile, plus sort/scan temporaries) fail with
  *     RTGS2D_ERR_CAPACITY and a message; use rtgs2d_forward for those.
  *   - Every call on a device shares the array and it keeps the last call's contents; calls whose
- *     GPU work overlaps (different host threads, or streams not ordered with each other) race.
- *   - The first call on each device looks the array's address up with that device current;
- *     make that first call before any stream capture.
+ *     GPU work overlaps on one device (different host threads, or streams not ordered with each
+ *     other) race. Calls on different devices share nothing: each device has its own array and
+ *     its own static host row for the statistics read back.
+ *   - The first call on each device looks the array's address up with that device current. With
+ *     lazy module loading (the CUDA 12 default) that first call is also what commits the 32 MiB
+ *     on the device, so it fails with RTGS2D_ERR_CUDA (out of memory) if another allocator has
+ *     already taken the device's free memory: make it at start-up, before other allocators
+ *     reserve memory and before any stream capture.
  *   - Synchronises `stream` once (the tile-entry count is read back to the host).
  */
 RTGS2D_API int rtgs2d_forward_noalloc(const float* xy, const float* conics, const float* colors,

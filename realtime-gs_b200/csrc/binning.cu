@@ -525,9 +525,10 @@ int check_long_tiles(BinBuffers& bb, const Geometry& g, cudaStream_t s) {
   return check_cuda(cudaGetLastError(), "long_tile_kernel");
 }
 
-int bin_entries(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s) {
+int read_bin_stats(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s) {
   bb.n_entries = 0;
   bb.n_pairs = 0;
+  bb.long_tile = false;
   if (m > INT32_MAX) return set_error(-1, "more than 2^31 gaussians in one call");
   RTGS_TRY(check_long_tiles(bb, g, s));
   if (!bb.host_stats) {
@@ -545,7 +546,12 @@ int bin_entries(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s) {
     return set_error(-4, "more than 2^31 (gaussian, tile) entries in one call");
   }
   bb.n_entries = static_cast<int64_t>(entries);
-  const bool radix = bb.host_stats[kStatLongTile] > 0;
+  bb.long_tile = bb.host_stats[kStatLongTile] > 0;
+  return 0;
+}
+
+int bin_known(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s) {
+  const bool radix = bb.long_tile;
   const bool have = bb.entries[0].ptr != nullptr &&
                     (radix ? bb.entries[1].ptr != nullptr : bb.list.ptr != nullptr);
   if (bb.capacity < bb.n_entries || !have) {
@@ -553,6 +559,11 @@ int bin_entries(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s) {
   }
   if (radix) return bin_radix(bb, g, m, bb.n_entries, s);
   return bin_scatter(bb, g, m, s);
+}
+
+int bin_entries(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s) {
+  RTGS_TRY(read_bin_stats(bb, g, m, s));
+  return bin_known(bb, g, m, s);
 }
 
 int bin_entries_async(BinBuffers& bb, const Geometry& g, int64_t m, bool radix, cudaStream_t s) {

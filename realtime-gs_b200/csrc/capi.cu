@@ -80,6 +80,16 @@ struct rtgs2d_arena {
     bool weights_written;
   } last_forward{};
   bool last_forward_valid = false;
+  // Stream ordering: every call that touches the arena's buffers first makes its stream wait for
+  // the event recorded at the end of the previous such call, then records it again on its own
+  // stream. Calls issued on different streams therefore run one after another on the device, so
+  // one call's kernels never overwrite records, entries or moments another call's kernels still
+  // read (the reference allocated fresh outputs per call, renderer2d_ext.cu:198-199).
+  cudaEvent_t done = nullptr;
+  bool done_recorded = false;
+  ~rtgs2d_arena() {
+    if (done) cudaEventDestroy(done);
+  }
 };
 
 namespace {
@@ -96,6 +106,29 @@ int check_arena(const rtgs2d_arena* a) {
   }
   return 0;
 }
+
+// Orders a call's work on `s` after the previous arena user's (see rtgs2d_arena::done) and, on
+// scope exit (error paths included), marks the end of this call's work for the next user.
+class ArenaUse {
+ public:
+  ArenaUse(rtgs2d_arena* a, cudaStream_t s) : a_(a), s_(s) {}
+  int begin() {
+    if (!a_->done) {
+      RTGS_CUDA(cudaEventCreateWithFlags(&a_->done, cudaEventDisableTiming), "cudaEventCreate");
+    }
+    if (a_->done_recorded) RTGS_CUDA(cudaStreamWaitEvent(s_, a_->done, 0), "cudaStreamWaitEvent");
+    active_ = true;
+    return 0;
+  }
+  ~ArenaUse() {
+    if (active_ && cudaEventRecord(a_->done, s_) == cudaSuccess) a_->done_recorded = true;
+  }
+
+ private:
+  rtgs2d_arena* a_;
+  cudaStream_t s_;
+  bool active_ = false;
+};
 
 int check_dims(int64_t m, int64_t n_views, int64_t height, int64_t width) {
   if (m < 0) return set_error(RTGS2D_ERR_INVALID, "number of gaussians must be non-negative");
@@ -140,6 +173,8 @@ int render_backward(rtgs2d_arena* arena, const float* grad_out, const float* gra
                                    static_cast<int>(width));
   BinBuffers& bb = arena->bb;
   const bool den = grad_den != nullptr;
+  ArenaUse use(arena, s);
+  RTGS_TRY(use.begin());
   const rtgs2d_arena::ForwardKey& k = arena->last_forward;
   const bool same = reuse && arena->last_forward_valid && k.xy == xy && k.chol == chol &&
                     k.color == color && k.weight == weight && k.n_views == n_views && k.n == n &&
@@ -213,6 +248,8 @@ int rtgs2d_forward(rtgs2d_arena* arena, const float* xy, const float* conics, co
   const Geometry g = make_geometry(static_cast<int>(n_views), static_cast<int>(height),
                                    static_cast<int>(width));
   BinBuffers& bb = arena->bb;
+  ArenaUse use(arena, s);
+  RTGS_TRY(use.begin());
   RTGS_TRY(launch_project_conic(bb, g, xy, conics, colors, weights, rects, view_index, m,
                                 den != nullptr, s));
   RTGS_TRY(bin_entries(bb, g, m, s));
@@ -245,6 +282,8 @@ int rtgs2d_backward(rtgs2d_arena* arena, const float* grad_out, const float* gra
                                    static_cast<int>(width));
   BinBuffers& bb = arena->bb;
   const bool den = grad_den != nullptr;
+  ArenaUse use(arena, s);
+  RTGS_TRY(use.begin());
   RTGS_TRY(launch_project_conic(bb, g, xy, conics, colors, weights, rects, view_index, m, den, s));
   RTGS_TRY(bin_entries(bb, g, m, s));
   arena->n_tiles = g.n_tiles();
@@ -272,6 +311,8 @@ int rtgs2d_render_forward(rtgs2d_arena* arena, const float* xy, const float* cho
                                    static_cast<int>(width));
   BinBuffers& bb = arena->bb;
   arena->last_forward_valid = false;
+  ArenaUse use(arena, s);
+  RTGS_TRY(use.begin());
   RTGS_TRY(launch_project_chol(bb, g, xy, chol, color, weight, m, n > 0 ? n : 1, den != nullptr, s));
   RTGS_TRY(bin_entries(bb, g, m, s));
   arena->n_tiles = g.n_tiles();
@@ -321,6 +362,8 @@ int rtgs2d_arena_copy_binning(const rtgs2d_arena* arena, int64_t max_entries, ui
   if (n_entries) *n_entries = ne;
   if (n_tiles) *n_tiles = nt;
   cudaStream_t s = as_stream(stream);
+  ArenaUse use(const_cast<rtgs2d_arena*>(arena), s);
+  RTGS_TRY(use.begin());
   // Per-tile ranges and the ids in read order (ascending inside each tile), on the host.
   std::vector<int32_t> rng(static_cast<size_t>(2 * nt), 0);
   std::vector<uint32_t> ids(static_cast<size_t>(ne), 0);

@@ -87,6 +87,7 @@ struct BinBuffers {
   int64_t capacity = 0;                       // entries the entry buffers can hold
   int64_t n_entries = 0;                      // host-known entry count (synchronous binning)
   int64_t n_pairs = 0;
+  bool long_tile = false;                     // host-known: some tile list exceeds kSegSortMax
   ~BinBuffers();
   void release();
 };
@@ -126,6 +127,11 @@ int launch_build_params(const float* raw, int64_t m, int height, int width, floa
 // grow the entry buffers to fit, then bin asynchronously -- by tile scatter when every tile list
 // fits kSegSortMax, else by the global radix sort. Requires a projection launcher before it.
 int bin_entries(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s);
+// The two halves of bin_entries: read_bin_stats flags long tile lists, reads the stats back into
+// bb.host_stats (synchronises `s`) and sets n_entries, n_pairs and long_tile; bin_known then grows
+// the entry buffers only if they cannot hold n_entries and bins (radix path when long_tile).
+int read_bin_stats(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s);
+int bin_known(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s);
 // stats[kStatLongTile] = the longest tile list if any is longer than kSegSortMax (tile counts
 // must be complete, i.e. after the projection).
 int check_long_tiles(BinBuffers& bb, const Geometry& g, cudaStream_t s);

@@ -17,7 +17,13 @@
 //     whose GPU work overlaps (two host threads, or two streams without ordering between them)
 //     race and corrupt each other; calls ordered on one stream are safe;
 //   - the first call on each device looks up the array's device address (cudaGetSymbolAddress)
-//     with that device current; make that first call before any stream capture.
+//     with that device current. With lazy module loading (the CUDA 12 default) that lookup is
+//     also what commits the array's 32 MiB on the device, so the first call can fail with
+//     RTGS2D_ERR_CUDA (out of memory) when another allocator already holds the device's memory:
+//     make the first call on each device at start-up, before other allocators reserve memory and
+//     before any stream capture;
+//   - the device statistics are read back into a static host row per device, so calls on
+//     different devices (from different host threads) share nothing.
 #include <cub/device/device_scan.cuh>
 
 #include <mutex>
@@ -37,9 +43,13 @@ static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 
 std::mutex g_mu;
 void* g_scratch_addr[kMaxDevices] = {};
-unsigned long long g_host_stats[rtgs2d::kStatSlots];  // entry-count readback (pageable, no host allocation)
+// Readback of the device statistics (entry count, long-tile flag), one row per device like the
+// scratch itself: calls on different devices never share it. Pageable static memory, so the host
+// side allocates nothing either.
+unsigned long long g_host_stats[kMaxDevices][rtgs2d::kStatSlots];
 
-int scratch_base(unsigned char** out) {
+// Device address of this device's scratch and its host readback row (with the device current).
+int scratch_base(unsigned char** out, unsigned long long** host_stats) {
   int dev = -1;
   RTGS_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) {
@@ -52,6 +62,7 @@ int scratch_base(unsigned char** out) {
     g_scratch_addr[dev] = p;
   }
   *out = static_cast<unsigned char*>(g_scratch_addr[dev]);
+  *host_stats = g_host_stats[dev];
   return 0;
 }
 
@@ -120,10 +131,11 @@ extern "C" int rtgs2d_forward_noalloc(const float* xy, const float* conics, cons
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
   unsigned char* base = nullptr;
-  RTGS_TRY(scratch_base(&base));
+  unsigned long long* host_stats = nullptr;
+  RTGS_TRY(scratch_base(&base, &host_stats));
   BorrowedBins holder;
   BinBuffers& bb = holder.bb;
-  bb.host_stats = g_host_stats;
+  bb.host_stats = host_stats;
 
   // Per-gaussian and per-tile buffers (the sizes the projection and binning launchers request).
   const size_t mm = static_cast<size_t>(m > 0 ? m : 1);
@@ -152,23 +164,20 @@ extern "C" int rtgs2d_forward_noalloc(const float* xy, const float* conics, cons
 
   RTGS_TRY(launch_project_conic(bb, g, xy, conics, colors, weights, rects, view_index, m,
                                 den != nullptr, s));
-  RTGS_TRY(check_long_tiles(bb, g, s));
-  // Entry count, to size the entry buffers before the binning writes any entry.
-  RTGS_CUDA(cudaMemcpyAsync(g_host_stats, bb.stats.ptr, kStatSlots * sizeof(unsigned long long),
-                            cudaMemcpyDeviceToHost, s),
-            "entry count readback");
-  RTGS_CUDA(cudaStreamSynchronize(s), "entry count sync");
-  const unsigned long long entries = g_host_stats[kStatEntries];
-  if (entries > static_cast<unsigned long long>(INT32_MAX)) return too_big(entries * 16);
-  const size_t e = static_cast<size_t>(entries > 0 ? entries : 1);
+  // Entry count and long-tile flag (one check, one readback, one synchronisation), to size the
+  // entry buffers before the binning writes any entry.
+  const int rc = read_bin_stats(bb, g, m, s);
+  if (rc == RTGS2D_ERR_CAPACITY) return too_big(static_cast<size_t>(bb.host_stats[kStatEntries]) * 16);
+  RTGS_TRY(rc);
+  const size_t e = static_cast<size_t>(bb.n_entries > 0 ? bb.n_entries : 1);
   // Both binnings need the entries; the tile scatter also the id list, the radix fallback (a
   // tile list longer than the tile sort) the entry double buffer.
-  const bool radix = g_host_stats[kStatLongTile] > 0;
+  const bool radix = bb.long_tile;
   const bool fits = c.take(bb.entries[0], e * sizeof(uint64_t)) &&
                     (radix ? c.take(bb.entries[1], e * sizeof(uint64_t))
                            : c.take(bb.list, e * sizeof(uint32_t)));
   if (!fits) return too_big(c.used + (radix ? 16 : 12) * e);
-  bb.capacity = static_cast<int64_t>(e);  // binning then fits without growing any buffer
-  RTGS_TRY(bin_entries(bb, g, m, s));
+  bb.capacity = static_cast<int64_t>(e);  // so bin_known grows no buffer
+  RTGS_TRY(bin_known(bb, g, m, s));
   return launch_raster_forward(bb, g, static_cast<float>(cutoff), out, den, s);
 }

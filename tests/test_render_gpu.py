@@ -174,3 +174,33 @@ def test_large_image_sampled_pixels_match_oracle():
         err = float((img[py, px] - ref).abs().max()) / max(float(ref.abs().max()), 1e-3)
         worst = max(worst, err)
     assert worst <= RENDER_TOL
+
+
+def test_renders_on_two_streams_sharing_the_arena_match_the_oracle():
+    """Two different scenes rendered (forward and backward) back to back on two torch streams with
+    no host synchronisation between the streams' work: both use the device's one scratch arena,
+    and each call's stream waits for the previous call's work on it, so neither overwrites what
+    the other's kernels still read."""
+    from gpu_helpers import oracle_grads
+
+    h, w = 96, 128
+    scenes = [stacked(21, 2, 3000, h, w, hi=8.0), stacked(22, 2, 2500, h, w, hi=6.0)]
+    ups = [torch.randn(2, h, w, 3, generator=torch.Generator().manual_seed(23 + k)) for k in range(2)]
+    dev = [cuda(*sc) for sc in scenes]
+    dev_ups = [u.to(DEV) for u in ups]
+    streams = [torch.cuda.Stream(DEV), torch.cuda.Stream(DEV)]
+    torch.cuda.synchronize()
+    results = []
+    for k in range(2):
+        with torch.cuda.stream(streams[k]):
+            leaves = [x.clone().requires_grad_(True) for x in dev[k]]
+            img = render_gaussians_2d_batched(*leaves, h, w, renderer="cuda")
+            (img * dev_ups[k]).sum().backward()
+            results.append((img, leaves))
+    torch.cuda.synchronize()
+    for k in range(2):
+        img, leaves = results[k]
+        assert rel_err(img, oracle_render(*scenes[k], h, w)) <= RENDER_TOL, k
+        ref = oracle_grads(*scenes[k], h, w, ups[k])
+        for leaf, r in zip(leaves, ref):
+            assert rel_err(leaf.grad, r) <= 1e-4, k
