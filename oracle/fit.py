@@ -66,6 +66,57 @@ def masked_psnr(pred: torch.Tensor, target: torch.Tensor, mask: torch.Tensor) ->
     return float(-10.0 * torch.log10(mse.clamp_min(1e-12)))
 
 
+class StackedFit:
+    """The stacked-view fit loop, one iteration per ``step`` (``fit_views`` runs it to the end;
+    bench.py's CPU baseline times single iterations of it from any parameter state)."""
+
+    def __init__(self, targets, init, iterations, lr=1e-2, masks=None, freeze_geometry=False, t_max=None):
+        self.targets, self.masks = targets, masks
+        self.n_views, self.height, self.width = targets.shape[:3]
+        self.raw = to_raw(*init, self.height, self.width)
+        names = ("color_raw", "weight_raw") if freeze_geometry else tuple(self.raw)
+        for name, value in self.raw.items():
+            value.requires_grad_(name in names)
+        self.opt = torch.optim.Adam([self.raw[n] for n in names], lr=lr)
+        self.sched = torch.optim.lr_scheduler.CosineAnnealingLR(self.opt, T_max=t_max or iterations,
+                                                                eta_min=lr * 0.1)
+        self.hist = [{"psnr": [], "stopped_iter": iterations - 1} for _ in range(self.n_views)]
+        if masks is not None:
+            self.mw = masks.to(targets).clamp(0, 1)
+            self.denom = self.mw.sum(dim=(1, 2)) * 3.0
+
+    def _psnr(self, pred, b):
+        if self.masks is None:
+            return psnr(pred, self.targets[b])
+        return masked_psnr(pred, self.targets[b], self.masks[b])
+
+    def step(self, it: int, log: bool = False) -> None:
+        self.opt.zero_grad()
+        xy, chol, color, weight = build(self.raw, self.height, self.width)
+        rendered = render2d.render_batched(xy, chol, color, weight, self.height, self.width)
+        if self.masks is None:
+            loss = (rendered - self.targets).square().mean(dim=(1, 2, 3)).sum()
+        else:
+            loss = (((rendered - self.targets) ** 2) * self.mw[..., None]).sum(dim=(1, 2, 3)).div(self.denom).sum()
+        if log:
+            with torch.no_grad():
+                for b in range(self.n_views):
+                    self.hist[b]["psnr"].append((it, self._psnr(rendered[b].clamp(0, 1), b)))
+        loss.backward()
+        self.opt.step()
+        self.sched.step()
+
+    def finish(self):
+        with torch.no_grad():
+            xy, chol, color, weight = build(self.raw, self.height, self.width)
+            final = render2d.render_batched(xy, chol, color, weight, self.height, self.width)
+            for b in range(self.n_views):
+                pred = final[b].clamp(0, 1)
+                self.hist[b]["final_psnr_full"] = psnr(pred, self.targets[b])
+                self.hist[b]["final_psnr"] = self._psnr(pred, b)
+        return (xy, chol, color, weight), self.hist
+
+
 def fit_views(
     targets: torch.Tensor,
     init: tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor],
@@ -74,58 +125,20 @@ def fit_views(
     log_every: int = 50,
     masks: torch.Tensor | None = None,
     freeze_geometry: bool = False,
+    t_max: int | None = None,
 ):
     """Fit stacked (B, H, W, 3) targets from a stacked (B, N, .) initialisation.
 
     Returns (params (xy, chol, color, weight) stacked, histories). With B == 1 and no mask this is
     the single-image native fit (the per-view MSE mean is the serial loss); with a (B, H, W) mask
-    the loss is the mask-restricted mean and PSNR is ``masked_psnr``.
+    the loss is the mask-restricted mean and PSNR is ``masked_psnr``. ``t_max`` (default
+    ``iterations``) is the cosine schedule's length, so the first iterations of a longer fit can be
+    run alone.
     """
-    n_views, height, width = targets.shape[:3]
-    xy0, chol0, color0, weight0 = init
-    raw = to_raw(xy0, chol0, color0, weight0, height, width)
-    names = ("color_raw", "weight_raw") if freeze_geometry else tuple(raw)
-    for name, value in raw.items():
-        value.requires_grad_(name in names)
-    params = [raw[n] for n in names]
-    opt = torch.optim.Adam(params, lr=lr)
-    sched = torch.optim.lr_scheduler.CosineAnnealingLR(opt, T_max=iterations, eta_min=lr * 0.1)
-    hist = [{"psnr": [], "stopped_iter": iterations - 1} for _ in range(n_views)]
-    if masks is not None:
-        mw = masks.to(targets).clamp(0, 1)
-        denom = mw.sum(dim=(1, 2)) * 3.0
-
-    def loss_and_log(rendered, it, log):
-        if masks is None:
-            loss = (rendered - targets).square().mean(dim=(1, 2, 3)).sum()
-        else:
-            loss = (((rendered - targets) ** 2) * mw[..., None]).sum(dim=(1, 2, 3)).div(denom).sum()
-        if log:
-            with torch.no_grad():
-                for b in range(n_views):
-                    pred = rendered[b].clamp(0, 1)
-                    val = psnr(pred, targets[b]) if masks is None else masked_psnr(pred, targets[b], masks[b])
-                    hist[b]["psnr"].append((it, val))
-        return loss
-
+    fit = StackedFit(targets, init, iterations, lr=lr, masks=masks, freeze_geometry=freeze_geometry, t_max=t_max)
     for it in range(iterations):
-        opt.zero_grad()
-        xy, chol, color, weight = build(raw, height, width)
-        rendered = render2d.render_batched(xy, chol, color, weight, height, width)
-        log = it % log_every == 0 or it == iterations - 1
-        loss = loss_and_log(rendered, it, log)
-        loss.backward()
-        opt.step()
-        sched.step()
-    with torch.no_grad():
-        xy, chol, color, weight = build(raw, height, width)
-        final = render2d.render_batched(xy, chol, color, weight, height, width)
-        for b in range(n_views):
-            pred = final[b].clamp(0, 1)
-            full = psnr(pred, targets[b])
-            hist[b]["final_psnr_full"] = full
-            hist[b]["final_psnr"] = full if masks is None else masked_psnr(pred, targets[b], masks[b])
-    return (xy, chol, color, weight), hist
+        fit.step(it, log=it % log_every == 0 or it == iterations - 1)
+    return fit.finish()
 
 
 def fit_serial(target, init, iterations, lr=1e-2, log_every=50, mask=None, coverage_weight=0.0):

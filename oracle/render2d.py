@@ -89,12 +89,23 @@ def accumulate(
     height: int,
     width: int,
     budget: int = 1 << 20,
+    origin: tuple[int, int] = (0, 0),
+    support_inputs: tuple[torch.Tensor, torch.Tensor] | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """Scatter-add every (gaussian, pixel-in-rect) pair; returns flat color sums and densities.
 
     Pairs are enumerated gaussian by gaussian in ascending index and, inside a rectangle, row by
     row; ``index_add`` then sums each pixel in that order (renderer2d.py:228-253). Differentiable
     with respect to xy, conics, color and weight through torch autograd, as in the reference.
+
+    ``origin`` = (x, y) renders a window of a larger frame: pixel coordinates (and rectangles)
+    stay those of the frame, the outputs hold the ``height`` x ``width`` window starting at the
+    origin, and the rectangles must lie inside that window.
+
+    ``support_inputs`` = (xy, conics) computes q from those tensors instead, for the support test
+    and the pair's value exp(-q/2), while the gradient follows q of the differentiable inputs:
+    with float32 support inputs and float64 differentiable inputs, every pair has the float32
+    reference's value and the sums are exact to float64.
     """
     dtype = xy.dtype
     n_pix = n_views * height * width
@@ -124,13 +135,27 @@ def accumulate(
                 off = torch.arange(total) - first[lid]
                 px = x0[gid] + off % nx[gid]
                 py = y0[gid] + off // nx[gid]
-                flat = view_index[gid].long() * (height * width) + py * width + px
+                flat = view_index[gid].long() * (height * width) + (py - origin[1]) * width + (px - origin[0])
             dx = (px.to(dtype) + 0.5) - xy[gid, 0]
             dy = (py.to(dtype) + 0.5) - xy[gid, 1]
             q = ((dx * dx) * conics[gid, 0] + ((2.0 * dx) * dy) * conics[gid, 1]) + (
                 dy * dy
             ) * conics[gid, 2]
-            support = q < CUTOFF
+            if support_inputs is None:
+                support = q < CUTOFF
+            else:
+                with torch.no_grad():
+                    s_xy, s_con = support_inputs
+                    sdx = (px.to(s_xy.dtype) + 0.5) - s_xy[gid, 0]
+                    sdy = (py.to(s_xy.dtype) + 0.5) - s_xy[gid, 1]
+                    sq = ((sdx * sdx) * s_con[gid, 0] + ((2.0 * sdx) * sdy) * s_con[gid, 1]) + (
+                        sdy * sdy
+                    ) * s_con[gid, 2]
+                    support = sq < CUTOFF
+                # The pair's value is the reference's: e at its float32 q (for very elongated
+                # gaussians q is a small difference of large terms, so the float32 and the exact q
+                # differ by far more than the tolerances); the derivative is that of the exact q.
+                q = q + (sq.to(q.dtype) - q).detach()
             e = torch.exp(-0.5 * q.clamp_max(CUTOFF * 4))
             w = torch.where(support, e * weight[gid], torch.zeros_like(e))
             color_sum = color_sum.index_add(0, flat, w[:, None] * color[gid])
@@ -147,16 +172,28 @@ def render_batched(
     height: int,
     width: int,
     with_density: bool = False,
+    accumulate_dtype: torch.dtype | None = None,
 ):
-    """(B, H, W, 3) render of stacked (B, N, .) gaussians, differentiable (renderer2d.py:72-125)."""
+    """(B, H, W, 3) render of stacked (B, N, .) gaussians, differentiable (renderer2d.py:72-125).
+
+    ``accumulate_dtype=torch.float64`` evaluates the reference's float32 pairs (rectangles, q and
+    so the support test and exp(-q/2) from the float32 inputs) with float64 products, derivatives
+    and sums: the float32 reference's render and gradients without the rounding error of float32
+    sums over many pixels.
+    """
     n_views, n = xy.shape[:2]
     xy_f = xy.reshape(-1, 2)
     chol_f = chol.reshape(-1, 3)
     rects = cuda_rects(xy_f, chol_f, height, width)
     conics = chol_conics(chol_f)
     view_index = torch.arange(n_views).repeat_interleave(n)
+    color_f, weight_f, support = color.reshape(-1, 3), weight.reshape(-1), None
+    if accumulate_dtype is not None and accumulate_dtype != xy.dtype:
+        support = (xy_f.detach(), conics.detach())
+        xy_f, color_f, weight_f = xy_f.to(accumulate_dtype), color_f.to(accumulate_dtype), weight_f.to(accumulate_dtype)
+        conics = chol_conics(chol_f.to(accumulate_dtype))
     img, den = accumulate(
-        xy_f, conics, color.reshape(-1, 3), weight.reshape(-1), rects, view_index, n_views, height, width
+        xy_f, conics, color_f, weight_f, rects, view_index, n_views, height, width, support_inputs=support
     )
     img = img.reshape(n_views, height, width, 3)
     if with_density:
@@ -202,6 +239,40 @@ def tile_binning(rects: np.ndarray, view_index: np.ndarray, finite: np.ndarray, 
     ranges[:, 0] = np.where(ends > starts, starts, 0)
     ranges[:, 1] = np.where(ends > starts, ends, 0)
     return vals, ranges
+
+
+def tile_binning_vectorized(rects: np.ndarray, view_index: np.ndarray, finite: np.ndarray, n_views: int,
+                            height: int, width: int):
+    """``tile_binning`` for large scenes (millions of entries): the same (gids, ranges), built with
+    whole-array numpy operations instead of a loop over gaussians (pinned to ``tile_binning`` by
+    the CPU tests)."""
+    tx_n = (width + TILE - 1) // TILE
+    ty_n = (height + TILE - 1) // TILE
+    t_per_view = tx_n * ty_n
+    n_tiles = n_views * t_per_view
+    x0, x1, y0, y1 = (rects[:, k].astype(np.int64) for k in range(4))
+    keep = (x1 >= x0) & (y1 >= y0) & finite
+    gid = np.nonzero(keep)[0]
+    tx_a, ty_a = x0[gid] // TILE, y0[gid] // TILE
+    ntx = x1[gid] // TILE - tx_a + 1
+    cnt = ntx * (y1[gid] // TILE - ty_a + 1)
+    total = int(cnt.sum())
+    ranges = np.zeros((n_tiles, 2), dtype=np.int64)
+    if total == 0:
+        return np.zeros(0, dtype=np.int64), ranges
+    owner = np.repeat(np.arange(gid.size), cnt)
+    local = np.arange(total, dtype=np.int64) - np.repeat(np.cumsum(cnt) - cnt, cnt)
+    tiles = (view_index[gid].astype(np.int64)[owner] * t_per_view
+             + (ty_a[owner] + local // ntx[owner]) * tx_n + tx_a[owner] + local % ntx[owner])
+    gids = gid[owner]
+    base = int(rects.shape[0])
+    key = np.sort(tiles * base + gids)  # unique keys: by tile, then ascending gaussian index
+    tiles, gids = key // base, key % base
+    starts = np.searchsorted(tiles, np.arange(n_tiles), side="left")
+    ends = np.searchsorted(tiles, np.arange(n_tiles), side="right")
+    ranges[:, 0] = np.where(ends > starts, starts, 0)
+    ranges[:, 1] = np.where(ends > starts, ends, 0)
+    return gids, ranges
 
 
 def pair_count(rects: torch.Tensor, finite: torch.Tensor) -> int:

@@ -63,9 +63,14 @@ def oracle_render(xy, chol, color, weight, height, width, with_density=False):
                                   with_density=with_density)
 
 
-def oracle_grads(xy, chol, color, weight, height, width, up, up_den=None):
+def oracle_grads(xy, chol, color, weight, height, width, up, up_den=None, accumulate_dtype=None):
+    """Oracle gradients of sum(render * up) (+ sum(density * up_den)); with
+    ``accumulate_dtype=torch.float64`` the reference's float32 support set with float64 sums."""
     leaves = [x.detach().cpu().clone().requires_grad_(True) for x in (xy, chol, color, weight)]
-    img, den = orender.render_batched(*leaves, height, width, with_density=True)
+    img, den = orender.render_batched(*leaves, height, width, with_density=True, accumulate_dtype=accumulate_dtype)
+    if accumulate_dtype is not None:
+        up = up.to(accumulate_dtype)
+        up_den = None if up_den is None else up_den.to(accumulate_dtype)
     loss = (img * up.cpu()).sum()
     if up_den is not None:
         loss = loss + (den * up_den.cpu()).sum()
