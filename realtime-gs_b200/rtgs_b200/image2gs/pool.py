@@ -1,18 +1,22 @@
-"""Fixed-capacity 2D-gaussian pool with a free list (reference: rtgs/image2gs/pool.py).
+"""Pooled (fixed-capacity, free-list) Stage-1 fitting (reference: src/rtgs/image2gs/pool.py).
 
-Opt-in (``FitConfig.pool``). ``capacity`` raw-parameter rows exist for the whole fit; a boolean
-``active`` mask marks live rows and the parked rows form the free list. The compositor is additive,
-so a parked row is simply not rendered: its contribution and its gradient are exactly zero. Periodic
-triage parks the lowest-weight live rows and spawns new rows at the pixels of largest residual,
-writing parameters in place and zeroing only the touched rows' Adam moments.
+``FitConfig.pool`` fits with ``capacity`` parameter rows allocated once. A byte/bool live mask
+selects the rows that are rendered; the others are spares. The renderer is additive (a pixel is the
+plain sum of its gaussians' weighted colours), so leaving a row out of the render removes exactly
+its contribution and gives it an exactly zero gradient: parking and reviving rows needs no tensor
+resize and no new optimizer, only row writes and a reset of the touched rows' optimizer moments.
 
-Two layers, as in the reference:
-* ``GaussianPool2D`` -- the row store with torch-optimizer park/activate (pool.py:55-151), for
-  callers that drive their own optimizer;
-* ``fit_pooled_from_initialization`` (pool.py:210-291) -- the pooled fit, run by the native fit
-  engine: parked rows are excluded by the engine's projection (``rtgs2d_fit_set_active``), and park
-  / activate become in-place row writes with moment resets (``rtgs2d_fit_write_rows``); the triage
-  itself runs between engine runs, on the device, with torch ops.
+What lives here:
+* ``fit_pooled_from_initialization`` (reference pool.py:210-291) runs the pooled fit inside the
+  native fit engine. The live mask is the engine's own (``rtgs2d_fit_set_active``: its projection
+  gives parked rows no tile entries), and rows are revived with ``rtgs2d_fit_write_rows`` (new raw
+  values plus zeroed Adam moments, in place on the device). Between engine runs a triage event
+  parks the weakest live rows and spawns new rows at the largest residuals of the engine's own
+  render of the current state.
+* ``GaussianPool2D`` (reference pool.py:55-151) is the same row lifecycle for callers that render
+  with ``render_gaussians_2d`` and step their own torch optimizer: five raw leaf tensors of
+  ``capacity`` rows in the optimizer's parameter order, the live mask, and park / activate, which
+  reset every per-row state tensor the optimizer keeps for the touched rows.
 """
 
 from __future__ import annotations
@@ -22,14 +26,13 @@ from typing import TYPE_CHECKING
 import numpy as np
 import torch
 
-from rtgs_b200.core.gaussians2d import Gaussians2D
 from rtgs_b200 import _native
+from rtgs_b200.core.gaussians2d import Gaussians2D
 from rtgs_b200.core.metrics import masked_psnr, psnr
 from rtgs_b200.image2gs.engine import acquire_engine, pack_mask_bits, psnr_values, release_engine
 from rtgs_b200.image2gs.fit import (
     _MIN_DIAG,
     _history_from_engine,
-    _softplus_inv,
     _validate_initial_gaussians,
     raw_from_gaussians,
 )
@@ -37,154 +40,159 @@ from rtgs_b200.image2gs.fit import (
 if TYPE_CHECKING:
     from rtgs_b200.image2gs.fit import FitConfig
 
-# Raw parameter names, in optimizer order (pool.py:41).
-_RAW_NAMES = ("xy_raw", "diag_raw", "off_raw", "color_raw", "weight_raw")
+# The raw fields of one row, in the order an optimizer receives them (the engine's order too).
+RAW_FIELDS = ("xy_raw", "diag_raw", "off_raw", "color_raw", "weight_raw")
+
+# Spawned rows start isotropic with this Cholesky diagonal: the reference sizes them as
+# 0.6 * sqrt(H * W / (number of residual pixels)), floored at _MIN_DIAG + 0.1, and the residual
+# map always has H * W pixels (pool.py:170), so the size is 0.6 pixels at every image size.
+SPAWN_DIAG = 0.6
+SPAWN_WEIGHT = 0.5
 
 
-def _raw_from_gaussians(g: Gaussians2D, wh: torch.Tensor) -> dict[str, torch.Tensor]:
-    """Unconstrained parameters of ``g`` (pool.py:44-52)."""
-    return {
-        "xy_raw": torch.logit((g.xy / wh).clamp(1e-4, 1 - 1e-4)),
-        "diag_raw": _softplus_inv(g.chol[:, [0, 2]] - _MIN_DIAG),
-        "off_raw": g.chol[:, 1].clone(),
-        "color_raw": torch.logit(g.color.clamp(1e-3, 1 - 1e-3)),
-        "weight_raw": torch.logit(g.weight.clamp(1e-3, 1 - 1e-3)),
-    }
+def _raw_rows(g: Gaussians2D, wh: torch.Tensor) -> dict[str, torch.Tensor]:
+    """Raw rows of ``g`` for an image of size wh = (W, H) (the fit's inverse transforms)."""
+    return raw_from_gaussians(g.xy, g.chol, g.color, g.weight, float(wh[1]), float(wh[0]))
+
+
+def _constrained(fields: dict[str, torch.Tensor], wh: torch.Tensor) -> Gaussians2D:
+    """The fit's parameter transforms (fit.py:402-417) applied to raw rows; differentiable."""
+    diag = torch.nn.functional.softplus(fields["diag_raw"]) + _MIN_DIAG
+    return Gaussians2D(
+        xy=torch.sigmoid(fields["xy_raw"]) * wh,
+        chol=torch.stack([diag[:, 0], fields["off_raw"], diag[:, 1]], dim=-1),
+        color=torch.sigmoid(fields["color_raw"]),
+        weight=torch.sigmoid(fields["weight_raw"]),
+    )
+
+
+def _zero_optimizer_rows(optimizer: torch.optim.Optimizer, params: list[torch.Tensor], rows: torch.Tensor) -> None:
+    """Zero, at ``rows``, every state tensor the optimizer keeps per parameter row (Adam's two
+    moments; any optimizer whose state tensors have the parameter's shape)."""
+    for param in params:
+        for value in optimizer.state.get(param, {}).values():
+            if isinstance(value, torch.Tensor) and value.shape == param.shape:
+                value[rows] = 0.0
 
 
 class GaussianPool2D:
-    """Fixed-capacity raw-parameter store with an ``active`` / free-list row lifecycle (pool.py:55-151)."""
+    """``capacity`` raw parameter rows with a live mask (API of the reference's pool.py:55-151).
+
+    Rows ``[0, g0.n)`` start live with ``g0``'s parameters, the rest are parked spares. ``params()``
+    are the five raw leaf tensors to hand to an optimizer; they are never reallocated.
+    """
 
     def __init__(self, g0: Gaussians2D, wh: torch.Tensor, capacity: int):
         if capacity < g0.n:
             raise ValueError(f"pool capacity {capacity} is below the initial count {g0.n}")
-        device, dtype = g0.xy.device, g0.xy.dtype
         self.capacity = int(capacity)
         self.wh = wh
-        self._raw: dict[str, torch.Tensor] = {}
-        seed = _raw_from_gaussians(g0, wh)
-        for name in _RAW_NAMES:
-            init = seed[name]
-            buffer = torch.zeros((capacity, *init.shape[1:]), device=device, dtype=dtype)
-            buffer[: g0.n] = init.detach()
-            buffer.requires_grad_(True)
-            self._raw[name] = buffer
-        self.active = torch.zeros(capacity, dtype=torch.bool, device=device)
-        self.active[: g0.n] = True
+        seed = _raw_rows(g0, wh)
+        self._leaves: dict[str, torch.Tensor] = {}
+        for name in RAW_FIELDS:
+            rows = seed[name].detach()
+            leaf = rows.new_zeros((self.capacity, *rows.shape[1:]))
+            leaf[: g0.n] = rows
+            self._leaves[name] = leaf.requires_grad_(True)
+        self.active = torch.arange(self.capacity, device=g0.xy.device) < g0.n
 
     def params(self) -> list[torch.Tensor]:
         """The raw leaf tensors, in optimizer order."""
-        return [self._raw[name] for name in _RAW_NAMES]
+        return [self._leaves[name] for name in RAW_FIELDS]
 
     @property
     def live_count(self) -> int:
         return int(self.active.sum())
 
     def active_indices(self) -> torch.Tensor:
-        return self.active.nonzero(as_tuple=True)[0]
+        return torch.nonzero(self.active).flatten()
 
     def free_rows(self) -> torch.Tensor:
-        """Parked-row indices (the free list), ascending -- the deterministic spend order."""
-        return (~self.active).nonzero(as_tuple=True)[0]
+        """Parked rows in ascending order: the order in which spawns take them."""
+        return torch.nonzero(~self.active).flatten()
 
     def _build_rows(self, rows: torch.Tensor) -> Gaussians2D:
-        diag = torch.nn.functional.softplus(self._raw["diag_raw"][rows]) + _MIN_DIAG
-        chol = torch.stack([diag[:, 0], self._raw["off_raw"][rows], diag[:, 1]], dim=-1)
-        return Gaussians2D(
-            xy=torch.sigmoid(self._raw["xy_raw"][rows]) * self.wh,
-            chol=chol,
-            color=torch.sigmoid(self._raw["color_raw"][rows]),
-            weight=torch.sigmoid(self._raw["weight_raw"][rows]),
-        )
+        return _constrained({name: leaf[rows] for name, leaf in self._leaves.items()}, self.wh)
 
     def build_active(self) -> Gaussians2D:
-        """Differentiable live-only gaussians (parked rows are omitted -> zero contribution)."""
+        """The live rows as differentiable gaussians; parked rows are simply absent."""
         return self._build_rows(self.active_indices())
 
     def to_gaussians2d(self) -> Gaussians2D:
-        """Detached snapshot of the live rows."""
+        """Detached copy of the live rows."""
         with torch.no_grad():
             return self._build_rows(self.active_indices()).detach()
 
     def built_weights(self) -> torch.Tensor:
-        """Detached ``(capacity,)`` amplitudes; parked rows report their stored (unused) value."""
+        """Amplitudes of all ``capacity`` rows (parked rows report their stored value), detached."""
         with torch.no_grad():
-            return torch.sigmoid(self._raw["weight_raw"])
-
-    def _zero_moments(self, optimizer: torch.optim.Optimizer, rows: torch.Tensor) -> None:
-        for param in self.params():
-            state = optimizer.state.get(param)
-            if not state:
-                continue
-            for key in ("exp_avg", "exp_avg_sq"):
-                if key in state:
-                    state[key][rows] = 0.0
+            return torch.sigmoid(self._leaves["weight_raw"])
 
     def park(self, rows: torch.Tensor, optimizer: torch.optim.Optimizer) -> None:
-        """Return ``rows`` to the free list; clears their optimizer momentum."""
+        """Stop rendering ``rows`` and clear their optimizer state."""
         self.active[rows] = False
-        self._zero_moments(optimizer, rows)
+        _zero_optimizer_rows(optimizer, self.params(), rows)
 
     def activate(self, rows: torch.Tensor, gaussians: Gaussians2D, optimizer: torch.optim.Optimizer) -> None:
-        """Write ``gaussians`` into free ``rows`` in place, mark them live, reset their moments."""
-        raw = _raw_from_gaussians(gaussians, self.wh)
+        """Overwrite ``rows`` with ``gaussians`` (in place), render them again, clear their state."""
+        new = _raw_rows(gaussians, self.wh)
         with torch.no_grad():
-            for name in _RAW_NAMES:
-                self._raw[name].data[rows] = raw[name].to(self._raw[name])
+            for name, leaf in self._leaves.items():
+                leaf[rows] = new[name].to(leaf)
         self.active[rows] = True
-        self._zero_moments(optimizer, rows)
+        _zero_optimizer_rows(optimizer, self.params(), rows)
 
 
-def _residual_spawn_gaussians(
-    target: torch.Tensor, rendered: torch.Tensor, mask: torch.Tensor | None, count: int
-) -> Gaussians2D | None:
-    """Seed up to ``count`` gaussians at the highest-error pixels, deterministic top-k (pool.py:154-182)."""
-    height, width = target.shape[:2]
-    error = (target - rendered).abs().sum(dim=-1)
+def _spawn_raw(target: torch.Tensor, rendered: torch.Tensor, mask: torch.Tensor | None, count: int,
+               wh: torch.Tensor) -> dict[str, torch.Tensor] | None:
+    """Raw rows of up to ``count`` new gaussians at the pixels of largest residual (reference
+    pool.py:154-182): residual = |target - render| summed over the channels (times the mask),
+    the ``count`` largest by torch.topk (ties in topk's order), only pixels with a non-zero
+    residual. Each sits at its pixel centre, isotropic with diagonal SPAWN_DIAG, with the target's
+    colour (clamped to [1e-3, 1 - 1e-3]) and weight SPAWN_WEIGHT."""
+    width = target.shape[1]
+    residual = (target - rendered).abs().sum(dim=-1)
     if mask is not None:
-        error = error * mask.to(error).clamp(0, 1)
-    flat = error.reshape(-1)
-    count = min(count, int((flat > 0).sum()))
+        residual = residual * mask.to(residual).clamp(0, 1)
+    residual = residual.reshape(-1)
+    count = min(count, int(torch.count_nonzero(residual)))
     if count <= 0:
         return None
-    idx = torch.topk(flat, count).indices
-    py = (idx // width).to(target.dtype) + 0.5
-    px = (idx % width).to(target.dtype) + 0.5
-    scale = max((height * width / max(flat.numel(), 1)) ** 0.5 * 0.6, _MIN_DIAG + 0.1)
-    chol = torch.zeros(count, 3, device=target.device, dtype=target.dtype)
-    chol[:, 0] = scale
-    chol[:, 2] = scale
-    return Gaussians2D(
-        xy=torch.stack([px, py], dim=-1),
-        chol=chol,
-        color=target.reshape(-1, 3)[idx].clamp(1e-3, 1 - 1e-3),
-        weight=torch.full((count,), 0.5, device=target.device, dtype=target.dtype),
-    )
+    pick = torch.topk(residual, count).indices
+    centre = torch.stack([pick % width, pick // width], dim=-1).to(target.dtype) + 0.5
+    chol = centre.new_zeros(count, 3)
+    chol[:, 0::2] = SPAWN_DIAG
+    seeds = Gaussians2D(xy=centre, chol=chol,
+                        color=target.reshape(-1, 3)[pick].clamp(1e-3, 1 - 1e-3),
+                        weight=centre.new_full((count,), SPAWN_WEIGHT))
+    return _raw_rows(seeds, wh)
 
 
 def _triage(engine, active: torch.Tensor, target: torch.Tensor, mask: torch.Tensor | None,
             config: FitConfig, wh: torch.Tensor) -> None:
-    """One in-place triage event on the engine's rows (pool.py:185-207): park the lowest-amplitude
-    live rows (keeping ``pool_min_live``), then spawn at the current residual peaks."""
-    live_count = int(active.sum())
-    prune = min(config.pool_prune_count, max(0, live_count - config.pool_min_live))
-    if prune > 0:
-        live = active.nonzero(as_tuple=True)[0]
-        weights = torch.sigmoid(engine.raw()["weight_raw"][0])[live]
-        victims = live[torch.topk(weights, prune, largest=False).indices]
-        active[victims] = False
-        engine.write_rows(victims)  # moments only
-    free = (~active).nonzero(as_tuple=True)[0]
-    budget = min(config.pool_spawn_count, int(free.numel()))
+    """One triage event on the engine's rows (reference pool.py:185-207): park the lowest-amplitude
+    live rows (keeping at least ``pool_min_live``), then spawn into the lowest free rows at the
+    residual peaks of the engine's render of the remaining live set."""
+    live = torch.nonzero(active).flatten()
+    n_park = min(config.pool_prune_count, max(0, live.numel() - config.pool_min_live))
+    if n_park > 0:
+        amplitude = torch.sigmoid(engine.raw()["weight_raw"][0, live])
+        parked = live[torch.topk(amplitude, n_park, largest=False).indices]
+        active[parked] = False
+        engine.write_rows(parked)  # zero their moments; the values stay (parked rows are inert)
+    free = torch.nonzero(~active).flatten()
     engine.set_active(active[None])
-    if budget > 0:
-        rendered, _ = engine.evaluate(want_render=True)
-        seeds = _residual_spawn_gaussians(target, rendered[0], mask, budget)
-        if seeds is not None:
-            rows = free[: seeds.n]
-            engine.write_rows(rows, _raw_from_gaussians(seeds, wh))
-            active[rows] = True
-            engine.set_active(active[None])
+    budget = min(config.pool_spawn_count, free.numel())
+    if budget <= 0:
+        return
+    render, _ = engine.evaluate(want_render=True)
+    seeds = _spawn_raw(target, render[0], mask, budget, wh)
+    if seeds is None:
+        return
+    rows = free[: seeds["weight_raw"].shape[0]]
+    engine.write_rows(rows, seeds)
+    active[rows] = True
+    engine.set_active(active[None])
 
 
 def fit_pooled_from_initialization(
