@@ -187,12 +187,76 @@ def pool_fixture(ref_src: str) -> None:
           final_psnr=hist["final_psnr"], live_count=hist["live_count"])
 
 
+def adapters_fixture(ref_src: str) -> None:
+    """9. Archive adapters (adapters.py:13-82): one archive per layout and naming variant, written
+    to a temporary folder, read by the reference's load_gaussians2d. Stored per case: the archive's
+    arrays (``<case>__in__<field>``), the requested source and the four output fields."""
+    import tempfile
+
+    sys.path.insert(0, ref_src)
+    from rtgs.image2gs.adapters import load_gaussians2d
+
+    gen = np.random.default_rng(9)
+    n = 50
+
+    def angles(k=n):
+        return gen.uniform(-np.pi, np.pi, k).astype(np.float32)
+
+    cases = {
+        "native": ("auto", dict(xy=gen.uniform(0, 40, (n, 2)), chol=np.stack([gen.uniform(0.4, 5, n),
+                   gen.normal(0, 1, n), gen.uniform(0.4, 5, n)], -1), color=gen.uniform(0, 1, (n, 3)),
+                   weight=gen.uniform(0, 1, n))),
+        "structsplat": ("auto", dict(means=gen.uniform(0, 40, (n, 2)), log_scales=gen.normal(0.5, 1.0, (n, 2)),
+                        rotations=angles(), colors=gen.normal(0.5, 0.6, (n, 3)), opacities=gen.normal(0, 2, n),
+                        filter_variance=gen.normal(0.1, 0.2, n))),
+        "structsplat_plain": ("auto", dict(means=gen.uniform(0, 40, (n, 2)), log_scales=gen.normal(0, 1.5, (n, 2)),
+                              rotations=angles(), colors=gen.uniform(0, 1, (n, 3)))),
+        "gi_scales_opacity": ("auto", dict(xy=gen.uniform(0, 40, (n, 2)), scales=gen.uniform(0.01, 9, (n, 2)),
+                              rotation=angles()[:, None], color=gen.normal(0.5, 0.6, (n, 3)),
+                              opacity=gen.normal(0.5, 0.6, (n, 1)))),
+        "gi_isotropic_weight": ("auto", dict(positions=gen.uniform(0, 40, (n, 2)), scale=gen.uniform(0.2, 4, n),
+                                angles=angles(), rgb=gen.uniform(0, 1, (n, 3)), weight=gen.uniform(-0.5, 1.5, n))),
+        "gi_no_weight": ("auto", dict(means=gen.uniform(0, 40, (n, 2)), scaling=gen.uniform(0.3, 3, (n, 2)),
+                         angle=angles(), colors=gen.uniform(0, 1, (n, 3)))),
+        "forced_gaussianimage": ("gaussianimage", dict(means=gen.uniform(0, 40, (n, 2)),
+                                 log_scales=gen.normal(0, 1, (n, 2)), rotations=angles(),
+                                 colors=gen.uniform(0, 1, (n, 3)), opacities=gen.normal(0, 1, n),
+                                 filter_variance=gen.uniform(0, 1, n))),
+        "forced_structsplat_scales": ("structsplat", dict(xy=gen.uniform(0, 40, (n, 2)),
+                                      scales=gen.uniform(0.5, 3, (n, 1)), rotation=angles(),
+                                      color=gen.uniform(0, 1, (n, 3)), filter_variance=gen.uniform(0, 1, (n, 1)))),
+    }
+    out = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        for name, (source, fields) in cases.items():
+            fields = {k: np.asarray(v, dtype=np.float32) for k, v in fields.items()}
+            path = Path(tmp) / f"{name}.npz"
+            np.savez(path, **fields)
+            g = load_gaussians2d(path, source=source)
+            for k, v in fields.items():
+                out[f"{name}__in__{k}"] = v
+            out[f"{name}__source"] = np.array(source)
+            for k in ("xy", "chol", "color", "weight"):
+                out[f"{name}__out__{k}"] = getattr(g, k).numpy()
+        missing = Path(tmp) / "missing.npz"
+        np.savez(missing, means=np.zeros((3, 2), np.float32), colors=np.zeros((3, 3), np.float32),
+                 scales=np.ones((3, 2), np.float32))
+        try:
+            load_gaussians2d(missing)
+        except ValueError as err:
+            out["missing__error"] = np.array(str(err))
+    out["cases"] = np.array(list(cases))
+    _save("adapters", **out)
+
+
 if __name__ == "__main__":
-    # make_golden.py [REF_SRC] [--only pool]
-    args = [a for a in sys.argv[1:] if not a.startswith("--")]
-    ref = args[0] if args and args[0] != "pool" else "/root/reference/src"
-    if "--only" in sys.argv:
-        pool_fixture(ref)
-    else:
+    # make_golden.py [REF_SRC] [--only main|pool|adapters]
+    args = [a for a in sys.argv[1:] if not a.startswith("--") and a not in ("main", "pool", "adapters")]
+    ref = args[0] if args else "/root/reference/src"
+    only = sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None
+    if only in (None, "main"):
         main(ref)
+    if only in (None, "pool"):
         pool_fixture(ref)
+    if only in (None, "adapters"):
+        adapters_fixture(ref)
