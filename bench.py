@@ -19,12 +19,23 @@ Also measured in the same run:
             on its launch stream around every raster launch of one extra fit of the same workload
             run right after the timed fits; algorithmic work = 68 FP32 flop per (gaussian,
             pixel-in-support-rectangle) pair.
+  ranks     per-rank fit and gather device times of the timed steps and their spread (N > 1).
+  sharded   the multi-view configurations through the product sharding API
+            (distributed.fit_views_sharded): the 64 images of batched_720p and the 256 masked
+            views of masked_540p split across the N ranks (strong scaling: total work fixed),
+            images/s from the max-over-ranks device time, per-rank fit / gather times, and e2e
+            with host images in and all fitted parameters back on the host.
   splat     the 4K micro-benchmark: 1,000,000 fixed gaussians on 3840x2160, forward + backward
-            through the renderer C ABI with an N(0,1) upstream gradient (Gpixel.gauss/s).
+            through the renderer C ABI with an N(0,1) upstream gradient (Gpixel.gauss/s), beside
+            the CPU oracle's forward + backward on a 1/16 subset of the gaussians.
+  single_small  the 128x128 / 2,000-gaussian / 200-iteration fit: on the GPU through the public
+            API, and on the CPU with the oracle, timed in full (N = 1).
   cpu_baseline  the CPU oracle (restatement of the reference's pure-PyTorch fit) on the host
-            cores, a bounded number of iterations of the same workload, scaled to fits/s.
+            cores: 5 timed iterations at the start, the middle and the end of the fit (parameter
+            states taken from the GPU fit), combined by the trapezoid rule into fits/s.
 
-``--impl reference`` times only that CPU implementation (rank 0; other ranks exit at once).
+``--impl reference`` times only that CPU implementation (rank 0; other ranks exit at once), on
+the same workload and config: each step is 5 oracle iterations from the fit's initial state.
 """
 
 from __future__ import annotations
@@ -64,7 +75,9 @@ def parse_args():
                     help="images fitted together in one engine per GPU and step (batched fit); value counts images")
     ap.add_argument("--no-splat", action="store_true", help="skip the 4K splat micro-benchmark")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--cpu-iters", type=int, default=2, help="oracle iterations per CPU sample step")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the multi-view configurations fitted through distributed.fit_views_sharded")
+    ap.add_argument("--sharded-steps", type=int, default=2, help="timed passes of each sharded configuration")
     ap.add_argument("--iterations", type=int, default=None, help="override the fit length (profiling runs)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the public-API end-to-end measurement")
     ap.add_argument("--only-splat", action="store_true", help="run only the 4K splat micro-benchmark")
@@ -124,13 +137,27 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------------------------
-def cpu_fit_sample(wl: dict, seed: int, iters: int, steps: int, warmup: int) -> dict:
-    """Time the CPU oracle fit (reference algorithm on torch CPU) for `iters` iterations per step."""
-    from oracle import fit as ofit
+CPU_SAMPLE_ITERS = 5  # oracle iterations timed per CPU sample (after one untimed iteration)
+
+
+def workload_config(name: str, wl: dict, views: int, world: int) -> dict:
+    """The ``config`` object of the JSON line: identical in the native and the reference arm."""
+    return {
+        "workload": name, "height": wl["height"], "width": wl["width"], "gaussians": wl["n_fit"],
+        "iterations": wl["iterations"], "source_gaussians": wl["n_sources"],
+        "source_sigma_px": list(wl["sigma"]), "noise_sd": wl["noise"],
+        "images_per_gpu_per_step": views, "parallelism": f"dp{world} (whole images)",
+        "loss": "L2 over mask pixels (bit-packed masks)" if wl.get("masked") else "L2",
+        "l2": f"256 MB buffer written between timed fits; a fit's own {wl['iterations']} iterations run L2-warm",
+    }
+
+
+def cpu_target(wl: dict, seed: int):
+    """(target (H, W, 3), init (xy, chol, color, weight) stacked (1, N, .), mask (1, H, W) or None)
+    of the workload on the CPU (oracle render of the sources)."""
     from oracle import render2d as orender
     from rtgs_b200.image2gs import synthetic
 
-    torch.set_num_threads(os.cpu_count() or 1)
     h, w = wl["height"], wl["width"]
     src = synthetic.source_gaussians(seed, wl["n_sources"], h, w, wl["sigma"])
     with torch.no_grad():
@@ -143,39 +170,124 @@ def cpu_fit_sample(wl: dict, seed: int, iters: int, steps: int, warmup: int) -> 
         mask = mask[None]
     else:
         init = synthetic.fit_init(seed, wl["n_fit"], h, w)
-    init = tuple(x[None] for x in (init.xy, init.chol, init.color, init.weight))
-    times = []
-    for k in range(warmup + steps):
-        t0 = time.perf_counter()
-        ofit.fit_views(target[None], init, iters, lr=1e-2, log_every=10**9, masks=mask)
-        dt = time.perf_counter() - t0
-        if k >= warmup:
-            times.append(dt)
-    # fit_views also renders the final state once: subtract nothing (conservative for the CPU).
-    per_iter = statistics.median(times) / (iters + 1)
-    fits_per_s = 1.0 / (per_iter * wl["iterations"])
-    return {"value": fits_per_s, "unit": "fits/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"{wl['height']}x{wl['width']} target{' (masked loss)' if mask is not None else ''}, "
-                      f"{wl['n_fit']} gaussians: {iters} oracle iterations "
-                      f"(+1 final render) per step, median of {steps} steps after {warmup} warm-up, "
-                      f"scaled to {wl['iterations']} iterations",
-            "s_per_iteration": per_iter}
+    return target, tuple(x[None] for x in (init.xy, init.chol, init.color, init.weight)), mask
 
 
-def run_reference(args, wl, rank: int) -> None:
+def oracle_seconds_per_iteration(target, state, wl: dict, mask, iters: int = CPU_SAMPLE_ITERS) -> float:
+    """Seconds per iteration of the CPU oracle fit loop (build, render, loss, backward, Adam,
+    cosine step) from parameter state ``state``: one untimed iteration, then ``iters`` timed."""
+    from oracle import fit as ofit
+
+    fit = ofit.StackedFit(target[None], tuple(x.detach().cpu().clone() for x in state), wl["iterations"],
+                          lr=1e-2, masks=mask)
+    fit.step(0)
+    t0 = time.perf_counter()
+    for it in range(1, iters + 1):
+        fit.step(it)
+    return (time.perf_counter() - t0) / iters
+
+
+def cpu_fit_estimate(target, states: dict[int, tuple], wl: dict, mask) -> dict:
+    """CPU oracle fits/s from timed samples at several points of the fit (iteration -> state):
+    the seconds per iteration are integrated over the fit by the trapezoid rule."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    points = sorted(states)
+    sec = {k: oracle_seconds_per_iteration(target, states[k], wl, mask) for k in points}
+    total = 0.0
+    for a, b in zip(points[:-1], points[1:]):
+        total += 0.5 * (sec[a] + sec[b]) * (b - a)
+    total += sec[points[-1]] * (wl["iterations"] - points[-1])  # the last sample covers the tail
+    total += sec[points[0]] * points[0]
+    return {"value": 1.0 / total, "unit": "fits/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{wl['height']}x{wl['width']}, {wl['n_fit']} gaussians: {CPU_SAMPLE_ITERS} oracle iterations "
+                      f"(after 1 untimed) from the parameter states at iterations {points} of the GPU fit, "
+                      f"seconds per iteration integrated over the {wl['iterations']} iterations (trapezoid)",
+            "s_per_iteration_at": {str(k): sec[k] for k in points},
+            "start_of_fit_value": 1.0 / (sec[points[0]] * wl["iterations"])}
+
+
+def run_reference(args, wl, rank: int, world: int) -> None:
+    """The reference arm: the CPU oracle alone, each step CPU_SAMPLE_ITERS iterations from the fit's
+    initial state (no GPU involved), scaled to the fit's iteration count."""
     if rank != 0:
         return
-    res = cpu_fit_sample(wl, 1000, args.cpu_iters, args.steps, args.warmup)
+    torch.set_num_threads(os.cpu_count() or 1)
+    target, init, mask = cpu_target(wl, 1000)
+    for _ in range(args.warmup):
+        oracle_seconds_per_iteration(target, init, wl, mask, iters=1)
+    per_iter = [oracle_seconds_per_iteration(target, init, wl, mask) for _ in range(args.steps)]
+    sec = statistics.median(per_iter)
+    value = 1.0 / (sec * wl["iterations"])
     line = {
-        "metric": "2D-gaussian image fits/sec", "value": res["value"], "unit": "fits/s", "impl": "reference",
+        "metric": "2D-gaussian image fits/sec", "value": value, "unit": "fits/s", "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": res["s_per_iteration"] * args.cpu_iters * 1e3, "higher_is_better": True,
+        "ms_per_step": sec * CPU_SAMPLE_ITERS * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, **{k: v for k, v in wl.items() if k != "sigma"}, "sigma": list(wl["sigma"])},
-        "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
-        "e2e": {"value": res["value"], "unit": "fits/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "config": workload_config(args.workload, wl, max(1, int(args.views)), world),
+        "cpu_baseline": {"value": value, "unit": "fits/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"each step: {CPU_SAMPLE_ITERS} oracle iterations (after 1 untimed) from the "
+                                   f"fit's initial state, {wl['height']}x{wl['width']}, {wl['n_fit']} gaussians; "
+                                   f"median of {args.steps} steps scaled to {wl['iterations']} iterations"},
+        "e2e": {"value": value, "unit": "fits/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def cpu_splat_sample(stride: int = 16) -> dict:
+    """CPU oracle forward + backward of the 4K splat on every ``stride``-th gaussian (same upstream
+    gradient); throughput in (gaussian, pixel-in-rectangle) pairs per second."""
+    from oracle import render2d as orender
+    from rtgs_b200.image2gs import synthetic
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    h, w = 2160, 3840
+    sc = synthetic.splat_scene(0)
+    sub = [x[::stride][None].clone().requires_grad_(True) for x in (sc.xy, sc.chol, sc.color, sc.weight)]
+    up = synthetic.splat_upstream_grad(0, 1, h, w)
+    rects = orender.cuda_rects(sub[0][0].detach(), sub[1][0].detach(), h, w)
+    pairs = orender.pair_count(rects, torch.isfinite(sub[0][0].detach()).all(1))
+    t0 = time.perf_counter()
+    img = orender.render_batched(*sub, h, w)
+    (img * up).sum().backward()
+    dt = time.perf_counter() - t0
+    return {"gpairs_per_s": pairs / dt / 1e9, "pairs": pairs, "s": dt, "cores": torch.get_num_threads(),
+            "sample": f"one forward + backward of every {stride}th gaussian ({sub[0].shape[1]} of 1,000,000) "
+                      f"on the 3840x2160 frame, oracle renderer"}
+
+
+def single_small_block(device) -> dict:
+    """The 128x128 / 2,000-gaussian / 200-iteration fit: GPU (device-timed engine fits and the public
+    API on host buffers) and the CPU oracle, each timed in full."""
+    from oracle import fit as ofit
+    from rtgs_b200.core.gaussians2d import Gaussians2D
+    from rtgs_b200.image2gs import synthetic
+    from rtgs_b200.image2gs.fit import FitConfig, fit_image_from_initialization
+
+    wl = synthetic.WORKLOADS["single_small"]
+    target, init, _ = cpu_target(wl, 0)
+    cfg = FitConfig(n_gaussians=wl["n_fit"], iterations=wl["iterations"], log_every=50)
+    host = [target.pin_memory()] + [x[0].pin_memory() for x in init]
+    times = []
+    for k in range(4):
+        torch.cuda.synchronize(device)
+        t0 = time.perf_counter()
+        dev = [x.to(device, non_blocking=True) for x in host]
+        fitted, hist = fit_image_from_initialization(dev[0], Gaussians2D(*dev[1:]), cfg)
+        out = fitted.xy.cpu(), fitted.chol.cpu(), fitted.color.cpu(), fitted.weight.cpu()
+        torch.cuda.synchronize(device)
+        if k > 0:
+            times.append(time.perf_counter() - t0)
+    torch.set_num_threads(os.cpu_count() or 1)
+    t0 = time.perf_counter()
+    _, ohist = ofit.fit_views(target[None], init, wl["iterations"], lr=1e-2, log_every=50)
+    cpu_s = time.perf_counter() - t0
+    e2e = 1.0 / statistics.median(times)
+    return {"workload": "single_small: 128x128, 500 sources, 2,000 gaussians, 200 iterations",
+            "e2e_fits_per_s": e2e, "api": "fit_image_from_initialization (host buffers in and out)",
+            "cpu_fits_per_s": 1.0 / cpu_s, "cpu_cores": torch.get_num_threads(),
+            "cpu_sample": "one complete oracle fit (200 iterations + final render), kind port",
+            "e2e_vs_cpu": e2e * cpu_s, "final_psnr_gpu": hist["final_psnr"],
+            "final_psnr_cpu": ohist[0]["final_psnr"]}
 
 
 # ---------------------------------------------------------------------------------------------
@@ -271,6 +383,137 @@ def e2e_fit(device, wl, targets_host, init_host, masks_host, steps: int) -> tupl
     return statistics.median(times), h2d, d2h, api
 
 
+def gather_floats(values: list[float], world: int) -> list[list[float]]:
+    """Every rank's list of floats (host objects through the process group); [values] at N = 1."""
+    if world == 1:
+        return [list(values)]
+    import torch.distributed as dist
+
+    out: list = [None] * world
+    dist.all_gather_object(out, list(values))
+    return out
+
+
+def max_over_ranks(value: float, device, world: int) -> float:
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+SHARDED_ENGINE_VIEWS = {"batched_720p": 8, "masked_540p": 32}
+
+
+def sharded_block(name: str, device, rank: int, world: int, steps: int, warmup: int) -> dict:
+    """All views of multi-view workload `name` fitted through distributed.fit_views_sharded: rank r
+    fits its contiguous block (the views of one engine at a time), then every rank gathers every
+    view's fitted parameters. Strong scaling: the total number of views is fixed."""
+    from rtgs_b200.image2gs import synthetic
+    from rtgs_b200.image2gs.batched import fit_stacked
+    from rtgs_b200.image2gs.distributed import fit_views_sharded, shard_range
+    from rtgs_b200.image2gs.fit import FitConfig
+    from rtgs_b200.image2gs.renderer2d import render_gaussians_2d_batched
+
+    wl = synthetic.WORKLOADS[name]
+    n_images, h, w, n = wl["n_views"], wl["height"], wl["width"], wl["n_fit"]
+    masked = bool(wl.get("masked"))
+    per_engine = SHARDED_ENGINE_VIEWS[name]
+    base_seed = 2000  # view i uses seed 2000 + i whatever the number of ranks
+    start, stop = shard_range(n_images, rank, world)
+    seeds = list(range(base_seed + start, base_seed + stop))
+    targets = [synthetic.make_target(sd, wl, render_gaussians_2d_batched, device) for sd in seeds]
+    masks = [synthetic.ellipse_mask(sd, h, w) for sd in seeds] if masked else None
+    inits = [synthetic.masked_fit_init(sd, n, m) if masked else synthetic.fit_init(sd, n, h, w)
+             for sd, m in zip(seeds, masks or [None] * len(seeds))]
+    init_rows = [(g.xy, g.chol, g.color, g.weight) for g in inits]
+    cfg = FitConfig(n_gaussians=n, iterations=wl["iterations"], log_every=50)
+    fit_end: list = []
+
+    def fit_fn(local, config, first_seed):
+        results, hists = [], []
+        for b0 in range(0, len(local), per_engine):
+            b1 = min(b0 + per_engine, len(local))
+            imgs = torch.stack([im.to(device, non_blocking=True) for im in local[b0:b1]])
+            init = tuple(torch.stack([row[k] for row in init_rows[b0:b1]]).to(device, non_blocking=True)
+                         for k in range(4))
+            m = torch.stack(masks[b0:b1]).to(device, non_blocking=True) if masked else None
+            r, hh = fit_stacked(imgs, init, config, masks=m)
+            results += r
+            hists += hh
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        fit_end.append(ev)
+        return results, hists
+
+    def run(images):
+        return fit_views_sharded(images, cfg, base_seed, fit_fn=fit_fn, device=device)
+
+    images = [None] * n_images
+    images[start:stop] = targets
+    for _ in range(warmup):
+        run(images)
+    torch.cuda.synchronize(device)
+    fit_ms, gather_ms, total_ms = [], [], []
+    psnr = []
+    for _ in range(steps):
+        barrier(world)
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        _, hist = run(images)
+        e1.record()
+        e1.synchronize()
+        total_ms.append(e0.elapsed_time(e1))
+        fit_ms.append(e0.elapsed_time(fit_end[-1]))
+        gather_ms.append(total_ms[-1] - fit_ms[-1])
+        psnr = [hh["final_psnr"] for hh in hist]
+    step_ms = max_over_ranks(statistics.median(total_ms), device, world)
+    # e2e: host images (and host masks / initial parameters) in, every view's parameters out
+    host_images = [None] * n_images
+    host_images[start:stop] = [t.cpu().pin_memory() for t in targets]
+    init_rows = [tuple(x.pin_memory() for x in row) for row in init_rows]
+    if masked:
+        masks = [m.pin_memory() for m in masks]
+    out_host = torch.empty(n_images, n, 9, pin_memory=True)
+    barrier(world)
+    torch.cuda.synchronize(device)
+    t0 = time.perf_counter()
+    fitted, _ = run(host_images)
+    packed = torch.stack([torch.cat([g.xy, g.chol, g.color, g.weight[:, None]], 1) for g in fitted])
+    out_host.copy_(packed, non_blocking=True)
+    torch.cuda.synchronize(device)
+    e2e_s = max_over_ranks(time.perf_counter() - t0, device, world)
+    ranks_fit = gather_floats([statistics.median(fit_ms)], world)
+    ranks_gather = gather_floats([statistics.median(gather_ms)], world)
+    fits = [r[0] for r in ranks_fit]
+    h2d = sum(t.numel() * 4 for t in targets) + sum(x.numel() * 4 for row in init_rows for x in row)
+    if masked:
+        h2d += sum(m.numel() * m.element_size() for m in masks)
+    return {
+        "workload": f"{name}: {n_images} views of {w}x{h}, {n} gaussians each, {wl['iterations']} iterations"
+                    + (", L2 over bit-packed ellipse masks" if masked else "")
+                    + f"; views split {n_images}/{world} per GPU through distributed.fit_views_sharded "
+                      f"({per_engine} views per engine), then one all-gather of every view's parameters",
+        "scaling": "strong", "value": n_images / (step_ms / 1e3), "unit": "images/s",
+        "ms_per_step": step_ms, "steps": steps, "warmup": warmup,
+        "rank_fit_ms": fits, "rank_gather_ms": [r[0] for r in ranks_gather],
+        "rank_fit_skew_ms": max(fits) - min(fits),
+        "e2e": {"value": n_images / e2e_s, "unit": "images/s", "h2d_bytes_per_step": int(max_over_ranks(h2d, device, world) * world),
+                "d2h_bytes_per_step": int(out_host.numel() * 4 * world),
+                "api": "distributed.fit_views_sharded with host images"},
+        "mean_final_psnr_db_rank0_views": float(np.mean(psnr)) if psnr else None,
+    }
+
+
 def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
     import torch.distributed as dist
 
@@ -308,11 +551,15 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
     mask_px = (masks.reshape(views, -1) > 0.5).sum(1).double().numpy() if masked else np.full(views, float(h * w))
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)  # > 126 MB L2
     gathered = torch.empty(world, views * n, 9, device=device) if world > 1 else None
+    fit_done = [None]
 
     def one_fit():
         engine.set_raw(raw)
         engine.run(iters)
         if world > 1:  # the single collective of the job: gather every rank's fitted parameters
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            fit_done[0] = ev
             xy, chol, color, weight = (t.reshape(views * n, -1) for t in engine.params())
             packed = torch.cat([xy, chol, color, weight], dim=1).contiguous()
             dist.all_gather_into_tensor(gathered, packed)
@@ -320,10 +567,9 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
     for _ in range(args.warmup):
         one_fit()
     torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier()
+    barrier(world)
     sampler = ClockSampler(device)
-    step_ms = []
+    step_ms, fit_ms = [], []
     t_wall = time.perf_counter()
     for _ in range(args.steps):
         flush.zero_()
@@ -333,9 +579,9 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
         e1.record()
         e1.synchronize()
         step_ms.append(e0.elapsed_time(e1))
+        fit_ms.append(e0.elapsed_time(fit_done[0]) if world > 1 else step_ms[-1])
     torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier()
+    barrier(world)
     wall_s = time.perf_counter() - t_wall
     clocks = sampler.stop()
     _, sums = engine.evaluate(want_render=False)
@@ -345,16 +591,24 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
     # of the timed fits because the event records themselves lengthen an iteration.
     engine.set_profiling(True)
     flush.zero_()
-    one_fit()
+    engine.set_raw(raw)
+    engine.run(iters)
     torch.cuda.synchronize(device)
     stages = engine.stage_times()
     engine.set_profiling(False)
+    # Parameter states for the CPU baseline's samples (start, middle and end of the fit).
+    cpu_states = {}
+    if world == 1 and not args.no_cpu and views == 1:
+        engine.set_raw(raw)
+        cpu_states[0] = tuple(x[:1].cpu() for x in init_stack)
+        for at in (iters // 2, iters - CPU_SAMPLE_ITERS - 1):
+            engine.run(at - engine.stats()["step"])
+            cpu_states[at] = tuple(x[:1].cpu() for x in engine.params())
 
-    total_ms = torch.tensor([sum(step_ms)], dtype=torch.float64, device=device)
-    if world > 1:
-        dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
-    total_ms = float(total_ms.item())
+    total_ms = max_over_ranks(sum(step_ms), device, world)
     value = world * views * args.steps / (total_ms / 1e3)
+    ranks_fit = [r[0] for r in gather_floats([statistics.median(fit_ms)], world)]
+    ranks_step = [r[0] for r in gather_floats([statistics.median(step_ms)], world)]
 
     # e2e through the public API with host buffers (all ranks concurrently).
     targets_host = targets.cpu().pin_memory()
@@ -364,18 +618,18 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
     e2e_value, h2d, d2h, e2e_api = None, 0, 0, None
     if not args.no_e2e:
         e2e_s, h2d, d2h, e2e_api = e2e_fit(device, wl, targets_host, init_host, masks_host, steps=2)
-        e2e_t = torch.tensor([e2e_s], dtype=torch.float64, device=device)
-        if world > 1:
-            dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
-        e2e_value = world * views / float(e2e_t.item())
+        e2e_value = world * views / max_over_ranks(e2e_s, device, world)
+
+    sharded = {}
+    if not args.no_sharded:
+        for name in ("batched_720p", "masked_540p"):
+            sharded[name] = sharded_block(name, device, rank, world, steps=args.sharded_steps, warmup=1)
 
     splat = None
     if not args.no_splat:
         splat = splat_microbench(device, steps=5, warmup=3)
-        st = torch.tensor([splat["ms"]], dtype=torch.float64, device=device)
-        if world > 1:
-            dist.all_reduce(st, op=dist.ReduceOp.MAX)
-        splat["aggregate_gpairs_per_s"] = world * splat["pairs"] / (float(st.item()) * 1e-3) / 1e9
+        st = max_over_ranks(splat["ms"], device, world)
+        splat["aggregate_gpairs_per_s"] = world * splat["pairs"] / (st * 1e-3) / 1e9
 
     if rank != 0:
         return
@@ -390,9 +644,17 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
     if prof.exists():
         traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
     cpu = None
+    small = None
+    cpu_splat = None
     if world == 1 and not args.no_cpu:
-        res = cpu_fit_sample(wl, seeds[0], args.cpu_iters, steps=1, warmup=1)
-        cpu = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        if cpu_states:
+            target_cpu = targets[0].cpu()
+            res = cpu_fit_estimate(target_cpu, cpu_states, wl, masks[:1] if masked else None)
+            cpu = {k: res[k] for k in ("value", "unit", "cores", "kind", "sample", "s_per_iteration_at",
+                                       "start_of_fit_value")}
+        small = single_small_block(device)
+        if splat is not None:
+            cpu_splat = cpu_splat_sample()
     # Own kernels per fit, per 64-iteration chunk of c iterations: the chunk's projection; the
     # first iteration's tile-count scan (own single-block kernel up to 8192 tiles, else CUB's two,
     # counted as library launches) and scatter; then per iteration tile sort, raster fit and Adam
@@ -416,13 +678,8 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
-        "config": {
-            "workload": args.workload, "height": h, "width": w, "gaussians": n, "iterations": iters,
-            "source_gaussians": wl["n_sources"], "images_per_gpu_per_step": views, "parallelism": f"dp{world} (whole images)",
-            "l2": f"256 MB buffer written between timed fits; a fit's own {iters} iterations run L2-warm",
-            "loss": "L2 over mask pixels (bit-packed masks)" if masked else "L2",
-            "final_psnr_db": final_psnr,
-        },
+        "config": workload_config(args.workload, wl, views, world),
+        "final_psnr_db": final_psnr,
         "e2e": {"value": e2e_value, "unit": "fits/s", "h2d_bytes_per_step": int(h2d * world),
                 "d2h_bytes_per_step": int(d2h * world), "api": e2e_api},
         "roofline": {
@@ -437,12 +694,21 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
             "stage_ms_per_iteration": {"project_bin": stages["bin_ms"] / its, "raster": stages["raster_ms"] / its,
                                        "adam": stages["adam_ms"] / its},
         },
+        "ranks": {"step_ms": ranks_step, "fit_ms": ranks_fit,
+                  "gather_ms": [a - b for a, b in zip(ranks_step, ranks_fit)],
+                  "fit_skew_ms": max(ranks_fit) - min(ranks_fit),
+                  "note": "median over the timed steps per rank; step = fit + the parameter all-gather, "
+                          "which waits for the slowest rank (each rank fits a different image)"},
         "cpu_baseline": cpu,
         "gpu_launches": args.steps * own_per_fit,
         "library_launches": args.steps * lib_per_fit,
         "clocks": clocks,
         "wall_s_timed_region": wall_s,
     }
+    if sharded:
+        line["sharded"] = sharded
+    if small is not None:
+        line["single_small"] = small
     if splat is not None:
         line["splat_fwd_bwd"] = {
             "workload": "splat_4k: 3840x2160, 1,000,000 gaussians, fixed parameters, N(0,1) upstream grad",
@@ -452,6 +718,8 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
             "achieved_tflops": FLOP_PER_PAIR * splat["pairs"] / (splat["ms"] * 1e-3) / 1e12,
             "frac_fp32": FLOP_PER_PAIR * splat["pairs"] / (splat["ms"] * 1e-3) / 1e12 / fp32_peak,
         }
+        if cpu_splat is not None:
+            line["splat_fwd_bwd"]["cpu_baseline"] = cpu_splat
     print(json.dumps(line), flush=True)
 
 
@@ -468,7 +736,7 @@ def main() -> None:
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
-        run_reference(args, wl, rank)
+        run_reference(args, wl, rank, world)
         return
     if world > 1:
         import torch.distributed as dist

@@ -53,8 +53,11 @@ def fit_views_sharded(
 ) -> tuple[list[Gaussians2D], list[dict]]:
     """Fit all `images` across the ranks of `group`; every rank returns every view's result.
 
-    ``images`` is the full list (each rank only touches its own block). ``fit_fn(local_images,
-    config, seed_of_first)`` defaults to the batched fit engine (``fit_views_batched``).
+    ``images`` is the full list; each rank reads only its own block, so entries outside it may be
+    None (a rank then never holds the other ranks' images). ``fit_fn(local_images, config,
+    seed_of_first)`` defaults to the batched fit engine (``fit_views_batched``). ``device`` is
+    where the gathered parameters live (default: the first local image's device; give a CUDA
+    device when the local images are host tensors).
     """
     if fit_fn is None:
         from rtgs_b200.image2gs.batched import fit_views_batched
@@ -68,7 +71,7 @@ def fit_views_sharded(
     n = config.n_gaussians
     per = -(-len(images) // world) if images else 0
     if device is None:
-        device = images[0].device if images else torch.device("cpu")
+        device = next((im.device for im in local if im is not None), torch.device("cpu"))
     packed = pack(results, per, n, device)
     gathered = torch.empty(world * per, n, PARAMS_PER_GAUSSIAN, device=device, dtype=torch.float32)
     dist.all_gather_into_tensor(gathered, packed, group=group)
