@@ -133,13 +133,16 @@ __device__ __forceinline__ void direct_commit(int64_t gid, int cnt, const TileSp
   }
 }
 
-// Record, span, tile count and entry offset of gaussian i. Must be called by every lane of a warp.
+// Record, span, tile count and entry offset of gaussian i. Must be called by every thread of a
+// block of kProjThreads threads (it synchronises the block).
 //
-// Entry offsets: a warp-wide exclusive scan of the tile counts plus the warp's base, reserved with
-// one atomic on stats[kStatEntries]. Warps reserve in arrival order, so a gaussian's entry index
-// varies from run to run; nothing reads entries in index order (the raster addresses its tile's
-// entries through the gaussian, the gradient gather reads a gaussian's own entries), so no result
-// depends on it.
+// Entry offsets: a warp-wide exclusive scan of the tile counts, the warps' totals scanned in
+// shared memory, and one atomic on stats[kStatEntries] per block for the block's base (the entry
+// and pair counters are single addresses that every block updates, so one update per block
+// instead of one per warp keeps them off the critical path). Blocks reserve in arrival order, so
+// a gaussian's entry index varies from run to run; nothing reads entries in index order (the
+// raster addresses its tile's entries through the gaussian, the gradient gather reads a
+// gaussian's own entries), so no result depends on it.
 __device__ __forceinline__ void project_tail(int64_t i, bool active, float mx, float my, Conic k,
                                              int x0, int x1, int y0, int y1, long long pixels,
                                              float w, float cr, float cg, float cb, int view,
@@ -180,16 +183,34 @@ __device__ __forceinline__ void project_tail(int64_t i, bool active, float mx, f
   unsigned long long p = static_cast<unsigned long long>(pairs);
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) p += __shfl_xor_sync(0xffffffffu, p, d);
-  if (lane == 0 && p) {
-    atomicAdd(&o.stats[kStatPairs], p);
-    atomicAdd(&o.stats[kStatPairsTotal], p);
+  constexpr int kWarps = kProjThreads / 32;
+  __shared__ int s_warp_base[kWarps];
+  __shared__ unsigned long long s_warp_pairs[kWarps];
+  __shared__ int s_block_base;
+  const int warp = threadIdx.x >> 5;
+  if (lane == 31) s_warp_base[warp] = incl;
+  if (lane == 0) s_warp_pairs[warp] = p;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int total = 0;
+    unsigned long long block_pairs = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const int c = s_warp_base[w];
+      s_warp_base[w] = total;
+      total += c;
+      block_pairs += s_warp_pairs[w];
+    }
+    s_block_base = total ? static_cast<int>(atomicAdd(&o.stats[kStatEntries],
+                                                      static_cast<unsigned long long>(total)))
+                         : 0;
+    if (block_pairs) {
+      atomicAdd(&o.stats[kStatPairs], block_pairs);
+      atomicAdd(&o.stats[kStatPairsTotal], block_pairs);
+    }
   }
-  int wbase = 0;
-  if (lane == 31 && incl) {
-    wbase = static_cast<int>(atomicAdd(&o.stats[kStatEntries], static_cast<unsigned long long>(incl)));
-  }
-  wbase = __shfl_sync(0xffffffffu, wbase, 31);
-  const int off = wbase + incl - cnt;
+  __syncthreads();
+  const int off = s_block_base + s_warp_base[warp] + incl - cnt;
   if (active) o.offsets[i] = off;
   if (o.seg) {  // direct placement (warp-uniform choice; all lanes reach this point)
     direct_commit(i, cnt, sp, o, dslots);
@@ -301,8 +322,8 @@ struct GeoGrad {
 __device__ __forceinline__ GeoGrad geo_grad(const Moments& mo, float i00, float i01, float i11,
                                             float l11, float l21, float l22, bool want_chol) {
   GeoGrad r;
-  r.gmx = fmaf(i00, mo.s[0], i01 * mo.s[1]);
-  r.gmy = fmaf(i01, mo.s[0], i11 * mo.s[1]);
+  r.gmx = mo.s[0];  // the raster applied Sigma^-1 (per pixel or per piece lane)
+  r.gmy = mo.s[1];
   r.gi00 = -0.5f * mo.s[2];
   r.gi01 = -mo.s[3];
   r.gi11 = -0.5f * mo.s[4];

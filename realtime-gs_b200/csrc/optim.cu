@@ -4,7 +4,7 @@
 // gaussian are contiguous (gaussian-major emission), so each gaussian sums its own entries in
 // index order -- deterministic, no atomics -- and applies the chain rule:
 //
-//   dL/dmx = i00*Sdx + i01*Sdy        dL/dmy = i01*Sdx + i11*Sdy
+//   dL/dmx = Gx = sum dq (i00 dx + i01 dy)        dL/dmy = Gy = sum dq (i01 dx + i11 dy)
 //   dL/di00 = -Sxx/2   dL/di01 = -Sxy   dL/di11 = -Syy/2        (q = i00 dx^2 + 2 i01 dx dy + i11 dy^2)
 //   dL/dcolor_k = weight * S_k         dL/dweight = sum_k color_k S_k (+ Sd for density)
 //

@@ -15,8 +15,9 @@
 //   backward  the tile's upstream gradients are staged in shared memory; every (gaussian, tile)
 //             entry's piece = support rectangle x tile is evaluated over exactly its pixels and
 //             8 moments
-//               Sdx = sum dq*dx, Sdy = sum dq*dy, Sxx = sum dq*dx^2, Sxy = sum dq*dx*dy,
-//               Syy = sum dq*dy^2, Sr/Sg/Sb = sum e*g_rgb       (e = exp(-q/2), dq = e * g.A)
+//               Gx = sum dq*(i00 dx + i01 dy), Gy = sum dq*(i01 dx + i11 dy), Sxx = sum dq*dx^2,
+//               Sxy = sum dq*dx*dy, Syy = sum dq*dy^2, Sr/Sg/Sb = sum e*g_rgb
+//               (e = exp(-q/2), dq = e * g.A; Gx, Gy are the mean gradient's sums)
 //             are written once per entry. Pieces are ordered by (orientation, step count) with a
 //             stable counting sort; a warp takes 4 pieces at a time, 8 lanes ("octet") per piece,
 //             each lane owning up to two columns (wide pieces, stepping down the rows) or two rows
@@ -267,12 +268,22 @@ __device__ __forceinline__ int piece_lanes(const float4& geo, const float4& app,
 // longest lane's count), and any_b is set when some lane of the warp has a pixel B.
 // The fixed coordinate's terms are computed once; q keeps the reference's rounding order
 // ((dx^2 i00 + dx dy 2 i01) + dy^2 i11), and pixel centres are exact (integers + 0.5).
-// Moments: S0 = sum dq dx, S1 = sum dq dy, S2 = sum dq dx^2, S3 = sum dq dx dy, S4 = sum dq dy^2,
+// Moments: S0 = sum dq (i00 dx + i01 dy), S1 = sum dq (i01 dx + i11 dy) (the mean gradient's two
+// sums, Sigma^-1 applied per lane), S2 = sum dq dx^2, S3 = sum dq dx dy, S4 = sum dq dy^2,
 // S5..S7 = sum e g_rgb, Sd = sum e g_den, with e = exp(-q/2) and dq = e (g . w c).
 // A lane's pixel keeps its fixed-axis offset f for the whole piece, so the dq moments factor:
-// per pixel only P0 = sum dq, P1 = sum dq v and P2 = sum dq v^2 (v = varying-axis offset) are
+// per pixel only P0 = sum dq, P1 = sum dq v' and P2 = sum dq v^2 (v = varying-axis offset) are
 // accumulated, and f, f^2 are applied once at the end (S for dx-dy = f P1, for f^2 = f^2 P0, ...).
-template <bool ROW, bool DEN>
+// CENTER (renderer backward): v' = v - vc, with vc = -i01 f / coef_var the centre of the ellipse
+// along the lane's line (of pixel A), else v' = v. The mean gradient sums
+//   sum dq (c_fix f + c_var v) = (c_fix f + c_var vc) P0 + c_var P1'
+// then combine terms of the size of the result: for a rotated, elongated gaussian c_fix f and
+// c_var v are large and nearly cancel along the line (by the factor i00 i11 / det, which grows with
+// the aspect ratio squared), and accumulating sum dq v itself would carry that cancellation into
+// float32 sums -- measured on the 4K frame's most elongated gaussians (aspect ratio 150-180) up to
+// 6 times the error of the reference's per-pair sums, and no more than them with the centring.
+// The fused fit kernel keeps v' = v (its gradients only steer Adam; one subtraction per step less).
+template <bool ROW, bool DEN, bool CENTER>
 __device__ __forceinline__ void backward_piece(const float4& geo, const float4& app, float wt,
                                                float pxc0, float pyc0, int sidx0, int r8,
                                                int start, unsigned a_first, unsigned a_len,
@@ -288,6 +299,12 @@ __device__ __forceinline__ void backward_piece(const float4& geo, const float4& 
   const float coef_fix = ROW ? geo.z : app.x;  // i00 for x, i11 for y
   const float coef_var = ROW ? app.x : geo.z;
   const float t_a = __fmul_rn(sq_a, coef_fix), t_b = __fmul_rn(sq_b, coef_fix);
+  const float i01 = 0.5f * geo.w;
+  float vc = 0.f;  // centre of the ellipse along pixel A's line (varying-axis offset)
+  if constexpr (CENTER) {
+    const float kappa = -__fdividef(i01, coef_var);
+    vc = isfinite(kappa) ? kappa * da : 0.f;
+  }
   constexpr int kStep = ROW ? kTile : 1;        // shared-memory stride of one step
   constexpr int kLaneStride = ROW ? 1 : kTile;  // and of one lane-axis pixel
   // The lane's steps [0, count) are the union of pixel A's span (from a_first, a_len steps) and
@@ -327,32 +344,38 @@ __device__ __forceinline__ void backward_piece(const float4& geo, const float4& 
     const float dv = __fsub_rn(fvar, ROW ? geo.y : geo.x);
     const float sq_v = __fmul_rn(dv, dv);
     const float t_v = __fmul_rn(sq_v, coef_var);
+    const float dvc = CENTER ? dv - vc : dv;
     const bool on = st < count;
     {
       const float t1 = __fmul_rn(__fmul_rn(da, dv), geo.w);  // dx dy (multiplication commutes)
       const float q = ROW ? __fadd_rn(__fadd_rn(t_a, t1), t_v) : __fadd_rn(__fadd_rn(t_v, t1), t_a);
-      accumulate(on && has_a && q < cutoff, sidx_a, dv, sq_v, q, pa);
+      accumulate(on && has_a && q < cutoff, sidx_a, dvc, sq_v, q, pa);
     }
     if (any_b) {
       const float t1 = __fmul_rn(__fmul_rn(db, dv), geo.w);
       const float q = ROW ? __fadd_rn(__fadd_rn(t_b, t1), t_v) : __fadd_rn(__fadd_rn(t_v, t1), t_b);
-      accumulate(on && has_b && q < cutoff, sidx_a + 8 * kLaneStride, dv, sq_v, q, pb);
+      accumulate(on && has_b && q < cutoff, sidx_a + 8 * kLaneStride, dvc, sq_v, q, pb);
     }
     fvar += 1.f;
     sidx_a += kStep;
   }
-  // Fixed-axis factors: f P0 (first moment), P1 (varying first moment), f P1 (cross), f^2 P0 and
-  // P2 (second moments), summed over the lane's pixels A and B.
-  const float m_f = fmaf(da, pa[0], db * pb[0]);
-  const float m_v = pa[1] + pb[1];
+  // Mean gradient: c_fix, c_var = coefficients of the fixed and the varying offset in
+  // (i00 dx + i01 dy) and (i01 dx + i11 dy).
+  const float cx_fix = ROW ? geo.z : i01, cx_var = ROW ? i01 : geo.z;
+  const float cy_fix = ROW ? i01 : app.x, cy_var = ROW ? app.x : i01;
+  const float p1 = pa[1] + pb[1];
+  S[0] = fmaf(fmaf(cx_var, vc, cx_fix * da), pa[0], fmaf(fmaf(cx_var, vc, cx_fix * db), pb[0], cx_var * p1));
+  S[1] = fmaf(fmaf(cy_var, vc, cy_fix * da), pa[0], fmaf(fmaf(cy_var, vc, cy_fix * db), pb[0], cy_var * p1));
+  // Second moments: f P0, sum dq v = P1' + vc P0, f (P1' + vc P0), f^2 P0 and P2, over A and B.
+  const float va = fmaf(vc, pa[0], pa[1]), vb = fmaf(vc, pb[0], pb[1]);
+  const float m_v = va + vb;
   const float m_ff = fmaf(sq_a, pa[0], sq_b * pb[0]);
-  const float m_fv = fmaf(da, pa[1], db * pb[1]);
+  const float m_fv = fmaf(da, va, db * vb);
   const float m_vv = pa[2] + pb[2];
-  S[0] = ROW ? m_f : m_v;    // sum dq dx
-  S[1] = ROW ? m_v : m_f;    // sum dq dy
   S[2] = ROW ? m_ff : m_vv;  // sum dq dx^2
   S[3] = m_fv;               // sum dq dx dy
   S[4] = ROW ? m_vv : m_ff;  // sum dq dy^2
+  (void)m_v;
 }
 
 // Register caps (measured on B200): the renderer backward (with line spans) is held to 56
@@ -380,9 +403,11 @@ raster_kernel(const RasterArgs a) {
   // Line spans of the support ellipse: renderer backward only (see kSpanMinSteps).
   constexpr bool kSpans = MODE == kBwd;
   __shared__ uint32_t s_lanes[kSpans ? kBatch * 8 : 1];  // packed step ranges per (piece, octet lane)
-  __shared__ int s_wcount[kDoBwd ? L::kWarps : 1][kBuckets];  // per-warp bucket counts, then starts
+  constexpr int kNB = kBuckets;
+  __shared__ int s_wcount[kDoBwd ? L::kWarps : 1][kNB];  // per-warp bucket counts, then starts
   static_assert(kBatch == L::kThreads, "the backward work list assigns one piece per thread");
-  static_assert(kBuckets == 32, "warp 0 scans one bucket per lane");
+  static_assert(kNB % 32 == 0 && kNB <= 64, "warp 0 scans kNB / 32 consecutive buckets per lane");
+  constexpr int kPerLane = kNB / 32;
   __shared__ int s_next;
   // Renderer forward: the walk is pruned to records whose support ellipse can reach a lane's
   // pixels (line spans along the sub-block's columns, in groups of 4 rows, one word per record,
@@ -655,7 +680,7 @@ raster_kernel(const RasterArgs a) {
       // the input. One piece per thread (kBatch == block size); ranks from match_any within a warp,
       // per-warp bucket counts for the order across warps.
       const int jb = threadIdx.x;
-      int bucket = kBuckets;
+      int bucket = kNB;
       if (jb < n) {
         const int pc = s_piece[jb];
         if constexpr (kSpans) {
@@ -664,17 +689,20 @@ raster_kernel(const RasterArgs a) {
           bucket = piece_bucket(pc);
         }
       }
-      for (int i = threadIdx.x; i < L::kWarps * kBuckets; i += L::kThreads) (&s_wcount[0][0])[i] = 0;
+      for (int i = threadIdx.x; i < L::kWarps * kNB; i += L::kThreads) (&s_wcount[0][0])[i] = 0;
       if (threadIdx.x == 0) s_next = 0;
       __syncthreads();
       const unsigned peers = __match_any_sync(0xffffffffu, bucket);
       const int rank = __popc(peers & ((1u << lane) - 1u));
-      if (bucket < kBuckets && rank == 0) s_wcount[warp][bucket] = __popc(peers);
+      if (bucket < kNB && rank == 0) s_wcount[warp][bucket] = __popc(peers);
       __syncthreads();
-      if (warp == 0) {  // lane l owns bucket l: start of each (warp, bucket) run
+      if (warp == 0) {  // lane l owns buckets l * kPerLane ...: start of each (warp, bucket) run
         int total = 0;
 #pragma unroll
-        for (int w = 0; w < L::kWarps; ++w) total += s_wcount[w][lane];
+        for (int u = 0; u < kPerLane; ++u) {
+#pragma unroll
+          for (int w = 0; w < L::kWarps; ++w) total += s_wcount[w][lane * kPerLane + u];
+        }
         int x = total;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -683,14 +711,17 @@ raster_kernel(const RasterArgs a) {
         }
         int run = x - total;
 #pragma unroll
-        for (int w = 0; w < L::kWarps; ++w) {
-          const int c = s_wcount[w][lane];
-          s_wcount[w][lane] = run;
-          run += c;
+        for (int u = 0; u < kPerLane; ++u) {
+#pragma unroll
+          for (int w = 0; w < L::kWarps; ++w) {
+            const int c = s_wcount[w][lane * kPerLane + u];
+            s_wcount[w][lane * kPerLane + u] = run;
+            run += c;
+          }
         }
       }
       __syncthreads();
-      if (bucket < kBuckets) s_list[s_wcount[warp][bucket] + rank] = jb;
+      if (bucket < kNB) s_list[s_wcount[warp][bucket] + rank] = jb;
       __syncthreads();
 
       const int n_tasks = (n + 3) >> 2;
@@ -741,13 +772,12 @@ raster_kernel(const RasterArgs a) {
         if constexpr (DEN) wt = s_wt[j];
         float S[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         float Sd = 0.f;
-        if (row) {
-          backward_piece<true, DEN>(geo, app, wt, pxc0, pyc0, ry0 * kTile + rx0, r8, start, a_first,
-                                    a_len, b_first, b_len, any_b, max_steps, a.cutoff, s_g, S, Sd);
-        } else {
-          backward_piece<false, DEN>(geo, app, wt, pxc0, pyc0, ry0 * kTile + rx0, r8, start, a_first,
-                                     a_len, b_first, b_len, any_b, max_steps, a.cutoff, s_g, S, Sd);
-        }
+#define RTGS_PIECE(R)                                                                                  \
+  backward_piece<R, DEN, MODE == kBwd>(geo, app, wt, pxc0, pyc0, ry0 * kTile + rx0, r8, start,      \
+                                       a_first, a_len, b_first, b_len, any_b, max_steps, a.cutoff,  \
+                                       s_g, S, Sd)
+        if (row) RTGS_PIECE(true); else RTGS_PIECE(false);
+#undef RTGS_PIECE
         const float red = octet_transpose_reduce8(S, lane);
         const int64_t e = s_entry[j];
         // Entries outside [0, capacity) belong to a dropped binning.

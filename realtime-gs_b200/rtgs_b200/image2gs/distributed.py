@@ -57,14 +57,16 @@ def fit_views_sharded(
     None (a rank then never holds the other ranks' images). ``fit_fn(local_images, config,
     seed_of_first)`` defaults to the batched fit engine (``fit_views_batched``). ``device`` is
     where the gathered parameters live (default: the first local image's device; give a CUDA
-    device when the local images are host tensors).
+    device when the local images are host tensors). Without an initialised process group (and
+    no ``group``) the calling process is the only rank: it fits every image and gathers nothing.
     """
     if fit_fn is None:
         from rtgs_b200.image2gs.batched import fit_views_batched
 
         fit_fn = fit_views_batched
-    world = dist.get_world_size(group)
-    rank = dist.get_rank(group)
+    single = group is None and not (dist.is_available() and dist.is_initialized())
+    world = 1 if single else dist.get_world_size(group)
+    rank = 0 if single else dist.get_rank(group)
     start, stop = shard_range(len(images), rank, world)
     local = images[start:stop]
     results, histories = fit_fn(local, config, seed + start) if local else ([], [])
@@ -73,10 +75,13 @@ def fit_views_sharded(
     if device is None:
         device = next((im.device for im in local if im is not None), torch.device("cpu"))
     packed = pack(results, per, n, device)
-    gathered = torch.empty(world * per, n, PARAMS_PER_GAUSSIAN, device=device, dtype=torch.float32)
-    dist.all_gather_into_tensor(gathered, packed, group=group)
-    all_hist: list[list[dict]] = [None] * world  # type: ignore[list-item]
-    dist.all_gather_object(all_hist, histories, group=group)
+    if single:  # no process group: this process is the only rank and nothing is exchanged
+        gathered, all_hist = packed, [histories]
+    else:
+        gathered = torch.empty(world * per, n, PARAMS_PER_GAUSSIAN, device=device, dtype=torch.float32)
+        dist.all_gather_into_tensor(gathered, packed, group=group)
+        all_hist: list[list[dict]] = [None] * world  # type: ignore[list-item]
+        dist.all_gather_object(all_hist, histories, group=group)
     out, hist = [], []
     for r in range(world):
         s, e = shard_range(len(images), r, world)
