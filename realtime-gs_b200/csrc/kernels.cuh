@@ -322,7 +322,7 @@ struct GeoGrad {
 __device__ __forceinline__ GeoGrad geo_grad(const Moments& mo, float i00, float i01, float i11,
                                             float l11, float l21, float l22, bool want_chol) {
   GeoGrad r;
-  r.gmx = mo.s[0];  // the raster applied Sigma^-1 (per pixel or per piece lane)
+  r.gmx = mo.s[0];  // the renderer backward applied Sigma^-1 per piece lane
   r.gmy = mo.s[1];
   r.gi00 = -0.5f * mo.s[2];
   r.gi01 = -mo.s[3];

@@ -5,6 +5,7 @@
 // index order -- deterministic, no atomics -- and applies the chain rule:
 //
 //   dL/dmx = Gx = sum dq (i00 dx + i01 dy)        dL/dmy = Gy = sum dq (i01 dx + i11 dy)
+//   (renderer moments; the fused fit kernel's are sum dq dx, sum dq dy, chained by the Adam kernel)
 //   dL/di00 = -Sxx/2   dL/di01 = -Sxy   dL/di11 = -Syy/2        (q = i00 dx^2 + 2 i01 dx dy + i11 dy^2)
 //   dL/dcolor_k = weight * S_k         dL/dweight = sum_k color_k S_k (+ Sd for density)
 //
@@ -130,7 +131,10 @@ adam_fit_kernel(int64_t m, int64_t cap, int* counts, const int* __restrict__ off
     const float l22 = __fadd_rn(softplus_f(r[kD1]), kMinDiag);
     const float l21 = r[kOff];
     const Conic k = conic_from_chol(l11, l21, l22);
-    const GeoGrad gg = geo_grad(mo, k.i00, k.i01, k.i11, l11, l21, l22, true);
+    GeoGrad gg = geo_grad(mo, k.i00, k.i01, k.i11, l11, l21, l22, true);
+    // The fused fit raster leaves the plain first moments sum dq dx, sum dq dy: apply Sigma^-1.
+    gg.gmx = fmaf(k.i00, mo.s[0], k.i01 * mo.s[1]);
+    gg.gmy = fmaf(k.i01, mo.s[0], k.i11 * mo.s[1]);
     const float cr = sigmoid_f(r[kCr]), cg = sigmoid_f(r[kCg]), cb = sigmoid_f(r[kCb]);
     const float w = sigmoid_f(r[kWr]);
 
