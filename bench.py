@@ -360,7 +360,8 @@ def e2e_fit(device, wl, targets_host, init_host, masks_host, steps: int) -> tupl
     # Fitted parameters come back into pinned host buffers (asynchronous copies, one wait).
     out = [torch.empty(x.shape, dtype=torch.float32, pin_memory=True) for x in init_host]
     d2h = sum(x.numel() * 4 for x in out)
-    for k in range(steps + 1):
+    warmup = 2  # the first call creates the pooled engine; the second reuses it once
+    for k in range(steps + warmup):
         torch.cuda.synchronize(device)
         t0 = time.perf_counter()
         images = targets_host.to(device, non_blocking=True)
@@ -378,7 +379,7 @@ def e2e_fit(device, wl, targets_host, init_host, masks_host, steps: int) -> tupl
             dst.copy_(src, non_blocking=True)
         torch.cuda.synchronize(device)
         dt = time.perf_counter() - t0
-        if k > 0:  # the first call is a warm-up
+        if k >= warmup:
             times.append(dt)
     return statistics.median(times), h2d, d2h, api
 
@@ -617,7 +618,7 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
     del engine
     e2e_value, h2d, d2h, e2e_api = None, 0, 0, None
     if not args.no_e2e:
-        e2e_s, h2d, d2h, e2e_api = e2e_fit(device, wl, targets_host, init_host, masks_host, steps=2)
+        e2e_s, h2d, d2h, e2e_api = e2e_fit(device, wl, targets_host, init_host, masks_host, steps=5)
         e2e_value = world * views / max_over_ranks(e2e_s, device, world)
 
     sharded = {}

@@ -218,6 +218,30 @@ RTGS2D_API int rtgs2d_fit_set_targets(rtgs2d_fit* fit, const float* targets, con
 RTGS2D_API int rtgs2d_fit_set_raw(rtgs2d_fit* fit, const float* xy_raw, const float* diag_raw,
                        const float* off_raw, const float* color_raw, const float* weight_raw,
                        void* stream);
+/*
+ * Initialisation from constrained parameters in one pass: the reference's checks of an initial
+ * Gaussians2D (src/rtgs/image2gs/fit.py:634-676) and its raw transform (fit.py:375-380, with the
+ * non-finite raw check of fit.py:134-141) run on the device, followed by rtgs2d_fit_set_raw's
+ * reset. Replaces the torch validation and transform ops of _fit_native_from_initialization
+ * (fit.py:355-380) before the engine. xy (B,N,2), chol (B,N,3), color (B,N,3), weight (B,N)
+ * float32 device arrays. *status receives 0 or the OR of the RTGS2D_INIT_* bits of the checks
+ * that failed for some gaussian; the caller decides which failures to report (the rows are not
+ * returned). The raw values are written whatever the status (the transform clamps as the
+ * reference does); with RTGS2D_INIT_NONFINITE_RAW set the engine refuses to run until parameters
+ * are set again. Synchronises `stream`.
+ */
+#define RTGS2D_INIT_NONFINITE_XY 1u
+#define RTGS2D_INIT_NONFINITE_CHOL 2u
+#define RTGS2D_INIT_NONFINITE_COLOR 4u
+#define RTGS2D_INIT_NONFINITE_WEIGHT 8u
+#define RTGS2D_INIT_OUTSIDE 16u        /* a mean outside [0, W) x [0, H) */
+#define RTGS2D_INIT_DIAG 32u           /* a Cholesky diagonal entry not above 0.3 */
+#define RTGS2D_INIT_COLOR_RANGE 64u    /* a colour outside [0, 1] */
+#define RTGS2D_INIT_WEIGHT_RANGE 128u  /* a weight outside [0, 1] */
+#define RTGS2D_INIT_NONFINITE_RAW 256u /* a non-finite raw parameter */
+RTGS2D_API int rtgs2d_fit_set_initial(rtgs2d_fit* fit, const float* xy, const float* chol,
+                                      const float* color, const float* weight, uint32_t* status,
+                                      void* stream);
 /* Runs `n_iterations` more iterations (capped at `iterations`). Synchronises `stream`. */
 RTGS2D_API int rtgs2d_fit_run(rtgs2d_fit* fit, int64_t n_iterations, void* stream);
 RTGS2D_API int rtgs2d_fit_get_raw(rtgs2d_fit* fit, float* xy_raw, float* diag_raw, float* off_raw,

@@ -58,6 +58,9 @@ struct rtgs2d_fit {
   cudaEvent_t fork_event = nullptr;
   cudaEvent_t join_event = nullptr;
   bool have_targets = false, have_raw = false;
+  bool scale_uploaded = false;            // view_scale holds the constant scale of the MSE modes
+  DevBuf init_status;                     // uint32: failed checks of rtgs2d_fit_set_initial
+  uint32_t* host_status = nullptr;        // pinned mirror of init_status
   // per-iteration constants of the current chunk, and the replayable chunks
   DevBuf iter_table;                  // IterScalars[kChunk]
   IterScalars* host_table = nullptr;  // pinned staging for iter_table
@@ -128,6 +131,62 @@ __global__ void unpack_raw_kernel(int64_t m, const float* __restrict__ raw, floa
     color[3 * i + 2] = raw[kCb * m + i];
   }
   if (weight) weight[i] = raw[kWr * m + i];
+}
+
+// rtgs2d_fit_set_initial: the reference's checks of an initialisation (fit.py:634-676: finite
+// fields, means inside the image, Cholesky diagonal above _MIN_DIAG, colours and weights in [0,1])
+// and its raw transform (fit.py:375-380: logit of the clamped normalised mean, inverse softplus of
+// the diagonal minus _MIN_DIAG, the off-diagonal as is, logit of the clamped colour and weight;
+// non-finite raw values are the reference's NonFiniteRawParameterError, fit.py:134-141), one
+// thread per gaussian, written straight into the planar raw parameters. Failed checks are OR-ed
+// into *status (RTGS2D_INIT_* bits).
+__device__ __forceinline__ float logit_f(float p) { return logf(__fdiv_rn(p, 1.0f - p)); }
+__device__ __forceinline__ float softplus_inv_f(float x) { return x + logf(-expm1f(-x)); }
+
+__global__ void init_raw_kernel(int64_t m, const float* __restrict__ xy, const float* __restrict__ chol,
+                                const float* __restrict__ color, const float* __restrict__ weight,
+                                int height, int width, float* __restrict__ raw, float* __restrict__ m1,
+                                float* __restrict__ m2, unsigned* __restrict__ status) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  if (i >= m) return;
+  const float x = xy[2 * i], y = xy[2 * i + 1];
+  const float l11 = chol[3 * i], l21 = chol[3 * i + 1], l22 = chol[3 * i + 2];
+  const float c[3] = {color[3 * i], color[3 * i + 1], color[3 * i + 2]};
+  const float w = weight[i];
+  unsigned bad = 0;
+  if (!(isfinite(x) && isfinite(y))) bad |= RTGS2D_INIT_NONFINITE_XY;
+  if (!(isfinite(l11) && isfinite(l21) && isfinite(l22))) bad |= RTGS2D_INIT_NONFINITE_CHOL;
+  if (!(isfinite(c[0]) && isfinite(c[1]) && isfinite(c[2]))) bad |= RTGS2D_INIT_NONFINITE_COLOR;
+  if (!isfinite(w)) bad |= RTGS2D_INIT_NONFINITE_WEIGHT;
+  if (!(x >= 0.f && x < static_cast<float>(width) && y >= 0.f && y < static_cast<float>(height))) {
+    bad |= RTGS2D_INIT_OUTSIDE;
+  }
+  if (!(l11 > kMinDiag && l22 > kMinDiag)) bad |= RTGS2D_INIT_DIAG;
+  if (!(c[0] >= 0.f && c[0] <= 1.f && c[1] >= 0.f && c[1] <= 1.f && c[2] >= 0.f && c[2] <= 1.f)) {
+    bad |= RTGS2D_INIT_COLOR_RANGE;
+  }
+  if (!(w >= 0.f && w <= 1.f)) bad |= RTGS2D_INIT_WEIGHT_RANGE;
+  // torch.clamp: NaN propagates (so a NaN input gives a non-finite raw value, as in the reference)
+  auto clamp = [](float v, float lo, float hi) { return v != v ? v : fminf(fmaxf(v, lo), hi); };
+  constexpr float kXyLo = 1e-4f, kXyHi = 1.0f - 1e-4f, kLo = 1e-3f, kHi = 1.0f - 1e-3f;
+  float r[kRawSlots];
+  r[kXr] = logit_f(clamp(__fdiv_rn(x, static_cast<float>(width)), kXyLo, kXyHi));
+  r[kYr] = logit_f(clamp(__fdiv_rn(y, static_cast<float>(height)), kXyLo, kXyHi));
+  r[kD0] = softplus_inv_f(__fsub_rn(l11, kMinDiag));
+  r[kD1] = softplus_inv_f(__fsub_rn(l22, kMinDiag));
+  r[kOff] = l21;
+  r[kCr] = logit_f(clamp(c[0], kLo, kHi));
+  r[kCg] = logit_f(clamp(c[1], kLo, kHi));
+  r[kCb] = logit_f(clamp(c[2], kLo, kHi));
+  r[kWr] = logit_f(clamp(w, kLo, kHi));
+#pragma unroll
+  for (int k = 0; k < kRawSlots; ++k) {
+    if (!isfinite(r[k])) bad |= RTGS2D_INIT_NONFINITE_RAW;
+    raw[k * m + i] = r[k];
+    m1[k * m + i] = 0.f;
+    m2[k * m + i] = 0.f;
+  }
+  if (bad) atomicOr(status, bad);
 }
 
 __global__ void mask_count_kernel(const uint8_t* __restrict__ bits, int64_t bytes_per_view,
@@ -527,6 +586,8 @@ int rtgs2d_fit_destroy(rtgs2d_fit* fit) {
   if (fit->fork_event) cudaEventDestroy(fit->fork_event);
   if (fit->join_event) cudaEventDestroy(fit->join_event);
   if (fit->host_table) cudaFreeHost(fit->host_table);
+  if (fit->host_status) cudaFreeHost(fit->host_status);
+  fit->init_status.release();
   delete fit;
   if (prev != dev) cudaSetDevice(prev);
   return RTGS2D_OK;
@@ -566,12 +627,18 @@ int rtgs2d_fit_set_targets(rtgs2d_fit* f, const float* targets, const uint8_t* m
                                 cudaMemcpyDeviceToDevice, s),
                 "copy mask");
     }
+    // The scale of these modes is a constant of the engine: uploaded by the first call only.
+    if (f->scale_uploaded) {
+      f->have_targets = true;
+      return RTGS2D_OK;
+    }
     for (auto& v : scale) v = static_cast<float>(2.0 / numel);
   }
   RTGS_CUDA(cudaMemcpyAsync(f->view_scale.ptr, scale.data(), scale.size() * sizeof(float),
                             cudaMemcpyHostToDevice, s),
             "view scale upload");
-  RTGS_CUDA(cudaStreamSynchronize(s), "set_targets sync");
+  RTGS_CUDA(cudaStreamSynchronize(s), "set_targets sync");  // `scale` is host stack memory
+  f->scale_uploaded = f->opt.loss_mode != RTGS2D_LOSS_MASK_ONLY;
   f->have_targets = true;
   return RTGS2D_OK;
 }
@@ -597,6 +664,37 @@ int rtgs2d_fit_set_raw(rtgs2d_fit* f, const float* xy_raw, const float* diag_raw
   f->log_iters.clear();
   f->total_pairs = 0.0;
   f->have_raw = true;
+  return RTGS2D_OK;
+}
+
+int rtgs2d_fit_set_initial(rtgs2d_fit* f, const float* xy, const float* chol, const float* color,
+                           const float* weight, uint32_t* status, void* stream) {
+  RTGS_TRY(check_fit(f));
+  if (!status) return set_error(RTGS2D_ERR_INVALID, "status is NULL");
+  if (f->m > 0 && (!xy || !chol || !color || !weight)) {
+    return set_error(RTGS2D_ERR_INVALID, "initial parameter pointer is NULL");
+  }
+  cudaStream_t s = as_stream(stream);
+  if (!f->host_status) {
+    RTGS_CUDA(cudaMallocHost(reinterpret_cast<void**>(&f->host_status), sizeof(uint32_t)), "pinned status");
+  }
+  RTGS_TRY(f->init_status.ensure(sizeof(uint32_t), s));
+  RTGS_CUDA(cudaMemsetAsync(f->init_status.ptr, 0, sizeof(uint32_t), s), "zero status");
+  if (f->m > 0) {
+    init_raw_kernel<<<grid_for(f->m), kThreads, 0, s>>>(f->m, xy, chol, color, weight, f->height,
+                                                        f->width, f->raw.as<float>(), f->m1.as<float>(),
+                                                        f->m2.as<float>(), f->init_status.as<unsigned>());
+    RTGS_CUDA(cudaGetLastError(), "init_raw_kernel");
+  }
+  RTGS_CUDA(cudaMemcpyAsync(f->host_status, f->init_status.ptr, sizeof(uint32_t), cudaMemcpyDeviceToHost, s),
+            "status readback");
+  RTGS_CUDA(cudaStreamSynchronize(s), "set_initial sync");
+  *status = *f->host_status;
+  f->step = 0;
+  f->lr_current = f->opt.lr;
+  f->log_iters.clear();
+  f->total_pairs = 0.0;
+  f->have_raw = (*status & RTGS2D_INIT_NONFINITE_RAW) == 0;
   return RTGS2D_OK;
 }
 

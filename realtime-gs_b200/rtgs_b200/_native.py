@@ -23,6 +23,8 @@ LOSS_MSE = 0
 LOSS_MASK_WEIGHTED = 1
 LOSS_MASK_ONLY = 2
 
+INIT_NONFINITE_RAW = 256  # RTGS2D_INIT_NONFINITE_RAW of rtgs2d_fit_set_initial
+
 
 class FitOptions(ctypes.Structure):
     _fields_ = [
@@ -79,6 +81,7 @@ _SIGNATURES = {
     "rtgs2d_fit_destroy": ([_vp], ctypes.c_int),
     "rtgs2d_fit_set_targets": ([_vp, _vp, _vp, _vp], ctypes.c_int),
     "rtgs2d_fit_set_raw": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
+    "rtgs2d_fit_set_initial": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
     "rtgs2d_fit_run": ([_vp, _c_int64, _vp], ctypes.c_int),
     "rtgs2d_fit_get_raw": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
     "rtgs2d_fit_get_params": ([_vp, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),

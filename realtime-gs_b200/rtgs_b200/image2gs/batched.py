@@ -81,8 +81,6 @@ def fit_stacked(
     _require_cuda(targets)
     n_views, height, width = targets.shape[:3]
     xy0, chol0, color0, weight0 = (t.to(targets.device, torch.float32) for t in init)
-    raw = raw_from_gaussians(xy0, chol0, color0, weight0, height, width)
-    _validate_raw_parameters(raw)
     loss_mode = _native.LOSS_MSE if masks is None else _native.LOSS_MASK_ONLY
     engine = acquire_engine(
         n_views, xy0.shape[1], height, width, lr=config.lr, iterations=config.iterations,
@@ -91,9 +89,15 @@ def fit_stacked(
     )
     ok = False
     try:
+        # Raw transform on the device; like the reference's batched fit, only non-finite raw
+        # parameters are rejected here (the per-view initialisers were validated by the caller).
+        status = engine.set_initial(xy0, chol0, color0, weight0)
+        if status & _native.INIT_NONFINITE_RAW:
+            ok = True
+            _validate_raw_parameters(raw_from_gaussians(xy0, chol0, color0, weight0, height, width))
+            raise RuntimeError("the engine found non-finite raw parameters that the host check does not")
         mask_bits = None if masks is None else pack_mask_bits(masks)
         engine.set_targets(targets, mask_bits)
-        engine.set_raw(raw)
         engine.run(config.iterations)
         if masks is None:
             counts = np.full(n_views, 3.0 * height * width)

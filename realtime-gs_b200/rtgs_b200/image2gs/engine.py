@@ -117,6 +117,24 @@ class FitEngine:
             _native.check(self._lib.rtgs2d_fit_set_raw(self._h, *(t.data_ptr() for t in ts), self._stream()))
             torch.cuda.current_stream(self.device).synchronize()
 
+    def set_initial(self, xy: torch.Tensor, chol: torch.Tensor, color: torch.Tensor,
+                    weight: torch.Tensor) -> int:
+        """Validate and transform constrained (B, N, .) initial parameters on the device
+        (rtgs2d_fit_set_initial); returns 0 or the RTGS2D_INIT_* bits of the failed checks."""
+        b, n = self.n_views, self.n
+        ts = []
+        for t, k in ((xy, 2), (chol, 3), (color, 3), (weight, 0)):
+            t = t.to(self.device, torch.float32).contiguous()
+            want = (b, n, k) if k else (b, n)
+            if t.numel() != b * n * max(k, 1):
+                raise ValueError(f"initial parameters must have {want} elements, got {tuple(t.shape)}")
+            ts.append(t)
+        status = ctypes.c_uint32()
+        with torch.cuda.device(self.device):
+            _native.check(self._lib.rtgs2d_fit_set_initial(self._h, *(t.data_ptr() for t in ts),
+                                                           ctypes.byref(status), self._stream()))
+        return int(status.value)
+
     # -- running ---------------------------------------------------------------------------------
     def run(self, n_iterations: int) -> None:
         with torch.cuda.device(self.device):

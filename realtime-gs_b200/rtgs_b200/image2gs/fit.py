@@ -142,6 +142,28 @@ def _validate_raw_parameters(raw_parameters: dict[str, torch.Tensor]) -> None:
         raise NonFiniteRawParameterError(name, rows, value)
 
 
+def _check_initial_shapes(g0: Gaussians2D) -> None:
+    """The host-side part of the initialiser checks (fit.py:634-653): shapes and dtypes. The
+    reference checks each field's shape, dtype and finiteness in turn, so with a malformed field
+    the earlier fields' finiteness decides which error comes first: that case takes the
+    field-by-field path."""
+    expected = {"xy": (g0.n, 2), "chol": (g0.n, 3), "color": (g0.n, 3), "weight": (g0.n,)}
+    for name, shape in expected.items():
+        value = getattr(g0, name)
+        if not isinstance(value, torch.Tensor) or tuple(value.shape) != shape or not value.is_floating_point():
+            for earlier, eshape in expected.items():
+                evalue = getattr(g0, earlier)
+                if not isinstance(evalue, torch.Tensor) or tuple(evalue.shape) != eshape:
+                    actual = None if not isinstance(evalue, torch.Tensor) else tuple(evalue.shape)
+                    raise ValueError(f"initial Gaussians2D {earlier} shape must be {eshape}, got {actual}")
+                if not evalue.is_floating_point():
+                    raise ValueError(f"initial Gaussians2D {earlier} must be floating point")
+                finite = torch.isfinite(evalue).reshape(g0.n, -1).all(dim=1)
+                if not bool(finite.all()):
+                    rows = torch.nonzero(~finite).flatten().tolist()
+                    raise ValueError(f"non-finite initial rows in {earlier}: {rows}")
+
+
 def _validate_initial_gaussians(g0: Gaussians2D, height: int, width: int) -> None:
     """Reject malformed initialiser fields (fit.py:634-676).
 
@@ -149,14 +171,8 @@ def _validate_initial_gaussians(g0: Gaussians2D, height: int, width: int) -> Non
     back with one synchronisation, and only a failing check gathers its rows, in the reference's
     order of checks (finiteness per field, bounds, Cholesky diagonal, colour / weight range).
     """
+    _check_initial_shapes(g0)
     expected = {"xy": (g0.n, 2), "chol": (g0.n, 3), "color": (g0.n, 3), "weight": (g0.n,)}
-    for name, shape in expected.items():
-        value = getattr(g0, name)
-        if not isinstance(value, torch.Tensor) or tuple(value.shape) != shape:
-            actual = None if not isinstance(value, torch.Tensor) else tuple(value.shape)
-            raise ValueError(f"initial Gaussians2D {name} shape must be {shape}, got {actual}")
-        if not value.is_floating_point():
-            raise ValueError(f"initial Gaussians2D {name} must be floating point")
     finite = {name: torch.isfinite(getattr(g0, name)).reshape(g0.n, -1).all(dim=1) for name in expected}
     inside = (g0.xy[:, 0] >= 0) & (g0.xy[:, 0] < width) & (g0.xy[:, 1] >= 0) & (g0.xy[:, 1] < height)
     diag_ok = (g0.chol[:, 0] > _MIN_DIAG) & (g0.chol[:, 2] > _MIN_DIAG)
@@ -265,14 +281,17 @@ def _fit_native_from_initialization(
     mask: torch.Tensor | None,
     xy_offset: torch.Tensor,
 ) -> tuple[Gaussians2D, dict]:
-    """Device fit loop for one image (fit.py:355-554)."""
+    """Device fit loop for one image (fit.py:355-554).
+
+    The initialiser's value checks and raw transform run in one engine call
+    (``FitEngine.set_initial``); only when a check fails are the torch checks run, to report the
+    failing rows with the reference's messages.
+    """
     _require_cuda(image)
     h, w = image.shape[:2]
-    _validate_initial_gaussians(g0, h, w)
+    _check_initial_shapes(g0)
     if config.mask_coverage_weight > 0.0 and mask is None:  # fit.py:371-372
         raise ValueError("mask_coverage_weight requires a mask")
-    raw = raw_from_gaussians(g0.xy, g0.chol, g0.color, g0.weight, h, w)
-    _validate_raw_parameters(raw)
     loss_mode = _native.LOSS_MSE if mask is None else _native.LOSS_MASK_WEIGHTED
     patience = int(config.convergence_patience)
     check_every = int(config.convergence_check_every) if patience else 0
@@ -283,9 +302,13 @@ def _fit_native_from_initialization(
     )
     ok = False
     try:
+        status = engine.set_initial(g0.xy, g0.chol, g0.color, g0.weight)
+        if status:
+            ok = True  # the engine itself is fine: keep it pooled
+            _raise_initial_errors(g0, h, w)
+        ok = False
         mask_bits = None if mask is None else pack_mask_bits(mask[None])
         engine.set_targets(target[None], mask_bits)
-        engine.set_raw({k: v[None] for k, v in raw.items()})
         counts = np.array([3.0 * h * w])
         stopped = config.iterations - 1
         if patience:
@@ -313,16 +336,30 @@ def _fit_native_from_initialization(
             history["psnr"] = [(i, v) for i, v in history["psnr"] if i <= stopped]
             history["stopped_iter"] = stopped
         xy, chol, color, weight = (t[0] for t in engine.params())
-        final, _ = engine.evaluate(want_render=True)
+        # Unmasked: the final PSNR from the evaluation's clamped squared-error sum (no render is
+        # materialised); masked: masked_psnr of the render against the uncropped-mask image.
+        final, sums = engine.evaluate(want_render=mask is not None)
         ok = True
     finally:
         release_engine(engine, reusable=ok)
     result = Gaussians2D(xy=xy, chol=chol, color=color, weight=weight)
-    pred = final[0].clamp(0, 1)
-    history["final_psnr_full"] = psnr(pred, target)
-    history["final_psnr"] = history["final_psnr_full"] if mask is None else masked_psnr(pred, image, mask)
+    if mask is None:
+        history["final_psnr_full"] = psnr_values(sums[:, 1], counts)[0]
+        history["final_psnr"] = history["final_psnr_full"]
+    else:
+        pred = final[0].clamp(0, 1)
+        history["final_psnr_full"] = psnr(pred, target)
+        history["final_psnr"] = masked_psnr(pred, image, mask)
     result.xy += xy_offset
     return result, history
+
+
+def _raise_initial_errors(g0: Gaussians2D, height: int, width: int) -> None:
+    """An initialisation the engine rejected: raise the reference's error for it (fit.py:634-676,
+    then fit.py:134-141 for non-finite raw parameters)."""
+    _validate_initial_gaussians(g0, height, width)
+    _validate_raw_parameters(raw_from_gaussians(g0.xy, g0.chol, g0.color, g0.weight, height, width))
+    raise RuntimeError("the engine rejected the initial gaussians but no check fails on the host")
 
 
 def fit_image(

@@ -266,16 +266,20 @@ def fit_pooled_from_initialization(
             history["psnr"] = [(i, v) for i, v in history["psnr"] if i <= stopped]
             history["stopped_iter"] = stopped
         xy, chol, color, weight = (t[0] for t in engine.params())
-        final, _ = engine.evaluate(want_render=True)
+        final, sums = engine.evaluate(want_render=mask is not None)
         ok = True
     finally:
         engine.set_active(None)
         release_engine(engine, reusable=ok)
     live = active.nonzero(as_tuple=True)[0]
     result = Gaussians2D(xy=xy[live], chol=chol[live], color=color[live], weight=weight[live])
-    pred = final[0].clamp(0, 1)
-    history["final_psnr_full"] = psnr(pred, target)
-    history["final_psnr"] = history["final_psnr_full"] if mask is None else masked_psnr(pred, image, mask)
+    if mask is None:  # as the native fit: from the evaluation's clamped squared-error sum
+        history["final_psnr_full"] = psnr_values(sums[:, 1], counts)[0]
+        history["final_psnr"] = history["final_psnr_full"]
+    else:
+        pred = final[0].clamp(0, 1)
+        history["final_psnr_full"] = psnr(pred, target)
+        history["final_psnr"] = masked_psnr(pred, image, mask)
     history["live_count"] = int(live.numel())
     history["pool_capacity"] = capacity
     result.xy += xy_offset
