@@ -242,6 +242,20 @@ RTGS2D_API int rtgs2d_fit_set_raw(rtgs2d_fit* fit, const float* xy_raw, const fl
 RTGS2D_API int rtgs2d_fit_set_initial(rtgs2d_fit* fit, const float* xy, const float* chol,
                                       const float* color, const float* weight, uint32_t* status,
                                       void* stream);
+/*
+ * Appearance parameterisation (FitConfig.appearance_parameterization, fit.py:27,381-411).
+ * WEIGHT_COLOR_9P (the default) optimises colour and weight logits; UNIT_WEIGHT_8P optimises one
+ * bounded amplitude per channel (colour = sigmoid(amplitude_raw)) with every weight fixed at 1.
+ * Under UNIT_WEIGHT_8P the colour arrays of rtgs2d_fit_set_raw, rtgs2d_fit_get_raw and
+ * rtgs2d_fit_write_rows carry amplitude_raw and their weight_raw arguments are ignored (NULL is
+ * allowed), rtgs2d_fit_set_initial writes amplitude_raw = logit(sigmoid(weight_raw) *
+ * sigmoid(color_raw)) from the clamped logits (fit.py:384-385), and rtgs2d_fit_get_params returns
+ * weights of exactly 1. A change of parameterisation invalidates the raw parameters: the engine
+ * refuses to run until rtgs2d_fit_set_raw or rtgs2d_fit_set_initial is called again.
+ */
+#define RTGS2D_APPEARANCE_WEIGHT_COLOR_9P 0
+#define RTGS2D_APPEARANCE_UNIT_WEIGHT_8P 1
+RTGS2D_API int rtgs2d_fit_set_appearance(rtgs2d_fit* fit, int32_t parameterization);
 /* Runs `n_iterations` more iterations (capped at `iterations`). Synchronises `stream`. */
 RTGS2D_API int rtgs2d_fit_run(rtgs2d_fit* fit, int64_t n_iterations, void* stream);
 RTGS2D_API int rtgs2d_fit_get_raw(rtgs2d_fit* fit, float* xy_raw, float* diag_raw, float* off_raw,

@@ -5,6 +5,8 @@ baseline leg; never by the product package.
 
 Restated reference behaviour (paths relative to the reference project):
   - raw reparameterisation and its inverse   src/rtgs/image2gs/fit.py:374-417
+    (both appearance parameterisations: weight_color_9p and unit_weight_bounded_8p, whose
+    amplitude_raw = logit(sigmoid(weight_raw) * sigmoid(color_raw)) and weight = 1)
   - torch Adam + CosineAnnealingLR(eta_min=0.1*lr)   src/rtgs/image2gs/fit.py:419-422
   - loop: zero_grad, build, render, MSE, backward, step, sched, PSNR log   fit.py:451-540
   - final render and PSNR                    src/rtgs/image2gs/fit.py:542-554
@@ -24,22 +26,37 @@ import torch
 from oracle import render2d
 
 MIN_DIAG = 0.3
+WEIGHT_COLOR_9P = "weight_color_9p"
+UNIT_WEIGHT_8P = "unit_weight_bounded_8p"
 
 
 def softplus_inv(x: torch.Tensor) -> torch.Tensor:
     return x + torch.log(-torch.expm1(-x))
 
 
-def to_raw(xy, chol, color, weight, height: int, width: int) -> dict[str, torch.Tensor]:
-    """Raw (unconstrained) parameters from constrained ones (fit.py:375-380); works on (..., k)."""
+def to_raw(xy, chol, color, weight, height: int, width: int,
+           appearance: str = WEIGHT_COLOR_9P) -> dict[str, torch.Tensor]:
+    """Raw (unconstrained) parameters from constrained ones (fit.py:375-387); works on (..., k)."""
     wh = xy.new_tensor([width, height])
-    return {
+    color_raw = torch.logit(color.clamp(1e-3, 1 - 1e-3))
+    weight_raw = torch.logit(weight.clamp(1e-3, 1 - 1e-3))
+    raw = {
         "xy_raw": torch.logit((xy / wh).clamp(1e-4, 1 - 1e-4)),
         "diag_raw": softplus_inv(chol[..., [0, 2]] - MIN_DIAG),
         "off_raw": chol[..., 1].clone(),
-        "color_raw": torch.logit(color.clamp(1e-3, 1 - 1e-3)),
-        "weight_raw": torch.logit(weight.clamp(1e-3, 1 - 1e-3)),
     }
+    if appearance == WEIGHT_COLOR_9P:
+        raw.update(color_raw=color_raw, weight_raw=weight_raw)
+    elif appearance == UNIT_WEIGHT_8P:
+        raw["amplitude_raw"] = torch.logit(torch.sigmoid(weight_raw)[..., None] * torch.sigmoid(color_raw))
+    else:
+        raise ValueError(f"unknown appearance parameterisation {appearance!r}")
+    return raw
+
+
+def appearance_names(raw: dict[str, torch.Tensor]) -> tuple[str, ...]:
+    """The raw parameters a geometry-frozen fit optimises (fit.py:393-397)."""
+    return ("amplitude_raw",) if "amplitude_raw" in raw else ("color_raw", "weight_raw")
 
 
 def build(raw: dict[str, torch.Tensor], height: int, width: int):
@@ -47,12 +64,13 @@ def build(raw: dict[str, torch.Tensor], height: int, width: int):
     wh = raw["xy_raw"].new_tensor([width, height])
     diag = torch.nn.functional.softplus(raw["diag_raw"]) + MIN_DIAG
     chol = torch.stack([diag[..., 0], raw["off_raw"], diag[..., 1]], dim=-1)
-    return (
-        torch.sigmoid(raw["xy_raw"]) * wh,
-        chol,
-        torch.sigmoid(raw["color_raw"]),
-        torch.sigmoid(raw["weight_raw"]),
-    )
+    if "amplitude_raw" in raw:
+        color = torch.sigmoid(raw["amplitude_raw"])
+        weight = torch.ones_like(color[..., 0])
+    else:
+        color = torch.sigmoid(raw["color_raw"])
+        weight = torch.sigmoid(raw["weight_raw"])
+    return torch.sigmoid(raw["xy_raw"]) * wh, chol, color, weight
 
 
 def psnr(pred: torch.Tensor, target: torch.Tensor) -> float:
@@ -70,11 +88,12 @@ class StackedFit:
     """The stacked-view fit loop, one iteration per ``step`` (``fit_views`` runs it to the end;
     bench.py's CPU baseline times single iterations of it from any parameter state)."""
 
-    def __init__(self, targets, init, iterations, lr=1e-2, masks=None, freeze_geometry=False, t_max=None):
+    def __init__(self, targets, init, iterations, lr=1e-2, masks=None, freeze_geometry=False, t_max=None,
+                 appearance=WEIGHT_COLOR_9P):
         self.targets, self.masks = targets, masks
         self.n_views, self.height, self.width = targets.shape[:3]
-        self.raw = to_raw(*init, self.height, self.width)
-        names = ("color_raw", "weight_raw") if freeze_geometry else tuple(self.raw)
+        self.raw = to_raw(*init, self.height, self.width, appearance)
+        names = appearance_names(self.raw) if freeze_geometry else tuple(self.raw)
         for name, value in self.raw.items():
             value.requires_grad_(name in names)
         self.opt = torch.optim.Adam([self.raw[n] for n in names], lr=lr)
@@ -126,6 +145,7 @@ def fit_views(
     masks: torch.Tensor | None = None,
     freeze_geometry: bool = False,
     t_max: int | None = None,
+    appearance: str = WEIGHT_COLOR_9P,
 ):
     """Fit stacked (B, H, W, 3) targets from a stacked (B, N, .) initialisation.
 
@@ -133,22 +153,24 @@ def fit_views(
     the single-image native fit (the per-view MSE mean is the serial loss); with a (B, H, W) mask
     the loss is the mask-restricted mean and PSNR is ``masked_psnr``. ``t_max`` (default
     ``iterations``) is the cosine schedule's length, so the first iterations of a longer fit can be
-    run alone.
+    run alone. ``appearance`` selects the raw appearance parameters (fit.py:381-387).
     """
-    fit = StackedFit(targets, init, iterations, lr=lr, masks=masks, freeze_geometry=freeze_geometry, t_max=t_max)
+    fit = StackedFit(targets, init, iterations, lr=lr, masks=masks, freeze_geometry=freeze_geometry, t_max=t_max,
+                     appearance=appearance)
     for it in range(iterations):
         fit.step(it, log=it % log_every == 0 or it == iterations - 1)
     return fit.finish()
 
 
-def fit_serial(target, init, iterations, lr=1e-2, log_every=50, mask=None, coverage_weight=0.0):
+def fit_serial(target, init, iterations, lr=1e-2, log_every=50, mask=None, coverage_weight=0.0,
+               appearance=WEIGHT_COLOR_9P):
     """The serial native fit loop (fit.py:451-554) of one (H, W, 3) target, with the serial loss
     (fit.py:557-563: MSE, or (0.1 + 0.9 mask)-weighted MSE with a mask) and the optional mask
     coverage penalty weight * mean(coverage * (1 - mask)), coverage = 1 - exp(-density)
     (fit.py:457-459, 566-572; renderer2d.py:128-140). Returns ((xy, chol, color, weight), history).
     """
     height, width = target.shape[:2]
-    raw = to_raw(*init, height, width)
+    raw = to_raw(*init, height, width, appearance)
     for value in raw.values():
         value.requires_grad_(True)
     opt = torch.optim.Adam(list(raw.values()), lr=lr)

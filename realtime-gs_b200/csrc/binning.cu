@@ -154,7 +154,7 @@ __device__ __forceinline__ uint32_t bitonic_shfl(uint32_t v, int i, int k, int j
 
 __global__ void __launch_bounds__(kTileSortWarps * 32)
 tile_sort_kernel(const int* __restrict__ tile_end, const int2* __restrict__ tile_seg,
-                 const int* __restrict__ fill, int64_t n_tiles, int64_t cap,
+                 int* __restrict__ fill, int64_t n_tiles, int64_t cap,
                  unsigned long long* __restrict__ stats, uint32_t* __restrict__ list,
                  int2* __restrict__ ranges) {
   __shared__ uint32_t s_buf[kTileSortWarps][kSegSortMax];
@@ -163,11 +163,17 @@ tile_sort_kernel(const int* __restrict__ tile_end, const int2* __restrict__ tile
   const int64_t t = static_cast<int64_t>(blockIdx.x) * kTileSortWarps + warp;
   if (t >= n_tiles) return;
   int64_t start, end;
-  if (tile_seg) {  // direct placement: the tile's segment and how much of it the projection filled
+  if (tile_seg) {  // direct placement: the tile's segment and how far the projection moved its cursor
     const int2 sg = tile_seg[t];
-    const int filled = fill[t];
+    int cursor = lane == 0 ? fill[t] : 0;
+    cursor = __shfl_sync(0xffffffffu, cursor, 0);
+    const int filled = cursor - sg.x;
     start = sg.x;
     end = start + (filled < sg.y ? filled : sg.y);
+    if (lane == 0) {
+      fill[t] = filled;  // the count, for the next layout
+      if (filled > sg.y) atomicMax(&stats[kStatSegOverflow], 1ull);  // ids spilled past the segment
+    }
   } else {    // scatter: inclusive scan of the tile counts
     start = t == 0 ? 0 : tile_end[t - 1];
     end = tile_end[t];
@@ -317,8 +323,8 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int* tot
 // Direct placement layout for the next binning: tile t gets a segment of count + 8 + count / 4
 // slots (count = this binning's entries of the tile; exactly count without slack), segments packed
 // in tile order and clipped to the list capacity. Counts come from the scan (tile_end, after a
-// scatter) or from the fill counters of a direct placement, which are then zeroed for the next
-// one. With `order`, the tiles are also counting-sorted by descending count (capped at 1023) into
+// scatter) or from the counts that the tile sort of a direct placement left in `fill`; `fill`
+// then receives every tile's cursor (its segment's start) for the next placement. With `order`, the tiles are also counting-sorted by descending count (capped at 1023) into
 // order[]: the next raster's block order. One block (it runs beside the raster, off the critical
 // path); each thread owns a run of consecutive tiles and reads their counts once per pass.
 __global__ void __launch_bounds__(kSmallScanThreads)
@@ -341,13 +347,13 @@ layout_kernel(const int* __restrict__ tile_end, int* __restrict__ fill, int n_ti
     if (order) atomicAdd(&s_bin[bin(c)], 1);
   }
   int start = block_exclusive_scan(sum, s_warp, nullptr);
-  const bool zero_here = !tile_end && !order;  // else the order pass zeroes the fill counters
+  const bool cursor_here = tile_end || !order;  // else the order pass, which reads the counts
   for (int t = i0; t < i1; ++t) {
     const int c = count(t);
     const int sc = seg_cap(c);
     const int room = list_cap - start;
     seg[t] = make_int2(start, sc < room ? sc : (room > 0 ? room : 0));
-    if (zero_here) fill[t] = 0;
+    if (cursor_here) fill[t] = start;
     start += sc;
   }
   if (!order) return;
@@ -357,7 +363,7 @@ layout_kernel(const int* __restrict__ tile_end, int* __restrict__ fill, int n_ti
   for (int t = i0; t < i1; ++t) {
     const int c = count(t);
     order[atomicAdd(&s_bin[bin(c)], 1)] = t;
-    if (!tile_end) fill[t] = 0;
+    if (!tile_end) fill[t] = seg[t].x;  // written by this thread above
   }
 }
 
@@ -455,7 +461,7 @@ int direct_layout(BinBuffers& bb, const Geometry& g, bool after_scatter, bool sl
       after_scatter ? bb.tile_end.as<int>() : nullptr, bb.tile_count.as<int>(),
       static_cast<int>(n_tiles), static_cast<int>(list_cap < INT32_MAX ? list_cap : INT32_MAX), slack,
       bb.seg.as<int2>(), order);
-  if (!after_scatter) bb.counts_cleared = true;  // the kernel zeroes the fill counters
+  bb.counts_cleared = true;  // tile_count holds the cursors of the next placement
   return check_cuda(cudaGetLastError(), "layout_kernel");
 }
 

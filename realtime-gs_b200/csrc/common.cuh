@@ -49,19 +49,22 @@ __device__ __forceinline__ int to_index_clamped(float v, int hi) {
 // torch clamp_min(x, 0): NaN propagates.
 __device__ __forceinline__ float clamp_min0(float x) { return x < 0.0f ? 0.0f : x; }
 
+// Sigma^-1 entries (i00, i01, i11) and the entries (a, b, c) of L^-1 = [[a, 0], [b, c]] they are
+// built from (zero when the conic was given directly).
 struct Conic {
   float i00, i01, i11;
+  float a = 0.f, b = 0.f, c = 0.f;
 };
 
 // Analytic Sigma^-1 from (l11, l21, l22), gaussians2d.py:34-44.
 __device__ __forceinline__ Conic conic_from_chol(float l11, float l21, float l22) {
-  float a = __frcp_rn(l11);
-  float b = __fdiv_rn(-l21, __fmul_rn(l11, l22));
-  float c = __frcp_rn(l22);
   Conic k;
-  k.i00 = __fadd_rn(__fmul_rn(a, a), __fmul_rn(b, b));
-  k.i01 = __fmul_rn(b, c);
-  k.i11 = __fmul_rn(c, c);
+  k.a = __frcp_rn(l11);
+  k.b = __fdiv_rn(-l21, __fmul_rn(l11, l22));
+  k.c = __frcp_rn(l22);
+  k.i00 = __fadd_rn(__fmul_rn(k.a, k.a), __fmul_rn(k.b, k.b));
+  k.i01 = __fmul_rn(k.b, k.c);
+  k.i11 = __fmul_rn(k.c, k.c);
   return k;
 }
 

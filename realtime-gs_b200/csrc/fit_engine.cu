@@ -58,6 +58,7 @@ struct rtgs2d_fit {
   cudaEvent_t fork_event = nullptr;
   cudaEvent_t join_event = nullptr;
   bool have_targets = false, have_raw = false;
+  bool unit_weight = false;  // RTGS2D_APPEARANCE_UNIT_WEIGHT_8P: weight = 1, no weight parameter
   bool scale_uploaded = false;            // view_scale holds the constant scale of the MSE modes
   DevBuf init_status;                     // uint32: failed checks of rtgs2d_fit_set_initial
   uint32_t* host_status = nullptr;        // pinned mirror of init_status
@@ -109,7 +110,7 @@ __global__ void pack_raw_kernel(int64_t m, const float* __restrict__ xy, const f
   raw[kCr * m + i] = color[3 * i];
   raw[kCg * m + i] = color[3 * i + 1];
   raw[kCb * m + i] = color[3 * i + 2];
-  raw[kWr * m + i] = weight[i];
+  raw[kWr * m + i] = weight ? weight[i] : 0.f;
 }
 
 __global__ void unpack_raw_kernel(int64_t m, const float* __restrict__ raw, float* xy, float* diag,
@@ -135,18 +136,21 @@ __global__ void unpack_raw_kernel(int64_t m, const float* __restrict__ raw, floa
 
 // rtgs2d_fit_set_initial: the reference's checks of an initialisation (fit.py:634-676: finite
 // fields, means inside the image, Cholesky diagonal above _MIN_DIAG, colours and weights in [0,1])
-// and its raw transform (fit.py:375-380: logit of the clamped normalised mean, inverse softplus of
-// the diagonal minus _MIN_DIAG, the off-diagonal as is, logit of the clamped colour and weight;
-// non-finite raw values are the reference's NonFiniteRawParameterError, fit.py:134-141), one
-// thread per gaussian, written straight into the planar raw parameters. Failed checks are OR-ed
-// into *status (RTGS2D_INIT_* bits).
+// and its raw transform (fit.py:375-387: logit of the clamped normalised mean, inverse softplus of
+// the diagonal minus _MIN_DIAG, the off-diagonal as is, logit of the clamped colour and weight --
+// or, with unit_weight, the amplitude logit(sigmoid(weight_raw) * sigmoid(color_raw)) in the
+// colour slots and nothing in the weight slot; non-finite raw values are the reference's
+// NonFiniteRawParameterError, fit.py:134-141), one thread per gaussian, written straight into the
+// planar raw parameters. Failed checks are OR-ed into *status (RTGS2D_INIT_* bits).
 __device__ __forceinline__ float logit_f(float p) { return logf(__fdiv_rn(p, 1.0f - p)); }
 __device__ __forceinline__ float softplus_inv_f(float x) { return x + logf(-expm1f(-x)); }
+__device__ __forceinline__ float sigmoid_rn(float x) { return __frcp_rn(__fadd_rn(1.0f, expf(-x))); }
 
 __global__ void init_raw_kernel(int64_t m, const float* __restrict__ xy, const float* __restrict__ chol,
                                 const float* __restrict__ color, const float* __restrict__ weight,
-                                int height, int width, float* __restrict__ raw, float* __restrict__ m1,
-                                float* __restrict__ m2, unsigned* __restrict__ status) {
+                                int height, int width, bool unit_weight, float* __restrict__ raw,
+                                float* __restrict__ m1, float* __restrict__ m2,
+                                unsigned* __restrict__ status) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
   if (i >= m) return;
   const float x = xy[2 * i], y = xy[2 * i + 1];
@@ -179,6 +183,11 @@ __global__ void init_raw_kernel(int64_t m, const float* __restrict__ xy, const f
   r[kCg] = logit_f(clamp(c[1], kLo, kHi));
   r[kCb] = logit_f(clamp(c[2], kLo, kHi));
   r[kWr] = logit_f(clamp(w, kLo, kHi));
+  if (unit_weight) {  // fit.py:384-385: one bounded amplitude per channel, weight fixed at 1
+    const float sw = sigmoid_rn(r[kWr]);
+    for (int ch = kCr; ch <= kCb; ++ch) r[ch] = logit_f(__fmul_rn(sw, sigmoid_rn(r[ch])));
+    r[kWr] = 0.f;
+  }
 #pragma unroll
   for (int k = 0; k < kRawSlots; ++k) {
     if (!isfinite(r[k])) bad |= RTGS2D_INIT_NONFINITE_RAW;
@@ -308,7 +317,7 @@ __global__ void write_rows_kernel(int64_t m, const int64_t* __restrict__ rows, i
     raw[kCr * m + i] = color[3 * r];
     raw[kCg * m + i] = color[3 * r + 1];
     raw[kCb * m + i] = color[3 * r + 2];
-    raw[kWr * m + i] = weight[r];
+    raw[kWr * m + i] = weight ? weight[r] : 0.f;
   }
 #pragma unroll
   for (int k = 0; k < kRawSlots; ++k) {
@@ -320,7 +329,7 @@ __global__ void write_rows_kernel(int64_t m, const int64_t* __restrict__ rows, i
 // Projection + synchronous binning (exact entry count; used outside the iteration loop).
 int project_and_bin(rtgs2d_fit* f, cudaStream_t s) {
   RTGS_TRY(launch_project_raw(f->bb, f->geo, f->raw.as<float>(), f->m, f->n, false, active_rows(f),
-                              coverage(f), s));
+                              coverage(f), f->unit_weight, s));
   RTGS_TRY(bin_entries(f->bb, f->geo, f->m, s));
   f->last_entries = f->bb.n_entries;
   f->last_pairs = f->bb.n_pairs;
@@ -365,7 +374,7 @@ std::vector<uintptr_t> chunk_key(const rtgs2d_fit* f, int64_t chunk) {
   const BinBuffers& bb = f->bb;
   std::vector<uintptr_t> k = {static_cast<uintptr_t>(chunk), static_cast<uintptr_t>(radix(f)),
                               static_cast<uintptr_t>(bb.capacity), static_cast<uintptr_t>(f->use_active),
-                              static_cast<uintptr_t>(direct_chunk(f))};
+                              static_cast<uintptr_t>(direct_chunk(f)), static_cast<uintptr_t>(f->unit_weight)};
   for (const DevBuf* b : {&bb.records, &bb.weights, &bb.spans, &bb.counts, &bb.offsets, &bb.list,
                           &bb.tile_count, &bb.tile_end, &bb.seg, &bb.tile_order, &bb.entries[0], &bb.entries[1], &bb.ranges,
                           &bb.partials, &bb.partial_d, &bb.cub_temp, &bb.sort_counts, &bb.stats,
@@ -391,7 +400,7 @@ int enqueue_chunk(rtgs2d_fit* f, int64_t chunk, cudaStream_t s, cudaEvent_t* ev,
     return capturing ? cudaEventRecordWithFlags(e, s, cudaEventRecordExternal) : cudaEventRecord(e, s);
   };
   RTGS_TRY(launch_project_raw(bb, f->geo, f->raw.as<float>(), f->m, f->n, true, active_rows(f),
-                              coverage(f), s));
+                              coverage(f), f->unit_weight, s));
   // Binning: the chunk's first iteration scatters the projection's entries; with direct placement
   // (direct_chunk), every later projection (fused into Adam) writes its ids straight into tile
   // segments sized from the previous binning, and the binning is just the tile sort.
@@ -428,7 +437,7 @@ int enqueue_chunk(rtgs2d_fit* f, int64_t chunk, cudaStream_t s, cudaEvent_t* ev,
     RTGS_TRY(launch_adam_fit(bb, f->geo, f->m, f->n, f->raw.as<float>(), f->m1.as<float>(),
                              f->m2.as<float>(), f->iter_table.as<IterScalars>(),
                              static_cast<int>(k), lg, k + 1 < chunk, active_rows(f), coverage(f),
-                             layout ? bb.seg.as<int2>() : nullptr, s));
+                             layout, s));
     if (e) RTGS_CUDA(record(e[3]), "event record");
   }
   return 0;
@@ -647,7 +656,7 @@ int rtgs2d_fit_set_raw(rtgs2d_fit* f, const float* xy_raw, const float* diag_raw
                        const float* off_raw, const float* color_raw, const float* weight_raw,
                        void* stream) {
   RTGS_TRY(check_fit(f));
-  if (f->m > 0 && (!xy_raw || !diag_raw || !off_raw || !color_raw || !weight_raw)) {
+  if (f->m > 0 && (!xy_raw || !diag_raw || !off_raw || !color_raw || (!weight_raw && !f->unit_weight))) {
     return set_error(RTGS2D_ERR_INVALID, "raw parameter pointer is NULL");
   }
   cudaStream_t s = as_stream(stream);
@@ -682,8 +691,9 @@ int rtgs2d_fit_set_initial(rtgs2d_fit* f, const float* xy, const float* chol, co
   RTGS_CUDA(cudaMemsetAsync(f->init_status.ptr, 0, sizeof(uint32_t), s), "zero status");
   if (f->m > 0) {
     init_raw_kernel<<<grid_for(f->m), kThreads, 0, s>>>(f->m, xy, chol, color, weight, f->height,
-                                                        f->width, f->raw.as<float>(), f->m1.as<float>(),
-                                                        f->m2.as<float>(), f->init_status.as<unsigned>());
+                                                        f->width, f->unit_weight, f->raw.as<float>(),
+                                                        f->m1.as<float>(), f->m2.as<float>(),
+                                                        f->init_status.as<unsigned>());
     RTGS_CUDA(cudaGetLastError(), "init_raw_kernel");
   }
   RTGS_CUDA(cudaMemcpyAsync(f->host_status, f->init_status.ptr, sizeof(uint32_t), cudaMemcpyDeviceToHost, s),
@@ -744,13 +754,14 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
       const double bc1 = 1.0 - std::pow(0.9, t);
       const double bc2 = 1.0 - std::pow(0.999, t);
       row.adam.neg_step_size = static_cast<float>(-(f->lr_current / bc1));
-      row.adam.bc2_sqrt = static_cast<float>(std::pow(bc2, 0.5));
+      row.adam.inv_bc2_sqrt = static_cast<float>(1.0 / std::sqrt(bc2));
       row.adam.beta1 = 0.9f;
       row.adam.beta2 = 0.999f;
       row.adam.one_minus_beta1 = static_cast<float>(1.0 - 0.9);
       row.adam.one_minus_beta2 = static_cast<float>(1.0 - 0.999);
       row.adam.eps = 1e-8f;
       row.adam.freeze_geometry = f->opt.freeze_geometry;
+      row.adam.unit_weight = f->unit_weight;
       row.log_slot = -1;
       if (is_log_iter(f->opt, it)) {
         const int64_t slot = static_cast<int64_t>(f->log_iters.size());
@@ -866,15 +877,29 @@ int rtgs2d_fit_write_rows(rtgs2d_fit* f, const int64_t* rows, int64_t n_rows, co
   if (n_rows < 0) return set_error(RTGS2D_ERR_INVALID, "n_rows must be >= 0");
   if (n_rows == 0 || f->m == 0) return RTGS2D_OK;
   if (!rows) return set_error(RTGS2D_ERR_INVALID, "rows is NULL");
+  if (f->unit_weight) weight_raw = nullptr;  // no weight parameter
   const int given = (xy_raw != nullptr) + (diag_raw != nullptr) + (off_raw != nullptr) +
                     (color_raw != nullptr) + (weight_raw != nullptr);
-  if (given != 0 && given != 5) {
-    return set_error(RTGS2D_ERR_INVALID, "give all five raw parameter arrays or none");
+  const int all = f->unit_weight ? 4 : 5;
+  if (given != 0 && given != all) {
+    return set_error(RTGS2D_ERR_INVALID, "give all raw parameter arrays or none");
   }
   write_rows_kernel<<<grid_for(n_rows), kThreads, 0, as_stream(stream)>>>(
       f->m, rows, n_rows, xy_raw, diag_raw, off_raw, color_raw, weight_raw, f->raw.as<float>(),
       f->m1.as<float>(), f->m2.as<float>());
   return check_cuda(cudaGetLastError(), "write_rows_kernel");
+}
+
+int rtgs2d_fit_set_appearance(rtgs2d_fit* f, int32_t parameterization) {
+  RTGS_TRY(check_fit(f));
+  if (parameterization != RTGS2D_APPEARANCE_WEIGHT_COLOR_9P &&
+      parameterization != RTGS2D_APPEARANCE_UNIT_WEIGHT_8P) {
+    return set_error(RTGS2D_ERR_INVALID, "unknown appearance parameterization");
+  }
+  const bool unit = parameterization == RTGS2D_APPEARANCE_UNIT_WEIGHT_8P;
+  if (unit != f->unit_weight) f->have_raw = false;  // the raw slots change meaning: set them again
+  f->unit_weight = unit;
+  return RTGS2D_OK;
 }
 
 int rtgs2d_fit_set_binning(rtgs2d_fit* f, int32_t mode) {
@@ -919,7 +944,8 @@ int rtgs2d_fit_get_raw(rtgs2d_fit* f, float* xy_raw, float* diag_raw, float* off
   RTGS_TRY(check_fit(f));
   if (f->m == 0) return RTGS2D_OK;
   unpack_raw_kernel<<<grid_for(f->m), kThreads, 0, as_stream(stream)>>>(
-      f->m, f->raw.as<float>(), xy_raw, diag_raw, off_raw, color_raw, weight_raw);
+      f->m, f->raw.as<float>(), xy_raw, diag_raw, off_raw, color_raw,
+      f->unit_weight ? nullptr : weight_raw);
   return check_cuda(cudaGetLastError(), "unpack_raw_kernel");
 }
 
@@ -929,8 +955,8 @@ int rtgs2d_fit_get_params(rtgs2d_fit* f, float* xy, float* chol, float* color, f
   if (f->m > 0 && (!xy || !chol || !color || !weight)) {
     return set_error(RTGS2D_ERR_INVALID, "output pointer is NULL");
   }
-  return launch_build_params(f->raw.as<float>(), f->m, f->height, f->width, xy, chol, color,
-                             weight, as_stream(stream));
+  return launch_build_params(f->raw.as<float>(), f->m, f->height, f->width, f->unit_weight, xy,
+                             chol, color, weight, as_stream(stream));
 }
 
 int rtgs2d_fit_evaluate(rtgs2d_fit* f, float* render, double* sums, void* stream) {

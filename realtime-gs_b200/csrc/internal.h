@@ -67,7 +67,7 @@ struct BinBuffers {
   DevBuf offsets;     // int[M]  entry index of each gaussian's first tile (see bin_entries)
   DevBuf list;        // uint32[capacity] gaussian ids grouped by tile, ascending inside a tile
   DevBuf tile_count;  // int[n_tiles] entries per tile (counted up by the projection, back down
-                      //   to zero by the scatter)
+                      //   to zero by the scatter); tile cursors during direct placement
   DevBuf tile_end;    // int[n_tiles] inclusive scan of tile_count
   DevBuf entries[2];  // uint64[capacity] (tile key << 32 | gaussian id), radix-sort double buffer
   DevBuf ranges;      // int2[n_tiles] [start, end) of every tile in the list (or sorted entries)
@@ -81,8 +81,9 @@ struct BinBuffers {
   unsigned long long* host_stats = nullptr;  // pinned mirror of `stats`
   int sorted_sel = 0;                         // which entries buffer holds the sorted result
   bool presorted = false;                     // radix path (entries + ranges) produced the binning
-  bool counts_cleared = false;                // the last binning left tile_count and stats
-                                              //   slots 0-1 at zero (the scatter path does)
+  bool counts_cleared = false;                // the last binning left stats slots 0-1 at zero
+                                              //   and tile_count ready for the next projection
+                                              //   (zeros after a scatter, cursors after a layout)
   bool entries_emitted = false;               // the last projection emitted the entries
   int64_t capacity = 0;                       // entries the entry buffers can hold
   int64_t n_entries = 0;                      // host-known entry count (synchronous binning)
@@ -112,15 +113,17 @@ int launch_project_chol(BinBuffers& bb, const Geometry& g, const float* xy, cons
 int launch_project_conic(BinBuffers& bb, const Geometry& g, const float* xy, const float* conics,
                          const float* colors, const float* weights, const int32_t* rects,
                          const int32_t* view_index, int64_t m, bool want_weights, cudaStream_t s);
+// unit_weight: weight = 1 instead of sigmoid(raw weight) (the unit-weight appearance).
 int launch_project_raw(BinBuffers& bb, const Geometry& g, const float* raw, int64_t m,
                        int64_t n_per_view, bool emit, const uint8_t* active, bool want_weights,
-                       cudaStream_t s);
+                       bool unit_weight, cudaStream_t s);
 // Bit-exact support rectangles only: rects (M,4) (x0, x1, y0, y1; x1 = x0 - 1 if empty), counts (M,).
 int launch_support_rects(const float* xy, const float* chol, int64_t m, int height, int width,
                          int32_t* rects, int64_t* counts, cudaStream_t s);
-// raw (planar 9 x M) -> constrained (xy (M,2), chol (M,3), color (M,3), weight (M))
-int launch_build_params(const float* raw, int64_t m, int height, int width, float* xy, float* chol,
-                        float* color, float* weight, cudaStream_t s);
+// raw (planar 9 x M) -> constrained (xy (M,2), chol (M,3), color (M,3), weight (M)); with
+// unit_weight every weight is 1.
+int launch_build_params(const float* raw, int64_t m, int height, int width, bool unit_weight,
+                        float* xy, float* chol, float* color, float* weight, cudaStream_t s);
 
 // ---- binning (binning.cu, sort.cu) --------------------------------------------------------------
 // Synchronous binning: scan counts, read the entry count back to the host (synchronises `s`),
@@ -141,13 +144,15 @@ int check_long_tiles(BinBuffers& bb, const Geometry& g, cudaStream_t s);
 // the capacity are dropped and show up as stats[kStatMaxEntries] > capacity; a tile list longer
 // than kSegSortMax on the scatter path is flagged by the raster in stats[kStatLongTile].
 int bin_entries_async(BinBuffers& bb, const Geometry& g, int64_t m, bool radix, cudaStream_t s);
-// Direct placement (fit loop): a projection with ProjOut::seg set writes each gaussian id straight
-// into its tile's segment (slot from the tile's fill counter, bb.tile_count), sized from the
-// previous binning's counts with slack; a full segment sets stats[kStatSegOverflow].
+// Direct placement (fit loop): a projection with ProjOut::list set writes each gaussian id straight
+// into its tile's segment, at the position that an atomic on the tile's cursor (bb.tile_count)
+// returns; segments are sized from the previous binning's counts with slack.
 // direct_layout computes the segments from the last binning (after_scatter: from tile_end; else
-// from the fill counters, which it zeroes; slack: count + count/4 + 8 slots, else count);
-// direct_sort sorts the filled segments into bb.ranges. Nothing but the next projection reads the
-// layout, so it can run beside the raster. With `order`, direct_layout also writes the tiles in
+// from the counts that direct_sort left in bb.tile_count; slack: count + count/4 + 8 slots, else
+// count) and sets every cursor to its segment's start; direct_sort turns the cursors back into
+// counts, flags a cursor past its segment's end in stats[kStatSegOverflow] and sorts the filled
+// segments into bb.ranges. Nothing but the next projection reads the layout, so it can run beside
+// the raster. With `order`, direct_layout also writes the tiles in
 // descending order of their entry count (a permutation of the tiles, ties in any order) for the
 // next raster: heaviest tiles first shortens the launch's tail. Up to kDirectMaxTiles tiles.
 constexpr int64_t kDirectMaxTiles = int64_t{1} << 20;
@@ -201,9 +206,10 @@ int launch_finalize_conic(const BinBuffers& bb, int64_t m, const float* conics,
 
 struct AdamScalars {
   float neg_step_size;   // -(lr / (1 - beta1^t))
-  float bc2_sqrt;        // sqrt(1 - beta2^t)
+  float inv_bc2_sqrt;    // 1 / sqrt(1 - beta2^t)
   float beta1, beta2, one_minus_beta1, one_minus_beta2, eps;
   int freeze_geometry;
+  int unit_weight;  // weight fixed at 1 (no weight parameter)
 };
 // Per-iteration constants of a fit chunk, read by the Adam kernel from a device table (so the
 // launches of every chunk are identical and can be replayed from one CUDA graph).
@@ -219,11 +225,11 @@ struct LossLog {
 };
 // Adam step from the last raster's entry moments, with the constants of table[k]; with
 // project_next the updated parameters are also projected (records, spans, counts, offsets,
-// stats) for the next iteration's binning: entries for the scatter path, or with `seg` the ids
-// placed directly into the tile segments (see direct_layout).
+// stats) for the next iteration's binning: entries for the scatter path, or with `direct` the ids
+// placed directly into the tile segments at the tile cursors (see direct_layout).
 int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_view, float* raw,
                     float* m1, float* m2, const IterScalars* table, int k, const LossLog& lg,
-                    bool project_next, const uint8_t* active, bool density, const int2* seg,
+                    bool project_next, const uint8_t* active, bool density, bool direct,
                     cudaStream_t s);
 
 }  // namespace rtgs2d

@@ -23,8 +23,8 @@ struct ProjOut {
   uint64_t* entries;          // null: count every entry; else emit (tile key << 32 | id) at
   int64_t cap;                //   each entry index below cap and count only those
   const uint8_t* active;      // null: every gaussian is live; else 0 = parked (not rendered)
-  const int2* seg;            // non-null: direct placement into tile segments (start, slots); the
-  uint32_t* list;             //   ids go to list, tile_count is the fill counter
+  uint32_t* list;             // non-null: direct placement; tile_count[t] is then tile t's cursor
+  int64_t list_cap;           //   (next free list position) and ids go to list below list_cap
   unsigned long long* stats;  // kStat* slots
   int tiles_x;
 };
@@ -66,15 +66,17 @@ __device__ __forceinline__ void for_each_span_tile(int64_t gid, int cnt, const T
   }
 }
 
-// Direct placement of gaussian gid into the segments of the tiles of its span: slot = the tile's
-// fill counter before this entry, position = segment start + slot; a slot past the segment sets
-// stats[kStatSegOverflow] (the binning is then invalid and the caller re-bins). Two halves, so the
-// caller can overlap their round trips with its own: direct_reserve issues a small span's counter
-// atomics and segment loads (nothing waits on them yet); direct_commit stores the ids, and walks
-// spans longer than kSmallSpan with the whole warp (all lanes of the warp must call it).
+// Direct placement of gaussian gid into the segments of the tiles of its span: the tile's cursor
+// (set to its segment's start by the layout) is advanced by one atomic, whose old value is the
+// entry's list position. Nothing here checks the segment's end: the tile sort compares each
+// cursor with its segment and flags an overrun in stats[kStatSegOverflow] (the chunk is then
+// re-binned and re-run, so ids that an overrun wrote into a neighbouring segment are never used);
+// positions past the list capacity are not written. Two halves, so the caller can overlap their
+// round trips with its own: direct_reserve issues a small span's cursor atomics (nothing waits on
+// them yet); direct_commit stores the ids, and walks spans longer than kSmallSpan with the whole
+// warp (all lanes of the warp must call it).
 struct DirectSlots {
-  int slot[kSmallSpan];
-  int2 seg[kSmallSpan];
+  int pos[kSmallSpan];
 };
 
 __device__ __forceinline__ void direct_reserve(int cnt, const TileSpan& sp, const ProjOut& o,
@@ -85,8 +87,7 @@ __device__ __forceinline__ void direct_reserve(int cnt, const TileSpan& sp, cons
   for (int j = 0; j < kSmallSpan; ++j) {
     if (j < cnt) {
       const int t = sp.key_base + ty * o.tiles_x + tx;
-      d.slot[j] = atomicAdd(&o.tile_count[t], 1);
-      d.seg[j] = o.seg[t];
+      d.pos[j] = atomicAdd(&o.tile_count[t], 1);
       if (++tx == sp.tx0 + sp.ntx) {
         tx = sp.tx0;
         ++ty;
@@ -100,13 +101,7 @@ __device__ __forceinline__ void direct_commit(int64_t gid, int cnt, const TileSp
   if (cnt > 0 && cnt <= kSmallSpan) {
 #pragma unroll
     for (int j = 0; j < kSmallSpan; ++j) {
-      if (j < cnt) {
-        if (d.slot[j] < d.seg[j].y) {
-          o.list[d.seg[j].x + d.slot[j]] = static_cast<uint32_t>(gid);
-        } else {
-          atomicMax(&o.stats[kStatSegOverflow], 1ull);
-        }
-      }
+      if (j < cnt && d.pos[j] < o.list_cap) o.list[d.pos[j]] = static_cast<uint32_t>(gid);
     }
   }
   const int lane = threadIdx.x & 31;
@@ -122,13 +117,8 @@ __device__ __forceinline__ void direct_commit(int64_t gid, int cnt, const TileSp
     const uint32_t g = static_cast<uint32_t>(__shfl_sync(0xffffffffu, static_cast<long long>(gid), src));
     for (int j = lane; j < c; j += 32) {
       const int t = kb + (ty0 + j / ntx) * o.tiles_x + tx0 + j % ntx;
-      const int sl = atomicAdd(&o.tile_count[t], 1);
-      const int2 sg = o.seg[t];
-      if (sl < sg.y) {
-        o.list[sg.x + sl] = g;
-      } else {
-        atomicMax(&o.stats[kStatSegOverflow], 1ull);
-      }
+      const int p = atomicAdd(&o.tile_count[t], 1);
+      if (p < o.list_cap) o.list[p] = g;
     }
   }
 }
@@ -172,7 +162,7 @@ __device__ __forceinline__ void project_tail(int64_t i, bool active, float mx, f
     o.counts[i] = cnt;
   }
   DirectSlots dslots;  // with direct placement its round trips overlap the offset reservation's
-  if (o.seg) direct_reserve(cnt, sp, o, dslots);
+  if (o.list) direct_reserve(cnt, sp, o, dslots);
   const int lane = threadIdx.x & 31;
   int incl = cnt;
 #pragma unroll
@@ -212,7 +202,7 @@ __device__ __forceinline__ void project_tail(int64_t i, bool active, float mx, f
   __syncthreads();
   const int off = s_block_base + s_warp_base[warp] + incl - cnt;
   if (active) o.offsets[i] = off;
-  if (o.seg) {  // direct placement (warp-uniform choice; all lanes reach this point)
+  if (o.list) {  // direct placement (warp-uniform choice; all lanes reach this point)
     direct_commit(i, cnt, sp, o, dslots);
     return;
   }
@@ -319,8 +309,10 @@ struct GeoGrad {
   float gl11, gl21, gl22;            // Cholesky gradient
 };
 
-__device__ __forceinline__ GeoGrad geo_grad(const Moments& mo, float i00, float i01, float i11,
-                                            float l11, float l21, float l22, bool want_chol) {
+// Conic and Cholesky gradients from a gaussian's summed moments; the Cholesky chain rule uses the
+// entries a, b, c of L^-1 that conic_from_chol computed (the same correctly rounded values as
+// dividing again).
+__device__ __forceinline__ GeoGrad geo_grad(const Moments& mo, const Conic& k, bool want_chol) {
   GeoGrad r;
   r.gmx = mo.s[0];  // the renderer backward applied Sigma^-1 per piece lane
   r.gmy = mo.s[1];
@@ -329,9 +321,7 @@ __device__ __forceinline__ GeoGrad geo_grad(const Moments& mo, float i00, float 
   r.gi11 = -0.5f * mo.s[4];
   r.gl11 = r.gl21 = r.gl22 = 0.f;
   if (want_chol) {
-    const float a = 1.0f / l11;
-    const float b = -l21 / (l11 * l22);
-    const float c = 1.0f / l22;
+    const float a = k.a, b = k.b, c = k.c;
     const float ga = 2.0f * a * r.gi00;
     const float gb = fmaf(2.0f * b, r.gi00, c * r.gi01);
     const float gc = fmaf(b, r.gi01, 2.0f * c * r.gi11);
@@ -343,13 +333,24 @@ __device__ __forceinline__ GeoGrad geo_grad(const Moments& mo, float i00, float 
 }
 
 // One Adam update of a single float parameter, in the order of torch's single-tensor Adam
-// (exp_avg.lerp_, exp_avg_sq.mul_.addcmul_, denom = sqrt(v)/bc2_sqrt + eps, p.addcdiv_).
+// (exp_avg.lerp_, exp_avg_sq.mul_.addcmul_, denom = sqrt(v)/bc2_sqrt + eps, p.addcdiv_). The
+// moment updates are rounded as torch rounds them; the square root is the hardware approximation
+// (sqrt.approx, relative error ~2^-23), the division by bc2_sqrt a multiplication by its
+// reciprocal and the final quotient __fdividef (~2 ulp; denom >= eps, so never the > 2^126 case):
+// correctly rounded square roots and divisions are tens of instructions each, 27 of them per
+// gaussian on the Adam kernel's dependent chain, and the fit's tolerances are far above ulps.
+__device__ __forceinline__ float sqrt_approx(float x) {
+  float r;
+  asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 __device__ __forceinline__ void adam_update(float& p, float& m1, float& m2, float g,
                                             const AdamScalars& a) {
   m1 = __fadd_rn(m1, __fmul_rn(a.one_minus_beta1, __fsub_rn(g, m1)));
   m2 = __fadd_rn(__fmul_rn(m2, a.beta2), __fmul_rn(__fmul_rn(a.one_minus_beta2, g), g));
-  const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(m2), a.bc2_sqrt), a.eps);
-  p = __fadd_rn(p, __fmul_rn(a.neg_step_size, __fdiv_rn(m1, denom)));
+  const float denom = fmaf(sqrt_approx(m2), a.inv_bc2_sqrt, a.eps);
+  p = fmaf(a.neg_step_size, __fdividef(m1, denom), p);
 }
 
 

@@ -38,7 +38,7 @@ finalize_chol_kernel(int64_t m, int64_t cap, const int* __restrict__ counts, con
   if (!active) return;
   const float l11 = chol[3 * i], l21 = chol[3 * i + 1], l22 = chol[3 * i + 2];
   const Conic k = conic_from_chol(l11, l21, l22);
-  const GeoGrad gg = geo_grad(mo, k.i00, k.i01, k.i11, l11, l21, l22, true);
+  const GeoGrad gg = geo_grad(mo, k, true);
   const float w = weight[i];
   const float cr = color[3 * i], cg = color[3 * i + 1], cb = color[3 * i + 2];
   if (grad_xy) {
@@ -74,7 +74,7 @@ finalize_conic_kernel(int64_t m, int64_t cap, const int* __restrict__ counts, co
   const Moments mo = gather_moments<DEN>(partials, partial_d, cnt, off);
   if (!active) return;
   const GeoGrad gg =
-      geo_grad(mo, conics[3 * i], conics[3 * i + 1], conics[3 * i + 2], 1.f, 0.f, 1.f, false);
+      geo_grad(mo, Conic{conics[3 * i], conics[3 * i + 1], conics[3 * i + 2]}, false);
   const float w = weights[i];
   grad_xy[2 * i] = gg.gmx;
   grad_xy[2 * i + 1] = gg.gmy;
@@ -131,12 +131,12 @@ adam_fit_kernel(int64_t m, int64_t cap, int* counts, const int* __restrict__ off
     const float l22 = __fadd_rn(softplus_f(r[kD1]), kMinDiag);
     const float l21 = r[kOff];
     const Conic k = conic_from_chol(l11, l21, l22);
-    GeoGrad gg = geo_grad(mo, k.i00, k.i01, k.i11, l11, l21, l22, true);
+    GeoGrad gg = geo_grad(mo, k, true);
     // The fused fit raster leaves the plain first moments sum dq dx, sum dq dy: apply Sigma^-1.
     gg.gmx = fmaf(k.i00, mo.s[0], k.i01 * mo.s[1]);
     gg.gmy = fmaf(k.i01, mo.s[0], k.i11 * mo.s[1]);
     const float cr = sigmoid_f(r[kCr]), cg = sigmoid_f(r[kCg]), cb = sigmoid_f(r[kCb]);
-    const float w = sigmoid_f(r[kWr]);
+    const float w = a.unit_weight ? 1.0f : sigmoid_f(r[kWr]);
 
     float grad[kRawSlots];
     grad[kXr] = gg.gmx * static_cast<float>(width) * (1.0f - sx) * sx;
@@ -152,9 +152,10 @@ adam_fit_kernel(int64_t m, int64_t cap, int* counts, const int* __restrict__ off
                 (1.0f - w) * w;
 
     const int first = a.freeze_geometry ? kCr : 0;
+    const int last = a.unit_weight ? kWr : kRawSlots;  // the unit-weight fit has no weight parameter
 #pragma unroll
     for (int s = 0; s < kRawSlots; ++s) {
-      if (s < first) continue;
+      if (s < first || s >= last) continue;
       adam_update(r[s], v1[s], v2[s], grad[s], a);
       raw[s * m + i] = r[s];
       m1[s * m + i] = v1[s];
@@ -178,7 +179,7 @@ adam_fit_kernel(int64_t m, int64_t cap, int* counts, const int* __restrict__ off
       cr = sigmoid_f(r[kCr]);
       cg = sigmoid_f(r[kCg]);
       cb = sigmoid_f(r[kCb]);
-      w = sigmoid_f(r[kWr]);
+      w = a.unit_weight ? 1.0f : sigmoid_f(r[kWr]);
       view = static_cast<int>(i / n_per_view);
     }
     project_tail(i, active, mx, my, k, rc.x0, rc.x1, rc.y0, rc.y1, rc.pixels, w, cr, cg, cb, view,
@@ -226,7 +227,7 @@ int launch_finalize_conic(const BinBuffers& bb, int64_t m, const float* conics,
 
 int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_view, float* raw,
                     float* m1, float* m2, const IterScalars* table, int k, const LossLog& lg,
-                    bool project_next, const uint8_t* active, bool density, const int2* seg,
+                    bool project_next, const uint8_t* active, bool density, bool direct,
                     cudaStream_t s) {
   if (m == 0) return 0;
   ProjOut o{};
@@ -243,8 +244,9 @@ int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_
     o.entries = bb.entries[0].as<uint64_t>();
     o.cap = bb.capacity;
     o.active = active;
-    o.seg = seg;  // direct placement into the tile segments laid out by direct_layout
-    o.list = seg ? bb.list.as<uint32_t>() : nullptr;
+    // direct placement into the tile segments laid out by direct_layout (cursors in tile_count)
+    o.list = direct ? bb.list.as<uint32_t>() : nullptr;
+    o.list_cap = static_cast<int64_t>(bb.list.bytes / sizeof(uint32_t));
     o.tiles_x = g.tiles_x;
     if (!bb.counts_cleared) {  // the scatter binning leaves both at zero; the radix path does not
       RTGS_TRY(reset_tile_counts(bb, g, s));

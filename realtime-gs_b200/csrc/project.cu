@@ -79,7 +79,7 @@ project_conic_kernel(const float* __restrict__ xy, const float* __restrict__ con
 
 __global__ void __launch_bounds__(kThreads)
 project_raw_kernel(const float* __restrict__ raw, int64_t m, int64_t n_per_view, int height,
-                   int width, int tiles_x, int tiles_per_view, ProjOut o) {
+                   int width, int tiles_x, int tiles_per_view, bool unit_weight, ProjOut o) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
   const bool active = i < m;
   float mx = 0.f, my = 0.f, w = 0.f, cr = 0.f, cg = 0.f, cb = 0.f;
@@ -97,7 +97,7 @@ project_raw_kernel(const float* __restrict__ raw, int64_t m, int64_t n_per_view,
     cr = sigmoid_f(raw[kCr * m + i]);
     cg = sigmoid_f(raw[kCg * m + i]);
     cb = sigmoid_f(raw[kCb * m + i]);
-    w = sigmoid_f(raw[kWr * m + i]);
+    w = unit_weight ? 1.0f : sigmoid_f(raw[kWr * m + i]);
     view = static_cast<int>(i / n_per_view);
   }
   project_tail(i, active, mx, my, k, r.x0, r.x1, r.y0, r.y1, r.pixels, w, cr, cg, cb, view,
@@ -106,7 +106,7 @@ project_raw_kernel(const float* __restrict__ raw, int64_t m, int64_t n_per_view,
 
 __global__ void __launch_bounds__(kThreads)
 build_params_kernel(const float* __restrict__ raw, int64_t m, int height, int width,
-                    float* __restrict__ xy, float* __restrict__ chol, float* __restrict__ color,
+                    bool unit_weight, float* __restrict__ xy, float* __restrict__ chol, float* __restrict__ color,
                     float* __restrict__ weight) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
   if (i >= m) return;
@@ -118,7 +118,7 @@ build_params_kernel(const float* __restrict__ raw, int64_t m, int height, int wi
   color[3 * i] = sigmoid_f(raw[kCr * m + i]);
   color[3 * i + 1] = sigmoid_f(raw[kCg * m + i]);
   color[3 * i + 2] = sigmoid_f(raw[kCb * m + i]);
-  weight[i] = sigmoid_f(raw[kWr * m + i]);
+  weight[i] = unit_weight ? 1.0f : sigmoid_f(raw[kWr * m + i]);
 }
 
 __global__ void __launch_bounds__(kThreads)
@@ -160,8 +160,8 @@ int prepare(BinBuffers& bb, const Geometry& g, int64_t m, bool want_weights, cud
   o->entries = nullptr;  // count only; a launcher that emits sets entries and cap
   o->cap = 0;
   o->active = nullptr;
-  o->seg = nullptr;  // direct placement is set up by the fit loop's Adam launcher only
-  o->list = nullptr;
+  o->list = nullptr;  // direct placement is set up by the fit loop's Adam launcher only
+  o->list_cap = 0;
   bb.entries_emitted = false;
   o->tiles_x = g.tiles_x;
   return 0;
@@ -197,7 +197,7 @@ int launch_project_conic(BinBuffers& bb, const Geometry& g, const float* xy, con
 
 int launch_project_raw(BinBuffers& bb, const Geometry& g, const float* raw, int64_t m,
                        int64_t n_per_view, bool emit, const uint8_t* active, bool want_weights,
-                       cudaStream_t s) {
+                       bool unit_weight, cudaStream_t s) {
   ProjOut o;
   RTGS_TRY(prepare(bb, g, m, want_weights, s, &o));
   o.active = active;
@@ -208,7 +208,7 @@ int launch_project_raw(BinBuffers& bb, const Geometry& g, const float* raw, int6
   }
   if (m == 0) return 0;
   project_raw_kernel<<<grid_for(m), kThreads, 0, s>>>(raw, m, n_per_view, g.height, g.width,
-                                                      g.tiles_x, g.tiles_per_view, o);
+                                                      g.tiles_x, g.tiles_per_view, unit_weight, o);
   return check_cuda(cudaGetLastError(), "project_raw_kernel");
 }
 
@@ -219,11 +219,11 @@ int launch_support_rects(const float* xy, const float* chol, int64_t m, int heig
   return check_cuda(cudaGetLastError(), "support_rects_kernel");
 }
 
-int launch_build_params(const float* raw, int64_t m, int height, int width, float* xy, float* chol,
-                        float* color, float* weight, cudaStream_t s) {
+int launch_build_params(const float* raw, int64_t m, int height, int width, bool unit_weight,
+                        float* xy, float* chol, float* color, float* weight, cudaStream_t s) {
   if (m == 0) return 0;
-  build_params_kernel<<<grid_for(m), kThreads, 0, s>>>(raw, m, height, width, xy, chol, color,
-                                                       weight);
+  build_params_kernel<<<grid_for(m), kThreads, 0, s>>>(raw, m, height, width, unit_weight, xy, chol,
+                                                       color, weight);
   return check_cuda(cudaGetLastError(), "build_params_kernel");
 }
 

@@ -40,6 +40,10 @@ namespace rtgs2d {
 namespace {
 
 constexpr int kBuckets = 2 * kTile;  // backward work-list buckets: (orientation, steps)
+// Row stride (in float4) of the tile's upstream gradients in shared memory: one float4 of padding
+// per row puts the 8 rows that a column-wise octet reads at one step in 8 different bank groups
+// (with a stride of 16 float4 = 64 words they all fall in the same 4 banks: an 8-way conflict).
+constexpr int kGStride = kTile + 1;
 
 template <int PPT>
 struct Layout {
@@ -306,8 +310,8 @@ __device__ __forceinline__ void backward_piece(const float4& geo, const float4& 
     const float kappa = -__fdividef(i01, coef_var);
     vc = isfinite(kappa) ? kappa * da : 0.f;
   }
-  constexpr int kStep = ROW ? kTile : 1;        // shared-memory stride of one step
-  constexpr int kLaneStride = ROW ? 1 : kTile;  // and of one lane-axis pixel
+  constexpr int kStep = ROW ? kGStride : 1;        // shared-memory stride of one step
+  constexpr int kLaneStride = ROW ? 1 : kGStride;  // and of one lane-axis pixel
   // The lane's steps [0, count) are the union of pixel A's span (from a_first, a_len steps) and
   // B's; a step inside the union but outside one pixel's own span is still inside the piece, where
   // that pixel's rounded q >= cutoff (line_span), so only the union bound is tested per step.
@@ -409,7 +413,7 @@ raster_kernel(const RasterArgs a) {
   __shared__ float s_wt[DEN ? kBatch : 1];
   __shared__ int s_entry[kDoBwd ? kBatch : 1];
   __shared__ int s_piece[kDoBwd ? kBatch : 1];      // rx0 | ry0 << 4 | (pw-1) << 8 | (ph-1) << 12
-  __shared__ float4 s_g[kDoBwd ? kTile * kTile : 1];  // upstream gradient (r, g, b, density) per pixel
+  __shared__ float4 s_g[kDoBwd ? kTile * kGStride : 1];  // upstream gradient (r, g, b, density) per pixel
   __shared__ int s_list[kDoBwd ? kBatch : 1];   // batch records sorted by octet steps, descending
   // Line spans of the support ellipse: renderer backward only (see kSpanMinSteps).
   constexpr bool kSpans = MODE == kBwd;
@@ -678,7 +682,7 @@ raster_kernel(const RasterArgs a) {
 #pragma unroll
     for (int k = 0; k < PPT; ++k) {
       const int lx = px - ox, ly = py[k] - oy;
-      s_g[ly * kTile + lx] = make_float4(g[k][0], g[k][1], g[k][2], gd[k]);
+      s_g[ly * kGStride + lx] = make_float4(g[k][0], g[k][1], g[k][2], gd[k]);
     }
     float* partials_f = reinterpret_cast<float*>(a.partials);
     const int r8 = lane & 7;
@@ -784,7 +788,7 @@ raster_kernel(const RasterArgs a) {
         float S[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         float Sd = 0.f;
 #define RTGS_PIECE(R)                                                                                  \
-  backward_piece<R, DEN, MODE == kBwd>(geo, app, wt, pxc0, pyc0, ry0 * kTile + rx0, r8, start,      \
+  backward_piece<R, DEN, MODE == kBwd>(geo, app, wt, pxc0, pyc0, ry0 * kGStride + rx0, r8, start,   \
                                        a_first, a_len, b_first, b_len, any_b, max_steps, a.cutoff,  \
                                        s_g, S, Sd)
         if (row) RTGS_PIECE(true); else RTGS_PIECE(false);

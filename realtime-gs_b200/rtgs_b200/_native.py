@@ -25,6 +25,9 @@ LOSS_MASK_ONLY = 2
 
 INIT_NONFINITE_RAW = 256  # RTGS2D_INIT_NONFINITE_RAW of rtgs2d_fit_set_initial
 
+APPEARANCE_WEIGHT_COLOR_9P = 0  # RTGS2D_APPEARANCE_* of rtgs2d_fit_set_appearance
+APPEARANCE_UNIT_WEIGHT_8P = 1
+
 
 class FitOptions(ctypes.Structure):
     _fields_ = [
@@ -82,6 +85,7 @@ _SIGNATURES = {
     "rtgs2d_fit_set_targets": ([_vp, _vp, _vp, _vp], ctypes.c_int),
     "rtgs2d_fit_set_raw": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
     "rtgs2d_fit_set_initial": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
+    "rtgs2d_fit_set_appearance": ([_vp, ctypes.c_int32], ctypes.c_int),
     "rtgs2d_fit_run": ([_vp, _c_int64, _vp], ctypes.c_int),
     "rtgs2d_fit_get_raw": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
     "rtgs2d_fit_get_params": ([_vp, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),

@@ -85,7 +85,7 @@ def fit_stacked(
     engine = acquire_engine(
         n_views, xy0.shape[1], height, width, lr=config.lr, iterations=config.iterations,
         log_every=config.log_every, freeze_geometry=config.freeze_geometry, loss_mode=loss_mode,
-        device=targets.device,
+        device=targets.device, appearance=config.appearance_parameterization,
     )
     ok = False
     try:
@@ -94,7 +94,8 @@ def fit_stacked(
         status = engine.set_initial(xy0, chol0, color0, weight0)
         if status & _native.INIT_NONFINITE_RAW:
             ok = True
-            _validate_raw_parameters(raw_from_gaussians(xy0, chol0, color0, weight0, height, width))
+            _validate_raw_parameters(raw_from_gaussians(xy0, chol0, color0, weight0, height, width,
+                                                        config.appearance_parameterization))
             raise RuntimeError("the engine found non-finite raw parameters that the host check does not")
         mask_bits = None if masks is None else pack_mask_bits(masks)
         engine.set_targets(targets, mask_bits)

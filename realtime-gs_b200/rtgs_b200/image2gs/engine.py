@@ -16,6 +16,12 @@ import torch
 from rtgs_b200 import _native
 
 _RAW_SHAPES = (("xy_raw", 2), ("diag_raw", 2), ("off_raw", 0), ("color_raw", 3), ("weight_raw", 0))
+# unit_weight_bounded_8p: the colour slots hold amplitude_raw and there is no weight parameter
+_RAW_SHAPES_8P = (("xy_raw", 2), ("diag_raw", 2), ("off_raw", 0), ("amplitude_raw", 3))
+WEIGHT_COLOR_9P = "weight_color_9p"
+UNIT_WEIGHT_8P = "unit_weight_bounded_8p"
+_APPEARANCE_CODES = {WEIGHT_COLOR_9P: _native.APPEARANCE_WEIGHT_COLOR_9P,
+                     UNIT_WEIGHT_8P: _native.APPEARANCE_UNIT_WEIGHT_8P}
 
 
 def pack_mask_bits(masks: torch.Tensor) -> torch.Tensor:
@@ -51,7 +57,10 @@ class FitEngine:
         loss_mode: int = _native.LOSS_MSE,
         device: torch.device | None = None,
         mask_coverage_weight: float = 0.0,
+        appearance: str = WEIGHT_COLOR_9P,
     ) -> None:
+        if appearance not in _APPEARANCE_CODES:
+            raise ValueError(f"unknown appearance parameterization {appearance!r}")
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         if self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
@@ -70,6 +79,9 @@ class FitEngine:
                                             ctypes.byref(opts), ctypes.byref(handle))
             )
         self._h = handle.value
+        self.appearance = appearance
+        self._raw_shapes = _RAW_SHAPES_8P if appearance == UNIT_WEIGHT_8P else _RAW_SHAPES
+        _native.check(self._lib.rtgs2d_fit_set_appearance(self._h, _APPEARANCE_CODES[appearance]))
 
     # -- lifecycle -------------------------------------------------------------------------------
     def close(self) -> None:
@@ -106,15 +118,18 @@ class FitEngine:
             )
 
     def set_raw(self, raw: dict[str, torch.Tensor]) -> None:
+        """Raw parameters by name: xy_raw, diag_raw, off_raw and color_raw + weight_raw, or
+        amplitude_raw for the unit-weight appearance."""
         ts = []
-        for name, k in _RAW_SHAPES:
+        for name, k in self._raw_shapes:
             t = raw[name].to(self.device, torch.float32).contiguous()
             want = (self.n_views, self.n, k) if k else (self.n_views, self.n)
             if tuple(t.shape) != want:
                 raise ValueError(f"{name} must have shape {want}, got {tuple(t.shape)}")
             ts.append(t)
+        ptrs = [t.data_ptr() for t in ts] + [None] * (5 - len(ts))
         with torch.cuda.device(self.device):
-            _native.check(self._lib.rtgs2d_fit_set_raw(self._h, *(t.data_ptr() for t in ts), self._stream()))
+            _native.check(self._lib.rtgs2d_fit_set_raw(self._h, *ptrs, self._stream()))
             torch.cuda.current_stream(self.device).synchronize()
 
     def set_initial(self, xy: torch.Tensor, chol: torch.Tensor, color: torch.Tensor,
@@ -157,12 +172,11 @@ class FitEngine:
     def raw(self) -> dict[str, torch.Tensor]:
         b, n = self.n_views, self.n
         out = {}
-        for name, k in _RAW_SHAPES:
+        for name, k in self._raw_shapes:
             out[name] = torch.empty((b, n, k) if k else (b, n), device=self.device, dtype=torch.float32)
+        ptrs = [t.data_ptr() for t in out.values()] + [None] * (5 - len(out))
         with torch.cuda.device(self.device):
-            _native.check(
-                self._lib.rtgs2d_fit_get_raw(self._h, *(out[nm].data_ptr() for nm, _ in _RAW_SHAPES), self._stream())
-            )
+            _native.check(self._lib.rtgs2d_fit_get_raw(self._h, *ptrs, self._stream()))
         return out
 
     def evaluate(self, want_render: bool = True) -> tuple[torch.Tensor | None, np.ndarray]:
@@ -229,9 +243,8 @@ class FitEngine:
         ptrs = [None] * 5
         keep = []
         if raw is not None:
-            shapes = {"xy_raw": 2, "diag_raw": 2, "off_raw": 1, "color_raw": 3, "weight_raw": 1}
-            for k, name in enumerate(("xy_raw", "diag_raw", "off_raw", "color_raw", "weight_raw")):
-                t = raw[name].to(self.device, torch.float32).reshape(n_rows, shapes[name]).contiguous()
+            for k, (name, width) in enumerate(self._raw_shapes):
+                t = raw[name].to(self.device, torch.float32).reshape(n_rows, max(width, 1)).contiguous()
                 keep.append(t)
                 ptrs[k] = t.data_ptr()
         with torch.cuda.device(self.device):
@@ -302,14 +315,14 @@ _POOL_MAX_IDLE = 4  # idle engines kept per process, least recently released clo
 def acquire_engine(n_views: int, n: int, height: int, width: int, *, lr: float, iterations: int,
                    log_every: int, check_every: int = 0, freeze_geometry: bool = False,
                    loss_mode: int = _native.LOSS_MSE, device: torch.device | None = None,
-                   mask_coverage_weight: float = 0.0) -> FitEngine:
+                   mask_coverage_weight: float = 0.0, appearance: str = WEIGHT_COLOR_9P) -> FitEngine:
     """An idle pooled engine of exactly this configuration, else a new one."""
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
     if dev.index is None:
         dev = torch.device("cuda", torch.cuda.current_device())
     key = (dev.index, int(n_views), int(n), int(height), int(width), float(lr), int(iterations),
            int(log_every), int(check_every), bool(freeze_geometry), int(loss_mode),
-           float(mask_coverage_weight))
+           float(mask_coverage_weight), str(appearance))
     with _POOL_LOCK:
         idle = _POOL.get(key)
         if idle:
@@ -319,7 +332,7 @@ def acquire_engine(n_views: int, n: int, height: int, width: int, *, lr: float, 
             return engine
     engine = FitEngine(n_views, n, height, width, lr=lr, iterations=iterations, log_every=log_every,
                        check_every=check_every, freeze_geometry=freeze_geometry, loss_mode=loss_mode,
-                       device=dev, mask_coverage_weight=mask_coverage_weight)
+                       device=dev, mask_coverage_weight=mask_coverage_weight, appearance=appearance)
     engine._pool_key = key
     return engine
 

@@ -6,10 +6,10 @@ projection from raw parameters, tile binning, one fused forward + L2-gradient + 
 and one fused chain-rule + Adam kernel per iteration, with torch's CosineAnnealingLR recursion
 evaluated on the host.
 
-Supported: ``backend="native"``, ``init_strategy="gradient"``, the default appearance
-parameterisation, fixed iterations or convergence early stopping, ``freeze_geometry``, binary
-masks (crop + 0.1/0.9-weighted loss, fit.py:262-269,557-563). Other reference options raise
-``ValueError`` naming the option.
+Supported: ``backend="native"``, ``init_strategy="gradient"``, both appearance
+parameterisations (weight_color_9p and unit_weight_bounded_8p, fit.py:381-411), fixed iterations
+or convergence early stopping, ``freeze_geometry``, binary masks (crop + 0.1/0.9-weighted loss,
+fit.py:262-269,557-563). Other reference options raise ``ValueError`` naming the option.
 """
 
 from __future__ import annotations
@@ -118,16 +118,24 @@ def init_gaussians_2d(
     return Gaussians2D(xy=xy, chol=chol, color=color, weight=weight)
 
 
-def raw_from_gaussians(xy, chol, color, weight, height: int, width: int) -> dict[str, torch.Tensor]:
-    """Raw parameters from constrained ones (fit.py:375-380); works on (..., k) tensors."""
+def raw_from_gaussians(xy, chol, color, weight, height: int, width: int,
+                       appearance: str = _CURRENT_APPEARANCE) -> dict[str, torch.Tensor]:
+    """Raw parameters from constrained ones (fit.py:375-387); works on (..., k) tensors. The
+    unit-weight appearance replaces color_raw and weight_raw by
+    amplitude_raw = logit(sigmoid(weight_raw) * sigmoid(color_raw))."""
     wh = xy.new_tensor([width, height])
-    return {
+    color_raw = torch.logit(color.clamp(1e-3, 1 - 1e-3))
+    weight_raw = torch.logit(weight.clamp(1e-3, 1 - 1e-3))
+    raw = {
         "xy_raw": torch.logit((xy / wh).clamp(1e-4, 1 - 1e-4)),
         "diag_raw": _softplus_inv(chol[..., [0, 2]] - _MIN_DIAG),
         "off_raw": chol[..., 1].clone(),
-        "color_raw": torch.logit(color.clamp(1e-3, 1 - 1e-3)),
-        "weight_raw": torch.logit(weight.clamp(1e-3, 1 - 1e-3)),
     }
+    if appearance == _CANDIDATE_APPEARANCE:
+        raw["amplitude_raw"] = torch.logit(torch.sigmoid(weight_raw)[..., None] * torch.sigmoid(color_raw))
+    else:
+        raw.update(color_raw=color_raw, weight_raw=weight_raw)
+    return raw
 
 
 def _validate_raw_parameters(raw_parameters: dict[str, torch.Tensor]) -> None:
@@ -216,9 +224,9 @@ def _validate_fit_controls(config: FitConfig, diagnostic_callback=None, diagnost
         raise ValueError("fit backend must be 'native' (StructSplat is not part of this package)")
     if config.init_strategy != "gradient":
         raise ValueError("init_strategy='structure_tensor' is not implemented by rtgs_b200")
-    if config.appearance_parameterization != _CURRENT_APPEARANCE:
-        raise ValueError("only the weight_color_9p appearance parameterization is implemented")
     if config.pool:  # fit.py:600-616
+        if config.appearance_parameterization != _CURRENT_APPEARANCE:
+            raise ValueError("pool fitting supports only the default appearance parameterization")
         if config.freeze_geometry:
             raise ValueError("pool fitting is incompatible with freeze_geometry")
         if diagnostic_callback is not None or tuple(diagnostic_steps):
@@ -299,13 +307,14 @@ def _fit_native_from_initialization(
         1, g0.n, h, w, lr=config.lr, iterations=config.iterations, log_every=config.log_every,
         check_every=check_every, freeze_geometry=config.freeze_geometry, loss_mode=loss_mode,
         device=image.device, mask_coverage_weight=config.mask_coverage_weight if mask is not None else 0.0,
+        appearance=config.appearance_parameterization,
     )
     ok = False
     try:
         status = engine.set_initial(g0.xy, g0.chol, g0.color, g0.weight)
         if status:
             ok = True  # the engine itself is fine: keep it pooled
-            _raise_initial_errors(g0, h, w)
+            _raise_initial_errors(g0, h, w, config.appearance_parameterization)
         ok = False
         mask_bits = None if mask is None else pack_mask_bits(mask[None])
         engine.set_targets(target[None], mask_bits)
@@ -354,11 +363,12 @@ def _fit_native_from_initialization(
     return result, history
 
 
-def _raise_initial_errors(g0: Gaussians2D, height: int, width: int) -> None:
+def _raise_initial_errors(g0: Gaussians2D, height: int, width: int,
+                          appearance: str = _CURRENT_APPEARANCE) -> None:
     """An initialisation the engine rejected: raise the reference's error for it (fit.py:634-676,
     then fit.py:134-141 for non-finite raw parameters)."""
     _validate_initial_gaussians(g0, height, width)
-    _validate_raw_parameters(raw_from_gaussians(g0.xy, g0.chol, g0.color, g0.weight, height, width))
+    _validate_raw_parameters(raw_from_gaussians(g0.xy, g0.chol, g0.color, g0.weight, height, width, appearance))
     raise RuntimeError("the engine rejected the initial gaussians but no check fails on the host")
 
 

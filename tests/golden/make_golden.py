@@ -249,9 +249,56 @@ def adapters_fixture(ref_src: str) -> None:
     _save("adapters", **out)
 
 
+def appearance_fixture(ref_src: str) -> None:
+    """10. The unit-weight appearance (fit.py:381-411): the native fit of the scene image from a
+    fixed initialisation with unit_weight_bounded_8p, its step-0 diagnostics (initial raw
+    parameters, the first gradients and the first update), a geometry-frozen run and the batched
+    fit (batched.py:87-119) of both scene views."""
+    sys.path.insert(0, ref_src)
+    from rtgs.data.synthetic import make_synthetic_scene
+    from rtgs.image2gs.batched import fit_views_batched
+    from rtgs.image2gs.fit import FitConfig, fit_image_from_initialization, init_gaussians_2d
+
+    arm = "unit_weight_bounded_8p"
+    scene = make_synthetic_scene(n_gaussians=25, n_cameras=8, image_size=32, seed=0)
+    images = torch.stack([scene.images[0], scene.images[1]])
+    g_init = init_gaussians_2d(images[0], 80, 0.7, torch.Generator().manual_seed(0))
+    snaps = []
+    cfg = FitConfig(n_gaussians=80, iterations=40, log_every=10, lr=1e-2, appearance_parameterization=arm)
+    fitted, hist = fit_image_from_initialization(images[0], g_init, cfg, diagnostic_callback=snaps.append,
+                                                 diagnostic_steps=(0, 1))
+    pre = next(s for s in snaps if s.event == "pre_update" and s.step == 0)
+    post = next(s for s in snaps if s.event == "post_update" and s.step == 1)
+    fcfg = FitConfig(n_gaussians=80, iterations=10, log_every=5, lr=1e-2, appearance_parameterization=arm,
+                     freeze_geometry=True)
+    frozen, fhist = fit_image_from_initialization(images[0], g_init, fcfg)
+    bcfg = FitConfig(n_gaussians=60, iterations=30, log_every=10, batch_views=True, appearance_parameterization=arm)
+    gs, hists = fit_views_batched([images[0], images[1]], bcfg, seed=0)
+    _save("fit_appearance", image=images[0], images=images, init_xy=g_init.xy, init_chol=g_init.chol,
+          init_color=g_init.color, init_weight=g_init.weight,
+          iterations=cfg.iterations, log_every=cfg.log_every, lr=cfg.lr,
+          init_amplitude_raw=pre.raw_parameters["amplitude_raw"],
+          grad0_xy_raw=pre.gradients["xy_raw"], grad0_diag_raw=pre.gradients["diag_raw"],
+          grad0_off_raw=pre.gradients["off_raw"], grad0_amplitude_raw=pre.gradients["amplitude_raw"],
+          step1_xy_raw=post.raw_parameters["xy_raw"], step1_diag_raw=post.raw_parameters["diag_raw"],
+          step1_off_raw=post.raw_parameters["off_raw"], step1_amplitude_raw=post.raw_parameters["amplitude_raw"],
+          out_xy=fitted.xy, out_chol=fitted.chol, out_color=fitted.color, out_weight=fitted.weight,
+          psnr_iters=np.array([i for i, _ in hist["psnr"]]),
+          psnr_vals=np.array([v for _, v in hist["psnr"]]),
+          final_psnr=hist["final_psnr"],
+          frozen_iterations=fcfg.iterations, frozen_log_every=fcfg.log_every,
+          frozen_xy=frozen.xy, frozen_chol=frozen.chol, frozen_color=frozen.color, frozen_weight=frozen.weight,
+          frozen_psnr_vals=np.array([v for _, v in fhist["psnr"]]), frozen_final_psnr=fhist["final_psnr"],
+          batched_iterations=bcfg.iterations, batched_log_every=bcfg.log_every,
+          batched_out_color=torch.stack([g.color for g in gs]), batched_out_xy=torch.stack([g.xy for g in gs]),
+          batched_out_weight=torch.stack([g.weight for g in gs]),
+          batched_psnr_vals=np.array([[v for _, v in h["psnr"]] for h in hists]),
+          batched_final_psnr=np.array([h["final_psnr"] for h in hists]))
+
+
 if __name__ == "__main__":
-    # make_golden.py [REF_SRC] [--only main|pool|adapters]
-    args = [a for a in sys.argv[1:] if not a.startswith("--") and a not in ("main", "pool", "adapters")]
+    # make_golden.py [REF_SRC] [--only main|pool|adapters|appearance]
+    args = [a for a in sys.argv[1:] if not a.startswith("--") and a not in ("main", "pool", "adapters", "appearance")]
     ref = args[0] if args else "/root/reference/src"
     only = sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None
     if only in (None, "main"):
@@ -260,3 +307,5 @@ if __name__ == "__main__":
         pool_fixture(ref)
     if only in (None, "adapters"):
         adapters_fixture(ref)
+    if only in (None, "appearance"):
+        appearance_fixture(ref)

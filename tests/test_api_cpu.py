@@ -84,6 +84,25 @@ def test_fit_rejects_cpu_images_and_unsupported_modes():
                 dict(pool=True, pool_prune_count=-1), dict(pool=True, pool_spawn_count=-1)):
         with pytest.raises(ValueError):
             fit_image(img, replace(FitConfig(n_gaussians=8, iterations=2), **bad), seed=0)
+    with pytest.raises(ValueError, match="appearance_parameterization must be one of"):
+        fit_image(img, FitConfig(n_gaussians=8, iterations=2, appearance_parameterization="rgb"), seed=0)
+    with pytest.raises(ValueError, match="pool fitting supports only the default appearance"):
+        fit_image(img, FitConfig(n_gaussians=8, iterations=2, pool=True,
+                                 appearance_parameterization="unit_weight_bounded_8p"), seed=0)
+
+
+def test_unit_weight_raw_transform_matches_oracle():
+    from oracle import fit as ofit
+    from rtgs_b200.image2gs.fit import raw_from_gaussians
+
+    g = load_golden("fit_appearance")
+    init = tuple(t(g[f"init_{n}"]) for n in ("xy", "chol", "color", "weight"))
+    ours = raw_from_gaussians(*init, 32, 32, "unit_weight_bounded_8p")
+    theirs = ofit.to_raw(*init, 32, 32, ofit.UNIT_WEIGHT_8P)
+    assert ours.keys() == theirs.keys()
+    for name in ours:
+        assert torch.equal(ours[name], theirs[name]), name
+    assert torch.equal(ours["amplitude_raw"], t(g["init_amplitude_raw"]))
 
 
 def test_fit_views_batched_rejects_unsupported_modes():
