@@ -264,6 +264,21 @@ RTGS2D_API int rtgs2d_fit_get_raw(rtgs2d_fit* fit, float* xy_raw, float* diag_ra
  * weight (B,N). */
 RTGS2D_API int rtgs2d_fit_get_params(rtgs2d_fit* fit, float* xy, float* chol, float* color, float* weight,
                           void* stream);
+/* The fit loss's gradient with respect to the raw parameters at the current state, as the next
+ * iteration's Adam step would receive it (the fit loop's own raster and chain rule), without an
+ * update: what the reference's raw_parameters[name].grad hold after loss.backward() (fit.py:451-460,
+ * read by its native fit diagnostics, fit.py:691-766). Layouts of rtgs2d_fit_get_raw; NULL
+ * outputs are skipped. With `render` (B,H,W,3) the current render, with `sums` (B,2) host the
+ * loss and clamped-PSNR numerators (as rtgs2d_fit_evaluate). Synchronises `stream`. */
+RTGS2D_API int rtgs2d_fit_gradients(rtgs2d_fit* fit, float* xy_raw, float* diag_raw, float* off_raw,
+                                    float* color_raw, float* weight_raw, float* render, double* sums,
+                                    void* stream);
+/* Adam moments of the raw parameters (torch Adam's exp_avg for which = 1, exp_avg_sq for 2, the
+ * optimizer state the reference's diagnostics copy, fit.py:710-714), in the layouts of
+ * rtgs2d_fit_get_raw; NULL outputs are skipped. The completed update count is rtgs2d_fit_stats'
+ * step. */
+RTGS2D_API int rtgs2d_fit_get_moments(rtgs2d_fit* fit, int32_t which, float* xy, float* diag, float* off,
+                                      float* color, float* weight, void* stream);
 /* Renders the current parameters; writes render (B,H,W,3) if not NULL and the per-view loss and
  * clamped-PSNR numerators to host sums (B,2). Synchronises `stream`. */
 RTGS2D_API int rtgs2d_fit_evaluate(rtgs2d_fit* fit, float* render, double* sums, void* stream);

@@ -41,6 +41,7 @@ struct rtgs2d_fit {
   DevBuf tile_loss;    // (n_tiles, 2) double
   DevBuf log;          // (max_logs, B, 2) double
   DevBuf eval_sums;    // (B, 2) double
+  DevBuf grad_raw;     // planar (9, M): rtgs2d_fit_gradients' scratch
   DevBuf active;       // (M,) uint8: 0 = parked row (rtgs2d_fit_set_active); unused until set
   bool use_active = false;
   int64_t max_logs = 0;
@@ -977,6 +978,48 @@ int rtgs2d_fit_evaluate(rtgs2d_fit* f, float* render, double* sums, void* stream
   }
   RTGS_CUDA(cudaStreamSynchronize(s), "evaluate sync");
   return RTGS2D_OK;
+}
+
+int rtgs2d_fit_gradients(rtgs2d_fit* f, float* xy_raw, float* diag_raw, float* off_raw,
+                         float* color_raw, float* weight_raw, float* render, double* sums,
+                         void* stream) {
+  RTGS_TRY(check_fit(f));
+  if (!f->have_targets || !f->have_raw) {
+    return set_error(RTGS2D_ERR_INVALID, "set targets and raw parameters before taking gradients");
+  }
+  cudaStream_t s = as_stream(stream);
+  RTGS_TRY(project_and_bin(f, s));
+  FitRasterArgs fa = raster_args(f);
+  fa.render_out = render;
+  RTGS_TRY(launch_raster_fit(f->bb, f->geo, kCutoff, fa, true, s));
+  RTGS_TRY(launch_loss_reduce(f->tile_loss.as<double>(), f->geo, f->eval_sums.as<double>(), s));
+  if (f->m > 0) {
+    RTGS_TRY(f->grad_raw.ensure(static_cast<size_t>(kRawSlots) * f->m * sizeof(float), s));
+    RTGS_TRY(launch_raw_grad(f->bb, f->m, f->height, f->width, f->raw.as<float>(), f->unit_weight,
+                             coverage(f), f->grad_raw.as<float>(), s));
+    unpack_raw_kernel<<<grid_for(f->m), kThreads, 0, s>>>(f->m, f->grad_raw.as<float>(), xy_raw, diag_raw,
+                                                          off_raw, color_raw,
+                                                          f->unit_weight ? nullptr : weight_raw);
+    RTGS_CUDA(cudaGetLastError(), "unpack_raw_kernel");
+  }
+  if (sums) {
+    RTGS_CUDA(cudaMemcpyAsync(sums, f->eval_sums.ptr, static_cast<size_t>(f->n_views) * 2 * sizeof(double),
+                              cudaMemcpyDeviceToHost, s),
+              "gradient sums readback");
+  }
+  RTGS_CUDA(cudaStreamSynchronize(s), "gradients sync");
+  return RTGS2D_OK;
+}
+
+int rtgs2d_fit_get_moments(rtgs2d_fit* f, int32_t which, float* xy, float* diag, float* off,
+                           float* color, float* weight, void* stream) {
+  RTGS_TRY(check_fit(f));
+  if (which != 1 && which != 2) return set_error(RTGS2D_ERR_INVALID, "which must be 1 or 2");
+  if (f->m == 0) return RTGS2D_OK;
+  const DevBuf& src = which == 1 ? f->m1 : f->m2;
+  unpack_raw_kernel<<<grid_for(f->m), kThreads, 0, as_stream(stream)>>>(
+      f->m, src.as<float>(), xy, diag, off, color, f->unit_weight ? nullptr : weight);
+  return check_cuda(cudaGetLastError(), "unpack_raw_kernel");
 }
 
 int rtgs2d_fit_history(const rtgs2d_fit* f, int64_t max_rows, int64_t* iters, double* sums,

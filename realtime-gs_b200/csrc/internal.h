@@ -22,6 +22,7 @@ int check_cuda(cudaError_t err, const char* what);
   } while (0)
 #define RTGS_CUDA(expr, what) RTGS_TRY(::rtgs2d::check_cuda((expr), (what)))
 
+
 // ---- device memory ------------------------------------------------------------------------------
 // A growable device buffer. ensure() reallocates only when more bytes are needed; before freeing
 // the old allocation it synchronises `stream` so no queued kernel still reads it.
@@ -223,6 +224,9 @@ struct LossLog {
   double* log;              // (rows, n_views, 2)
   int n_views, tiles_per_view;
 };
+// The raw-parameter gradients (planar 9 x M) from the last fit raster's entry moments, no update.
+int launch_raw_grad(const BinBuffers& bb, int64_t m, int height, int width, const float* raw,
+                    bool unit_weight, bool density, float* grad_out, cudaStream_t s);
 // Adam step from the last raster's entry moments, with the constants of table[k]; with
 // project_next the updated parameters are also projected (records, spans, counts, offsets,
 // stats) for the next iteration's binning: entries for the scatter path, or with `direct` the ids

@@ -88,6 +88,60 @@ finalize_conic_kernel(int64_t m, int64_t cap, const int* __restrict__ counts, co
                          fmaf(colors[3 * i + 1], mo.s[6], colors[3 * i + 2] * mo.s[7])) + mo.sd;
 }
 
+// Gradient of the fit loss with respect to one gaussian's raw parameters (slots kXr .. kWr) from
+// its summed entry moments: the chain rule through Sigma^-1 of the Cholesky factor and the raw
+// transforms of fit.py:402-417 (sigmoid for the mean, colour and weight, softplus + _MIN_DIAG for
+// the diagonal). With unit_weight the weight is 1 and has no gradient (the unit-weight fit).
+template <bool DEN>
+__device__ __forceinline__ void raw_gradient(const float (&r)[kRawSlots], const Moments& mo, int height,
+                                             int width, bool unit_weight, float (&grad)[kRawSlots]) {
+  const float sx = sigmoid_f(r[kXr]), sy = sigmoid_f(r[kYr]);
+  const float l11 = __fadd_rn(softplus_f(r[kD0]), kMinDiag);
+  const float l22 = __fadd_rn(softplus_f(r[kD1]), kMinDiag);
+  const float l21 = r[kOff];
+  const Conic k = conic_from_chol(l11, l21, l22);
+  GeoGrad gg = geo_grad(mo, k, true);
+  // The fused fit raster leaves the plain first moments sum dq dx, sum dq dy: apply Sigma^-1.
+  gg.gmx = fmaf(k.i00, mo.s[0], k.i01 * mo.s[1]);
+  gg.gmy = fmaf(k.i01, mo.s[0], k.i11 * mo.s[1]);
+  const float cr = sigmoid_f(r[kCr]), cg = sigmoid_f(r[kCg]), cb = sigmoid_f(r[kCb]);
+  const float w = unit_weight ? 1.0f : sigmoid_f(r[kWr]);
+  grad[kXr] = gg.gmx * static_cast<float>(width) * (1.0f - sx) * sx;
+  grad[kYr] = gg.gmy * static_cast<float>(height) * (1.0f - sy) * sy;
+  grad[kD0] = gg.gl11 * softplus_grad_f(r[kD0]);
+  grad[kD1] = gg.gl22 * softplus_grad_f(r[kD1]);
+  grad[kOff] = gg.gl21;
+  grad[kCr] = w * mo.s[5] * (1.0f - cr) * cr;
+  grad[kCg] = w * mo.s[6] * (1.0f - cg) * cg;
+  grad[kCb] = w * mo.s[7] * (1.0f - cb) * cb;
+  // dL/dweight = sum_k color_k S_k (+ the density moment of the mask coverage penalty)
+  grad[kWr] = unit_weight ? 0.f
+                          : (fmaf(cr, mo.s[5], fmaf(cg, mo.s[6], cb * mo.s[7])) + (DEN ? mo.sd : 0.f)) *
+                                (1.0f - w) * w;
+}
+
+// rtgs2d_fit_gradients: the raw-parameter gradient of every gaussian, planar (9, M), without an
+// Adam step.
+template <bool DEN>
+__global__ void __launch_bounds__(kThreads)
+raw_grad_kernel(int64_t m, int64_t cap, const int* __restrict__ counts, const int* __restrict__ offsets,
+                const float4* __restrict__ partials, const float* __restrict__ partial_d, int height,
+                int width, const float* __restrict__ raw, bool unit_weight, float* __restrict__ grad_out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  const bool active = i < m;
+  int cnt = active ? counts[i] : 0;
+  const int off = cnt > 0 ? offsets[i] : 0;
+  cnt = clamp_to_capacity(cnt, off, cap);
+  const Moments mo = gather_moments<DEN>(partials, partial_d, cnt, off);
+  if (!active) return;
+  float r[kRawSlots], grad[kRawSlots];
+#pragma unroll
+  for (int k = 0; k < kRawSlots; ++k) r[k] = raw[k * m + i];
+  raw_gradient<DEN>(r, mo, height, width, unit_weight, grad);
+#pragma unroll
+  for (int k = 0; k < kRawSlots; ++k) grad_out[k * m + i] = grad[k];
+}
+
 // Adam step of every gaussian from the previous raster's entry moments; with PROJECT the updated
 // parameters are projected for the next iteration in the same pass (the projection of
 // project_raw_kernel), which saves a launch and a re-read of the raw parameters per iteration.
@@ -126,31 +180,8 @@ adam_fit_kernel(int64_t m, int64_t cap, int* counts, const int* __restrict__ off
   const Moments mo = gather_moments<DEN>(partials, partial_d, cnt, off);
 
   if (active) {
-    const float sx = sigmoid_f(r[kXr]), sy = sigmoid_f(r[kYr]);
-    const float l11 = __fadd_rn(softplus_f(r[kD0]), kMinDiag);
-    const float l22 = __fadd_rn(softplus_f(r[kD1]), kMinDiag);
-    const float l21 = r[kOff];
-    const Conic k = conic_from_chol(l11, l21, l22);
-    GeoGrad gg = geo_grad(mo, k, true);
-    // The fused fit raster leaves the plain first moments sum dq dx, sum dq dy: apply Sigma^-1.
-    gg.gmx = fmaf(k.i00, mo.s[0], k.i01 * mo.s[1]);
-    gg.gmy = fmaf(k.i01, mo.s[0], k.i11 * mo.s[1]);
-    const float cr = sigmoid_f(r[kCr]), cg = sigmoid_f(r[kCg]), cb = sigmoid_f(r[kCb]);
-    const float w = a.unit_weight ? 1.0f : sigmoid_f(r[kWr]);
-
     float grad[kRawSlots];
-    grad[kXr] = gg.gmx * static_cast<float>(width) * (1.0f - sx) * sx;
-    grad[kYr] = gg.gmy * static_cast<float>(height) * (1.0f - sy) * sy;
-    grad[kD0] = gg.gl11 * softplus_grad_f(r[kD0]);
-    grad[kD1] = gg.gl22 * softplus_grad_f(r[kD1]);
-    grad[kOff] = gg.gl21;
-    grad[kCr] = w * mo.s[5] * (1.0f - cr) * cr;
-    grad[kCg] = w * mo.s[6] * (1.0f - cg) * cg;
-    grad[kCb] = w * mo.s[7] * (1.0f - cb) * cb;
-    // dL/dweight = sum_k color_k S_k (+ the density moment of the mask coverage penalty)
-    grad[kWr] = (fmaf(cr, mo.s[5], fmaf(cg, mo.s[6], cb * mo.s[7])) + (DEN ? mo.sd : 0.f)) *
-                (1.0f - w) * w;
-
+    raw_gradient<DEN>(r, mo, height, width, a.unit_weight, grad);
     const int first = a.freeze_geometry ? kCr : 0;
     const int last = a.unit_weight ? kWr : kRawSlots;  // the unit-weight fit has no weight parameter
 #pragma unroll
@@ -223,6 +254,21 @@ int launch_finalize_conic(const BinBuffers& bb, int64_t m, const float* conics,
         colors, weights, grad_xy, grad_conics, grad_colors, grad_weights);
   }
   return check_cuda(cudaGetLastError(), "finalize_conic_kernel");
+}
+
+int launch_raw_grad(const BinBuffers& bb, int64_t m, int height, int width, const float* raw,
+                    bool unit_weight, bool density, float* grad_out, cudaStream_t s) {
+  if (m == 0) return 0;
+  if (density) {
+    raw_grad_kernel<true><<<grid_for(m), kThreads, 0, s>>>(
+        m, bb.capacity, bb.counts.as<int>(), bb.offsets.as<int>(), bb.partials.as<float4>(),
+        bb.partial_d.as<float>(), height, width, raw, unit_weight, grad_out);
+  } else {
+    raw_grad_kernel<false><<<grid_for(m), kThreads, 0, s>>>(
+        m, bb.capacity, bb.counts.as<int>(), bb.offsets.as<int>(), bb.partials.as<float4>(), nullptr,
+        height, width, raw, unit_weight, grad_out);
+  }
+  return check_cuda(cudaGetLastError(), "raw_grad_kernel");
 }
 
 int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_view, float* raw,

@@ -90,6 +90,8 @@ _SIGNATURES = {
     "rtgs2d_fit_get_raw": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
     "rtgs2d_fit_get_params": ([_vp, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
     "rtgs2d_fit_evaluate": ([_vp, _vp, _vp, _vp], ctypes.c_int),
+    "rtgs2d_fit_gradients": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
+    "rtgs2d_fit_get_moments": ([_vp, ctypes.c_int32, _vp, _vp, _vp, _vp, _vp, _vp], ctypes.c_int),
     "rtgs2d_fit_history": ([_vp, _c_int64, _vp, _vp, ctypes.POINTER(_c_int64)], ctypes.c_int),
     "rtgs2d_fit_set_profiling": ([_vp, ctypes.c_int32], ctypes.c_int),
     "rtgs2d_fit_set_graphs": ([_vp, ctypes.c_int32], ctypes.c_int),

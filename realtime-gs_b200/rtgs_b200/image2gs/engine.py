@@ -170,14 +170,41 @@ class FitEngine:
         return xy, chol, color, weight
 
     def raw(self) -> dict[str, torch.Tensor]:
-        b, n = self.n_views, self.n
-        out = {}
-        for name, k in self._raw_shapes:
-            out[name] = torch.empty((b, n, k) if k else (b, n), device=self.device, dtype=torch.float32)
+        out = self._raw_like()
         ptrs = [t.data_ptr() for t in out.values()] + [None] * (5 - len(out))
         with torch.cuda.device(self.device):
             _native.check(self._lib.rtgs2d_fit_get_raw(self._h, *ptrs, self._stream()))
         return out
+
+    def _raw_like(self) -> dict[str, torch.Tensor]:
+        b, n = self.n_views, self.n
+        return {name: torch.empty((b, n, k) if k else (b, n), device=self.device, dtype=torch.float32)
+                for name, k in self._raw_shapes}
+
+    def gradients(self, want_render: bool = True) -> tuple[dict[str, torch.Tensor], torch.Tensor | None, np.ndarray]:
+        """The fit loss's raw-parameter gradients at the current state, without an update
+        (rtgs2d_fit_gradients); returns (gradients by raw name, render (B,H,W,3) or None, sums (B,2))."""
+        grads = self._raw_like()
+        render = None
+        if want_render:
+            render = torch.empty(self.n_views, self.height, self.width, 3, device=self.device, dtype=torch.float32)
+        sums = np.zeros((self.n_views, 2), dtype=np.float64)
+        ptrs = [t.data_ptr() for t in grads.values()] + [None] * (5 - len(grads))
+        with torch.cuda.device(self.device):
+            _native.check(self._lib.rtgs2d_fit_gradients(self._h, *ptrs, _native.ptr(render), sums.ctypes.data,
+                                                         self._stream()))
+        return grads, render, sums
+
+    def moments(self) -> tuple[dict[str, torch.Tensor], dict[str, torch.Tensor]]:
+        """Adam's (exp_avg, exp_avg_sq) by raw parameter name (rtgs2d_fit_get_moments)."""
+        out = []
+        for which in (1, 2):
+            m = self._raw_like()
+            ptrs = [t.data_ptr() for t in m.values()] + [None] * (5 - len(m))
+            with torch.cuda.device(self.device):
+                _native.check(self._lib.rtgs2d_fit_get_moments(self._h, which, *ptrs, self._stream()))
+            out.append(m)
+        return out[0], out[1]
 
     def evaluate(self, want_render: bool = True) -> tuple[torch.Tensor | None, np.ndarray]:
         """Render the current parameters; returns (render (B,H,W,3) or None, sums (B, 2))."""

@@ -9,7 +9,9 @@ evaluated on the host.
 Supported: ``backend="native"``, ``init_strategy="gradient"``, both appearance
 parameterisations (weight_color_9p and unit_weight_bounded_8p, fit.py:381-411), fixed iterations
 or convergence early stopping, ``freeze_geometry``, binary masks (crop + 0.1/0.9-weighted loss,
-fit.py:262-269,557-563). Other reference options raise ``ValueError`` naming the option.
+fit.py:262-269,557-563), native fit diagnostics (``diagnostic_callback`` / ``diagnostic_steps``,
+fit.py:96-131,423-520; see ``diagnostics``). Other reference options raise ``ValueError`` naming
+the option.
 """
 
 from __future__ import annotations
@@ -24,6 +26,7 @@ import torch
 from rtgs_b200 import _native
 from rtgs_b200.core.gaussians2d import Gaussians2D
 from rtgs_b200.core.metrics import masked_psnr, psnr
+from rtgs_b200.image2gs.diagnostics import DiagnosticFit, NativeFitDiagnostic, NativeFitDiagnosticCallback  # noqa: F401
 from rtgs_b200.image2gs.engine import FitEngine, acquire_engine, pack_mask_bits, psnr_values, release_engine
 
 _MIN_DIAG = 0.3
@@ -218,6 +221,13 @@ def _validate_fit_controls(config: FitConfig, diagnostic_callback=None, diagnost
         raise ValueError("structure_sampling must be 'wse' or 'density'")
     if config.init_strategy != "structure_tensor" and config.structure_sampling != "wse":
         raise ValueError("structure_sampling='density' requires init_strategy='structure_tensor'")
+    steps = tuple(diagnostic_steps)  # fit.py:593-599
+    if diagnostic_callback is None and steps:
+        raise ValueError("diagnostic_steps require diagnostic_callback")
+    if any(isinstance(step, bool) or not isinstance(step, int) for step in steps):
+        raise ValueError("diagnostic_steps must contain integers")
+    if any(step < 0 or step > config.iterations for step in steps):
+        raise ValueError("diagnostic_steps must lie in [0, iterations]")
     if config.mask_coverage_weight < 0.0:
         raise ValueError("mask_coverage_weight must be non-negative")
     if config.backend != "native":
@@ -240,8 +250,6 @@ def _validate_fit_controls(config: FitConfig, diagnostic_callback=None, diagnost
                 raise ValueError(f"{name} must be non-negative")
     if config.mask_coverage_weight > 0.0 and (config.batch_views or config.pool):  # fit.py:618-622
         raise ValueError("mask_coverage_weight is not supported with batch_views or the pool")
-    if diagnostic_callback is not None or tuple(diagnostic_steps):
-        raise ValueError("native fit diagnostics are not implemented by rtgs_b200")
     if config.iterations < 1:
         raise ValueError("iterations must be >= 1")
 
@@ -288,12 +296,17 @@ def _fit_native_from_initialization(
     config: FitConfig,
     mask: torch.Tensor | None,
     xy_offset: torch.Tensor,
+    diagnostic_callback: NativeFitDiagnosticCallback | None = None,
+    diagnostic_steps: Collection[int] = (),
+    initializer_rng_state_before: torch.Tensor | None = None,
+    initializer_rng_state_after: torch.Tensor | None = None,
 ) -> tuple[Gaussians2D, dict]:
     """Device fit loop for one image (fit.py:355-554).
 
     The initialiser's value checks and raw transform run in one engine call
     (``FitEngine.set_initial``); only when a check fails are the torch checks run, to report the
-    failing rows with the reference's messages.
+    failing rows with the reference's messages. With a ``diagnostic_callback`` the loop runs one
+    iteration at a time and emits the reference's snapshots (``diagnostics.DiagnosticFit``).
     """
     _require_cuda(image)
     h, w = image.shape[:2]
@@ -320,7 +333,22 @@ def _fit_native_from_initialization(
         engine.set_targets(target[None], mask_bits)
         counts = np.array([3.0 * h * w])
         stopped = config.iterations - 1
-        if patience:
+        if diagnostic_callback is not None:
+            coverage_fn = None
+            if config.mask_coverage_weight > 0.0 and mask is not None:
+                from rtgs_b200.image2gs.renderer2d import render_gaussian_coverage_2d
+
+                outside = 1.0 - mask.to(target).clamp(0, 1)
+
+                def coverage_fn(g: Gaussians2D) -> torch.Tensor:  # fit.py:566-572
+                    return config.mask_coverage_weight * (render_gaussian_coverage_2d(g, h, w) * outside).mean()
+
+            stopped = DiagnosticFit(
+                engine, config=config, g0=g0, target=target, mask=mask, callback=diagnostic_callback,
+                steps=diagnostic_steps, rng_state_before=initializer_rng_state_before,
+                rng_state_after=initializer_rng_state_after, coverage_fn=coverage_fn,
+            ).run(counts, patience, check_every, config.convergence_tol)
+        elif patience:
             best, stale = -float("inf"), 0
             done = 0
             while done < config.iterations:
@@ -396,14 +424,23 @@ def fit_image(
     if mask is not None:
         target = image * mask.to(image).clamp(0, 1)[..., None]
     gen = None
+    rng_state_before = rng_state_after = None
     if seed is not None:
         gen = torch.Generator(device=image.device).manual_seed(seed)
+        if diagnostic_callback is not None:
+            rng_state_before = gen.get_state().clone()
     g0 = init_gaussians_2d(target, config.n_gaussians, config.grad_init_mix, gen)
+    if diagnostic_callback is not None and gen is not None:
+        rng_state_after = gen.get_state().clone()
     if config.pool:
         from rtgs_b200.image2gs.pool import fit_pooled_from_initialization
 
         return fit_pooled_from_initialization(image, target, g0, config, mask, xy_offset)
-    return _fit_native_from_initialization(image, target, g0, config, mask, xy_offset)
+    return _fit_native_from_initialization(
+        image, target, g0, config, mask, xy_offset, diagnostic_callback=diagnostic_callback,
+        diagnostic_steps=diagnostic_steps, initializer_rng_state_before=rng_state_before,
+        initializer_rng_state_after=rng_state_after,
+    )
 
 
 def fit_image_from_initialization(
@@ -430,7 +467,9 @@ def fit_image_from_initialization(
         from rtgs_b200.image2gs.pool import fit_pooled_from_initialization
 
         return fit_pooled_from_initialization(image, target, g0, config, mask, xy_offset)
-    return _fit_native_from_initialization(image, target, g0, config, mask, xy_offset)
+    return _fit_native_from_initialization(image, target, g0, config, mask, xy_offset,
+                                           diagnostic_callback=diagnostic_callback,
+                                           diagnostic_steps=diagnostic_steps)
 
 
 def fit_views(

@@ -86,6 +86,13 @@ def test_fit_rejects_cpu_images_and_unsupported_modes():
             fit_image(img, replace(FitConfig(n_gaussians=8, iterations=2), **bad), seed=0)
     with pytest.raises(ValueError, match="appearance_parameterization must be one of"):
         fit_image(img, FitConfig(n_gaussians=8, iterations=2, appearance_parameterization="rgb"), seed=0)
+    cfg = FitConfig(n_gaussians=8, iterations=2)
+    for steps, cb, msg in (((1,), None, "require diagnostic_callback"), ((True,), print, "integers"),
+                           ((3,), print, r"lie in \[0, iterations\]"), ((-1,), print, "lie in")):
+        with pytest.raises(ValueError, match=msg):  # the reference's checks (fit.py:593-599)
+            fit_image(img, cfg, seed=0, diagnostic_callback=cb, diagnostic_steps=steps)
+    with pytest.raises(ValueError, match="pool fitting does not support native fit diagnostics"):
+        fit_image(img, replace(cfg, pool=True), seed=0, diagnostic_callback=print)
     with pytest.raises(ValueError, match="pool fitting supports only the default appearance"):
         fit_image(img, FitConfig(n_gaussians=8, iterations=2, pool=True,
                                  appearance_parameterization="unit_weight_bounded_8p"), seed=0)
