@@ -82,30 +82,6 @@ struct RasterArgs {
   FitRasterArgs fit;
 };
 
-__device__ __forceinline__ float warp_transpose_reduce8(const float (&v)[8], int lane) {
-  const bool u16 = lane & 16, u8 = lane & 8, u4 = lane & 4;
-  float a[4];
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float send = u16 ? v[k] : v[k + 4];
-    const float keep = u16 ? v[k + 4] : v[k];
-    a[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-  }
-  float b[2];
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const float send = u8 ? a[k] : a[k + 2];
-    const float keep = u8 ? a[k + 2] : a[k];
-    b[k] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-  }
-  const float send = u4 ? b[0] : b[1];
-  const float keep = u4 ? b[1] : b[0];
-  float c = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-  c += __shfl_xor_sync(0xffffffffu, c, 2);
-  c += __shfl_xor_sync(0xffffffffu, c, 1);
-  return c;  // sum of v[(lane >> 2) & 7] over the warp
-}
-
 // Transpose butterfly inside each 8-lane octet: returns, in lane r of the octet, the octet-wide sum
 // of v[r].
 __device__ __forceinline__ float octet_transpose_reduce8(const float (&v)[8], int lane) {
