@@ -100,3 +100,27 @@ def test_unit_weight_batched_fit_matches_reference():
         assert abs(hists[b]["final_psnr"] - float(g["batched_final_psnr"][b])) < PSNR_TOL
         assert torch.equal(gs[b].weight, torch.ones_like(gs[b].weight))
         assert torch.allclose(gs[b].xy.cpu(), t(g["batched_out_xy"][b]), atol=2e-3)
+
+
+def test_appearance_switch_requires_new_raw_parameters_and_rejects_unknown_codes():
+    import ctypes
+
+    from rtgs_b200 import _native
+
+    g = load_golden("fit_appearance")
+    image = t(g["image"])
+    h, w = image.shape[:2]
+    init = _init(g)
+    engine = FitEngine(1, init[0].shape[0], h, w, lr=1e-2, iterations=4, log_every=50, device=DEV)
+    try:
+        engine.set_targets(image[None].to(DEV))
+        assert engine.set_initial(*(x[None].to(DEV) for x in init)) == 0
+        lib = _native.lib()
+        assert lib.rtgs2d_fit_set_appearance(ctypes.c_void_p(engine._h), 7) != 0  # unknown code
+        _native.check(lib.rtgs2d_fit_set_appearance(ctypes.c_void_p(engine._h), _native.APPEARANCE_UNIT_WEIGHT_8P))
+        with pytest.raises(RuntimeError, match="set targets and raw parameters"):
+            engine.run(1)  # the raw slots changed meaning: the engine refuses until they are set again
+        assert engine.set_initial(*(x[None].to(DEV) for x in init)) == 0
+        engine.run(1)
+    finally:
+        engine.close()
