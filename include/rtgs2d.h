@@ -285,6 +285,22 @@ RTGS2D_API int rtgs2d_fit_evaluate(rtgs2d_fit* fit, float* render, double* sums,
 /* Recorded loss sums: copies up to max_rows rows; iters (rows,), sums (rows,B,2) on the host. */
 RTGS2D_API int rtgs2d_fit_history(const rtgs2d_fit* fit, int64_t max_rows, int64_t* iters, double* sums,
                        int64_t* n_rows);
+/*
+ * Fused Adam step over up to RTGS2D_ADAM_MAX_TENSORS float32 device tensors in one launch: the
+ * update of torch.optim.Adam (fit.py:419; no weight decay, amsgrad or maximize) that the fit loop
+ * applies inside its Adam kernel, for callers that keep their own loop (a reference-style loop of
+ * render, backward and optimizer step; rtgs_b200.image2gs.optim.FusedAdam wraps it). For every
+ * element: exp_avg += (1 - beta1) (grad - exp_avg); exp_avg_sq = beta2 exp_avg_sq + (1 - beta2)
+ * grad^2; param -= lr / (1 - beta1^step) * exp_avg / (sqrt(exp_avg_sq) / sqrt(1 - beta2^step)
+ * + eps), the square root and the last division as fast hardware approximations (relative error
+ * ~1e-7). `step` counts the updates including this one (1 for the first). Stream-ordered, no
+ * synchronisation. Replaces the per-parameter ATen Adam kernels of the reference's loop.
+ */
+#define RTGS2D_ADAM_MAX_TENSORS 16
+RTGS2D_API int rtgs2d_adam_step(int32_t n_tensors, float* const* params, const float* const* grads,
+                                float* const* exp_avgs, float* const* exp_avg_sqs, const int64_t* sizes,
+                                double lr, double beta1, double beta2, double eps, int64_t step,
+                                void* stream);
 /* No reference counterpart: tile-entry capacity of the fit loop. The loop bins into a fixed number
  * of (gaussian, tile) entries; a chunk of iterations that needed more is rolled back and re-run
  * with more room (results are unchanged). rtgs2d_fit_reserve pre-sizes the capacity;

@@ -13,6 +13,9 @@
 // carries no per-gaussian constants. Conic -> Cholesky follows gaussians2d.py:34-44, the raw
 // transforms fit.py:402-417, and the update torch.optim.Adam (fit.py:419) with the cosine
 // schedule's learning rate supplied by the host.
+#include <cmath>
+
+#include "../../include/rtgs2d.h"
 #include "internal.h"
 #include "kernels.cuh"
 
@@ -316,4 +319,83 @@ int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_
   return check_cuda(cudaGetLastError(), "adam_fit_kernel");
 }
 
+// ---- rtgs2d_adam_step: torch.optim.Adam's update over several tensors in one launch ----------
+
+namespace {
+
+constexpr int kMaxAdamTensors = RTGS2D_ADAM_MAX_TENSORS;
+
+struct AdamTensors {
+  float* param[kMaxAdamTensors];
+  const float* grad[kMaxAdamTensors];
+  float* exp_avg[kMaxAdamTensors];
+  float* exp_avg_sq[kMaxAdamTensors];
+  int64_t end[kMaxAdamTensors];  // inclusive prefix of the sizes: tensor k owns [end[k-1], end[k])
+  int n;
+};
+
+// Grid-stride over the concatenated elements; each element finds its tensor by a scan of the
+// (at most 16) prefix ends, then takes adam_update (the same update as the fit loop).
+__global__ void __launch_bounds__(256)
+adam_step_kernel(const AdamTensors t, int64_t total, AdamScalars a) {
+  for (int64_t idx = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * 256) {
+    int k = 0;
+    while (k + 1 < t.n && idx >= t.end[k]) ++k;
+    const int64_t j = idx - (k > 0 ? t.end[k - 1] : 0);
+    float p = t.param[k][j], m1 = t.exp_avg[k][j], m2 = t.exp_avg_sq[k][j];
+    adam_update(p, m1, m2, t.grad[k][j], a);
+    t.param[k][j] = p;
+    t.exp_avg[k][j] = m1;
+    t.exp_avg_sq[k][j] = m2;
+  }
+}
+
+}  // namespace
 }  // namespace rtgs2d
+
+using namespace rtgs2d;
+
+int rtgs2d_adam_step(int32_t n_tensors, float* const* params, const float* const* grads,
+                     float* const* exp_avgs, float* const* exp_avg_sqs, const int64_t* sizes,
+                     double lr, double beta1, double beta2, double eps, int64_t step, void* stream) {
+  if (n_tensors < 0 || n_tensors > kMaxAdamTensors) {
+    return set_error(RTGS2D_ERR_INVALID, "n_tensors must be in [0, RTGS2D_ADAM_MAX_TENSORS]");
+  }
+  if (step < 1) return set_error(RTGS2D_ERR_INVALID, "step must be >= 1 (the step this update completes)");
+  if (n_tensors == 0) return RTGS2D_OK;
+  if (!params || !grads || !exp_avgs || !exp_avg_sqs || !sizes) {
+    return set_error(RTGS2D_ERR_INVALID, "tensor array pointer is NULL");
+  }
+  AdamTensors t{};
+  int64_t total = 0;
+  for (int k = 0; k < n_tensors; ++k) {
+    if (sizes[k] < 0) return set_error(RTGS2D_ERR_INVALID, "tensor size is negative");
+    if (sizes[k] > 0 && (!params[k] || !grads[k] || !exp_avgs[k] || !exp_avg_sqs[k])) {
+      return set_error(RTGS2D_ERR_INVALID, "tensor pointer is NULL");
+    }
+    t.param[k] = params[k];
+    t.grad[k] = grads[k];
+    t.exp_avg[k] = exp_avgs[k];
+    t.exp_avg_sq[k] = exp_avg_sqs[k];
+    total += sizes[k];
+    t.end[k] = total;
+  }
+  t.n = n_tensors;
+  if (total == 0) return RTGS2D_OK;
+  // Bias corrections in double, as torch evaluates them on the host (Python floats).
+  const double bc1 = 1.0 - std::pow(beta1, static_cast<double>(step));
+  const double bc2 = 1.0 - std::pow(beta2, static_cast<double>(step));
+  AdamScalars a{};
+  a.neg_step_size = static_cast<float>(-(lr / bc1));
+  a.inv_bc2_sqrt = static_cast<float>(1.0 / std::sqrt(bc2));
+  a.beta1 = static_cast<float>(beta1);
+  a.beta2 = static_cast<float>(beta2);
+  a.one_minus_beta1 = static_cast<float>(1.0 - beta1);
+  a.one_minus_beta2 = static_cast<float>(1.0 - beta2);
+  a.eps = static_cast<float>(eps);
+  const int64_t blocks64 = (total + 255) / 256;
+  const unsigned blocks = static_cast<unsigned>(blocks64 < 148 * 16 ? blocks64 : 148 * 16);
+  adam_step_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(t, total, a);
+  return check_cuda(cudaGetLastError(), "adam_step_kernel");
+}

@@ -106,6 +106,10 @@ _SIGNATURES = {
          ctypes.POINTER(_dbl)],
         ctypes.c_int,
     ),
+    "rtgs2d_adam_step": (
+        [ctypes.c_int32, _vp, _vp, _vp, _vp, _vp, _dbl, _dbl, _dbl, _dbl, _c_int64, _vp],
+        ctypes.c_int,
+    ),
     "rtgs2d_fit_stats": (
         [_vp, ctypes.POINTER(_c_int64), ctypes.POINTER(_c_int64), ctypes.POINTER(_c_int64),
          ctypes.POINTER(ctypes.c_double)],
