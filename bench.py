@@ -658,13 +658,14 @@ def run_native(args, wl, rank: int, world: int, local_rank: int) -> None:
             cpu_splat = cpu_splat_sample()
     # Own kernels per fit, per 64-iteration chunk of c iterations: the chunk's projection; the
     # first iteration's tile-count scan (own single-block kernel up to 8192 tiles, else CUB's two,
-    # counted as library launches) and scatter; then per iteration tile sort, raster fit and Adam
-    # (+ the next projection), and for all but the last the next segment layout and tile order
-    # (direct placement): 4c + 2 own launches (4c + 1 plus 2 library ones above 8192 tiles).
+    # counted as library launches), scatter and tile sort; then per iteration raster fit (which
+    # sorts its own tile's list after the first iteration) and Adam (+ the next projection with
+    # direct placement), and for all but the last the next segment layout and tile order:
+    # 3c + 3 own launches (3c + 2 plus 2 library ones above 8192 tiles).
     chunk_lens = [64] * (iters // 64) + ([iters % 64] if iters % 64 else [])
     n_tiles = views * ((h + 15) // 16) * ((w + 15) // 16)
     small_scan = n_tiles <= 8192
-    own_per_fit = sum(4 * c + (2 if small_scan else 1) for c in chunk_lens)
+    own_per_fit = sum(3 * c + (3 if small_scan else 2) for c in chunk_lens)
     lib_per_fit = 0 if small_scan else 2 * len(chunk_lens)
     line = {
         "metric": "2D-gaussian image fits/sec",

@@ -336,10 +336,13 @@ RTGS2D_API int rtgs2d_fit_chunk_counts(const rtgs2d_fit* fit, int64_t* graph_chu
  *   RTGS2D_BINNING_AUTO     the first iteration of a chunk scatters its entries into tile lists;
  *                           each later projection writes its ids straight into per-tile segments
  *                           sized from the previous binning with slack (count + count/4 + 8), and
- *                           the binning is the per-tile sort. A segment that fills up invalidates
- *                           the chunk, which re-runs with SCATTER. The rasters of later
- *                           iterations take their tiles heaviest first. Up to 2^20 tiles (all
- *                           views); more use SCATTER.
+ *                           the fit raster sorts each tile's segment itself (lists up to 512; a
+ *                           longer one makes the fit use SORTED from that chunk on). A segment
+ *                           that fills up invalidates the chunk, which re-runs with SCATTER. The
+ *                           rasters of later iterations take their tiles heaviest first. Up to
+ *                           2^20 tiles (all views); more use SCATTER.
+ *   RTGS2D_BINNING_SORTED   AUTO with the segments sorted by a separate per-tile sort kernel
+ *                           before the raster (lists up to 2048).
  *   RTGS2D_BINNING_SCATTER  every iteration: entries, tile-count scan, scatter, per-tile sort.
  *   RTGS2D_BINNING_RADIX    every iteration: entries, radix sort by (tile, id), tile ranges.
  *   RTGS2D_BINNING_TIGHT    AUTO with segments of exactly the previous counts (no slack): any tile
@@ -349,6 +352,7 @@ RTGS2D_API int rtgs2d_fit_chunk_counts(const rtgs2d_fit* fit, int64_t* graph_chu
 #define RTGS2D_BINNING_SCATTER 1
 #define RTGS2D_BINNING_RADIX 2
 #define RTGS2D_BINNING_TIGHT 3
+#define RTGS2D_BINNING_SORTED 4
 RTGS2D_API int rtgs2d_fit_set_binning(rtgs2d_fit* fit, int32_t mode);
 RTGS2D_API int rtgs2d_fit_stage_times(const rtgs2d_fit* fit, double* bin_ms, double* raster_ms,
                                       double* adam_ms, int64_t* iterations_timed,

@@ -28,20 +28,6 @@ namespace {
 
 constexpr int kThreads = 256;
 
-// Retire the projection's stats: the largest entry count so far, copies of the entry and pair
-// counts (slots "last"), then slots 0-1 zeroed for the next projection (scatter path only, where
-// nothing later reads them).
-__device__ __forceinline__ void retire_projection_stats(unsigned long long* stats, bool zero) {
-  const unsigned long long e = stats[kStatEntries];
-  atomicMax(&stats[kStatMaxEntries], e);
-  stats[kStatLastEntries] = e;
-  stats[kStatLastPairs] = stats[kStatPairs];
-  if (zero) {
-    stats[kStatEntries] = 0;
-    stats[kStatPairs] = 0;
-  }
-}
-
 // Entries of every gaussian, (tile key << 32 | id) at offsets[g] + j, up to the capacity. With
 // `stats` (radix path) thread 0 also retires the projection's stats (slots 0-1 kept).
 __global__ void __launch_bounds__(kThreads)
@@ -96,36 +82,6 @@ constexpr int kTileSortWarps = 4;
 constexpr int kRegSortMax = 512;
 
 template <int E>
-__device__ __forceinline__ void warp_sort_striped(uint32_t (&v)[E], int lane) {
-#pragma unroll
-  for (int k = 2; k <= 32 * E; k <<= 1) {
-#pragma unroll
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      if (j >= 32) {
-        const int je = j >> 5;
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-          if ((e & je) == 0) {
-            const bool up = ((e * 32) & k) == 0;  // k >= 64 here: the lane bits do not matter
-            const uint32_t x = v[e], y = v[e ^ je];
-            v[e] = up ? min(x, y) : max(x, y);
-            v[e ^ je] = up ? max(x, y) : min(x, y);
-          }
-        }
-      } else {
-        const bool lower = (lane & j) == 0;
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-          const bool up = ((e * 32 + lane) & k) == 0;
-          const uint32_t y = __shfl_xor_sync(0xffffffffu, v[e], j);
-          v[e] = (lower == up) ? min(v[e], y) : max(v[e], y);
-        }
-      }
-    }
-  }
-}
-
-template <int E>
 __device__ __forceinline__ void sort_tile_regs(uint32_t* seg, int len, int lane) {
   uint32_t v[E];
 #pragma unroll
@@ -154,7 +110,7 @@ __device__ __forceinline__ uint32_t bitonic_shfl(uint32_t v, int i, int k, int j
 
 __global__ void __launch_bounds__(kTileSortWarps * 32)
 tile_sort_kernel(const int* __restrict__ tile_end, const int2* __restrict__ tile_seg,
-                 int* __restrict__ fill, int64_t n_tiles, int64_t cap,
+                 const int* __restrict__ cursor, int64_t n_tiles, int64_t cap,
                  unsigned long long* __restrict__ stats, uint32_t* __restrict__ list,
                  int2* __restrict__ ranges) {
   __shared__ uint32_t s_buf[kTileSortWarps][kSegSortMax];
@@ -165,15 +121,12 @@ tile_sort_kernel(const int* __restrict__ tile_end, const int2* __restrict__ tile
   int64_t start, end;
   if (tile_seg) {  // direct placement: the tile's segment and how far the projection moved its cursor
     const int2 sg = tile_seg[t];
-    int cursor = lane == 0 ? fill[t] : 0;
-    cursor = __shfl_sync(0xffffffffu, cursor, 0);
-    const int filled = cursor - sg.x;
+    int cur = lane == 0 ? cursor[t] : 0;
+    cur = __shfl_sync(0xffffffffu, cur, 0);
+    const int filled = cur - sg.x;
     start = sg.x;
     end = start + (filled < sg.y ? filled : sg.y);
-    if (lane == 0) {
-      fill[t] = filled;  // the count, for the next layout
-      if (filled > sg.y) atomicMax(&stats[kStatSegOverflow], 1ull);  // ids spilled past the segment
-    }
+    if (lane == 0 && filled > sg.y) atomicMax(&stats[kStatSegOverflow], 1ull);  // ids spilled past the segment
   } else {    // scatter: inclusive scan of the tile counts
     start = t == 0 ? 0 : tile_end[t - 1];
     end = tile_end[t];
@@ -323,19 +276,24 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int* tot
 // Direct placement layout for the next binning: tile t gets a segment of count + 8 + count / 4
 // slots (count = this binning's entries of the tile; exactly count without slack), segments packed
 // in tile order and clipped to the list capacity. Counts come from the scan (tile_end, after a
-// scatter) or from the counts that the tile sort of a direct placement left in `fill`; `fill`
-// then receives every tile's cursor (its segment's start) for the next placement. With `order`, the tiles are also counting-sorted by descending count (capped at 1023) into
-// order[]: the next raster's block order. One block (it runs beside the raster, off the critical
-// path); each thread owns a run of consecutive tiles and reads their counts once per pass.
+// scatter) or from the current placement (cursor_in - seg_in start: the ids the projection placed,
+// including any that overran the segment). The segments and cursors (each set to its segment's
+// start) go to seg_out / cursor_out, the other buffer of the pair, so a raster can still read the
+// current ones. With `order`, the tiles are also counting-sorted by descending count (capped at
+// 1023) into order[]: the next raster's block order. One block (it runs beside the raster, off the
+// critical path); each thread owns a run of consecutive tiles.
 __global__ void __launch_bounds__(kSmallScanThreads)
-layout_kernel(const int* __restrict__ tile_end, int* __restrict__ fill, int n_tiles,
-              int list_cap, bool slack, int2* __restrict__ seg, int* __restrict__ order) {
+layout_kernel(const int* __restrict__ tile_end, const int2* __restrict__ seg_in,
+              const int* __restrict__ cursor_in, int n_tiles, int list_cap, bool slack,
+              int2* __restrict__ seg_out, int* __restrict__ cursor_out, int* __restrict__ order) {
   __shared__ int s_warp[kSmallScanThreads / 32 + 1];
   __shared__ int s_bin[kSmallScanThreads];
   const int per = (n_tiles + kSmallScanThreads - 1) / kSmallScanThreads;
   const int i0 = min(static_cast<int>(threadIdx.x) * per, n_tiles);
   const int i1 = min(i0 + per, n_tiles);
-  auto count = [&](int t) { return tile_end ? tile_end[t] - (t > 0 ? tile_end[t - 1] : 0) : fill[t]; };
+  auto count = [&](int t) {
+    return tile_end ? tile_end[t] - (t > 0 ? tile_end[t - 1] : 0) : cursor_in[t] - seg_in[t].x;
+  };
   auto seg_cap = [slack](int c) { return slack ? c + 8 + (c >> 2) : c; };
   auto bin = [](int c) { return kSmallScanThreads - 1 - min(c, kSmallScanThreads - 1); };
   if (order) s_bin[threadIdx.x] = 0;
@@ -347,24 +305,19 @@ layout_kernel(const int* __restrict__ tile_end, int* __restrict__ fill, int n_ti
     if (order) atomicAdd(&s_bin[bin(c)], 1);
   }
   int start = block_exclusive_scan(sum, s_warp, nullptr);
-  const bool cursor_here = tile_end || !order;  // else the order pass, which reads the counts
   for (int t = i0; t < i1; ++t) {
     const int c = count(t);
     const int sc = seg_cap(c);
     const int room = list_cap - start;
-    seg[t] = make_int2(start, sc < room ? sc : (room > 0 ? room : 0));
-    if (cursor_here) fill[t] = start;
+    seg_out[t] = make_int2(start, sc < room ? sc : (room > 0 ? room : 0));
+    cursor_out[t] = start;
     start += sc;
   }
   if (!order) return;
   const int first = block_exclusive_scan(s_bin[threadIdx.x], s_warp, nullptr);
   s_bin[threadIdx.x] = first;  // every thread read its own bin before the scan's barriers
   __syncthreads();
-  for (int t = i0; t < i1; ++t) {
-    const int c = count(t);
-    order[atomicAdd(&s_bin[bin(c)], 1)] = t;
-    if (!tile_end) fill[t] = seg[t].x;  // written by this thread above
-  }
+  for (int t = i0; t < i1; ++t) order[atomicAdd(&s_bin[bin(count(t))], 1)] = t;
 }
 
 template <bool INCLUSIVE>
@@ -451,27 +404,31 @@ bool direct_binning_supported(const Geometry& g) {
   return g.n_tiles() > 0 && g.n_tiles() <= kDirectMaxTiles;
 }
 
-int direct_layout(BinBuffers& bb, const Geometry& g, bool after_scatter, bool slack, int* order,
-                  cudaStream_t s) {
+int direct_layout(BinBuffers& bb, const Geometry& g, bool after_scatter, bool slack, int out,
+                  int* order, cudaStream_t s) {
   const int64_t n_tiles = g.n_tiles();
   if (!direct_binning_supported(g)) return set_error(-1, "direct binning: too many tiles");
-  RTGS_TRY(bb.seg.ensure(static_cast<size_t>(n_tiles) * sizeof(int2), s));
+  if (out != 0 && out != 1) return set_error(-1, "direct binning: segment buffer must be 0 or 1");
+  RTGS_TRY(bb.seg.ensure(static_cast<size_t>(2 * n_tiles) * sizeof(int2), s));
+  RTGS_TRY(bb.cursor.ensure(static_cast<size_t>(2 * n_tiles) * sizeof(int), s));
   const int64_t list_cap = static_cast<int64_t>(bb.list.bytes / sizeof(uint32_t));
+  const int in = 1 - out;
   layout_kernel<<<1, kSmallScanThreads, 0, s>>>(
-      after_scatter ? bb.tile_end.as<int>() : nullptr, bb.tile_count.as<int>(),
-      static_cast<int>(n_tiles), static_cast<int>(list_cap < INT32_MAX ? list_cap : INT32_MAX), slack,
-      bb.seg.as<int2>(), order);
-  bb.counts_cleared = true;  // tile_count holds the cursors of the next placement
+      after_scatter ? bb.tile_end.as<int>() : nullptr, bb.seg.as<int2>() + in * n_tiles,
+      bb.cursor.as<int>() + in * n_tiles, static_cast<int>(n_tiles),
+      static_cast<int>(list_cap < INT32_MAX ? list_cap : INT32_MAX), slack,
+      bb.seg.as<int2>() + out * n_tiles, bb.cursor.as<int>() + out * n_tiles, order);
   return check_cuda(cudaGetLastError(), "layout_kernel");
 }
 
-int direct_sort(BinBuffers& bb, const Geometry& g, cudaStream_t s) {
+int direct_sort(BinBuffers& bb, const Geometry& g, int in, cudaStream_t s) {
   const int64_t n_tiles = g.n_tiles();
+  if (in != 0 && in != 1) return set_error(-1, "direct binning: segment buffer must be 0 or 1");
   RTGS_TRY(bb.ranges.ensure(static_cast<size_t>(n_tiles) * sizeof(int2), s));
   bb.presorted = false;
   const unsigned blocks = static_cast<unsigned>((n_tiles + kTileSortWarps - 1) / kTileSortWarps);
   tile_sort_kernel<<<blocks, kTileSortWarps * 32, 0, s>>>(
-      nullptr, bb.seg.as<int2>(), bb.tile_count.as<int>(), n_tiles,
+      nullptr, bb.seg.as<int2>() + in * n_tiles, bb.cursor.as<int>() + in * n_tiles, n_tiles,
       static_cast<int64_t>(bb.list.bytes / sizeof(uint32_t)), bb.stats.as<unsigned long long>(),
       bb.list.as<uint32_t>(), bb.ranges.as<int2>());
   return check_cuda(cudaGetLastError(), "tile_sort_kernel");

@@ -54,7 +54,7 @@ void DevBuf::release() {
 
 void BinBuffers::release() {
   for (DevBuf* b : {&records, &weights, &spans, &counts, &offsets, &list, &tile_count, &tile_end,
-                    &entries[0], &entries[1], &ranges, &seg, &tile_order, &partials, &partial_d, &cub_temp,
+                    &entries[0], &entries[1], &ranges, &seg, &cursor, &tile_order, &partials, &partial_d, &cub_temp,
                     &sort_counts, &stats}) {
     b->release();
   }

@@ -54,6 +54,7 @@ struct rtgs2d_fit {
   bool use_radix = false;  // some tile list exceeded the shared-memory sort: bin by radix sort
   int32_t binning = RTGS2D_BINNING_AUTO;  // rtgs2d_fit_set_binning
   bool direct_retry = false;   // the current chunk overflowed a segment: re-run it by scatter
+  bool fused_off = false;      // a tile list exceeded the fit raster's own sort: tile-sort kernel
   int64_t segment_retries = 0;
   cudaStream_t side_stream = nullptr;  // segment layout beside the raster
   cudaEvent_t fork_event = nullptr;
@@ -269,8 +270,15 @@ bool radix(const rtgs2d_fit* f) { return f->use_radix || f->binning == RTGS2D_BI
 // Direct placement for this chunk: not on the radix path, at most 2^20 tiles, and not right after
 // a chunk that overflowed a tile segment (that chunk re-runs with the scatter binning).
 bool direct_chunk(const rtgs2d_fit* f) {
-  const bool mode = f->binning == RTGS2D_BINNING_AUTO || f->binning == RTGS2D_BINNING_TIGHT;
+  const bool mode = f->binning == RTGS2D_BINNING_AUTO || f->binning == RTGS2D_BINNING_TIGHT ||
+                    f->binning == RTGS2D_BINNING_SORTED;
   return mode && !f->direct_retry && !radix(f) && direct_binning_supported(f->geo);
+}
+
+// In a direct chunk, the fit raster sorts its own tile's list (no tile-sort kernel) unless the
+// caller chose the separate sort, or a list of this fit exceeded kFusedSortMax.
+bool fused_sort(const rtgs2d_fit* f) {
+  return direct_chunk(f) && f->binning != RTGS2D_BINNING_SORTED && !f->fused_off;
 }
 
 // The stream and events that run the segment layout beside the raster.
@@ -288,7 +296,8 @@ int ensure_segment_room(rtgs2d_fit* f, cudaStream_t s) {
   if (!direct_binning_supported(f->geo)) return 0;
   const int64_t cap = f->bb.capacity;
   const size_t want = static_cast<size_t>(cap + cap / 4 + 16 * f->geo.n_tiles()) * sizeof(uint32_t);
-  RTGS_TRY(f->bb.seg.ensure(static_cast<size_t>(f->geo.n_tiles()) * sizeof(int2), s));
+  RTGS_TRY(f->bb.seg.ensure(static_cast<size_t>(2 * f->geo.n_tiles()) * sizeof(int2), s));
+  RTGS_TRY(f->bb.cursor.ensure(static_cast<size_t>(2 * f->geo.n_tiles()) * sizeof(int), s));
   RTGS_TRY(f->bb.tile_order.ensure(static_cast<size_t>(2 * f->geo.n_tiles()) * sizeof(int), s));
   return f->bb.list.ensure(want, s);
 }
@@ -375,9 +384,10 @@ std::vector<uintptr_t> chunk_key(const rtgs2d_fit* f, int64_t chunk) {
   const BinBuffers& bb = f->bb;
   std::vector<uintptr_t> k = {static_cast<uintptr_t>(chunk), static_cast<uintptr_t>(radix(f)),
                               static_cast<uintptr_t>(bb.capacity), static_cast<uintptr_t>(f->use_active),
-                              static_cast<uintptr_t>(direct_chunk(f)), static_cast<uintptr_t>(f->unit_weight)};
+                              static_cast<uintptr_t>(direct_chunk(f)), static_cast<uintptr_t>(fused_sort(f)),
+                              static_cast<uintptr_t>(f->unit_weight)};
   for (const DevBuf* b : {&bb.records, &bb.weights, &bb.spans, &bb.counts, &bb.offsets, &bb.list,
-                          &bb.tile_count, &bb.tile_end, &bb.seg, &bb.tile_order, &bb.entries[0], &bb.entries[1], &bb.ranges,
+                          &bb.tile_count, &bb.tile_end, &bb.seg, &bb.cursor, &bb.tile_order, &bb.entries[0], &bb.entries[1], &bb.ranges,
                           &bb.partials, &bb.partial_d, &bb.cub_temp, &bb.sort_counts, &bb.stats,
                           &f->raw, &f->m1, &f->m2, &f->targets, &f->mask, &f->view_scale,
                           &f->tile_loss, &f->log, &f->iter_table, &f->active}) {
@@ -404,41 +414,50 @@ int enqueue_chunk(rtgs2d_fit* f, int64_t chunk, cudaStream_t s, cudaEvent_t* ev,
                               coverage(f), f->unit_weight, s));
   // Binning: the chunk's first iteration scatters the projection's entries; with direct placement
   // (direct_chunk), every later projection (fused into Adam) writes its ids straight into tile
-  // segments sized from the previous binning, and the binning is just the tile sort.
+  // segments sized from the previous binning, and the binning is just the per-tile sort: done by
+  // the fit raster itself (fused_sort), or by the tile-sort kernel.
   // The layout of the next segments runs on the side stream beside the raster and joins before
-  // Adam (the projection that fills them).
+  // Adam (the projection that fills them). Segments, cursors and tile orders alternate between two
+  // buffers: the layout of iteration k writes buffer (k + 1) & 1 while raster k reads buffer k & 1.
   const bool direct = direct_chunk(f);
+  const bool fuse = fused_sort(f);
   if (direct) RTGS_TRY(ensure_side_stream(f));
+  const int64_t n_tiles = f->geo.n_tiles();
+  int* orders = bb.tile_order.as<int>();
   for (int64_t k = 0; k < chunk; ++k) {
     cudaEvent_t* e = ev ? ev + 4 * k : nullptr;
+    const int cur = static_cast<int>(k & 1), next = static_cast<int>((k + 1) & 1);
     if (e) RTGS_CUDA(record(e[0]), "event record");
     if (direct && k > 0) {
-      RTGS_TRY(direct_sort(bb, f->geo, s));
+      if (!fuse) RTGS_TRY(direct_sort(bb, f->geo, cur, s));
     } else {
       RTGS_TRY(bin_entries_async(bb, f->geo, f->m, radix(f), s));
     }
-    // Tile orders alternate between two buffers: the layout of iteration k writes the order of
-    // raster k + 1 while raster k reads the one written beside raster k - 1.
     const bool layout = direct && k + 1 < chunk;
-    int* orders = bb.tile_order.as<int>();
-    const int64_t n_tiles = f->geo.n_tiles();
     if (layout) {
       RTGS_CUDA(cudaEventRecord(f->fork_event, s), "fork record");
       RTGS_CUDA(cudaStreamWaitEvent(f->side_stream, f->fork_event, 0), "fork wait");
-      RTGS_TRY(direct_layout(bb, f->geo, k == 0, f->binning != RTGS2D_BINNING_TIGHT,
-                             orders + ((k + 1) & 1) * n_tiles, f->side_stream));
+      RTGS_TRY(direct_layout(bb, f->geo, k == 0, f->binning != RTGS2D_BINNING_TIGHT, next,
+                             orders + next * n_tiles, f->side_stream));
       RTGS_CUDA(cudaEventRecord(f->join_event, f->side_stream), "join record");
     }
     if (e) RTGS_CUDA(record(e[1]), "event record");
     FitRasterArgs fk = fa;
-    if (direct && k > 0) fk.tile_order = orders + (k & 1) * n_tiles;
+    if (direct && k > 0) {
+      fk.tile_order = orders + cur * n_tiles;
+      if (fuse) {
+        fk.seg = bb.seg.as<int2>() + cur * n_tiles;
+        fk.cursor = bb.cursor.as<int>() + cur * n_tiles;
+        fk.stats = bb.stats.as<unsigned long long>();
+      }
+    }
     RTGS_TRY(launch_raster_fit(bb, f->geo, kCutoff, fk, true, s));
     if (e) RTGS_CUDA(record(e[2]), "event record");
     if (layout) RTGS_CUDA(cudaStreamWaitEvent(s, f->join_event, 0), "join wait");
     RTGS_TRY(launch_adam_fit(bb, f->geo, f->m, f->n, f->raw.as<float>(), f->m1.as<float>(),
                              f->m2.as<float>(), f->iter_table.as<IterScalars>(),
                              static_cast<int>(k), lg, k + 1 < chunk, active_rows(f), coverage(f),
-                             layout, s));
+                             layout ? bb.cursor.as<int>() + next * n_tiles : nullptr, s));
     if (e) RTGS_CUDA(record(e[3]), "event record");
   }
   return 0;
@@ -790,7 +809,8 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
     const int64_t max_entries = static_cast<int64_t>(bb.host_stats[kStatMaxEntries]);
     const bool long_tile = !radix(f) && bb.host_stats[kStatLongTile] > 0;
     const bool seg_full = bb.host_stats[kStatSegOverflow] > 0;
-    if (max_entries > bb.capacity || long_tile || seg_full) {
+    const bool fused_long = bb.host_stats[kStatFusedLong] > 0;
+    if (max_entries > bb.capacity || long_tile || seg_full || fused_long) {
       // Entries were dropped in this chunk: roll back and re-run it with room for them.
       if (max_entries > INT32_MAX) return set_error(RTGS2D_ERR_CAPACITY, "more than 2^31 tile entries");
       RTGS_TRY(snapshot(f, false, s));
@@ -799,6 +819,7 @@ int rtgs2d_fit_run(rtgs2d_fit* f, int64_t n_iterations, void* stream) {
       f->log_iters.resize(logs0);
       f->retries += 1;
       if (long_tile) f->use_radix = true;  // a tile list too long for the tile sort
+      if (fused_long) f->fused_off = true;  // a tile list too long for the raster's own sort
       if (seg_full) {                      // a tile segment too short: this chunk bins by scatter
         f->direct_retry = true;
         f->segment_retries += 1;
@@ -905,7 +926,7 @@ int rtgs2d_fit_set_appearance(rtgs2d_fit* f, int32_t parameterization) {
 
 int rtgs2d_fit_set_binning(rtgs2d_fit* f, int32_t mode) {
   RTGS_TRY(check_fit(f));
-  if (mode < RTGS2D_BINNING_AUTO || mode > RTGS2D_BINNING_TIGHT) {
+  if (mode < RTGS2D_BINNING_AUTO || mode > RTGS2D_BINNING_SORTED) {
     return set_error(RTGS2D_ERR_INVALID, "unknown binning mode");
   }
   f->binning = mode;

@@ -52,12 +52,17 @@ enum StatSlot : int {
   kStatLastEntries = 5,  // entries of the last binned projection (copied by the binning)
   kStatLastPairs = 6,    // pairs of the last binned projection
   kStatSegOverflow = 7,  // a direct placement found a tile segment full (its binning is invalid)
-  kStatSlots = 8
+  kStatFusedLong = 8,    // a fit raster that sorts its own tile found a list above kFusedSortMax
+  kStatSlots = 9
 };
 
 // Tile lists up to this length are sorted by the tile-sort kernel (one warp per tile, in shared
 // memory); a binning with a longer list uses the global radix sort instead.
 constexpr int kSegSortMax = 2048;
+// Tile lists up to this length are sorted by the fused fit raster itself (one warp, in registers),
+// in the direct-placement iterations of the fit loop; a longer list makes the chunk re-run with
+// the separate tile-sort kernel.
+constexpr int kFusedSortMax = 512;
 
 // Scratch used by projection + tile binning + raster for one render / one fit iteration.
 struct BinBuffers {
@@ -68,11 +73,12 @@ struct BinBuffers {
   DevBuf offsets;     // int[M]  entry index of each gaussian's first tile (see bin_entries)
   DevBuf list;        // uint32[capacity] gaussian ids grouped by tile, ascending inside a tile
   DevBuf tile_count;  // int[n_tiles] entries per tile (counted up by the projection, back down
-                      //   to zero by the scatter); tile cursors during direct placement
+                      //   to zero by the scatter)
   DevBuf tile_end;    // int[n_tiles] inclusive scan of tile_count
   DevBuf entries[2];  // uint64[capacity] (tile key << 32 | gaussian id), radix-sort double buffer
   DevBuf ranges;      // int2[n_tiles] [start, end) of every tile in the list (or sorted entries)
-  DevBuf seg;         // int2[n_tiles] direct placement: (start, slots) of each tile's segment
+  DevBuf seg;         // int2[2][n_tiles] direct placement: (start, slots) of each tile's segment
+  DevBuf cursor;      // int[2][n_tiles] direct placement: next free list position of each tile
   DevBuf tile_order;  // int[2][n_tiles] raster block order (tiles by descending entry count)
   DevBuf partials;    // float[capacity][8] per (gaussian, tile) gradient moments
   DevBuf partial_d;   // float[capacity]   per (gaussian, tile) density-gradient moment
@@ -83,8 +89,8 @@ struct BinBuffers {
   int sorted_sel = 0;                         // which entries buffer holds the sorted result
   bool presorted = false;                     // radix path (entries + ranges) produced the binning
   bool counts_cleared = false;                // the last binning left stats slots 0-1 at zero
-                                              //   and tile_count ready for the next projection
-                                              //   (zeros after a scatter, cursors after a layout)
+                                              //   and tile_count at zero for the next projection
+                                              //   (after a scatter; a layout leaves fresh cursors)
   bool entries_emitted = false;               // the last projection emitted the entries
   int64_t capacity = 0;                       // entries the entry buffers can hold
   int64_t n_entries = 0;                      // host-known entry count (synchronous binning)
@@ -146,21 +152,23 @@ int check_long_tiles(BinBuffers& bb, const Geometry& g, cudaStream_t s);
 // than kSegSortMax on the scatter path is flagged by the raster in stats[kStatLongTile].
 int bin_entries_async(BinBuffers& bb, const Geometry& g, int64_t m, bool radix, cudaStream_t s);
 // Direct placement (fit loop): a projection with ProjOut::list set writes each gaussian id straight
-// into its tile's segment, at the position that an atomic on the tile's cursor (bb.tile_count)
-// returns; segments are sized from the previous binning's counts with slack.
-// direct_layout computes the segments from the last binning (after_scatter: from tile_end; else
-// from the counts that direct_sort left in bb.tile_count; slack: count + count/4 + 8 slots, else
-// count) and sets every cursor to its segment's start; direct_sort turns the cursors back into
-// counts, flags a cursor past its segment's end in stats[kStatSegOverflow] and sorts the filled
-// segments into bb.ranges. Nothing but the next projection reads the layout, so it can run beside
-// the raster. With `order`, direct_layout also writes the tiles in
-// descending order of their entry count (a permutation of the tiles, ties in any order) for the
-// next raster: heaviest tiles first shortens the launch's tail. Up to kDirectMaxTiles tiles.
+// into its tile's segment, at the position that an atomic on the tile's cursor returns; segments
+// are sized from the previous binning's counts with slack. Segments and cursors are double
+// buffered (bb.seg, bb.cursor: buffer 0 and 1 of n_tiles each), so that the layout for the next
+// placement can run beside a raster that still reads the current one.
+// direct_layout computes the segments of buffer `out` from the last binning (after_scatter: from
+// tile_end; else from buffer 1 - out: count = cursor - segment start; slack: count + count/4 + 8
+// slots, else count) and sets every cursor of buffer `out` to its segment's start; direct_sort
+// reads buffer `in` (count = cursor - start), flags a cursor past its segment's end in
+// stats[kStatSegOverflow] and sorts the filled segments into bb.ranges. With `order`,
+// direct_layout also writes the tiles in descending order of their entry count (a permutation of
+// the tiles, ties in any order) for the next raster: heaviest tiles first shortens the launch's
+// tail. Up to kDirectMaxTiles tiles.
 constexpr int64_t kDirectMaxTiles = int64_t{1} << 20;
 bool direct_binning_supported(const Geometry& g);
-int direct_layout(BinBuffers& bb, const Geometry& g, bool after_scatter, bool slack, int* order,
-                  cudaStream_t s);
-int direct_sort(BinBuffers& bb, const Geometry& g, cudaStream_t s);
+int direct_layout(BinBuffers& bb, const Geometry& g, bool after_scatter, bool slack, int out,
+                  int* order, cudaStream_t s);
+int direct_sort(BinBuffers& bb, const Geometry& g, int in, cudaStream_t s);
 // Allocate the entry-sized buffers (list, entries, partials[, partial_d]) for `capacity` entries.
 int ensure_entry_capacity(BinBuffers& bb, int64_t capacity, bool density, cudaStream_t s);
 // Zero per-tile counts before a projection (projection launchers call it).
@@ -185,6 +193,12 @@ struct FitRasterArgs {
   float* render_out = nullptr;        // optional (B, H, W, 3)
   float coverage_coef = 0.f;          // > 0: mask coverage penalty weight / (H * W) (density pass)
   const int* tile_order = nullptr;    // optional: block b rasterises tile tile_order[b]
+  // Optional (direct placement): the raster sorts its own tile's list -- tile t's ids are
+  // list[seg[t].x, seg[t].x + cursor[t] - seg[t].x), clipped to seg[t].y -- instead of reading
+  // the ranges of a tile-sort kernel; block 0 retires the projection's stats.
+  const int2* seg = nullptr;
+  const int* cursor = nullptr;
+  unsigned long long* stats = nullptr;
 };
 
 int launch_raster_forward(const BinBuffers& bb, const Geometry& g, float cutoff, float* out,
@@ -231,9 +245,11 @@ int launch_raw_grad(const BinBuffers& bb, int64_t m, int height, int width, cons
 // project_next the updated parameters are also projected (records, spans, counts, offsets,
 // stats) for the next iteration's binning: entries for the scatter path, or with `direct` the ids
 // placed directly into the tile segments at the tile cursors (see direct_layout).
+// `cursors` (direct placement) are the tile cursors of the segment buffer the placement fills
+// (bb.cursor + buffer * n_tiles); null projects for the scatter binning.
 int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_view, float* raw,
                     float* m1, float* m2, const IterScalars* table, int k, const LossLog& lg,
-                    bool project_next, const uint8_t* active, bool density, bool direct,
+                    bool project_next, const uint8_t* active, bool density, int* cursors,
                     cudaStream_t s);
 
 }  // namespace rtgs2d

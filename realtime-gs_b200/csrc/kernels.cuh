@@ -222,6 +222,54 @@ __device__ __forceinline__ void project_tail(int64_t i, bool active, float mx, f
   });
 }
 
+// Retire the projection's stats: the largest entry count so far, copies of the entry and pair
+// counts (slots "last"), then slots 0-1 zeroed for the next projection (scatter path and direct
+// placement, where nothing later reads them).
+__device__ __forceinline__ void retire_projection_stats(unsigned long long* stats, bool zero) {
+  const unsigned long long e = stats[kStatEntries];
+  atomicMax(&stats[kStatMaxEntries], e);
+  stats[kStatLastEntries] = e;
+  stats[kStatLastPairs] = stats[kStatPairs];
+  if (zero) {
+    stats[kStatEntries] = 0;
+    stats[kStatPairs] = 0;
+  }
+}
+
+// Ascending bitonic sort of 32 * E values held by one warp in striped order (value e of lane l is
+// element e * 32 + l): partner strides below 32 are shuffles, strides of 32 and more
+// compare-exchanges inside the lane. Fully unrolled per E. Used by the tile sort (binning.cu) and
+// by the fit raster that sorts its own tile (raster.cu).
+template <int E>
+__device__ __forceinline__ void warp_sort_striped(uint32_t (&v)[E], int lane) {
+#pragma unroll
+  for (int k = 2; k <= 32 * E; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j >= 32) {
+        const int je = j >> 5;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          if ((e & je) == 0) {
+            const bool up = ((e * 32) & k) == 0;  // k >= 64 here: the lane bits do not matter
+            const uint32_t x = v[e], y = v[e ^ je];
+            v[e] = up ? min(x, y) : max(x, y);
+            v[e ^ je] = up ? max(x, y) : min(x, y);
+          }
+        }
+      } else {
+        const bool lower = (lane & j) == 0;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const bool up = ((e * 32 + lane) & k) == 0;
+          const uint32_t y = __shfl_xor_sync(0xffffffffu, v[e], j);
+          v[e] = (lower == up) ? min(v[e], y) : max(v[e], y);
+        }
+      }
+    }
+  }
+}
+
 // Entries at or past the entry capacity were never written (an overflowed binning, whose results
 // the caller discards); never read them. A negative offset (an entry count past 2^31, which the
 // host rejects after the fact) reads nothing either.

@@ -276,7 +276,7 @@ int launch_raw_grad(const BinBuffers& bb, int64_t m, int height, int width, cons
 
 int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_view, float* raw,
                     float* m1, float* m2, const IterScalars* table, int k, const LossLog& lg,
-                    bool project_next, const uint8_t* active, bool density, bool direct,
+                    bool project_next, const uint8_t* active, bool density, int* cursors,
                     cudaStream_t s) {
   if (m == 0) return 0;
   ProjOut o{};
@@ -289,17 +289,23 @@ int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_
     o.counts = bb.counts.as<int>();
     o.offsets = bb.offsets.as<int>();
     o.stats = bb.stats.as<unsigned long long>();
-    o.tile_count = bb.tile_count.as<int>();
     o.entries = bb.entries[0].as<uint64_t>();
     o.cap = bb.capacity;
     o.active = active;
-    // direct placement into the tile segments laid out by direct_layout (cursors in tile_count)
-    o.list = direct ? bb.list.as<uint32_t>() : nullptr;
-    o.list_cap = static_cast<int64_t>(bb.list.bytes / sizeof(uint32_t));
     o.tiles_x = g.tiles_x;
-    if (!bb.counts_cleared) {  // the scatter binning leaves both at zero; the radix path does not
-      RTGS_TRY(reset_tile_counts(bb, g, s));
-      RTGS_CUDA(cudaMemsetAsync(bb.stats.ptr, 0, 2 * sizeof(unsigned long long), s), "memset stats");
+    if (cursors) {
+      // Direct placement into the segments of a layout (direct_layout): the tile cursors advance
+      // and the ids go to the list. The binning before this kernel (tile sort, or the fit raster
+      // that sorts its own tile) left stats slots 0-1 at zero.
+      o.tile_count = cursors;
+      o.list = bb.list.as<uint32_t>();
+      o.list_cap = static_cast<int64_t>(bb.list.bytes / sizeof(uint32_t));
+    } else {
+      o.tile_count = bb.tile_count.as<int>();
+      if (!bb.counts_cleared) {  // the scatter binning leaves both at zero; the radix path does not
+        RTGS_TRY(reset_tile_counts(bb, g, s));
+        RTGS_CUDA(cudaMemsetAsync(bb.stats.ptr, 0, 2 * sizeof(unsigned long long), s), "memset stats");
+      }
     }
     bb.counts_cleared = false;
     bb.entries_emitted = true;

@@ -4,7 +4,9 @@
 // 2 elsewhere, see kPPT). Each warp owns an 8 x (4*PPT) pixel sub-block and each lane PPT adjacent
 // pixels of one column (rows PPT*r .. PPT*r + PPT-1, so that a small gaussian usually covers all
 // of them). The tile's gaussian list (ascending gaussian index, from the binning step) is staged
-// through shared memory in batches of one record per thread.
+// through shared memory in batches of one record per thread. In the fit loop's direct-placement
+// iterations the fit raster sorts its own tile's list first (fused_tile_sort: warp 0, in
+// registers, into shared memory), which replaces a separate tile-sort launch per iteration.
 //
 //   forward   per 32 staged records, 8 + 4*PPT ballots give every lane a 32-bit mask of the
 //             records whose support rectangle covers each of its pixels (in the renderer forward
@@ -369,12 +371,90 @@ __device__ __forceinline__ void backward_piece(const float4& geo, const float4& 
   S[4] = ROW ? m_vv : m_ff;  // sum dq dy^2
 }
 
+// Fused tile sort of the fit raster (direct placement): warp 0 reads tile `tile`'s segment and
+// cursor, flags a segment overrun (stats[kStatSegOverflow]) or a list above kFusedSortMax
+// (stats[kStatFusedLong]: the chunk re-runs with the separate tile-sort kernel), sorts the list
+// ascending in registers and leaves it in s_ids; block 0 retires the projection's stats (what the
+// tile-sort kernel does otherwise). Called by every thread of the block; returns the list length
+// (0 for a list that is not sorted here, whose results the engine discards).
+template <int E>
+__device__ __forceinline__ void sort_ids_to_shared(const uint32_t* src, int len, uint32_t* dst, int lane) {
+  uint32_t v[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i = e * 32 + lane;
+    v[e] = i < len ? src[i] : 0xffffffffu;
+  }
+  warp_sort_striped<E>(v, lane);
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i = e * 32 + lane;
+    if (i < len) dst[i] = v[e];
+  }
+}
+
+__device__ __forceinline__ int fused_tile_sort(const FitRasterArgs& f, const uint32_t* list, int tile,
+                                               uint32_t* s_ids, int* s_len) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) {
+    int sx = 0, sy = 0, cur = 0;
+    if (lane == 0) {
+      const int2 sg = f.seg[tile];
+      sx = sg.x;
+      sy = sg.y;
+      cur = f.cursor[tile];
+    }
+    sx = __shfl_sync(0xffffffffu, sx, 0);
+    sy = __shfl_sync(0xffffffffu, sy, 0);
+    cur = __shfl_sync(0xffffffffu, cur, 0);
+    const int filled = cur - sx;
+    const int len = max(min(filled, sy), 0);
+    if (lane == 0) {
+      if (filled > sy) atomicMax(&f.stats[kStatSegOverflow], 1ull);  // ids spilled past the segment
+      if (len > kFusedSortMax) atomicMax(&f.stats[kStatFusedLong], static_cast<unsigned long long>(len));
+      *s_len = len <= kFusedSortMax ? len : 0;
+    }
+    const uint32_t* src = list + sx;
+    if (len <= 32) {
+      sort_ids_to_shared<1>(src, len, s_ids, lane);
+    } else if (len <= 64) {
+      sort_ids_to_shared<2>(src, len, s_ids, lane);
+    } else if (len <= 128) {
+      sort_ids_to_shared<4>(src, len, s_ids, lane);
+    } else if (len <= 256) {
+      sort_ids_to_shared<8>(src, len, s_ids, lane);
+    } else if (len <= kFusedSortMax) {
+      // 257..512 ids (rare): bitonic network over 512 slots in shared memory, one
+      // compare-exchange per pair and step (16 ids per lane in registers would spill).
+      for (int i = lane; i < kFusedSortMax; i += 32) s_ids[i] = i < len ? src[i] : 0xffffffffu;
+      __syncwarp();
+      for (int k = 2; k <= kFusedSortMax; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+          for (int p = lane; p < kFusedSortMax / 2; p += 32) {
+            const int i = ((p & ~(j - 1)) << 1) | (p & (j - 1));
+            const uint32_t x = s_ids[i], y = s_ids[i | j];
+            if ((x > y) == ((i & k) == 0)) {
+              s_ids[i] = y;
+              s_ids[i | j] = x;
+            }
+          }
+          __syncwarp();
+        }
+      }
+    }
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) retire_projection_stats(f.stats, true);
+  __syncthreads();
+  return *s_len;
+}
+static_assert(kFusedSortMax == 16 * 32, "the fused sort holds at most 16 ids per lane");
+
 // Register caps (measured on B200): the renderer backward (with line spans) is held to 56
 // registers, 9 blocks of 128 threads per SM; the fit kernel without the density channel to 48,
 // 10 blocks (no spills; 76.7 -> 76.2 ms per 1024x768 / 50k-gaussian fit; 12 blocks spill and are
 // slower); the renderer forward without density to 48, 20 blocks of 64 threads (the reach masks
 // would take it to 64 registers; 1.73 -> 1.68 ms per 4K forward call with the cap).
-template <int PPT, int MODE, bool DEN>
+template <int PPT, int MODE, bool DEN, bool FUSE = false>
 __global__ void __launch_bounds__(Layout<PPT>::kThreads,
                                   MODE == kBwd ? 9 : (MODE == kFit && !DEN ? 10 : (MODE == kFwd && !DEN ? 20 : 0)))
 raster_kernel(const RasterArgs a) {
@@ -431,11 +511,27 @@ raster_kernel(const RasterArgs a) {
   const int sub_col = lane & 7, sub_row0 = PPT * (lane >> 3);
   const int64_t view_base = static_cast<int64_t>(view) * a.height * a.width;
   // The tile's ids in ascending order: list[range) (tile sort) or the sorted entries (radix path).
-  const int2 range = a.ranges[tile];
+  // The fit raster of a direct-placement iteration sorts its own tile's list into s_ids (then the
+  // list is [0, len) of s_ids); otherwise the list is ranges[tile] of the tile sort (or of the
+  // sorted entries on the radix path).
+  static_assert(!FUSE || MODE == kFit, "only the fit raster sorts its own tile");
+  __shared__ uint32_t s_ids[FUSE ? kFusedSortMax : 1];
+  __shared__ int s_fused_len;
+  int2 range;
+  if constexpr (FUSE) {
+    range = make_int2(0, fused_tile_sort(a.fit, a.list, tile, s_ids, &s_fused_len));
+  } else {
+    range = a.ranges[tile];
+  }
   // Stage records [base, base + n) of this tile's list into shared memory.
   auto stage = [&](int base, int n, bool with_entry) {
     for (int j = threadIdx.x; j < n; j += L::kThreads) {
-      const uint32_t gid = a.presorted ? static_cast<uint32_t>(a.entries[base + j]) : a.list[base + j];
+      uint32_t gid;
+      if constexpr (FUSE) {
+        gid = s_ids[base + j];
+      } else {
+        gid = a.presorted ? static_cast<uint32_t>(a.entries[base + j]) : a.list[base + j];
+      }
       const GaussRecord r = a.records[gid];
       s_geo[j] = r.geo;
       s_app[j] = r.app;
@@ -818,12 +914,12 @@ RasterArgs base_args(const BinBuffers& bb, const Geometry& g, float cutoff) {
   return a;
 }
 
-template <int MODE, bool DEN>
+template <int MODE, bool DEN, bool FUSE = false>
 int launch(const RasterArgs& a, const Geometry& g, cudaStream_t s, const char* name) {
   const int64_t n_tiles = g.n_tiles();
   if (n_tiles == 0) return 0;
   if (n_tiles > INT32_MAX) return set_error(-1, "too many tiles");
-  raster_kernel<kPPT<MODE>, MODE, DEN>
+  raster_kernel<kPPT<MODE>, MODE, DEN, FUSE>
       <<<static_cast<unsigned>(n_tiles), Layout<kPPT<MODE>>::kThreads, 0, s>>>(a);
   return check_cuda(cudaGetLastError(), name);
 }
@@ -864,10 +960,14 @@ int launch_raster_fit(BinBuffers& bb, const Geometry& g, float cutoff, const Fit
   RasterArgs a = base_args(bb, g, cutoff);
   a.partials = bb.partials.as<float4>();
   a.fit = fa;
+  const bool fuse = fa.seg != nullptr;
+  if (fuse && (!backward || !fa.cursor || !fa.stats)) return set_error(-1, "raster fit: incomplete own-sort arguments");
   if (backward && fa.coverage_coef > 0.f) {
     a.partial_d = bb.partial_d.as<float>();
+    if (fuse) return launch<kFit, true, true>(a, g, s, "raster fit (coverage, own sort)");
     return launch<kFit, true>(a, g, s, "raster fit (coverage)");
   }
+  if (backward && fuse) return launch<kFit, false, true>(a, g, s, "raster fit (own sort)");
   if (backward) return launch<kFit, false>(a, g, s, "raster fit");
   return launch<kEval, false>(a, g, s, "raster eval");
 }

@@ -281,16 +281,18 @@ class FitEngine:
         """Replay repeated 64-iteration chunks from a captured CUDA graph (default on)."""
         _native.check(self._lib.rtgs2d_fit_set_graphs(self._h, int(bool(enable))))
 
-    BINNING_MODES = {"auto": 0, "scatter": 1, "radix": 2, "tight": 3}
+    BINNING_MODES = {"auto": 0, "scatter": 1, "radix": 2, "tight": 3, "sorted": 4}
 
     def set_binning(self, mode: str = "auto") -> None:
         """How the fit loop bins (gaussian, tile) entries; every mode gives identical results.
 
         "auto": the first iteration of each 64-iteration chunk scatters its entries into tile
         lists, later projections place their ids directly into per-tile segments sized from the
-        previous binning (a full segment re-runs the chunk with "scatter"); "scatter" and "radix"
-        bin every iteration by scatter or by radix sort; "tight" is "auto" with segments of
-        exactly the previous counts, which overflow whenever a tile gains an entry.
+        previous binning (a full segment re-runs the chunk with "scatter") and the fit raster
+        sorts each tile's segment itself; "sorted" is "auto" with a separate per-tile sort kernel
+        before the raster; "scatter" and "radix" bin every iteration by scatter or by radix sort;
+        "tight" is "auto" with segments of exactly the previous counts, which overflow whenever a
+        tile gains an entry.
         """
         if mode not in self.BINNING_MODES:
             raise ValueError(f"binning mode must be one of {sorted(self.BINNING_MODES)}, got {mode!r}")

@@ -256,10 +256,11 @@ def test_graph_replay_matches_eager_chunks_bitwise():
 
 
 def test_binning_modes_give_identical_fits():
-    """Direct placement into per-tile segments, scatter and radix binning build the same sorted
-    tile lists, so fits end bitwise equal (history included). Tight segments (no slack) overflow
-    as soon as a tile gains an entry: those chunks re-run with scatter binning and still end equal;
-    a multi-view engine (two views' tiles in one binning) covers the view offsets of the segments."""
+    """Direct placement into per-tile segments (lists sorted by the fit raster itself, or by the
+    tile-sort kernel), scatter and radix binning build the same sorted tile lists, so fits end
+    bitwise equal (history included). Tight segments (no slack) overflow as soon as a tile gains an
+    entry: those chunks re-run with scatter binning and still end equal; a multi-view engine (two
+    views' tiles in one binning) covers the view offsets of the segments."""
     h, w, n, iters = 96, 128, 600, 200
     src = synthetic.source_gaussians(12, 40, h, w, (3.0, 12.0))
     target = (orender.render(src.xy, src.chol, src.color, src.weight, h, w)).clamp(0, 1).to(DEV)
@@ -269,7 +270,7 @@ def test_binning_modes_give_identical_fits():
         targets = torch.stack([target, target.flip(1)][:views])
         raws = {k: torch.stack([v] * views) for k, v in raw.items()}
         results = {}
-        for mode in ("auto", "scatter", "radix", "tight"):
+        for mode in ("auto", "sorted", "scatter", "radix", "tight"):
             with FitEngine(views, n, h, w, lr=1e-2, iterations=iters, log_every=25, device=DEV) as engine:
                 engine.set_binning(mode)
                 engine.set_targets(targets)
@@ -278,7 +279,8 @@ def test_binning_modes_give_identical_fits():
                 results[mode] = (engine.params(), engine.history(), engine.capacity()[1])
         p_a, h_a, _ = results["auto"]
         assert results["tight"][2] > 0  # overflowing segments re-ran chunks
-        for mode in ("scatter", "radix", "tight"):
+        assert results["auto"][2] == 0 and results["sorted"][2] == 0
+        for mode in ("sorted", "scatter", "radix", "tight"):
             p_m, h_m, _ = results[mode]
             for a, b in zip(p_a, p_m):
                 assert torch.equal(a, b), mode
@@ -299,14 +301,52 @@ def test_binning_modes_agree_above_single_block_scan_size():
         raws.append(raw_from_gaussians(*(x.to(DEV) for x in (init.xy, init.chol, init.color, init.weight)), h, w))
     raw = {k: torch.stack([r[k] for r in raws]) for k in raws[0]}
     results = {}
-    for mode in ("auto", "scatter"):
+    for mode in ("auto", "sorted", "scatter"):
         with FitEngine(views, n, h, w, lr=1e-2, iterations=iters, log_every=10, device=DEV) as engine:
             engine.set_binning(mode)
             engine.set_targets(torch.stack(targets))
             engine.set_raw(raw)
             engine.run(iters)
             results[mode] = (engine.params(), engine.history())
-    (p_a, h_a), (p_s, h_s) = results["auto"], results["scatter"]
+    p_a, h_a = results["auto"]
+    for mode in ("sorted", "scatter"):
+        p_s, h_s = results[mode]
+        for a, b in zip(p_a, p_s):
+            assert torch.equal(a, b), mode
+        assert np.array_equal(h_a[0], h_s[0]) and np.array_equal(h_a[1], h_s[1]), mode
+
+
+@pytest.mark.parametrize("n_crowd", [400, 700])
+def test_crowded_tile_lists_in_the_fit_raster_sort(n_crowd):
+    """Gaussians crowded into one 16x16 tile: with 400 the tile's list (257..512 ids) takes the fit
+    raster's shared-memory sort; with 700 it exceeds what the raster sorts itself, so the chunk
+    re-runs with the tile-sort kernel. Both fits end bitwise where the scatter-binned fit ends."""
+    h, w, iters = 64, 64, 70  # a full chunk of 64 and a tail of 6
+    gen = torch.Generator().manual_seed(40 + n_crowd)
+    n = n_crowd + 100
+    xy = torch.cat([16.0 + 16.0 * torch.rand(n_crowd, 2, generator=gen),
+                    torch.rand(100, 2, generator=gen) * torch.tensor([w - 1e-3, h - 1e-3])])
+    chol = torch.stack([0.5 + torch.rand(n, generator=gen), 0.1 * torch.randn(n, generator=gen),
+                        0.5 + torch.rand(n, generator=gen)], -1)
+    color, weight = torch.rand(n, 3, generator=gen), torch.full((n,), 0.5)
+    src = synthetic.source_gaussians(41, 30, h, w, (2.0, 8.0))
+    target = orender.render(src.xy, src.chol, src.color, src.weight, h, w).clamp(0, 1).to(DEV)
+    raw = raw_from_gaussians(*(x.to(DEV) for x in (xy, chol, color, weight)), h, w)
+    results = {}
+    for mode in ("auto", "scatter"):
+        with FitEngine(1, n, h, w, lr=1e-2, iterations=iters, log_every=10, device=DEV) as engine:
+            engine.set_binning(mode)
+            engine.set_targets(target[None])
+            engine.set_raw({k: v[None] for k, v in raw.items()})
+            engine.run(iters)
+            results[mode] = (engine.params(), engine.history(), engine.capacity()[1], engine.stats())
+    p_a, h_a, retries_a, stats_a = results["auto"]
+    p_s, h_s, _, _ = results["scatter"]
+    assert stats_a["last_entries"] > 0
+    if n_crowd > 512:
+        assert retries_a > 0  # the first direct chunk found a list above the raster's own sort
+    else:
+        assert retries_a == 0
     for a, b in zip(p_a, p_s):
         assert torch.equal(a, b)
     assert np.array_equal(h_a[0], h_s[0]) and np.array_equal(h_a[1], h_s[1])
