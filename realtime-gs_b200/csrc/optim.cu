@@ -157,15 +157,16 @@ adam_fit_kernel(int64_t m, int64_t cap, int* counts, const int* __restrict__ off
                 float* __restrict__ m1, float* __restrict__ m2,
                 const IterScalars* __restrict__ table, int k_iter, LossLog lg, int64_t n_per_view,
                 int tiles_x, int tiles_per_view, ProjOut o) {
+  // With direct placement this kernel is a programmatic dependent of the fit raster before it
+  // (launch_adam_fit): it may start while the raster still runs. Everything read before the
+  // griddepcontrol.wait below (the iteration's constants, the raw parameters and Adam moments, the
+  // previous projection's tile counts and entry offsets) was written before that raster started;
+  // the entry moments and tile losses are read after it. The next raster may launch right away: it
+  // waits for this kernel before it reads anything this kernel writes.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
   const AdamScalars a = table[k_iter].adam;
   const int log_slot = table[k_iter].log_slot;
-  if (log_slot >= 0) {  // the first blocks also log this iteration's loss, one view per block
-    for (int v = blockIdx.x; v < lg.n_views; v += gridDim.x) {
-      reduce_view_loss(lg.tile_loss, lg.tiles_per_view, v,
-                       lg.log + static_cast<int64_t>(log_slot) * lg.n_views * 2);
-    }
-  }
   const bool active = i < m;
   float r[kRawSlots], v1[kRawSlots], v2[kRawSlots];
   if (active) {
@@ -179,6 +180,13 @@ adam_fit_kernel(int64_t m, int64_t cap, int* counts, const int* __restrict__ off
   int cnt = active ? counts[i] : 0;
   const int off_any = active ? offsets[i] : 0;  // loaded together with counts[i], not after it
   const int off = cnt > 0 ? off_any : 0;
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the raster's entry moments and tile losses
+  if (log_slot >= 0) {  // the first blocks also log this iteration's loss, one view per block
+    for (int v = blockIdx.x; v < lg.n_views; v += gridDim.x) {
+      reduce_view_loss(lg.tile_loss, lg.tiles_per_view, v,
+                       lg.log + static_cast<int64_t>(log_slot) * lg.n_views * 2);
+    }
+  }
   cnt = clamp_to_capacity(cnt, off, cap);
   const Moments mo = gather_moments<DEN>(partials, partial_d, cnt, off);
 
@@ -310,12 +318,27 @@ int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_
     bb.counts_cleared = false;
     bb.entries_emitted = true;
   }
-  const unsigned grid = grid_for(m);
-#define RTGS_ADAM(P, D)                                                                            \
-  adam_fit_kernel<P, D><<<grid, kThreads, 0, s>>>(m, bb.capacity, bb.counts.as<int>(),             \
-                                                  bb.offsets.as<int>(), bb.partials.as<float4>(),  \
-                                                  pd, g.height, g.width, raw, m1, m2, table, k, lg, \
-                                                  n_per_view, g.tiles_x, g.tiles_per_view, o)
+  // With direct placement, a programmatic dependent launch of the fit raster before it: the blocks
+  // are scheduled during the raster's last wave and load what does not depend on it (the kernel
+  // waits before it reads the raster's output), which hides the launch gap and that round trip.
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid_for(m));
+  cfg.blockDim = dim3(kThreads);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = cursors ? 1 : 0;
+  const int64_t cap = bb.capacity;
+  int* counts = bb.counts.as<int>();
+  const int* offsets = bb.offsets.as<int>();
+  const float4* partials = bb.partials.as<float4>();
+#define RTGS_ADAM(P, D)                                                                              \
+  RTGS_CUDA(cudaLaunchKernelEx(&cfg, adam_fit_kernel<P, D>, m, cap, counts, offsets, partials, pd,  \
+                               g.height, g.width, raw, m1, m2, table, k, lg, n_per_view, g.tiles_x, \
+                               g.tiles_per_view, o),                                                 \
+            "adam_fit_kernel")
   if (project_next) {
     if (density) RTGS_ADAM(true, true); else RTGS_ADAM(true, false);
   } else {

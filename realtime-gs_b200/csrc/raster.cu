@@ -519,6 +519,12 @@ raster_kernel(const RasterArgs a) {
   __shared__ int s_fused_len;
   int2 range;
   if constexpr (FUSE) {
+    // Launched as a programmatic dependent of the Adam kernel before it (launch_raster_fit): the
+    // block may start while that kernel still runs, and waits here for it to complete (records,
+    // lists, cursors). Only after the wait does it let the next Adam kernel launch, so that the
+    // next Adam's early loads never overlap the writes of the Adam kernel before this raster.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     range = make_int2(0, fused_tile_sort(a.fit, a.list, tile, s_ids, &s_fused_len));
   } else {
     range = a.ranges[tile];
@@ -919,6 +925,20 @@ int launch(const RasterArgs& a, const Geometry& g, cudaStream_t s, const char* n
   const int64_t n_tiles = g.n_tiles();
   if (n_tiles == 0) return 0;
   if (n_tiles > INT32_MAX) return set_error(-1, "too many tiles");
+  if constexpr (FUSE) {
+    // Programmatic dependent launch: the blocks are scheduled while the Adam kernel before them
+    // finishes, which hides the launch gap between the two.
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(n_tiles));
+    cfg.blockDim = dim3(Layout<kPPT<MODE>>::kThreads);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return check_cuda(cudaLaunchKernelEx(&cfg, raster_kernel<kPPT<MODE>, MODE, DEN, FUSE>, a), name);
+  }
   raster_kernel<kPPT<MODE>, MODE, DEN, FUSE>
       <<<static_cast<unsigned>(n_tiles), Layout<kPPT<MODE>>::kThreads, 0, s>>>(a);
   return check_cuda(cudaGetLastError(), name);
