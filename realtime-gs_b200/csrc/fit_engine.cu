@@ -385,6 +385,7 @@ std::vector<uintptr_t> chunk_key(const rtgs2d_fit* f, int64_t chunk) {
   std::vector<uintptr_t> k = {static_cast<uintptr_t>(chunk), static_cast<uintptr_t>(radix(f)),
                               static_cast<uintptr_t>(bb.capacity), static_cast<uintptr_t>(f->use_active),
                               static_cast<uintptr_t>(direct_chunk(f)), static_cast<uintptr_t>(fused_sort(f)),
+                              static_cast<uintptr_t>(adam_single_wave(f->m, coverage(f))),
                               static_cast<uintptr_t>(f->unit_weight)};
   for (const DevBuf* b : {&bb.records, &bb.weights, &bb.spans, &bb.counts, &bb.offsets, &bb.list,
                           &bb.tile_count, &bb.tile_end, &bb.seg, &bb.cursor, &bb.tile_order, &bb.entries[0], &bb.entries[1], &bb.ranges,
@@ -421,6 +422,8 @@ int enqueue_chunk(rtgs2d_fit* f, int64_t chunk, cudaStream_t s, cudaEvent_t* ev,
   // buffers: the layout of iteration k writes buffer (k + 1) & 1 while raster k reads buffer k & 1.
   const bool direct = direct_chunk(f);
   const bool fuse = fused_sort(f);
+  // Raster and Adam as programmatic dependents of each other: only with a single wave of Adam blocks.
+  const bool pdl = fuse && adam_single_wave(f->m, coverage(f));
   if (direct) RTGS_TRY(ensure_side_stream(f));
   const int64_t n_tiles = f->geo.n_tiles();
   int* orders = bb.tile_order.as<int>();
@@ -449,6 +452,7 @@ int enqueue_chunk(rtgs2d_fit* f, int64_t chunk, cudaStream_t s, cudaEvent_t* ev,
         fk.seg = bb.seg.as<int2>() + cur * n_tiles;
         fk.cursor = bb.cursor.as<int>() + cur * n_tiles;
         fk.stats = bb.stats.as<unsigned long long>();
+        fk.pdl = pdl;
       }
     }
     RTGS_TRY(launch_raster_fit(bb, f->geo, kCutoff, fk, true, s));
@@ -457,7 +461,7 @@ int enqueue_chunk(rtgs2d_fit* f, int64_t chunk, cudaStream_t s, cudaEvent_t* ev,
     RTGS_TRY(launch_adam_fit(bb, f->geo, f->m, f->n, f->raw.as<float>(), f->m1.as<float>(),
                              f->m2.as<float>(), f->iter_table.as<IterScalars>(),
                              static_cast<int>(k), lg, k + 1 < chunk, active_rows(f), coverage(f),
-                             layout ? bb.cursor.as<int>() + next * n_tiles : nullptr, s));
+                             layout ? bb.cursor.as<int>() + next * n_tiles : nullptr, pdl, s));
     if (e) RTGS_CUDA(record(e[3]), "event record");
   }
   return 0;

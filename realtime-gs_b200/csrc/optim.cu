@@ -285,7 +285,7 @@ int launch_raw_grad(const BinBuffers& bb, int64_t m, int height, int width, cons
 int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_view, float* raw,
                     float* m1, float* m2, const IterScalars* table, int k, const LossLog& lg,
                     bool project_next, const uint8_t* active, bool density, int* cursors,
-                    cudaStream_t s) {
+                    bool pdl, cudaStream_t s) {
   if (m == 0) return 0;
   ProjOut o{};
   const float* pd = density ? bb.partial_d.as<float>() : nullptr;
@@ -318,9 +318,10 @@ int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_
     bb.counts_cleared = false;
     bb.entries_emitted = true;
   }
-  // With direct placement, a programmatic dependent launch of the fit raster before it: the blocks
-  // are scheduled during the raster's last wave and load what does not depend on it (the kernel
-  // waits before it reads the raster's output), which hides the launch gap and that round trip.
+  // With direct placement and `pdl`, a programmatic dependent launch of the fit raster before it:
+  // the blocks are scheduled during the raster's last wave and load what does not depend on it
+  // (the kernel waits before it reads the raster's output), which hides the launch gap and that
+  // round trip.
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid_for(m));
   cfg.blockDim = dim3(kThreads);
@@ -329,7 +330,7 @@ int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = cursors ? 1 : 0;
+  cfg.numAttrs = cursors && pdl ? 1 : 0;
   const int64_t cap = bb.capacity;
   int* counts = bb.counts.as<int>();
   const int* offsets = bb.offsets.as<int>();
@@ -346,6 +347,23 @@ int launch_adam_fit(BinBuffers& bb, const Geometry& g, int64_t m, int64_t n_per_
   }
 #undef RTGS_ADAM
   return check_cuda(cudaGetLastError(), "adam_fit_kernel");
+}
+
+bool adam_single_wave(int64_t m, bool density) {
+  int dev = 0, sms = 0, per_sm = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  const cudaError_t err = density
+      ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, adam_fit_kernel<true, true>, kThreads, 0)
+      : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, adam_fit_kernel<true, false>, kThreads, 0);
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return static_cast<int64_t>(grid_for(m)) <= static_cast<int64_t>(per_sm) * sms;
 }
 
 // ---- rtgs2d_adam_step: torch.optim.Adam's update over several tensors in one launch ----------

@@ -925,7 +925,7 @@ int launch(const RasterArgs& a, const Geometry& g, cudaStream_t s, const char* n
   const int64_t n_tiles = g.n_tiles();
   if (n_tiles == 0) return 0;
   if (n_tiles > INT32_MAX) return set_error(-1, "too many tiles");
-  if constexpr (FUSE) {
+  if (FUSE && a.fit.pdl) {
     // Programmatic dependent launch: the blocks are scheduled while the Adam kernel before them
     // finishes, which hides the launch gap between the two.
     cudaLaunchConfig_t cfg{};
