@@ -394,19 +394,20 @@ __device__ __forceinline__ void sort_ids_to_shared(const uint32_t* src, int len,
 }
 
 __device__ __forceinline__ int fused_tile_sort(const FitRasterArgs& f, const uint32_t* list, int tile,
-                                               uint32_t* s_ids, int* s_len) {
+                                               int2 sg, uint32_t* s_ids, int* s_len) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0) {
-    int sx = 0, sy = 0, cur = 0;
-    if (lane == 0) {
-      const int2 sg = f.seg[tile];
-      sx = sg.x;
-      sy = sg.y;
-      cur = f.cursor[tile];
+    // The segment (sg, read before the wait) bounds the list, so the cursor and the segment's
+    // first 128 slots are loaded in one round trip; slots past the count are ignored.
+    const int sx = sg.x, sy = sg.y;
+    constexpr int kPre = 4;
+    uint32_t pre[kPre];
+    const int cur = f.cursor[tile];
+#pragma unroll
+    for (int e = 0; e < kPre; ++e) {
+      const int i = e * 32 + lane;
+      pre[e] = i < sy ? list[sx + i] : 0xffffffffu;
     }
-    sx = __shfl_sync(0xffffffffu, sx, 0);
-    sy = __shfl_sync(0xffffffffu, sy, 0);
-    cur = __shfl_sync(0xffffffffu, cur, 0);
     const int filled = cur - sx;
     const int len = max(min(filled, sy), 0);
     if (lane == 0) {
@@ -414,13 +415,28 @@ __device__ __forceinline__ int fused_tile_sort(const FitRasterArgs& f, const uin
       if (len > kFusedSortMax) atomicMax(&f.stats[kStatFusedLong], static_cast<unsigned long long>(len));
       *s_len = len <= kFusedSortMax ? len : 0;
     }
+#pragma unroll
+    for (int e = 0; e < kPre; ++e) {
+      if (e * 32 + lane >= len) pre[e] = 0xffffffffu;
+    }
     const uint32_t* src = list + sx;
     if (len <= 32) {
-      sort_ids_to_shared<1>(src, len, s_ids, lane);
+      uint32_t v[1] = {pre[0]};
+      warp_sort_striped<1>(v, lane);
+      if (lane < len) s_ids[lane] = v[0];
     } else if (len <= 64) {
-      sort_ids_to_shared<2>(src, len, s_ids, lane);
+      uint32_t v[2] = {pre[0], pre[1]};
+      warp_sort_striped<2>(v, lane);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        if (e * 32 + lane < len) s_ids[e * 32 + lane] = v[e];
+      }
     } else if (len <= 128) {
-      sort_ids_to_shared<4>(src, len, s_ids, lane);
+      warp_sort_striped<4>(pre, lane);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (e * 32 + lane < len) s_ids[e * 32 + lane] = pre[e];
+      }
     } else if (len <= 256) {
       sort_ids_to_shared<8>(src, len, s_ids, lane);
     } else if (len <= kFusedSortMax) {
@@ -488,7 +504,9 @@ raster_kernel(const RasterArgs a) {
   constexpr bool kEllMask = MODE == kFwd && PPT == 4;
   __shared__ double s_loss[L::kWarps][2];
 
-  const int tile = a.fit.tile_order ? a.fit.tile_order[blockIdx.x] : static_cast<int>(blockIdx.x);
+  // The tile order is read from L2 (__ldcg): the fit raster may run before its predecessor ends
+  // (programmatic dependent launch), and the order's buffer was read two iterations ago.
+  const int tile = a.fit.tile_order ? __ldcg(&a.fit.tile_order[blockIdx.x]) : static_cast<int>(blockIdx.x);
   const int view = tile / a.tiles_per_view;
   const int tin = tile - view * a.tiles_per_view;
   const int tile_y = tin / a.tiles_x;
@@ -523,9 +541,13 @@ raster_kernel(const RasterArgs a) {
     // block may start while that kernel still runs, and waits here for it to complete (records,
     // lists, cursors). Only after the wait does it let the next Adam kernel launch, so that the
     // next Adam's early loads never overlap the writes of the Adam kernel before this raster.
+    // The tile's segment comes from the segment layout, which completed before the Adam kernel
+    // started: read it before the wait (from L2: its buffer was read two iterations ago).
+    int2 sg = make_int2(0, 0);
+    if (threadIdx.x < 32) sg = __ldcg(&a.fit.seg[tile]);
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    range = make_int2(0, fused_tile_sort(a.fit, a.list, tile, s_ids, &s_fused_len));
+    range = make_int2(0, fused_tile_sort(a.fit, a.list, tile, sg, s_ids, &s_fused_len));
   } else {
     range = a.ranges[tile];
   }
