@@ -21,13 +21,15 @@
 //               Sxy = sum dq*dx*dy, Syy = sum dq*dy^2, Sr/Sg/Sb = sum e*g_rgb
 //               (e = exp(-q/2), dq = e * g.A; Gx, Gy are the mean gradient's sums)
 //             are written once per entry. Pieces are ordered by (orientation, step count) with a
-//             stable counting sort; a warp takes 4 pieces at a time, 8 lanes ("octet") per piece,
-//             each lane owning up to two columns (wide pieces, stepping down the rows) or two rows
-//             (tall pieces, stepping across the columns). In the renderer backward a lane steps
-//             only through the conservative span where its lines can meet the support ellipse
-//             (line_span; the exact support test still runs on every pixel), and the step count
-//             that orders the pieces is the longest lane's. An 8-lane transpose butterfly leaves
-//             moment r in lane r of each octet: one 32-byte store per entry. A per-gaussian pass
+//             stable counting sort; in the fused fit kernel a warp takes 4 pieces at a time, 8
+//             lanes ("octet") per piece, each lane owning up to two columns (wide pieces, stepping
+//             down the rows) or two rows (tall pieces, stepping across the columns), and an 8-lane
+//             transpose butterfly leaves moment r in lane r of each octet: one 32-byte store per
+//             entry. The renderer backward takes 8 pieces at a time, 4 lanes ("quad") per piece,
+//             each lane owning up to four lines (backward_quad; the quad's transpose leaves moments
+//             2q, 2q + 1 in lane q), and a lane steps only through the conservative span where its
+//             lines can meet the support ellipse (line_span; the exact support test still runs on
+//             every pixel); the step count that orders the pieces is the longest lane's. A per-gaussian pass
 //             (optim.cu) sums a gaussian's entries in order and applies the chain rule:
 //             deterministic, no global atomics.
 //   fit       forward -> L2 loss gradient in registers -> backward, in one kernel: the rendered
@@ -371,6 +373,167 @@ __device__ __forceinline__ void backward_piece(const float4& geo, const float4& 
   S[4] = ROW ? m_vv : m_ff;  // sum dq dy^2
 }
 
+// Renderer backward: quad tasks. A warp takes 8 pieces at a time, 4 lanes ("quad") per piece,
+// each lane owning up to four lines of its piece (lines q, q + 4, q + 8, q + 12 of the lane axis):
+// the per-piece work outside the pixel loop (work-list entry, piece decode, setup, reduction,
+// store) is shared by twice as many pieces per warp as with octets, which at 4K is a third of the
+// backward. Spans per quad lane, packed in two words: word 0 = start | first0 << 4 | len0 << 8 |
+// first1 << 13 | len1 << 17, word 1 = first2 | len2 << 4 | first3 << 9 | len3 << 13 (first: the
+// line's first step after start, len: its step count; line_span as for the octets).
+__device__ __forceinline__ int piece_quads(const float4& geo, const float4& app, int pc, int ox,
+                                           int oy, float cutoff, uint32_t* out) {
+  const int rx0 = pc & 15, ry0 = (pc >> 4) & 15;
+  const int pw = ((pc >> 8) & 15) + 1, ph = ((pc >> 12) & 15) + 1;
+  const bool row = pw >= ph;
+  const int lane_dim = row ? pw : ph, step_dim = row ? ph : pw;
+  const float pxc0 = static_cast<float>(ox + rx0) + 0.5f;
+  const float pyc0 = static_cast<float>(oy + ry0) + 0.5f;
+  const float fix0 = row ? pxc0 : pyc0;
+  const float mean_fix = row ? geo.x : geo.y;
+  LineCoef lc = line_coef(row ? geo.z : app.x, row ? app.x : geo.z, geo.w, row ? geo.y : geo.x,
+                          row ? pyc0 : pxc0, cutoff);
+  lc.pd = lc.pd && step_dim >= kSpanMinSteps;
+  int longest = 0;
+  for (int q = 0; q < 4; ++q) {
+    int lo[4], hi[4];
+    int start = 16;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int line = q + 4 * m;
+      lo[m] = 0;
+      hi[m] = line < lane_dim ? step_dim - 1 : -1;
+      const float d = __fsub_rn(fix0 + static_cast<float>(line), mean_fix);
+      line_span(lc, d, __fmul_rn(d, d), step_dim, lo[m], hi[m]);
+      if (lo[m] <= hi[m]) start = min(start, lo[m]);
+    }
+    if (start == 16) start = 0;
+    uint32_t f[4], n[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const bool has = lo[m] <= hi[m];
+      f[m] = has ? static_cast<uint32_t>(lo[m] - start) : 0u;
+      n[m] = has ? static_cast<uint32_t>(hi[m] - lo[m] + 1) : 0u;
+      longest = max(longest, static_cast<int>(f[m] + n[m]));
+    }
+    out[2 * q] = static_cast<uint32_t>(start) | f[0] << 4 | n[0] << 8 | f[1] << 13 | n[1] << 17;
+    out[2 * q + 1] = f[2] | n[2] << 4 | f[3] << 9 | n[3] << 13;
+  }
+  return longest;
+}
+
+// One quad lane's part of a renderer-backward piece: the octet's backward_piece with four lines
+// per lane (same rounding of q, same centred moments), each line centred on the ellipse's centre
+// along it and with its own accumulators (sums of the same length as an octet lane's; with one
+// centre and one second-moment sum shared by the four lines, the band test's worst Cholesky
+// gradient error was 2.5 times the float32 reference's). Lines B, C, D run only when some lane of
+// the warp has one (any_b, any_c, any_d).
+template <bool ROW, bool DEN>
+__device__ __forceinline__ void backward_quad(const float4& geo, const float4& app, float wt,
+                                              float pxc0, float pyc0, int sidx0, int q4, int start,
+                                              const unsigned (&first)[4], const unsigned (&len)[4],
+                                              bool any_b, bool any_c, bool any_d, int max_steps,
+                                              float cutoff, const float4* s_g, float (&S)[8],
+                                              float& Sd) {
+  const float fix_base = (ROW ? pxc0 : pyc0) + static_cast<float>(q4);
+  const float mean_fix = ROW ? geo.x : geo.y;
+  const float coef_fix = ROW ? geo.z : app.x;
+  const float coef_var = ROW ? app.x : geo.z;
+  float d[4], t[4];
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    d[m] = __fsub_rn(fix_base + static_cast<float>(4 * m), mean_fix);
+    t[m] = __fmul_rn(__fmul_rn(d[m], d[m]), coef_fix);
+  }
+  const float i01 = 0.5f * geo.w;
+  float kappa = -__fdividef(i01, coef_var);
+  kappa = isfinite(kappa) ? kappa : 0.f;
+  constexpr int kStep = ROW ? kGStride : 1;
+  constexpr int kLaneStride = ROW ? 1 : kGStride;
+  unsigned count = 0;
+  bool has[4];
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    count = max(count, first[m] + len[m]);
+    has[m] = len[m] > 0;
+  }
+  const bool any[4] = {true, any_b, any_c, any_d};
+  int sidx = sidx0 + q4 * kLaneStride + start * kStep;
+  float fvar = (ROW ? pyc0 : pxc0) + static_cast<float>(start);
+  float P0[4] = {0.f, 0.f, 0.f, 0.f}, P1[4] = {0.f, 0.f, 0.f, 0.f}, P2[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int st = 0; st < max_steps; ++st) {
+    const float dv = __fsub_rn(fvar, ROW ? geo.y : geo.x);
+    const float sq_v = __fmul_rn(dv, dv);
+    const float t_v = __fmul_rn(sq_v, coef_var);
+    const bool on = static_cast<unsigned>(st) < count;
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      if (!any[m]) continue;
+      const float t1 = __fmul_rn(__fmul_rn(d[m], dv), geo.w);
+      const float q = ROW ? __fadd_rn(__fadd_rn(t[m], t1), t_v) : __fadd_rn(__fadd_rn(t_v, t1), t[m]);
+      const bool in = on && has[m] && q < cutoff;
+      float4 gv = make_float4(0.f, 0.f, 0.f, 0.f);
+      float e = 0.f, dq = 0.f;
+      if (in) {
+        gv = s_g[sidx + 4 * m * kLaneStride];
+        e = falloff(q);
+        float v = gv.x * app.y;
+        v = fmaf(gv.y, app.z, v);
+        v = fmaf(gv.z, app.w, v);
+        if constexpr (DEN) v = fmaf(gv.w, wt, v);
+        dq = e * v;
+      }
+      P0[m] += dq;
+      P1[m] = fmaf(dq, fmaf(-kappa, d[m], dv), P1[m]);  // offset from the line's ellipse centre
+      P2[m] = fmaf(dq, sq_v, P2[m]);
+      S[5] = fmaf(e, gv.x, S[5]);
+      S[6] = fmaf(e, gv.y, S[6]);
+      S[7] = fmaf(e, gv.z, S[7]);
+      if constexpr (DEN) Sd = fmaf(e, gv.w, Sd);
+    }
+    fvar += 1.f;
+    sidx += kStep;
+  }
+  const float cx_fix = ROW ? geo.z : i01, cx_var = ROW ? i01 : geo.z;
+  const float cy_fix = ROW ? i01 : app.x, cy_var = ROW ? app.x : i01;
+  float s0 = 0.f, s1 = 0.f, p1 = 0.f, m_ff = 0.f, m_fv = 0.f, m_vv = 0.f;
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    const float vc = kappa * d[m];  // the ellipse's centre along line m (varying-axis offset)
+    s0 = fmaf(fmaf(cx_var, vc, cx_fix * d[m]), P0[m], s0);
+    s1 = fmaf(fmaf(cy_var, vc, cy_fix * d[m]), P0[m], s1);
+    p1 += P1[m];
+    m_ff = fmaf(__fmul_rn(d[m], d[m]), P0[m], m_ff);
+    m_fv = fmaf(d[m], fmaf(vc, P0[m], P1[m]), m_fv);
+    m_vv += P2[m];
+  }
+  S[0] = fmaf(cx_var, p1, s0);
+  S[1] = fmaf(cy_var, p1, s1);
+  S[2] = ROW ? m_ff : m_vv;  // sum dq dx^2
+  S[3] = m_fv;               // sum dq dx dy
+  S[4] = ROW ? m_vv : m_ff;  // sum dq dy^2
+}
+
+// Sum of v[k] over the 4 lanes of a quad, transposed: lane q of the quad returns moments 2q and
+// 2q + 1 (two shuffle rounds).
+__device__ __forceinline__ float2 quad_transpose_reduce8(const float (&v)[8], int lane) {
+  const bool u2 = lane & 2, u1 = lane & 1;
+  float a[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float send = u2 ? v[k] : v[k + 4];
+    const float keep = u2 ? v[k + 4] : v[k];
+    a[k] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  float b[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const float send = u1 ? a[k] : a[k + 2];
+    const float keep = u1 ? a[k + 2] : a[k];
+    b[k] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+  }
+  return make_float2(b[0], b[1]);
+}
+
 // Fused tile sort of the fit raster (direct placement): warp 0 reads tile `tile`'s segment and
 // cursor, flags a segment overrun (stats[kStatSegOverflow]) or a list above kFusedSortMax
 // (stats[kStatFusedLong]: the chunk re-runs with the separate tile-sort kernel), sorts the list
@@ -465,14 +628,15 @@ __device__ __forceinline__ int fused_tile_sort(const FitRasterArgs& f, const uin
 }
 static_assert(kFusedSortMax == 16 * 32, "the fused sort holds at most 16 ids per lane");
 
-// Register caps (measured on B200): the renderer backward (with line spans) is held to 56
-// registers, 9 blocks of 128 threads per SM; the fit kernel without the density channel to 48,
+// Register caps (measured on B200): the renderer backward (quad tasks with line spans) is held to
+// 64 registers, 8 blocks of 128 threads per SM (4K splat backward 2.56 ms; held to 56 registers,
+// 9 blocks, it takes 2.99 ms); the fit kernel without the density channel to 48,
 // 10 blocks (no spills; 76.7 -> 76.2 ms per 1024x768 / 50k-gaussian fit; 12 blocks spill and are
 // slower); the renderer forward without density to 48, 20 blocks of 64 threads (the reach masks
 // would take it to 64 registers; 1.73 -> 1.68 ms per 4K forward call with the cap).
 template <int PPT, int MODE, bool DEN, bool FUSE = false>
 __global__ void __launch_bounds__(Layout<PPT>::kThreads,
-                                  MODE == kBwd ? 9 : (MODE == kFit && !DEN ? 10 : (MODE == kFwd && !DEN ? 20 : 0)))
+                                  MODE == kBwd ? 8 : (MODE == kFit && !DEN ? 10 : (MODE == kFwd && !DEN ? 20 : 0)))
 raster_kernel(const RasterArgs a) {
   using L = Layout<PPT>;
   constexpr bool kDoFwd = MODE != kBwd;
@@ -799,7 +963,7 @@ raster_kernel(const RasterArgs a) {
       if (jb < n) {
         const int pc = s_piece[jb];
         if constexpr (kSpans) {
-          bucket = piece_bucket_spans(pc, piece_lanes(s_geo[jb], s_app[jb], pc, ox, oy, a.cutoff, &s_lanes[8 * jb]));
+          bucket = piece_bucket_spans(pc, piece_quads(s_geo[jb], s_app[jb], pc, ox, oy, a.cutoff, &s_lanes[8 * jb]));
         } else {
           bucket = piece_bucket(pc);
         }
@@ -839,70 +1003,142 @@ raster_kernel(const RasterArgs a) {
       if (bucket < kNB) s_list[s_wcount[warp][bucket] + rank] = jb;
       __syncthreads();
 
-      const int n_tasks = (n + 3) >> 2;
-      while (true) {
-        int task = 0;
-        if (lane == 0) task = atomicAdd(&s_next, 1);
-        task = __shfl_sync(0xffffffffu, task, 0);
-        if (task >= n_tasks) break;
-        const int p = 4 * task + (lane >> 3);
-        const bool valid = p < n;
-        const int j = valid ? s_list[p] : s_list[0];
-        const float4 geo = s_geo[j];
-        const float4 app = s_app[j];
-        const int pc = s_piece[j];
-        const int rx0 = pc & 15, ry0 = (pc >> 4) & 15;
-        const int pw = ((pc >> 8) & 15) + 1, ph = ((pc >> 12) & 15) + 1;
-        // The task runs in the orientation of its first piece (the bucket order groups pieces of
-        // one orientation): row-wise, each octet lane owns columns r8 and r8 + 8 of its piece and
-        // steps down the rows; column-wise, rows r8 and r8 + 8, stepping across the columns. Any
-        // piece is correct in either orientation: one of the other orientation (a task across the
-        // boundary of the two bucket groups) walks whole lines.
-        const bool row = __shfl_sync(0xffffffffu, pw >= ph, 0);
-        const int lane_dim = row ? pw : ph, step_dim = row ? ph : pw;
-        // Steps of the lane: whole lines (start 0, pixels on for the piece's step count), or the
-        // ellipse line spans that piece_lanes packed (its own orientation only).
-        const int my_steps = valid ? step_dim : 0;
-        int start = 0;
-        unsigned a_first = 0, a_len = r8 < lane_dim ? my_steps : 0;
-        unsigned b_first = 0, b_len = r8 + 8 < lane_dim ? my_steps : 0;
-        int max_steps;
-        if constexpr (kSpans) {
-          if (valid && (pw >= ph) == row) {
-            const uint32_t w = s_lanes[8 * j + r8];
-            start = w & 15;
-            a_first = (w >> 4) & 15;
-            a_len = (w >> 8) & 31;
-            b_first = (w >> 13) & 15;
-            b_len = (w >> 17) & 31;
+      if constexpr (MODE == kBwd) {
+        // Quad tasks: 8 pieces per warp, 4 lanes each (backward_quad).
+        const int q4 = lane & 3;
+        const int n_tasks = (n + 7) >> 3;
+        while (true) {
+          int task = 0;
+          if (lane == 0) task = atomicAdd(&s_next, 1);
+          task = __shfl_sync(0xffffffffu, task, 0);
+          if (task >= n_tasks) break;
+          const int p = 8 * task + (lane >> 2);
+          const bool valid = p < n;
+          const int j = valid ? s_list[p] : s_list[0];
+          const float4 geo = s_geo[j];
+          const float4 app = s_app[j];
+          const int pc = s_piece[j];
+          const int rx0 = pc & 15, ry0 = (pc >> 4) & 15;
+          const int pw = ((pc >> 8) & 15) + 1, ph = ((pc >> 12) & 15) + 1;
+          // As for the octets: the task runs in its first piece's orientation; a piece of the
+          // other orientation walks whole lines.
+          const bool row = __shfl_sync(0xffffffffu, pw >= ph, 0);
+          const int lane_dim = row ? pw : ph, step_dim = row ? ph : pw;
+          int start = 0;
+          unsigned first[4] = {0u, 0u, 0u, 0u}, len[4];
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            len[m] = valid && q4 + 4 * m < lane_dim ? static_cast<unsigned>(step_dim) : 0u;
           }
-          max_steps = static_cast<int>(__reduce_max_sync(0xffffffffu, max(a_first + a_len, b_first + b_len)));
-        } else {
-          max_steps = static_cast<int>(__reduce_max_sync(0xffffffffu, static_cast<unsigned>(my_steps)));
+          if (valid && (pw >= ph) == row) {
+            const uint32_t w0 = s_lanes[8 * j + 2 * q4], w1 = s_lanes[8 * j + 2 * q4 + 1];
+            start = w0 & 15;
+            first[0] = (w0 >> 4) & 15;
+            len[0] = (w0 >> 8) & 31;
+            first[1] = (w0 >> 13) & 15;
+            len[1] = (w0 >> 17) & 31;
+            first[2] = w1 & 15;
+            len[2] = (w1 >> 4) & 31;
+            first[3] = (w1 >> 9) & 15;
+            len[3] = (w1 >> 13) & 31;
+          }
+          unsigned count = 0;
+#pragma unroll
+          for (int m = 0; m < 4; ++m) count = max(count, first[m] + len[m]);
+          const int max_steps = static_cast<int>(__reduce_max_sync(0xffffffffu, count));
+          const bool any_b = __any_sync(0xffffffffu, len[1] > 0);
+          const bool any_c = __any_sync(0xffffffffu, len[2] > 0);
+          const bool any_d = __any_sync(0xffffffffu, len[3] > 0);
+          const float pxc0 = static_cast<float>(ox + rx0) + 0.5f;
+          const float pyc0 = static_cast<float>(oy + ry0) + 0.5f;
+          float wt = 0.f;
+          if constexpr (DEN) wt = s_wt[j];
+          float S[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          float Sd = 0.f;
+          if (row) {
+            backward_quad<true, DEN>(geo, app, wt, pxc0, pyc0, ry0 * kGStride + rx0, q4, start, first, len,
+                                     any_b, any_c, any_d, max_steps, a.cutoff, s_g, S, Sd);
+          } else {
+            backward_quad<false, DEN>(geo, app, wt, pxc0, pyc0, ry0 * kGStride + rx0, q4, start, first, len,
+                                      any_b, any_c, any_d, max_steps, a.cutoff, s_g, S, Sd);
+          }
+          const float2 red = quad_transpose_reduce8(S, lane);
+          const int64_t e = s_entry[j];
+          // Entries outside [0, capacity) belong to a dropped binning.
+          const bool store = valid && e >= 0 && e < a.cap;
+          if (store) reinterpret_cast<float2*>(partials_f + 8 * e)[q4] = red;
+          if constexpr (DEN) {
+            Sd += __shfl_xor_sync(0xffffffffu, Sd, 2);
+            Sd += __shfl_xor_sync(0xffffffffu, Sd, 1);
+            if (store && q4 == 0) a.partial_d[e] = Sd;
+          }
         }
-        const bool any_b = __any_sync(0xffffffffu, b_len > 0);
-        const float pxc0 = static_cast<float>(ox + rx0) + 0.5f;  // integer + 0.5 sums stay exact
-        const float pyc0 = static_cast<float>(oy + ry0) + 0.5f;
-        float wt = 0.f;
-        if constexpr (DEN) wt = s_wt[j];
-        float S[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        float Sd = 0.f;
-#define RTGS_PIECE(R)                                                                                  \
-  backward_piece<R, DEN, MODE == kBwd>(geo, app, wt, pxc0, pyc0, ry0 * kGStride + rx0, r8, start,   \
-                                       a_first, a_len, b_first, b_len, any_b, max_steps, a.cutoff,  \
-                                       s_g, S, Sd)
-        if (row) RTGS_PIECE(true); else RTGS_PIECE(false);
-#undef RTGS_PIECE
-        const float red = octet_transpose_reduce8(S, lane);
-        const int64_t e = s_entry[j];
-        // Entries outside [0, capacity) belong to a dropped binning.
-        const bool store = valid && e >= 0 && e < a.cap;
-        if (store) partials_f[8 * e + r8] = red;
-        if constexpr (DEN) {
-          Sd += __shfl_xor_sync(0xffffffffu, Sd, 4);
-          Sd += __shfl_xor_sync(0xffffffffu, Sd, 2);
-          Sd += __shfl_xor_sync(0xffffffffu, Sd, 1);
-          if (store && r8 == 0) a.partial_d[e] = Sd;
+      } else {
+        const int n_tasks = (n + 3) >> 2;
+        while (true) {
+          int task = 0;
+          if (lane == 0) task = atomicAdd(&s_next, 1);
+          task = __shfl_sync(0xffffffffu, task, 0);
+          if (task >= n_tasks) break;
+          const int p = 4 * task + (lane >> 3);
+          const bool valid = p < n;
+          const int j = valid ? s_list[p] : s_list[0];
+          const float4 geo = s_geo[j];
+          const float4 app = s_app[j];
+          const int pc = s_piece[j];
+          const int rx0 = pc & 15, ry0 = (pc >> 4) & 15;
+          const int pw = ((pc >> 8) & 15) + 1, ph = ((pc >> 12) & 15) + 1;
+          // The task runs in the orientation of its first piece (the bucket order groups pieces of
+          // one orientation): row-wise, each octet lane owns columns r8 and r8 + 8 of its piece and
+          // steps down the rows; column-wise, rows r8 and r8 + 8, stepping across the columns. Any
+          // piece is correct in either orientation: one of the other orientation (a task across the
+          // boundary of the two bucket groups) walks whole lines.
+          const bool row = __shfl_sync(0xffffffffu, pw >= ph, 0);
+          const int lane_dim = row ? pw : ph, step_dim = row ? ph : pw;
+          // Steps of the lane: whole lines (start 0, pixels on for the piece's step count), or the
+          // ellipse line spans that piece_lanes packed (its own orientation only).
+          const int my_steps = valid ? step_dim : 0;
+          int start = 0;
+          unsigned a_first = 0, a_len = r8 < lane_dim ? my_steps : 0;
+          unsigned b_first = 0, b_len = r8 + 8 < lane_dim ? my_steps : 0;
+          int max_steps;
+          if constexpr (kSpans) {
+            if (valid && (pw >= ph) == row) {
+              const uint32_t w = s_lanes[8 * j + r8];
+              start = w & 15;
+              a_first = (w >> 4) & 15;
+              a_len = (w >> 8) & 31;
+              b_first = (w >> 13) & 15;
+              b_len = (w >> 17) & 31;
+            }
+            max_steps = static_cast<int>(__reduce_max_sync(0xffffffffu, max(a_first + a_len, b_first + b_len)));
+          } else {
+            max_steps = static_cast<int>(__reduce_max_sync(0xffffffffu, static_cast<unsigned>(my_steps)));
+          }
+          const bool any_b = __any_sync(0xffffffffu, b_len > 0);
+          const float pxc0 = static_cast<float>(ox + rx0) + 0.5f;  // integer + 0.5 sums stay exact
+          const float pyc0 = static_cast<float>(oy + ry0) + 0.5f;
+          float wt = 0.f;
+          if constexpr (DEN) wt = s_wt[j];
+          float S[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          float Sd = 0.f;
+  #define RTGS_PIECE(R)                                                                                  \
+    backward_piece<R, DEN, MODE == kBwd>(geo, app, wt, pxc0, pyc0, ry0 * kGStride + rx0, r8, start,   \
+                                         a_first, a_len, b_first, b_len, any_b, max_steps, a.cutoff,  \
+                                         s_g, S, Sd)
+          if (row) RTGS_PIECE(true); else RTGS_PIECE(false);
+  #undef RTGS_PIECE
+          const float red = octet_transpose_reduce8(S, lane);
+          const int64_t e = s_entry[j];
+          // Entries outside [0, capacity) belong to a dropped binning.
+          const bool store = valid && e >= 0 && e < a.cap;
+          if (store) partials_f[8 * e + r8] = red;
+          if constexpr (DEN) {
+            Sd += __shfl_xor_sync(0xffffffffu, Sd, 4);
+            Sd += __shfl_xor_sync(0xffffffffu, Sd, 2);
+            Sd += __shfl_xor_sync(0xffffffffu, Sd, 1);
+            if (store && r8 == 0) a.partial_d[e] = Sd;
+          }
         }
       }
     }
