@@ -142,7 +142,7 @@ __device__ __forceinline__ int piece_bucket(int pc) {
   return pw >= ph ? kTile - ph : 2 * kTile - pw;
 }
 
-// The same order with the step count of the longest lane's line spans (piece_lanes).
+// The same order with the step count of the longest lane's line spans (piece_quads).
 __device__ __forceinline__ int piece_bucket_spans(int pc, int steps) {
   const int pw = ((pc >> 8) & 15) + 1, ph = ((pc >> 12) & 15) + 1;
   return (pw >= ph ? kTile : 2 * kTile) - max(steps, 1);
@@ -209,42 +209,6 @@ __device__ __forceinline__ void line_span(const LineCoef& c, float d, float dsq,
   hi = static_cast<int>(fmaxf(fminf(floorf(ctr + half), static_cast<float>(steps - 1)), -1.f));
 }
 
-// Step ranges of one backward piece for each of its 8 octet lanes, packed in one word per lane:
-// bits 0-3 the lane's first step, 4-7 pixel A's first step after it, 8-12 A's step count, 13-16
-// B's first step after the lane's, 17-21 B's count (pixel A = lane-axis line r, B = line r + 8).
-// Pieces with at least kSpanMinSteps steps and a positive definite conic get the line spans of the
-// support ellipse (line_span); others walk their whole lines. Returns the longest lane's steps.
-__device__ __forceinline__ int piece_lanes(const float4& geo, const float4& app, int pc, int ox,
-                                           int oy, float cutoff, uint32_t* out) {
-  const int rx0 = pc & 15, ry0 = (pc >> 4) & 15;
-  const int pw = ((pc >> 8) & 15) + 1, ph = ((pc >> 12) & 15) + 1;
-  const bool row = pw >= ph;
-  const int lane_dim = row ? pw : ph, step_dim = row ? ph : pw;
-  const float pxc0 = static_cast<float>(ox + rx0) + 0.5f;  // integer + 0.5 sums stay exact
-  const float pyc0 = static_cast<float>(oy + ry0) + 0.5f;
-  const float fix0 = row ? pxc0 : pyc0;
-  const float mean_fix = row ? geo.x : geo.y;
-  LineCoef lc = line_coef(row ? geo.z : app.x, row ? app.x : geo.z, geo.w, row ? geo.y : geo.x,
-                          row ? pyc0 : pxc0, cutoff);
-  lc.pd = lc.pd && step_dim >= kSpanMinSteps;
-  int longest = 0;
-  for (int r = 0; r < 8; ++r) {
-    int lo_a = 0, hi_a = r < lane_dim ? step_dim - 1 : -1;
-    int lo_b = 0, hi_b = r + 8 < lane_dim ? step_dim - 1 : -1;
-    const float da = __fsub_rn(fix0 + static_cast<float>(r), mean_fix);
-    const float db = __fsub_rn(fix0 + static_cast<float>(r + 8), mean_fix);
-    line_span(lc, da, __fmul_rn(da, da), step_dim, lo_a, hi_a);
-    line_span(lc, db, __fmul_rn(db, db), step_dim, lo_b, hi_b);
-    const bool has_a = lo_a <= hi_a, has_b = lo_b <= hi_b;
-    const int start = has_a ? (has_b ? min(lo_a, lo_b) : lo_a) : (has_b ? lo_b : 0);
-    const int a_first = has_a ? lo_a - start : 0, a_len = has_a ? hi_a - lo_a + 1 : 0;
-    const int b_first = has_b ? lo_b - start : 0, b_len = has_b ? hi_b - lo_b + 1 : 0;
-    out[r] = static_cast<uint32_t>(start | a_first << 4 | a_len << 8 | b_first << 13 | b_len << 17);
-    longest = max(longest, max(a_first + a_len, b_first + b_len));
-  }
-  return longest;
-}
-
 // One octet lane's part of a backward piece: up to two pixels per step along the lane axis
 // (a = r8 and r8 + 8) and, along the other axis (rows when ROW, columns otherwise), the lane's
 // steps start .. start + max(a_first + a_len, b_first + b_len) - 1 (pixel A on for a_len steps
@@ -252,23 +216,16 @@ __device__ __forceinline__ int piece_lanes(const float4& geo, const float4& app,
 // longest lane's count), and any_b is set when some lane of the warp has a pixel B.
 // The fixed coordinate's terms are computed once; q keeps the reference's rounding order
 // ((dx^2 i00 + dx dy 2 i01) + dy^2 i11), and pixel centres are exact (integers + 0.5).
-// Moments: S0 = sum dq (i00 dx + i01 dy), S1 = sum dq (i01 dx + i11 dy) (the mean gradient's two
-// sums, Sigma^-1 applied per lane; the fused fit kernel leaves S0 = sum dq dx, S1 = sum dq dy),
+// Moments: S0 = sum dq dx, S1 = sum dq dy (the Adam kernel applies Sigma^-1),
 // S2 = sum dq dx^2, S3 = sum dq dx dy, S4 = sum dq dy^2,
 // S5..S7 = sum e g_rgb, Sd = sum e g_den, with e = exp(-q/2) and dq = e (g . w c).
 // A lane's pixel keeps its fixed-axis offset f for the whole piece, so the dq moments factor:
-// per pixel only P0 = sum dq, P1 = sum dq v' and P2 = sum dq v^2 (v = varying-axis offset) are
+// per pixel only P0 = sum dq, P1 = sum dq v and P2 = sum dq v^2 (v = varying-axis offset) are
 // accumulated, and f, f^2 are applied once at the end (S for dx-dy = f P1, for f^2 = f^2 P0, ...).
-// CENTER (renderer backward): v' = v - vc, with vc = -i01 f / coef_var the centre of the ellipse
-// along the lane's line (of pixel A), else v' = v. The mean gradient sums
-//   sum dq (c_fix f + c_var v) = (c_fix f + c_var vc) P0 + c_var P1'
-// then combine terms of the size of the result: for a rotated, elongated gaussian c_fix f and
-// c_var v are large and nearly cancel along the line (by the factor i00 i11 / det, which grows with
-// the aspect ratio squared), and accumulating sum dq v itself would carry that cancellation into
-// float32 sums -- measured on the 4K frame's most elongated gaussians (aspect ratio 150-180) up to
-// 6 times the error of the reference's per-pair sums, and no more than them with the centring.
-// The fused fit kernel keeps v' = v (its gradients only steer Adam; one subtraction per step less).
-template <bool ROW, bool DEN, bool CENTER>
+// This octet form serves the fused fit kernel, whose gaussians are small and nearly
+// axis-aligned: its lanes walk whole lines and P1 sums dq v itself (the renderer backward's quad
+// tasks centre each line on its ellipse centre, see backward_quad).
+template <bool ROW, bool DEN>
 __device__ __forceinline__ void backward_piece(const float4& geo, const float4& app, float wt,
                                                float pxc0, float pyc0, int sidx0, int r8,
                                                int start, unsigned a_first, unsigned a_len,
@@ -284,12 +241,6 @@ __device__ __forceinline__ void backward_piece(const float4& geo, const float4& 
   const float coef_fix = ROW ? geo.z : app.x;  // i00 for x, i11 for y
   const float coef_var = ROW ? app.x : geo.z;
   const float t_a = __fmul_rn(sq_a, coef_fix), t_b = __fmul_rn(sq_b, coef_fix);
-  const float i01 = 0.5f * geo.w;
-  float vc = 0.f;  // centre of the ellipse along pixel A's line (varying-axis offset)
-  if constexpr (CENTER) {
-    const float kappa = -__fdividef(i01, coef_var);
-    vc = isfinite(kappa) ? kappa * da : 0.f;
-  }
   constexpr int kStep = ROW ? kGStride : 1;        // shared-memory stride of one step
   constexpr int kLaneStride = ROW ? 1 : kGStride;  // and of one lane-axis pixel
   // The lane's steps [0, count) are the union of pixel A's span (from a_first, a_len steps) and
@@ -329,44 +280,29 @@ __device__ __forceinline__ void backward_piece(const float4& geo, const float4& 
     const float dv = __fsub_rn(fvar, ROW ? geo.y : geo.x);
     const float sq_v = __fmul_rn(dv, dv);
     const float t_v = __fmul_rn(sq_v, coef_var);
-    const float dvc = CENTER ? dv - vc : dv;
     const bool on = st < count;
     {
       const float t1 = __fmul_rn(__fmul_rn(da, dv), geo.w);  // dx dy (multiplication commutes)
       const float q = ROW ? __fadd_rn(__fadd_rn(t_a, t1), t_v) : __fadd_rn(__fadd_rn(t_v, t1), t_a);
-      accumulate(on && has_a && q < cutoff, sidx_a, dvc, sq_v, q, pa);
+      accumulate(on && has_a && q < cutoff, sidx_a, dv, sq_v, q, pa);
     }
     if (any_b) {
       const float t1 = __fmul_rn(__fmul_rn(db, dv), geo.w);
       const float q = ROW ? __fadd_rn(__fadd_rn(t_b, t1), t_v) : __fadd_rn(__fadd_rn(t_v, t1), t_b);
-      accumulate(on && has_b && q < cutoff, sidx_a + 8 * kLaneStride, dvc, sq_v, q, pb);
+      accumulate(on && has_b && q < cutoff, sidx_a + 8 * kLaneStride, dv, sq_v, q, pb);
     }
     fvar += 1.f;
     sidx_a += kStep;
   }
-  // Mean gradient: c_fix, c_var = coefficients of the fixed and the varying offset in
-  // (i00 dx + i01 dy) and (i01 dx + i11 dy).
-  const float cx_fix = ROW ? geo.z : i01, cx_var = ROW ? i01 : geo.z;
-  const float cy_fix = ROW ? i01 : app.x, cy_var = ROW ? app.x : i01;
+  // Plain first moments S0 = sum dq dx, S1 = sum dq dy (the Adam kernel applies Sigma^-1; measured
+  // 1.7 us per launch faster than applying it here at the 48-register cap).
   const float p1 = pa[1] + pb[1];
-  float va, vb;  // sum dq v over pixel A, B
-  if constexpr (CENTER) {
-    S[0] = fmaf(fmaf(cx_var, vc, cx_fix * da), pa[0], fmaf(fmaf(cx_var, vc, cx_fix * db), pb[0], cx_var * p1));
-    S[1] = fmaf(fmaf(cy_var, vc, cy_fix * da), pa[0], fmaf(fmaf(cy_var, vc, cy_fix * db), pb[0], cy_var * p1));
-    va = fmaf(vc, pa[0], pa[1]);  // P1' + vc P0
-    vb = fmaf(vc, pb[0], pb[1]);
-  } else {
-    // Fused fit kernel: plain first moments S0 = sum dq dx, S1 = sum dq dy (the Adam kernel applies
-    // Sigma^-1); measured 1.7 us per launch faster than applying it here at the 48-register cap.
-    const float m_f = fmaf(da, pa[0], db * pb[0]);
-    S[0] = ROW ? m_f : p1;
-    S[1] = ROW ? p1 : m_f;
-    va = pa[1];
-    vb = pb[1];
-  }
+  const float m_f = fmaf(da, pa[0], db * pb[0]);
+  S[0] = ROW ? m_f : p1;
+  S[1] = ROW ? p1 : m_f;
   // Second moments: f^2 P0, f sum dq v and P2, over A and B.
   const float m_ff = fmaf(sq_a, pa[0], sq_b * pb[0]);
-  const float m_fv = fmaf(da, va, db * vb);
+  const float m_fv = fmaf(da, pa[1], db * pb[1]);
   const float m_vv = pa[2] + pb[2];
   S[2] = ROW ? m_ff : m_vv;  // sum dq dx^2
   S[3] = m_fv;               // sum dq dx dy
@@ -422,8 +358,15 @@ __device__ __forceinline__ int piece_quads(const float4& geo, const float4& app,
 }
 
 // One quad lane's part of a renderer-backward piece: the octet's backward_piece with four lines
-// per lane (same rounding of q, same centred moments), each line centred on the ellipse's centre
-// along it and with its own accumulators (sums of the same length as an octet lane's; with one
+// per lane (same rounding of q), each line's varying offset centred on the ellipse's centre along
+// it, v' = v - vc with vc = -i01 f / coef_var, so that the mean gradient's sums
+//   sum dq (c_fix f + c_var v) = (c_fix f + c_var vc) P0 + c_var P1'
+// combine terms of the size of the result: for a rotated, elongated gaussian c_fix f and c_var v
+// are large and nearly cancel along the line (by the factor i00 i11 / det, which grows with the
+// aspect ratio squared), and accumulating sum dq v itself would carry that cancellation into
+// float32 sums -- measured on the 4K frame's most elongated gaussians (aspect ratio 150-180) up to
+// 6 times the error of the reference's per-pair sums, and no more than them with the centring.
+// Every line has its own accumulators (sums of the same length as an octet lane's; with one
 // centre and one second-moment sum shared by the four lines, the band test's worst Cholesky
 // gradient error was 2.5 times the float32 reference's). Lines B, C, D run only when some lane of
 // the warp has one (any_b, any_c, any_d).
@@ -1095,26 +1038,12 @@ raster_kernel(const RasterArgs a) {
           // boundary of the two bucket groups) walks whole lines.
           const bool row = __shfl_sync(0xffffffffu, pw >= ph, 0);
           const int lane_dim = row ? pw : ph, step_dim = row ? ph : pw;
-          // Steps of the lane: whole lines (start 0, pixels on for the piece's step count), or the
-          // ellipse line spans that piece_lanes packed (its own orientation only).
+          // Steps of the lane: whole lines (pixels on for the piece's step count).
           const int my_steps = valid ? step_dim : 0;
-          int start = 0;
-          unsigned a_first = 0, a_len = r8 < lane_dim ? my_steps : 0;
-          unsigned b_first = 0, b_len = r8 + 8 < lane_dim ? my_steps : 0;
-          int max_steps;
-          if constexpr (kSpans) {
-            if (valid && (pw >= ph) == row) {
-              const uint32_t w = s_lanes[8 * j + r8];
-              start = w & 15;
-              a_first = (w >> 4) & 15;
-              a_len = (w >> 8) & 31;
-              b_first = (w >> 13) & 15;
-              b_len = (w >> 17) & 31;
-            }
-            max_steps = static_cast<int>(__reduce_max_sync(0xffffffffu, max(a_first + a_len, b_first + b_len)));
-          } else {
-            max_steps = static_cast<int>(__reduce_max_sync(0xffffffffu, static_cast<unsigned>(my_steps)));
-          }
+          const int start = 0;
+          const unsigned a_first = 0, a_len = r8 < lane_dim ? my_steps : 0;
+          const unsigned b_first = 0, b_len = r8 + 8 < lane_dim ? my_steps : 0;
+          const int max_steps = static_cast<int>(__reduce_max_sync(0xffffffffu, static_cast<unsigned>(my_steps)));
           const bool any_b = __any_sync(0xffffffffu, b_len > 0);
           const float pxc0 = static_cast<float>(ox + rx0) + 0.5f;  // integer + 0.5 sums stay exact
           const float pyc0 = static_cast<float>(oy + ry0) + 0.5f;
@@ -1123,9 +1052,8 @@ raster_kernel(const RasterArgs a) {
           float S[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
           float Sd = 0.f;
   #define RTGS_PIECE(R)                                                                                  \
-    backward_piece<R, DEN, MODE == kBwd>(geo, app, wt, pxc0, pyc0, ry0 * kGStride + rx0, r8, start,   \
-                                         a_first, a_len, b_first, b_len, any_b, max_steps, a.cutoff,  \
-                                         s_g, S, Sd)
+    backward_piece<R, DEN>(geo, app, wt, pxc0, pyc0, ry0 * kGStride + rx0, r8, start, a_first, a_len, \
+                           b_first, b_len, any_b, max_steps, a.cutoff, s_g, S, Sd)
           if (row) RTGS_PIECE(true); else RTGS_PIECE(false);
   #undef RTGS_PIECE
           const float red = octet_transpose_reduce8(S, lane);
