@@ -6,11 +6,12 @@
 //
 // Two ways to build the lists, both deterministic in what the raster kernels read:
 //   tile scatter (default)  the projection counts entries per tile (and in the fit loop emits the
-//                           (tile, id) entries; otherwise emit_kernel does); an inclusive scan of
-//                           the tile counts gives every tile's [start, end); each entry claims a
-//                           slot in its tile by counting that tile's count back down (so the
-//                           counts are zero again for the next projection), and one warp per tile
-//                           then sorts the tile's ids (lists up to kSegSortMax).
+//                           (tile, id) entries); an inclusive scan of the tile counts gives every
+//                           tile's [start, end); each entry claims a slot in its tile by counting
+//                           that tile's count back down (so the counts are zero again for the next
+//                           projection) -- emitted entries one thread each (scatter_kernel), else
+//                           every gaussian its own tiles' slots (place_kernel) -- and one warp per
+//                           tile then sorts the tile's ids (lists up to kSegSortMax).
 //   radix                   entries emitted gaussian-major as (tile key << 32 | id), stable radix
 //                           sort by key (sort.cu), per-tile ranges; used when some tile list is
 //                           longer than kSegSortMax. Emission order must follow the gaussian
@@ -68,6 +69,66 @@ scatter_kernel(const uint64_t* __restrict__ entries, const unsigned long long* _
   const int t = static_cast<int>(v >> 32);
   const int pos = tile_end[t] - atomicSub(&tile_count[t], 1);
   if (pos >= 0 && pos < cap) list[pos] = static_cast<uint32_t>(v);
+}
+
+// The same slots without the entries in between (projections that only counted): one thread per
+// gaussian claims a slot in each of its tiles, tile_end[t] minus the tile count before it counted
+// that count down, and writes its id there. Only entries below the capacity are placed, as
+// emit_kernel + scatter_kernel do. A span of up to kSmallSpan tiles issues its claims together
+// (their round trips overlap) before its stores; longer spans are walked by the whole warp.
+__global__ void __launch_bounds__(kThreads)
+place_kernel(int64_t m, const int* __restrict__ counts, const int* __restrict__ offsets,
+             const TileSpan* __restrict__ spans, int tiles_x, int64_t cap,
+             const int* __restrict__ tile_end, int* __restrict__ tile_count,
+             uint32_t* __restrict__ list) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  int cnt = 0, n_place = 0;
+  TileSpan sp{0, 0, 1, 0};
+  if (i < m) {
+    cnt = counts[i];
+    if (cnt > 0) {
+      const int off = offsets[i];
+      sp = spans[i];
+      const int64_t room = off >= 0 ? cap - off : 0;  // entries off + j below the capacity
+      n_place = static_cast<int>(room < cnt ? (room > 0 ? room : 0) : cnt);
+    }
+  }
+  if (cnt <= kSmallSpan) {
+    int pos[kSmallSpan];
+    int tx = sp.tx0, ty = sp.ty0;
+#pragma unroll
+    for (int j = 0; j < kSmallSpan; ++j) {
+      if (j < n_place) {
+        const int t = sp.key_base + ty * tiles_x + tx;
+        pos[j] = __ldg(&tile_end[t]) - atomicSub(&tile_count[t], 1);
+        if (++tx == sp.tx0 + sp.ntx) {
+          tx = sp.tx0;
+          ++ty;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kSmallSpan; ++j) {
+      if (j < n_place && pos[j] >= 0 && pos[j] < cap) list[pos[j]] = static_cast<uint32_t>(i);
+    }
+  }
+  const int lane = threadIdx.x & 31;
+  unsigned big = __ballot_sync(0xffffffffu, cnt > kSmallSpan);
+  while (big) {
+    const int src = __ffs(big) - 1;
+    big &= big - 1;
+    const int c = __shfl_sync(0xffffffffu, n_place, src);
+    const int tx0 = __shfl_sync(0xffffffffu, sp.tx0, src);
+    const int ty0 = __shfl_sync(0xffffffffu, sp.ty0, src);
+    const int ntx = __shfl_sync(0xffffffffu, sp.ntx, src);
+    const int kb = __shfl_sync(0xffffffffu, sp.key_base, src);
+    const uint32_t g = static_cast<uint32_t>(__shfl_sync(0xffffffffu, static_cast<long long>(i), src));
+    for (int j = lane; j < c; j += 32) {
+      const int t = kb + (ty0 + j / ntx) * tiles_x + tx0 + j % ntx;
+      const int p = __ldg(&tile_end[t]) - atomicSub(&tile_count[t], 1);
+      if (p >= 0 && p < cap) list[p] = g;
+    }
+  }
 }
 
 // One warp per tile: sort list[start, end) ascending (bitonic network over the length padded to a
@@ -369,12 +430,6 @@ int bin_scatter(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s) {
   bb.presorted = false;
   bb.counts_cleared = false;
   if (n_tiles == 0) return 0;
-  if (m > 0 && !bb.entries_emitted && bb.capacity > 0) {
-    emit_kernel<<<grid_for(m), kThreads, 0, s>>>(m, bb.counts.as<int>(), bb.offsets.as<int>(),
-                                                  bb.spans.as<TileSpan>(), g.tiles_x, bb.capacity,
-                                                  nullptr, bb.entries[0].as<uint64_t>());
-    RTGS_CUDA(cudaGetLastError(), "emit_kernel");
-  }
   if (n_tiles <= kSmallScanMax) {
     small_inclusive_scan_kernel<<<1, kSmallScanThreads, 0, s>>>(bb.tile_count.as<int>(),
                                                                 bb.tile_end.as<int>(),
@@ -383,11 +438,17 @@ int bin_scatter(BinBuffers& bb, const Geometry& g, int64_t m, cudaStream_t s) {
   } else {
     RTGS_TRY(cub_scan<true>(bb, bb.tile_count.as<int>(), bb.tile_end.as<int>(), n_tiles, s));
   }
-  if (m > 0 && bb.capacity > 0) {
+  if (m > 0 && bb.capacity > 0 && bb.entries_emitted) {
     scatter_kernel<<<grid_for(bb.capacity), kThreads, 0, s>>>(
         bb.entries[0].as<uint64_t>(), bb.stats.as<unsigned long long>(), bb.capacity,
         bb.tile_end.as<int>(), bb.tile_count.as<int>(), bb.list.as<uint32_t>());
     RTGS_CUDA(cudaGetLastError(), "scatter_kernel");
+  } else if (m > 0 && bb.capacity > 0) {
+    place_kernel<<<grid_for(m), kThreads, 0, s>>>(m, bb.counts.as<int>(), bb.offsets.as<int>(),
+                                                  bb.spans.as<TileSpan>(), g.tiles_x, bb.capacity,
+                                                  bb.tile_end.as<int>(), bb.tile_count.as<int>(),
+                                                  bb.list.as<uint32_t>());
+    RTGS_CUDA(cudaGetLastError(), "place_kernel");
   }
   bb.counts_cleared = true;
   const unsigned blocks = static_cast<unsigned>((n_tiles + kTileSortWarps - 1) / kTileSortWarps);
