@@ -71,21 +71,23 @@ scatter_kernel(const uint64_t* __restrict__ entries, const unsigned long long* _
   if (pos >= 0 && pos < cap) list[pos] = static_cast<uint32_t>(v);
 }
 
-// The same slots without the entries in between (projections that only counted): one thread per
-// gaussian claims a slot in each of its tiles, tile_end[t] minus the tile count before it counted
-// that count down, and writes its id there. Only entries below the capacity are placed, as
-// emit_kernel + scatter_kernel do. A span of up to kSmallSpan tiles issues its claims together
-// (their round trips overlap) before its stores; longer spans are walked by the whole warp.
+// The same slots without the entries in between (projections that only counted): each warp walks
+// the entries of its 32 gaussians in gaussian-major order, 32 per round, lane k taking the round's
+// k-th entry (its gaussian found by a binary search over the warp's inclusive count scan), and
+// claims its slot as scatter_kernel does, tile_end[t] minus the tile count before it counted that
+// count down. Consecutive lanes mostly hit one gaussian's consecutive tiles, so a round's atomics
+// share cache lines, and the lanes stay busy whatever the spans' sizes. Only entries below the
+// capacity are placed, as emit_kernel + scatter_kernel do.
 __global__ void __launch_bounds__(kThreads)
 place_kernel(int64_t m, const int* __restrict__ counts, const int* __restrict__ offsets,
              const TileSpan* __restrict__ spans, int tiles_x, int64_t cap,
              const int* __restrict__ tile_end, int* __restrict__ tile_count,
              uint32_t* __restrict__ list) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
-  int cnt = 0, n_place = 0;
+  int n_place = 0;
   TileSpan sp{0, 0, 1, 0};
   if (i < m) {
-    cnt = counts[i];
+    const int cnt = counts[i];
     if (cnt > 0) {
       const int off = offsets[i];
       sp = spans[i];
@@ -93,40 +95,32 @@ place_kernel(int64_t m, const int* __restrict__ counts, const int* __restrict__ 
       n_place = static_cast<int>(room < cnt ? (room > 0 ? room : 0) : cnt);
     }
   }
-  if (cnt <= kSmallSpan) {
-    int pos[kSmallSpan];
-    int tx = sp.tx0, ty = sp.ty0;
-#pragma unroll
-    for (int j = 0; j < kSmallSpan; ++j) {
-      if (j < n_place) {
-        const int t = sp.key_base + ty * tiles_x + tx;
-        pos[j] = __ldg(&tile_end[t]) - atomicSub(&tile_count[t], 1);
-        if (++tx == sp.tx0 + sp.ntx) {
-          tx = sp.tx0;
-          ++ty;
-        }
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < kSmallSpan; ++j) {
-      if (j < n_place && pos[j] >= 0 && pos[j] < cap) list[pos[j]] = static_cast<uint32_t>(i);
-    }
-  }
   const int lane = threadIdx.x & 31;
-  unsigned big = __ballot_sync(0xffffffffu, cnt > kSmallSpan);
-  while (big) {
-    const int src = __ffs(big) - 1;
-    big &= big - 1;
-    const int c = __shfl_sync(0xffffffffu, n_place, src);
-    const int tx0 = __shfl_sync(0xffffffffu, sp.tx0, src);
-    const int ty0 = __shfl_sync(0xffffffffu, sp.ty0, src);
-    const int ntx = __shfl_sync(0xffffffffu, sp.ntx, src);
-    const int kb = __shfl_sync(0xffffffffu, sp.key_base, src);
-    const uint32_t g = static_cast<uint32_t>(__shfl_sync(0xffffffffu, static_cast<long long>(i), src));
-    for (int j = lane; j < c; j += 32) {
+  int incl = n_place;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += y;
+  }
+  const int excl = incl - n_place;
+  const int total = __shfl_sync(0xffffffffu, incl, 31);
+  for (int base = 0; base < total; base += 32) {
+    const int q = base + lane;
+    int o = 0;  // owner lane: the number of lanes whose inclusive count is <= q
+#pragma unroll
+    for (int step = 16; step >= 1; step >>= 1) {
+      if (__shfl_sync(0xffffffffu, incl, o + step - 1) <= q) o += step;
+    }
+    const int j = q - __shfl_sync(0xffffffffu, excl, o);
+    const int tx0 = __shfl_sync(0xffffffffu, sp.tx0, o);
+    const int ty0 = __shfl_sync(0xffffffffu, sp.ty0, o);
+    const int ntx = __shfl_sync(0xffffffffu, sp.ntx, o);
+    const int kb = __shfl_sync(0xffffffffu, sp.key_base, o);
+    const uint32_t g = static_cast<uint32_t>(__shfl_sync(0xffffffffu, static_cast<int>(i), o));
+    if (q < total) {
       const int t = kb + (ty0 + j / ntx) * tiles_x + tx0 + j % ntx;
-      const int p = __ldg(&tile_end[t]) - atomicSub(&tile_count[t], 1);
-      if (p >= 0 && p < cap) list[p] = g;
+      const int pos = __ldg(&tile_end[t]) - atomicSub(&tile_count[t], 1);
+      if (pos >= 0 && pos < cap) list[pos] = g;
     }
   }
 }
