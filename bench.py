@@ -27,7 +27,7 @@ Also measured in the same run:
             with host images in and all fitted parameters back on the host.
   splat     the 4K micro-benchmark: 1,000,000 fixed gaussians on 3840x2160, forward + backward
             through the renderer C ABI with an N(0,1) upstream gradient (Gpixel.gauss/s), beside
-            the CPU oracle's forward + backward on a 1/16 subset of the gaussians.
+            the CPU oracle's forward + backward on a 1/64 subset of the gaussians.
   single_small  the 128x128 / 2,000-gaussian / 200-iteration fit: on the GPU through the public
             API, and on the CPU with the oracle, timed in full (N = 1).
   cpu_baseline  the CPU oracle (restatement of the reference's pure-PyTorch fit) on the host
@@ -36,6 +36,10 @@ Also measured in the same run:
 
 ``--impl reference`` times only that CPU implementation (rank 0; other ranks exit at once), on
 the same workload and config: each step is 5 oracle iterations from the fit's initial state.
+Every CPU timing renders with the reference's pair chunks (max(64 x width, 65536) pairs per
+index_add, each into a new copy of the frame): that chunk size, not the arithmetic, sets much of
+the reference's CPU time (the oracle's renders do not depend on it, its gradients only to float32
+rounding).
 """
 
 from __future__ import annotations
@@ -152,6 +156,13 @@ def workload_config(name: str, wl: dict, views: int, world: int) -> dict:
     }
 
 
+def orender_budget(wl: dict) -> int:
+    """Pairs per index_add chunk of the reference's torch renderer at this workload's width."""
+    from oracle import render2d as orender
+
+    return orender.reference_budget(wl["width"])
+
+
 def cpu_target(wl: dict, seed: int):
     """(target (H, W, 3), init (xy, chol, color, weight) stacked (1, N, .), mask (1, H, W) or None)
     of the workload on the CPU (oracle render of the sources)."""
@@ -177,9 +188,10 @@ def oracle_seconds_per_iteration(target, state, wl: dict, mask, iters: int = CPU
     """Seconds per iteration of the CPU oracle fit loop (build, render, loss, backward, Adam,
     cosine step) from parameter state ``state``: one untimed iteration, then ``iters`` timed."""
     from oracle import fit as ofit
+    from oracle import render2d as orender
 
     fit = ofit.StackedFit(target[None], tuple(x.detach().cpu().clone() for x in state), wl["iterations"],
-                          lr=1e-2, masks=mask)
+                          lr=1e-2, masks=mask, budget=orender.reference_budget(wl["width"]))
     fit.step(0)
     t0 = time.perf_counter()
     for it in range(1, iters + 1):
@@ -201,7 +213,8 @@ def cpu_fit_estimate(target, states: dict[int, tuple], wl: dict, mask) -> dict:
     return {"value": 1.0 / total, "unit": "fits/s", "cores": torch.get_num_threads(), "kind": "port",
             "sample": f"{wl['height']}x{wl['width']}, {wl['n_fit']} gaussians: {CPU_SAMPLE_ITERS} oracle iterations "
                       f"(after 1 untimed) from the parameter states at iterations {points} of the GPU fit, "
-                      f"seconds per iteration integrated over the {wl['iterations']} iterations (trapezoid)",
+                      f"seconds per iteration integrated over the {wl['iterations']} iterations (trapezoid); "
+                      f"the reference's {orender_budget(wl)}-pair index_add chunks",
             "s_per_iteration_at": {str(k): sec[k] for k in points},
             "start_of_fit_value": 1.0 / (sec[points[0]] * wl["iterations"])}
 
@@ -227,15 +240,17 @@ def run_reference(args, wl, rank: int, world: int) -> None:
         "cpu_baseline": {"value": value, "unit": "fits/s", "cores": torch.get_num_threads(), "kind": "port",
                          "sample": f"each step: {CPU_SAMPLE_ITERS} oracle iterations (after 1 untimed) from the "
                                    f"fit's initial state, {wl['height']}x{wl['width']}, {wl['n_fit']} gaussians; "
-                                   f"median of {args.steps} steps scaled to {wl['iterations']} iterations"},
+                                   f"median of {args.steps} steps scaled to {wl['iterations']} iterations; "
+                                   f"the reference's {orender_budget(wl)}-pair index_add chunks"},
         "e2e": {"value": value, "unit": "fits/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def cpu_splat_sample(stride: int = 16) -> dict:
+def cpu_splat_sample(stride: int = 64) -> dict:
     """CPU oracle forward + backward of the 4K splat on every ``stride``-th gaussian (same upstream
-    gradient); throughput in (gaussian, pixel-in-rectangle) pairs per second."""
+    gradient, the reference's pair chunks); throughput in (gaussian, pixel-in-rectangle) pairs per
+    second. The chunk count grows with the pairs, so the rate does not depend on the stride."""
     from oracle import render2d as orender
     from rtgs_b200.image2gs import synthetic
 
@@ -247,12 +262,13 @@ def cpu_splat_sample(stride: int = 16) -> dict:
     rects = orender.cuda_rects(sub[0][0].detach(), sub[1][0].detach(), h, w)
     pairs = orender.pair_count(rects, torch.isfinite(sub[0][0].detach()).all(1))
     t0 = time.perf_counter()
-    img = orender.render_batched(*sub, h, w)
+    img = orender.render_batched(*sub, h, w, budget=orender.reference_budget(w))
     (img * up).sum().backward()
     dt = time.perf_counter() - t0
     return {"gpairs_per_s": pairs / dt / 1e9, "pairs": pairs, "s": dt, "cores": torch.get_num_threads(),
             "sample": f"one forward + backward of every {stride}th gaussian ({sub[0].shape[1]} of 1,000,000) "
-                      f"on the 3840x2160 frame, oracle renderer"}
+                      f"on the 3840x2160 frame, oracle renderer with the reference's "
+                      f"{orender.reference_budget(w)}-pair index_add chunks"}
 
 
 def single_small_block(device) -> dict:
@@ -278,14 +294,16 @@ def single_small_block(device) -> dict:
         if k > 0:
             times.append(time.perf_counter() - t0)
     torch.set_num_threads(os.cpu_count() or 1)
+    budget = orender_budget(wl)
     t0 = time.perf_counter()
-    _, ohist = ofit.fit_views(target[None], init, wl["iterations"], lr=1e-2, log_every=50)
+    _, ohist = ofit.fit_views(target[None], init, wl["iterations"], lr=1e-2, log_every=50, budget=budget)
     cpu_s = time.perf_counter() - t0
     e2e = 1.0 / statistics.median(times)
     return {"workload": "single_small: 128x128, 500 sources, 2,000 gaussians, 200 iterations",
             "e2e_fits_per_s": e2e, "api": "fit_image_from_initialization (host buffers in and out)",
             "cpu_fits_per_s": 1.0 / cpu_s, "cpu_cores": torch.get_num_threads(),
-            "cpu_sample": "one complete oracle fit (200 iterations + final render), kind port",
+            "cpu_sample": "one complete oracle fit (200 iterations + final render), kind port, with the "
+                          f"reference's {budget}-pair index_add chunks",
             "e2e_vs_cpu": e2e * cpu_s, "final_psnr_gpu": hist["final_psnr"],
             "final_psnr_cpu": ohist[0]["final_psnr"]}
 

@@ -89,8 +89,9 @@ class StackedFit:
     bench.py's CPU baseline times single iterations of it from any parameter state)."""
 
     def __init__(self, targets, init, iterations, lr=1e-2, masks=None, freeze_geometry=False, t_max=None,
-                 appearance=WEIGHT_COLOR_9P):
+                 appearance=WEIGHT_COLOR_9P, budget=render2d.DEFAULT_BUDGET):
         self.targets, self.masks = targets, masks
+        self.budget = budget  # pairs per index_add chunk (the time; gradients only to float32 rounding)
         self.n_views, self.height, self.width = targets.shape[:3]
         self.raw = to_raw(*init, self.height, self.width, appearance)
         names = appearance_names(self.raw) if freeze_geometry else tuple(self.raw)
@@ -112,7 +113,7 @@ class StackedFit:
     def step(self, it: int, log: bool = False) -> None:
         self.opt.zero_grad()
         xy, chol, color, weight = build(self.raw, self.height, self.width)
-        rendered = render2d.render_batched(xy, chol, color, weight, self.height, self.width)
+        rendered = render2d.render_batched(xy, chol, color, weight, self.height, self.width, budget=self.budget)
         if self.masks is None:
             loss = (rendered - self.targets).square().mean(dim=(1, 2, 3)).sum()
         else:
@@ -128,7 +129,7 @@ class StackedFit:
     def finish(self):
         with torch.no_grad():
             xy, chol, color, weight = build(self.raw, self.height, self.width)
-            final = render2d.render_batched(xy, chol, color, weight, self.height, self.width)
+            final = render2d.render_batched(xy, chol, color, weight, self.height, self.width, budget=self.budget)
             for b in range(self.n_views):
                 pred = final[b].clamp(0, 1)
                 self.hist[b]["final_psnr_full"] = psnr(pred, self.targets[b])
@@ -146,6 +147,7 @@ def fit_views(
     freeze_geometry: bool = False,
     t_max: int | None = None,
     appearance: str = WEIGHT_COLOR_9P,
+    budget: int = render2d.DEFAULT_BUDGET,
 ):
     """Fit stacked (B, H, W, 3) targets from a stacked (B, N, .) initialisation.
 
@@ -153,10 +155,11 @@ def fit_views(
     the single-image native fit (the per-view MSE mean is the serial loss); with a (B, H, W) mask
     the loss is the mask-restricted mean and PSNR is ``masked_psnr``. ``t_max`` (default
     ``iterations``) is the cosine schedule's length, so the first iterations of a longer fit can be
-    run alone. ``appearance`` selects the raw appearance parameters (fit.py:381-387).
+    run alone. ``appearance`` selects the raw appearance parameters (fit.py:381-387). ``budget`` is
+    the pairs per index_add chunk (``render2d.reference_budget`` for the reference's).
     """
     fit = StackedFit(targets, init, iterations, lr=lr, masks=masks, freeze_geometry=freeze_geometry, t_max=t_max,
-                     appearance=appearance)
+                     appearance=appearance, budget=budget)
     for it in range(iterations):
         fit.step(it, log=it % log_every == 0 or it == iterations - 1)
     return fit.finish()

@@ -28,6 +28,16 @@ import torch
 
 CUTOFF = 12.0
 TILE = 16
+DEFAULT_BUDGET = 1 << 20  # pairs per index_add chunk in tests (large chunks run fastest here)
+
+
+def reference_budget(width: int, row_chunk: int = 64) -> int:
+    """Pairs per index_add chunk in the reference's torch renderer: max(row_chunk * width, 65536)
+    (renderer2d.py:227) with FitConfig.row_chunk = 64 (fit.py:65). Every chunk adds into a new copy
+    of the whole frame, so the chunk size sets much of the reference's CPU time: the CPU baselines
+    time the oracle with this budget. Renders do not depend on it; gradients only to float32
+    rounding (the order of autograd's scatter-add over a gaussian's pairs)."""
+    return max(int(row_chunk) * int(width), 65_536)
 
 
 def chol_covariance(chol: torch.Tensor) -> torch.Tensor:
@@ -88,7 +98,7 @@ def accumulate(
     n_views: int,
     height: int,
     width: int,
-    budget: int = 1 << 20,
+    budget: int = DEFAULT_BUDGET,
     origin: tuple[int, int] = (0, 0),
     support_inputs: tuple[torch.Tensor, torch.Tensor] | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
@@ -173,6 +183,7 @@ def render_batched(
     width: int,
     with_density: bool = False,
     accumulate_dtype: torch.dtype | None = None,
+    budget: int = DEFAULT_BUDGET,
 ):
     """(B, H, W, 3) render of stacked (B, N, .) gaussians, differentiable (renderer2d.py:72-125).
 
@@ -193,7 +204,8 @@ def render_batched(
         xy_f, color_f, weight_f = xy_f.to(accumulate_dtype), color_f.to(accumulate_dtype), weight_f.to(accumulate_dtype)
         conics = chol_conics(chol_f.to(accumulate_dtype))
     img, den = accumulate(
-        xy_f, conics, color_f, weight_f, rects, view_index, n_views, height, width, support_inputs=support
+        xy_f, conics, color_f, weight_f, rects, view_index, n_views, height, width, budget=budget,
+        support_inputs=support,
     )
     img = img.reshape(n_views, height, width, 3)
     if with_density:
