@@ -166,11 +166,15 @@ def fit_views(
 
 
 def fit_serial(target, init, iterations, lr=1e-2, log_every=50, mask=None, coverage_weight=0.0,
-               appearance=WEIGHT_COLOR_9P):
+               appearance=WEIGHT_COLOR_9P, image=None):
     """The serial native fit loop (fit.py:451-554) of one (H, W, 3) target, with the serial loss
     (fit.py:557-563: MSE, or (0.1 + 0.9 mask)-weighted MSE with a mask) and the optional mask
     coverage penalty weight * mean(coverage * (1 - mask)), coverage = 1 - exp(-density)
     (fit.py:457-459, 566-572; renderer2d.py:128-140). Returns ((xy, chol, color, weight), history).
+
+    With a mask, the reference fits the masked image (target = image * mask, fit.py:333-336) and
+    reports final_psnr = masked_psnr of the final render against the unmasked ``image``
+    (fit.py:546-552; ``image`` defaults to ``target``), final_psnr_full = PSNR against the target.
     """
     height, width = target.shape[:2]
     raw = to_raw(*init, height, width, appearance)
@@ -202,7 +206,9 @@ def fit_serial(target, init, iterations, lr=1e-2, log_every=50, mask=None, cover
     with torch.no_grad():
         params = build(raw, height, width)
         final = render2d.render(*params, height, width)
-    hist["final_psnr"] = psnr(final.clamp(0, 1), target)
+    hist["final_psnr_full"] = psnr(final.clamp(0, 1), target)
+    hist["final_psnr"] = hist["final_psnr_full"] if mask is None else masked_psnr(
+        final.clamp(0, 1), target if image is None else image, mask)
     return tuple(p.detach() for p in params), hist
 
 

@@ -296,9 +296,45 @@ def appearance_fixture(ref_src: str) -> None:
           batched_final_psnr=np.array([h["final_psnr"] for h in hists]))
 
 
+def masked_fixture(ref_src: str) -> None:
+    """11. The masked serial fit (fit.py:309-352, 355-554): crop to the mask's box + margin
+    (fit.py:792-807), target = image * mask, (0.1 + 0.9 mask)-weighted MSE (fit.py:557-563), the
+    optional coverage penalty outside the mask (fit.py:566-572), final_psnr = masked_psnr against
+    the unmasked crop, centres restored by the crop offset. Without and with the penalty."""
+    sys.path.insert(0, ref_src)
+    from rtgs.core.gaussians2d import Gaussians2D
+    from rtgs.data.synthetic import make_synthetic_scene
+    from rtgs.image2gs.fit import FitConfig, _crop_to_mask, fit_image_from_initialization, init_gaussians_2d
+
+    scene = make_synthetic_scene(n_gaussians=25, n_cameras=8, image_size=32, seed=0)
+    image = scene.images[0]
+    mask = torch.zeros(32, 32)
+    mask[8:24, 6:22] = 1.0
+    mask[12:16, 20:26] = 1.0
+    crop, crop_mask, offset = _crop_to_mask(image, mask)
+    g_init = init_gaussians_2d(crop * crop_mask[..., None], 60, 0.7, torch.Generator().manual_seed(3))
+    out = {"image": image, "mask": mask, "crop": crop, "crop_mask": crop_mask, "offset": offset,
+           "init_xy": g_init.xy, "init_chol": g_init.chol, "init_color": g_init.color,
+           "init_weight": g_init.weight}
+    for tag, lam in (("plain", 0.0), ("penalised", 2.0)):
+        cfg = FitConfig(n_gaussians=60, iterations=40, log_every=10, lr=1e-2, mask_coverage_weight=lam)
+        fitted, hist = fit_image_from_initialization(image, Gaussians2D(g_init.xy.clone(), g_init.chol.clone(),
+                                                                        g_init.color.clone(),
+                                                                        g_init.weight.clone()), cfg, mask=mask)
+        out.update({f"{tag}_weight_lambda": lam, f"{tag}_iterations": cfg.iterations,
+                    f"{tag}_log_every": cfg.log_every, f"{tag}_lr": cfg.lr,
+                    f"{tag}_out_xy": fitted.xy, f"{tag}_out_chol": fitted.chol,
+                    f"{tag}_out_color": fitted.color, f"{tag}_out_weight": fitted.weight,
+                    f"{tag}_psnr_iters": np.array([i for i, _ in hist["psnr"]]),
+                    f"{tag}_psnr_vals": np.array([v for _, v in hist["psnr"]]),
+                    f"{tag}_final_psnr": hist["final_psnr"], f"{tag}_final_psnr_full": hist["final_psnr_full"]})
+    _save("fit_masked", **out)
+
+
 if __name__ == "__main__":
     # make_golden.py [REF_SRC] [--only main|pool|adapters|appearance]
-    args = [a for a in sys.argv[1:] if not a.startswith("--") and a not in ("main", "pool", "adapters", "appearance")]
+    args = [a for a in sys.argv[1:]
+            if not a.startswith("--") and a not in ("main", "pool", "adapters", "appearance", "masked")]
     ref = args[0] if args else "/root/reference/src"
     only = sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None
     if only in (None, "main"):
@@ -309,3 +345,5 @@ if __name__ == "__main__":
         adapters_fixture(ref)
     if only in (None, "appearance"):
         appearance_fixture(ref)
+    if only in (None, "masked"):
+        masked_fixture(ref)
