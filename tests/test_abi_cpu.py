@@ -55,3 +55,42 @@ def test_null_arguments_are_rejected_before_any_device_work():
     assert b"NULL" in lib.rtgs2d_last_error()
     rc = lib.rtgs2d_fit_create(1, 4, 8, 8, None, ctypes.byref(ctypes.c_void_p()))
     assert rc == -1
+
+
+def _header_defines() -> dict[str, int]:
+    text = HEADER.read_text()
+    return {m.group(1): int(m.group(2))
+            for m in re.finditer(r"^#define RTGS2D_(\w+)\s+\(?(-?\d+)u?\)?", text, flags=re.M)}
+
+
+def test_python_constants_match_the_header():
+    """The binding's copies of the header's loss, appearance, status and binning codes."""
+    from rtgs_b200.image2gs.engine import FitEngine
+
+    d = _header_defines()
+    for name in ("LOSS_MSE", "LOSS_MASK_WEIGHTED", "LOSS_MASK_ONLY", "APPEARANCE_WEIGHT_COLOR_9P",
+                 "APPEARANCE_UNIT_WEIGHT_8P", "INIT_NONFINITE_RAW"):
+        assert getattr(_native, name) == d[name], name
+    binning = {k[len("BINNING_"):].lower(): v for k, v in d.items() if k.startswith("BINNING_")}
+    assert FitEngine.BINNING_MODES == binning
+    from rtgs_b200.image2gs import optim
+
+    assert optim.MAX_TENSORS == d["ADAM_MAX_TENSORS"]
+
+
+def test_fit_options_layout_matches_the_header(tmp_path):
+    """ctypes' FitOptions has the C struct's size and field offsets (compiled against the header)."""
+    fields = [name for name, _ in _native.FitOptions._fields_]
+    src = tmp_path / "layout.c"
+    src.write_text(
+        "#include <stdio.h>\n#include <stddef.h>\n#include \"rtgs2d.h\"\nint main(void) {\n"
+        "  printf(\"size %zu\\n\", sizeof(rtgs2d_fit_options));\n"
+        + "".join(f"  printf(\"{f} %zu\\n\", offsetof(rtgs2d_fit_options, {f}));\n" for f in fields)
+        + "  return 0;\n}\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c99", "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
+    out = dict(line.split() for line in subprocess.run([str(exe)], check=True, capture_output=True,
+                                                        text=True).stdout.splitlines())
+    assert int(out["size"]) == ctypes.sizeof(_native.FitOptions)
+    for f in fields:
+        assert int(out[f]) == getattr(_native.FitOptions, f).offset, f
