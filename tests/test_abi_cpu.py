@@ -94,3 +94,42 @@ def test_fit_options_layout_matches_the_header(tmp_path):
     assert int(out["size"]) == ctypes.sizeof(_native.FitOptions)
     for f in fields:
         assert int(out[f]) == getattr(_native.FitOptions, f).offset, f
+
+
+_SCALARS = {"int64_t": ctypes.c_int64, "int32_t": ctypes.c_int32, "int": ctypes.c_int,
+            "double": ctypes.c_double, "float": ctypes.c_float, "uint32_t": ctypes.c_uint32,
+            "uint64_t": ctypes.c_uint64, "size_t": ctypes.c_size_t}
+
+
+def _prototypes() -> dict[str, tuple[str, list[str]]]:
+    text = re.sub(r"/\*.*?\*/", " ", HEADER.read_text(), flags=re.S)
+    protos = {}
+    for m in re.finditer(r"^RTGS2D_API\s+([\w\s\*]+?)\s*\b(rtgs2d_\w+)\s*\(([^;]*?)\)\s*;", text, flags=re.M | re.S):
+        params = " ".join(m.group(3).split())
+        args = [] if params in ("", "void") else [p.strip() for p in params.split(",")]
+        protos[m.group(2)] = (" ".join(m.group(1).split()), args)
+    return protos
+
+
+def _is_pointer_type(t) -> bool:
+    return t in (ctypes.c_void_p, ctypes.c_char_p) or (isinstance(t, type) and issubclass(t, ctypes._Pointer))
+
+
+def test_binding_signatures_match_the_header_prototypes():
+    """Every entry point's argument list in the binding against its prototype: the same count,
+    pointers where the header has pointers, and the exact scalar type and width elsewhere."""
+    protos = _prototypes()
+    assert set(protos) == set(_native._SIGNATURES)
+    for name, (ret, args) in protos.items():
+        argtypes, restype = _native._SIGNATURES[name]
+        assert len(argtypes) == len(args), name
+        for c_arg, py in zip(args, argtypes):
+            if "*" in c_arg:
+                assert _is_pointer_type(py), (name, c_arg, py)
+            else:
+                base = c_arg.replace("const ", "").split()[0]
+                assert py is _SCALARS[base], (name, c_arg, py)
+        if "*" in ret:
+            assert _is_pointer_type(restype), (name, ret)
+        else:
+            assert restype is _SCALARS[ret.replace("const ", "")], (name, ret, restype)
