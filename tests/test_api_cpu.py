@@ -235,3 +235,14 @@ def test_loaded_gaussians_round_trip_through_native_npz(tmp_path):
     back = load_gaussians2d(tmp_path / "native.npz")
     for name in ("xy", "chol", "color", "weight"):
         assert torch.equal(getattr(back, name), getattr(g, name))
+
+
+def test_crop_to_mask_matches_reference():
+    """The masked fit's crop to the mask's box + margin (reference fit.py:792-807), against the
+    reference's crop of the golden masked fit."""
+    from rtgs_b200.image2gs.fit import _crop_to_mask
+
+    g = load_golden("fit_masked")
+    crop, crop_mask, offset = _crop_to_mask(t(g["image"]), t(g["mask"]))
+    assert torch.equal(crop, t(g["crop"])) and torch.equal(crop_mask, t(g["crop_mask"]))
+    assert torch.equal(offset, t(g["offset"]))
